@@ -1,0 +1,111 @@
+"""CPU checkers for the quantized GEMV path -- TEST INFRASTRUCTURE ONLY.
+
+Two libraries, both built by oracle/Makefile:
+
+* ``port``      -- oracle/build/liboracle.so, the C restatement in
+                   nexus_oracle.c (bit-identical to the reference build on the
+                   golden vectors).
+* ``reference`` -- oracle/_ref/libnexus_ref.so, NexusLLM's own
+                   src/quantization.cpp compiled unmodified (only present where
+                   the reference sources were available at build time).
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg may
+import this package, and only to check or to time the CPU path; the product
+library never calls into it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PORT_SO = os.path.join(HERE, "build", "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libnexus_ref.so")
+
+# NexusLLM DataType values (include/nexus_common.hpp:244-260)
+_NAMES = {1: "fp16", 7: "q4_0", 9: "q8_0", 11: "q5_k", 12: "q6_k"}
+_VP, _SZ = ctypes.c_void_p, ctypes.c_size_t
+
+
+def _ptr(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(_VP)
+
+
+class _Lib:
+    def __init__(self, path: str, prefix_gemv: str, prefix_deq: str, f16: str):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} is not built (run `make -C oracle`)")
+        self.path = path
+        self.lib = ctypes.CDLL(path)
+        self._g, self._d = prefix_gemv, prefix_deq
+        fn = getattr(self.lib, f16)
+        fn.restype = ctypes.c_float
+        fn.argtypes = [ctypes.c_uint16]
+        self._f16 = fn
+        for name in _NAMES.values():
+            f = getattr(self.lib, prefix_gemv + name)
+            f.restype = None
+            f.argtypes = [_VP, _VP, _VP, _SZ, _SZ]
+
+    def fp16_to_fp32(self, h: int) -> float:
+        return self._f16(h)
+
+    def gemv(self, dtype: int, W: np.ndarray, x: np.ndarray, rows: int, cols: int) -> np.ndarray:
+        """y[rows] = W . x with x float32[cols]; W raw blocks (or uint16 halves)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.zeros(rows, np.float32)
+        getattr(self.lib, self._g + _NAMES[int(dtype)])(_ptr(W), _ptr(x), _ptr(y), rows, cols)
+        return y
+
+    def gemv_batched(self, dtype: int, W: np.ndarray, X: np.ndarray, rows: int, cols: int) -> np.ndarray:
+        """M independent batch-1 GEMVs (the reference has no batched path)."""
+        X = np.ascontiguousarray(X, dtype=np.float32).reshape(-1, cols)
+        return np.stack([self.gemv(dtype, W, X[m], rows, cols) for m in range(X.shape[0])])
+
+    def dequantize(self, dtype: int, W: np.ndarray, count: int) -> np.ndarray:
+        name = _NAMES[int(dtype)]
+        out = np.zeros(count, np.float32)
+        if name == "fp16" and self._d == "ref_dequantize_":
+            # the reference has no named FP16 dequantizer: element-wise decoder
+            return np.array([self.fp16_to_fp32(int(h)) for h in W.reshape(-1)[:count]], np.float32)
+        per = 1 if name == "fp16" else (32 if name in ("q4_0", "q8_0") else 256)
+        f = getattr(self.lib, self._d + name)
+        f.restype = None
+        f.argtypes = [_VP, _VP, _SZ]
+        f(_ptr(W), _ptr(out), count // per)
+        return out
+
+
+def port() -> _Lib:
+    lib = _Lib(PORT_SO, "oracle_gemv_", "oracle_dequantize_", "oracle_fp16_to_fp32")
+    return lib
+
+
+def reference() -> "_Lib":
+    lib = _Lib(REF_SO, "ref_fused_gemv_", "ref_dequantize_", "ref_fp16_to_fp32")
+    f = lib.lib.ref_fused_gemv_threaded
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_uint, _VP, _VP, _VP, _SZ, _SZ, ctypes.c_int]
+    return lib
+
+
+def reference_available() -> bool:
+    return os.path.exists(REF_SO)
+
+
+def gemv_threaded(lib: _Lib, dtype: int, W, x, y, rows: int, cols: int, threads: int) -> None:
+    """The reference's GEMV over `threads` host threads (oracle/ref_driver.cpp)."""
+    rc = lib.lib.ref_fused_gemv_threaded(int(dtype), _ptr(W), _ptr(x), _ptr(y), rows, cols, threads)
+    if rc != 0:
+        raise ValueError(f"ref_fused_gemv_threaded returned {rc}")
+
+
+def l2_rel(a: np.ndarray, b: np.ndarray) -> float:
+    """||a - b||_2 / ||b||_2 in float64 (the parity metric of the north star)."""
+    a = np.asarray(a, np.float64).reshape(-1)
+    b = np.asarray(b, np.float64).reshape(-1)
+    nb = np.linalg.norm(b)
+    return float(np.linalg.norm(a - b) / nb) if nb > 0 else float(np.linalg.norm(a - b))

@@ -1,0 +1,157 @@
+"""Generate tests/golden/golden.npz from NexusLLM's own quantization code.
+
+Run from the repository root, where oracle/_ref/libnexus_ref.so has been
+built from the reference sources (``make -C oracle ref REF=<checkout>``):
+
+    python tests/golden/make_golden.py
+
+Every expected output in the fixture comes from the reference build
+(src/quantization.cpp compiled unmodified with its build.sh flags, AVX2+FMA
+branch).  The one exception is Q8_0 dequantization, which the reference only
+does inline (``out = qs[j] * d``, src/forward_pass.cpp:379-384): its expected
+values are the reference's own fp16 decoder output times the int8 value, one
+float32 multiply, computed here with numpy.
+
+Inputs are seeded (numpy PCG64) and include edge blocks: special fp16 scales
+(zero, subnormal, max, Inf, NaN), extreme quant codes, every Q5_K 6-bit
+scale/min code, negative Q6_K scales, and the constant blocks of the
+reference's own GGUF fixture (tests/test_gguf_binary_mmap.py:62,81 in the
+reference: Q8_0 d=0x3C00 with qs=1, Q4_0 d=0x3C00 with nibbles 0x11).
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, ROOT)
+
+import oracle  # noqa: E402
+from nexusllm_b200 import synth  # noqa: E402
+from nexusllm_b200.formats import DataType  # noqa: E402
+
+OUT = os.path.join(ROOT, "tests", "golden", "golden.npz")
+
+# fp16 bit patterns whose decoding the reference treats specially or that sit
+# on the edges of the format
+FP16_KAT = [0x0000, 0x8000, 0x0001, 0x03FF, 0x0400, 0x3C00, 0x7BFF, 0x7C00, 0xFC00, 0x7E00,
+            0xFFFF, 0x8001, 0x3555, 0xC000, 0x83FF, 0xFBFF]
+D_SPECIAL = [0x0000, 0x8000, 0x0001, 0x03FF, 0x0400, 0x3C00, 0x7BFF, 0x7C00, 0xFC00, 0x7E00, 0xBC00]
+
+GEMV_SHAPES = {
+    DataType.GGUF_Q4_0: [(1, 32), (37, 96), (40, 512), (67, 1024), (3, 4096)],
+    DataType.GGUF_Q8_0: [(1, 32), (37, 96), (40, 512), (67, 1024), (3, 4096)],
+    DataType.GGUF_Q5_K: [(1, 256), (37, 768), (19, 2048), (3, 4096)],
+    DataType.GGUF_Q6_K: [(1, 256), (37, 768), (19, 2048), (3, 4096)],
+    DataType.FP16: [(1, 8), (37, 100), (24, 520), (16, 33), (3, 4096)],
+}
+
+
+def _set_d(a: np.ndarray, off: int, vals) -> None:
+    v = np.asarray(vals, np.uint16)
+    a[: len(v), off] = (v & 0xFF).astype(np.uint8)
+    a[: len(v), off + 1] = (v >> 8).astype(np.uint8)
+
+
+def edge_blocks(dt: DataType, seed: int) -> np.ndarray:
+    """Seeded random blocks with edge cases written into the first rows."""
+    per = 32 if dt in (DataType.GGUF_Q4_0, DataType.GGUF_Q8_0) else 256
+    nb = 64
+    a = synth.blocks_numpy(dt, 1, nb * per, seed).reshape(nb, -1).copy()
+    if dt == DataType.GGUF_Q4_0:
+        _set_d(a, 0, D_SPECIAL)
+        a[11, 2:] = 0x00
+        a[12, 2:] = 0xFF
+        a[13, 0:2] = [0x00, 0x3C]
+        a[13, 2:] = 0x11  # the reference fixture's Q4_0 block (value -7)
+        a[14, 2:] = np.arange(16, dtype=np.uint8) * 17
+    elif dt == DataType.GGUF_Q8_0:
+        _set_d(a, 0, D_SPECIAL)
+        a[11, 2:] = np.uint8(127)
+        a[12, 2:] = np.int8(-127).view(np.uint8)
+        a[13, 2:] = np.int8(-128).view(np.uint8)
+        a[14, 0:2] = [0x00, 0x3C]
+        a[14, 2:] = 1  # the reference fixture's Q8_0 block
+        a[15, 2:] = np.arange(-128, 128, 8).astype(np.int8).view(np.uint8)
+    elif dt == DataType.GGUF_Q5_K:
+        _set_d(a, 0, D_SPECIAL)          # d
+        _set_d(a[11:], 2, D_SPECIAL)     # dmin
+        a[22, 4:16] = 0xFF               # every scale and min = 63 with high bits
+        a[23, 4:16] = 0x00
+        a[24, 4:16] = [0x3F, 0x7F, 0xBF, 0xFF, 0x00, 0x40, 0x80, 0xC0, 0x0F, 0xF0, 0x5A, 0xA5]
+        a[25, 16:48] = 0xFF
+        a[26, 16:48] = 0x00
+        a[27, 16:48] = 0xAA
+        a[28, 16:48] = 0x55
+        a[29, 48:] = 0xFF
+        _set_d(a[30:], 2, [0x0001, 0x0200, 0x03FF, 0x8001])  # dmin subnormal
+    else:  # Q6_K
+        _set_d(a, 208, D_SPECIAL)
+        a[11, 192:208] = np.int8(-128).view(np.uint8)
+        a[12, 192:208] = np.uint8(127)
+        a[13, 192:208] = np.int8(-1).view(np.uint8)
+        a[14, 0:192] = 0xFF              # v = 31 everywhere
+        a[15, 0:192] = 0x00              # v = -32 everywhere
+        a[16, 128:192] = 0xAA
+        a[17, 128:192] = 0x55
+    return a.reshape(-1)
+
+
+def main() -> None:
+    ref = oracle.reference()
+    g = {}
+    f16 = np.array(FP16_KAT, np.uint16)
+    g["fp16/kat_in"] = f16
+    g["fp16/kat_out"] = np.array([ref.fp16_to_fp32(int(h)) for h in FP16_KAT], np.float32)
+    table = np.array([ref.fp16_to_fp32(h) for h in range(65536)], np.float32)
+    g["fp16/table_sha256"] = np.frombuffer(hashlib.sha256(table.tobytes()).digest(), np.uint8)
+
+    # dequantization
+    for i, dt in enumerate([DataType.GGUF_Q4_0, DataType.GGUF_Q8_0, DataType.GGUF_Q5_K, DataType.GGUF_Q6_K]):
+        W = edge_blocks(dt, 9000 + i)
+        per = 32 if dt in (DataType.GGUF_Q4_0, DataType.GGUF_Q8_0) else 256
+        nbytes = 18 if dt == DataType.GGUF_Q4_0 else 34 if dt == DataType.GGUF_Q8_0 else 176 if dt == DataType.GGUF_Q5_K else 210
+        nb = W.size // nbytes
+        if dt == DataType.GGUF_Q8_0:
+            blk = W.reshape(nb, 34)
+            d = np.array([ref.fp16_to_fp32(int(h)) for h in blk[:, 0:2].copy().view(np.uint16).reshape(-1)], np.float32)
+            out = (blk[:, 2:].view(np.int8).astype(np.float32) * d[:, None]).astype(np.float32).reshape(-1)
+        else:
+            out = ref.dequantize(int(dt), W, nb * per)
+        g[f"deq/{int(dt)}/W"] = W
+        g[f"deq/{int(dt)}/out"] = out
+    fp16_all = np.concatenate([np.array(FP16_KAT + D_SPECIAL, np.uint16),
+                               synth.blocks_numpy(DataType.FP16, 1, 230, 9010)])
+    g["deq/1/W"] = fp16_all
+    g["deq/1/out"] = ref.dequantize(1, fp16_all, fp16_all.size)
+
+    # GEMV
+    for dt, shapes in GEMV_SHAPES.items():
+        for j, (rows, cols) in enumerate(shapes):
+            seed = 9100 + 10 * int(dt) + j
+            W = synth.blocks_numpy(dt, rows, cols, seed)
+            x = synth.activations_numpy(1, cols, seed + 5000)[0]
+            y = ref.gemv(int(dt), W, x, rows, cols)
+            key = f"gemv/{int(dt)}/{rows}x{cols}"
+            g[key + "/W"] = W
+            g[key + "/x"] = x
+            g[key + "/y"] = y
+    # the reference's own GGUF fixture blocks (constant), as whole matrices
+    q8 = np.tile(np.concatenate([[0x00, 0x3C], np.ones(32, np.uint8)]).astype(np.uint8), 64 * 2)
+    q4 = np.tile(np.concatenate([[0x00, 0x3C], np.full(16, 0x11, np.uint8)]).astype(np.uint8), 128 * 2)
+    for dt, W, rows, cols in [(DataType.GGUF_Q8_0, q8, 64, 64), (DataType.GGUF_Q4_0, q4, 128, 64)]:
+        x = synth.activations_numpy(1, cols, 9999)[0]
+        key = f"gemv/{int(dt)}/fixture{rows}x{cols}"
+        g[key + "/W"] = W
+        g[key + "/x"] = x
+        g[key + "/y"] = ref.gemv(int(dt), W, x, rows, cols)
+
+    np.savez_compressed(OUT, **g)
+    print(f"wrote {OUT}: {len(g)} arrays, {os.path.getsize(OUT)} bytes")
+
+
+if __name__ == "__main__":
+    main()
