@@ -1,0 +1,503 @@
+"""Benchmark: quantized GEMV HBM throughput and decode layer-stack tokens/s.
+
+Workload (M=1): one decode token through a
+Llama-3-8B-shaped Q4_0 stack -- 32 layers x {q 4096x4096, k 1024x4096,
+v 1024x4096, o 4096x4096, gate 14336x4096, up 14336x4096, down 4096x14336}
+plus the LM head 128256x4096 -- 225 fused GEMVs, 4.22 GB of weights, far
+larger than L2 (so every step streams weights from HBM; no L2 flush needed).
+Within a layer each GEMV consumes the previous one's output (q feeds o as a
+stand-in for attention, o feeds gate and up, gate feeds down); every layer
+starts from the same resident hidden state.  Weights are seeded synthetic
+GGUF blocks with the configuration's distributions (nexusllm_b200/synth.py),
+generated on the device.
+
+A step = one token = the 225 GEMVs, captured once in a CUDA graph and
+replayed.  With --gpus N > 1 (torchrun, one rank per GPU) every matrix is
+row-sharded over the ranks and each GEMV's output slices are all-gathered with
+NCCL (strong scaling: the same model at every N).
+
+Reported (one JSON line on rank 0):
+  value     whole-job algorithmic GB/s = (weight + x + y bytes per step) x
+            steps / device time (max over ranks)
+  e2e       same metric through the reference-facing C ABI with host
+            buffers (N=1: nexus_gpu_gemv_dispatch per GEMV, pinned host x/y,
+            copies and syncs inside the timed region)
+  roofline  the fused Q4_0 GEMV on the FFN matrices (81% of the step's
+            bytes), timed alone with CUDA events, against MEASURED_PEAKS.json
+  cpu_baseline  NexusLLM's own AVX2 GEMV (oracle/_ref) on this host's cores
+            over one decode layer
+
+--impl reference times only the reference CPU path (rank 0), same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HIDDEN, KV, FFN, VOCAB, LAYERS = 4096, 1024, 14336, 128256, 32
+LAYER_SHAPES = [("q", HIDDEN, HIDDEN), ("k", KV, HIDDEN), ("v", KV, HIDDEN), ("o", HIDDEN, HIDDEN),
+                ("gate", FFN, HIDDEN), ("up", FFN, HIDDEN), ("down", HIDDEN, FFN)]
+DTYPE = 7  # GGUF_Q4_0
+NOMINAL_HBM_GBS = 8000.0
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ------------------------------------------------------------------ helpers
+def q4_bytes(rows, cols):
+    return rows * (cols // 32) * 18
+
+
+def step_bytes(include_head=True):
+    b = 0
+    for _, n, k in LAYER_SHAPES:
+        b += q4_bytes(n, k) + 4 * k + 4 * n
+    b *= LAYERS
+    if include_head:
+        b += q4_bytes(VOCAB, HIDDEN) + 4 * HIDDEN + 4 * VOCAB
+    return b
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clock and throttle reasons during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu = gpu_id  # nvidia-smi -i accepts an index or a GPU UUID
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": smax, "reasons": ["no samples"]}
+        load = sorted(sm)[len(sm) // 2:]  # upper half: samples under load
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+# ------------------------------------------------------------ reference arm
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def gpu_uuid(torch, local):
+    try:
+        u = str(torch.cuda.get_device_properties(local).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return str(local)
+
+
+def time_reference_layer(reps: int, threads: int, min_seconds: float = 0.0):
+    """NexusLLM's own GEMV (oracle/_ref, AVX2+FMA) over one decode layer's 7
+    matrices; returns (GB/s, seconds per layer, kind, sample description)."""
+    import numpy as np
+
+    import oracle
+    from nexusllm_b200 import synth
+
+    if oracle.reference_available():
+        lib, kind = oracle.reference(), "reference"
+    else:  # the reference sources were not available at build time
+        lib, kind = oracle.port(), "port"
+    mats = []
+    for i, (name, n, k) in enumerate(LAYER_SHAPES):
+        W = synth.blocks_numpy(DTYPE, n, k, 3000 + i)
+        x = synth.activations_numpy(1, k, 3100 + i)[0]
+        mats.append((W, x, np.zeros(n, np.float32), n, k))
+    layer_bytes = sum(q4_bytes(n, k) + 4 * k + 4 * n for _, n, k in LAYER_SHAPES)
+
+    def run_layer():
+        for W, x, y, n, k in mats:
+            if kind == "reference":
+                oracle.gemv_threaded(lib, DTYPE, W, x, y, n, k, threads)
+            else:
+                y[:] = lib.gemv(DTYPE, W, x, n, k)
+
+    run_layer()  # warm-up (page-in)
+    t = []
+    start = time.perf_counter()
+    while len(t) < reps or time.perf_counter() - start < min_seconds:
+        t0 = time.perf_counter()
+        run_layer()
+        t.append(time.perf_counter() - t0)
+    reps = len(t)
+    sec = statistics.median(t)
+    sample = (f"one Llama-3-8B Q4_0 decode layer (7 GEMVs, {layer_bytes / 1e6:.1f} MB of weights) x {reps}, "
+              f"rows split over {threads} threads, each thread calling the unmodified reference function")
+    return layer_bytes / sec / 1e9, sec, kind, sample
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = cpu_threads()
+    reps = max(1, args.steps)
+    for _ in range(args.warmup):
+        pass
+    gbs, sec, kind, sample = time_reference_layer(reps, threads)
+    reps = max(reps, 1)
+    tok_s = gbs * 1e9 / step_bytes()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": reps, "warmup": args.warmup,
+        "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(args, reference=True),
+        "tokens_per_s": round(tok_s, 6),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+METRIC = "quant GEMV achieved HBM GB/s (% of 8 TB/s) & decode layer-stack tokens/s @1/2/4/8"
+
+
+def workload_config(args, reference=False):
+    return {
+        "workload": "configs[3]: Llama-3-8B Q4_0 decode stack (32 layers x q,k,v,o,gate,up,down + LM head "
+                    "128256x4096), batch M=1, fp32 activations",
+        "model": "Llama-3-8B shapes (hidden 4096, kv 1024, ffn 14336, vocab 128256)",
+        "weight_format": "GGUF Q4_0", "global_batch": 1, "gemvs_per_step": 7 * LAYERS + 1,
+        "parallelism": "cpu" if reference else (f"row-shard x{args.gpus} + NCCL all-gather" if args.gpus > 1
+                                                else "single GPU"),
+        "l2": "working set 4.22 GB per step >> 126 MB L2 (no flush needed)",
+    }
+
+
+# -------------------------------------------------------------- our arm
+def build_stack(torch, rank, world):
+    """Weights for this rank: every matrix's row slice [rank*n/W, (rank+1)*n/W)."""
+    from nexusllm_b200 import synth
+
+    layers = []
+    for l in range(LAYERS):
+        mats = {}
+        for i, (name, n, k) in enumerate(LAYER_SHAPES):
+            nl = n // world
+            mats[name] = synth.blocks_torch(DTYPE, nl, k, 1000 * 3 + 10 * l + i + 100000 * rank)
+        layers.append(mats)
+    head = synth.blocks_torch(DTYPE, VOCAB // world, HIDDEN, 1000 * 3 + 999 + 100000 * rank)
+    return layers, head
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE {world}"
+
+    from nexusllm_b200 import _native
+    from nexusllm_b200.backend import CUDABackend
+
+    be = CUDABackend()
+    L = _native.lib()
+    dev = torch.device("cuda", local)
+    layers, head = build_stack(torch, rank, world)
+    stream = torch.cuda.Stream(dev)
+    h0 = torch.randn(HIDDEN, generator=torch.Generator(device=dev).manual_seed(5), device=dev)
+
+    # activation buffers: full vectors (inputs) and this rank's output slices
+    def buf(n):
+        return torch.empty(n, dtype=torch.float32, device=dev)
+
+    full = {"q": buf(HIDDEN), "k": buf(KV), "v": buf(KV), "o": buf(HIDDEN), "gate": buf(FFN), "up": buf(FFN),
+            "down": buf(HIDDEN), "head": buf(VOCAB)}
+    part = {k: buf(v.numel() // world) for k, v in full.items()}
+    # one workspace, sized for the largest K, passed explicitly (never allocates during capture)
+    ws_bytes = max(L.nexus_gpu_gemv_workspace_size(DTYPE, 1, 1, k) for _, _, k in LAYER_SHAPES)
+    ws = torch.empty(ws_bytes + 256, dtype=torch.uint8, device=dev)
+    inputs_of = {"q": None, "k": None, "v": None, "o": "q", "gate": "o", "up": "o", "down": "gate"}
+    pg = dist.group.WORLD if world > 1 else None
+
+    def gemv(W, x, name):
+        n_local = part[name].numel()
+        k = x.numel()
+        st = torch.cuda.current_stream(dev).cuda_stream
+        rc = L.nexus_gpu_gemv_ws(W.data_ptr(), DTYPE, x.data_ptr(), 0, part[name].data_ptr(), 1, n_local, k,
+                                 ws.data_ptr(), ws.numel(), st)
+        if rc:
+            _native.check(rc)
+        if world > 1:
+            dist.all_gather_into_tensor(full[name], part[name], group=pg)
+            return full[name]
+        return part[name]
+
+    def step():
+        for mats in layers:
+            for name, _, _ in LAYER_SHAPES:
+                src = inputs_of[name]
+                x = h0 if src is None else out[src]
+                out[name] = gemv(mats[name], x, name)
+        out["head"] = gemv(head, h0, "head")
+
+    out = {}
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step()  # eager warm-up before capture (also warms NCCL)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    torch.cuda.synchronize(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def timed(fn, iters):
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(iters):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    for _ in range(args.warmup):
+        graph.replay()
+    with Clocks(gpu_uuid(torch, local)) as clk:
+        ms = timed(graph.replay, args.steps)
+    clocks = clk.summary()
+    sb = step_bytes()
+    value = sb * args.steps / (ms / 1e3) / 1e9
+    ms_step = ms / args.steps
+
+    # ---- roofline: the fused Q4_0 GEMV alone on the 96 FFN matrices
+    ffn = [(mats[name], name) for mats in layers for name in ("gate", "up", "down")]
+    g2 = torch.cuda.CUDAGraph()
+    xin = {"gate": h0, "up": h0, "down": out["gate"]}
+    with torch.cuda.stream(stream):
+        torch.cuda.synchronize(dev)
+        with torch.cuda.graph(g2, stream=stream):
+            for W, name in ffn:
+                k = xin[name].numel()
+                L.nexus_gpu_gemv_ws(W.data_ptr(), DTYPE, xin[name].data_ptr(), 0, part[name].data_ptr(), 1,
+                                    part[name].numel(), k, ws.data_ptr(), ws.numel(),
+                                    torch.cuda.current_stream(dev).cuda_stream)
+    for _ in range(3):
+        g2.replay()
+    reps = max(3, args.steps // 5)
+    ms_ffn = timed(g2.replay, reps)
+    launches = len(ffn) * reps
+    ffn_bytes = sum(W.numel() + 4 * (FFN if n == "down" else HIDDEN) + 4 * part[n].numel() for W, n in ffn)
+    avg_launch_us = ms_ffn * 1e3 / launches
+    peak, peak_kind = load_peaks()
+    achieved = ffn_bytes / len(ffn) / (avg_launch_us * 1e-6) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                "kernel": "gemv_m1_kernel<FmtQ4_0> (+ xquant_kernel), FFN 14336x4096 / 4096x14336",
+                "bytes_per_launch": int(ffn_bytes / len(ffn)), "avg_launch_us": round(avg_launch_us, 3),
+                "traffic": TRAFFIC_PER_FFN_LAUNCH}
+
+    # ---- e2e
+    e2e = None
+    if world == 1:
+        e2e = e2e_host_api(torch, L, layers, head, h0, args)
+    else:
+        e2e = e2e_resident(torch, graph, h0, full, stream, dev, args, timed, sb)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        gbs, sec, kind, sample = time_reference_layer(3, cpu_threads(), min_seconds=10.0)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cpu_threads(), "kind": kind, "sample": sample}
+
+    launches_per_step = 2 * (7 * LAYERS + 1)  # xquant + fused GEMV per call
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8+fp32",
+        "dtype_note": "Q4_0 codes x 16-bit fixed-point x in int8 dp4a limbs, fp32 accumulation",
+        "data": "synthetic (seeded GGUF Q4_0 blocks, x ~ N(0,1))",
+        "config": workload_config(args),
+        "pct_of_8tbs": round(100 * value / NOMINAL_HBM_GBS, 2),
+        "pct_of_measured_hbm": round(100 * value / peak, 2),
+        "tokens_per_s": round(1e3 / ms_step, 2),
+        "gemv_calls_per_s": round((7 * LAYERS + 1) * 1e3 / ms_step, 1),
+        "bytes_per_step": sb,
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
+        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches_note": f"{launches_per_step} per step (xquant + gemv per GEMV) x {args.steps} steps"
+                             + (f"; plus {7 * LAYERS + 1} NCCL all-gathers per step" if world > 1 else ""),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graph, g2
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+# bytes read + written by one FFN launch in an ncu capture (profiles/); None
+# until a capture has been summarised there
+TRAFFIC_PER_FFN_LAUNCH = None
+
+
+def e2e_host_api(torch, L, layers, head, h0, args):
+    """The same step through the reference-facing C ABI: nexus_gpu_gemv_dispatch
+    with HOST weights (cached on the device after the first call), host x and
+    host y (pinned), one synchronous call per GEMV as the reference's forward
+    pass makes them (src/forward_pass.cpp:504-585)."""
+    import numpy as np
+
+    host_layers = [{n: W.cpu().numpy() for n, W in mats.items()} for mats in layers]
+    host_head = head.cpu().numpy()
+
+    def pinned(n):
+        return torch.empty(n, dtype=torch.float32, pin_memory=True).numpy()
+
+    hx = pinned(HIDDEN)
+    hx[:] = h0.cpu().numpy()
+    outs = {"q": pinned(HIDDEN), "k": pinned(KV), "v": pinned(KV), "o": pinned(HIDDEN), "gate": pinned(FFN),
+            "up": pinned(FFN), "down": pinned(HIDDEN), "head": pinned(VOCAB)}
+    srcs = {"q": hx, "k": hx, "v": hx, "o": outs["q"], "gate": outs["o"], "up": outs["o"], "down": outs["gate"]}
+    h2d = d2h = 0
+    for _, n, k in LAYER_SHAPES:
+        h2d += 4 * k
+        d2h += 4 * n
+    h2d = h2d * LAYERS + 4 * HIDDEN
+    d2h = d2h * LAYERS + 4 * VOCAB
+
+    def step():
+        for hm in host_layers:
+            for name, n, k in LAYER_SHAPES:
+                rc = L.nexus_gpu_gemv_dispatch(hm[name].ctypes.data, DTYPE, srcs[name].ctypes.data,
+                                               outs[name].ctypes.data, n, k)
+                if rc:
+                    raise RuntimeError(L.nexus_gpu_last_error())
+        rc = L.nexus_gpu_gemv_dispatch(host_head.ctypes.data, DTYPE, hx.ctypes.data, outs["head"].ctypes.data,
+                                       VOCAB, HIDDEN)
+        if rc:
+            raise RuntimeError(L.nexus_gpu_last_error())
+
+    for _ in range(3):
+        step()  # first call uploads every weight into the device cache
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        step()
+    sec = (time.perf_counter() - t0) / args.e2e_steps
+    L.nexus_gpu_weight_cache_invalidate(None)
+    del host_layers, host_head
+    return {"value": round(step_bytes() / sec / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": round(sec * 1e3, 3), "tokens_per_s": round(1 / sec, 2),
+            "api": "nexus_gpu_gemv_dispatch (host pointers, synchronous, weights cached on device)",
+            "steps": args.e2e_steps}
+
+
+def e2e_resident(torch, graph, h0, full, stream, dev, args, timed, sb):
+    """N > 1: per step, the token's hidden state comes from pinned host memory
+    and the logits go back to pinned host memory around the graph replay."""
+    hin = torch.empty(HIDDEN, dtype=torch.float32, pin_memory=True)
+    hin.copy_(h0.cpu())
+    hout = torch.empty(VOCAB, dtype=torch.float32, pin_memory=True)
+
+    def one():
+        h0.copy_(hin, non_blocking=True)
+        graph.replay()
+        hout.copy_(full["head"], non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        ms = timed(one, args.e2e_steps)
+    return {"value": round(sb * args.e2e_steps / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
+            "h2d_bytes_per_step": 4 * HIDDEN, "d2h_bytes_per_step": 4 * VOCAB,
+            "api": "device-resident stack; host hidden state in, host logits out per step"}
+
+
+if __name__ == "__main__":
+    main()

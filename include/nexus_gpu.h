@@ -1,0 +1,172 @@
+/*
+ * nexus_gpu.h -- C ABI of libnexus_gpu.so, the B200 (sm_100a) implementation
+ * of NexusLLM's fused quantized GEMV path.
+ *
+ * Plain C types only (pointers, sizes, integers); no CUDA or torch types in
+ * any signature.  CUDA streams are passed as `void*` (a cudaStream_t; NULL
+ * means the legacy default stream).
+ *
+ * Three layers, each replacing one reference interface:
+ *
+ *  1. Drop-in kernels with the reference's own signatures and semantics:
+ *     host pointers in, host pointers out, synchronous, `void` return.
+ *     They replace nexus::QuantizationKernel::fused_gemv_* and
+ *     dequantize_gguf_* (include/quantization.hpp:80-153) and follow the C ABI
+ *     precedent nexus_fused_gemv_int4/fp8 (include/nexus_abi.h:136-150,
+ *     src/nexus_abi.cpp:462-480).  Weight matrices are uploaded once and kept
+ *     in a device cache keyed by (host pointer, dtype, rows, cols); see
+ *     nexus_gpu_weight_cache_invalidate.  On error they print one line to
+ *     stderr and leave y untouched, as a void function must.
+ *
+ *  2. The backend hook INexusComputeBackend::gemv_dispatch
+ *     (include/nexus_backend.hpp:55-62; CUDABackend at
+ *     src/nexus_backend.cpp:239-367) plus the backend's device-memory calls
+ *     (allocate_device_memory / copy_*_async / synchronize,
+ *     include/nexus_backend.hpp:46-52).  Same argument meaning; returns a
+ *     NexusStatus value instead of void.
+ *
+ *  3. The device-pointer API, asynchronous on a caller's stream, for callers
+ *     that keep weights and activations resident in HBM (batched M >= 1,
+ *     fp32 or bf16 activations).  New in this library; no reference
+ *     counterpart (the reference has no device memory and no batched GEMV).
+ *
+ * Status codes are NexusStatus values (include/nexus_common.hpp:329-340),
+ * extended with NEXUS_GPU_ERROR_* below for conditions the reference has no
+ * code for.
+ */
+#ifndef NEXUS_GPU_H
+#define NEXUS_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NEXUS_GPU_API __attribute__((visibility("default")))
+
+/* nexus::DataType values (include/nexus_common.hpp:244-260) accepted here. */
+enum {
+    NEXUS_GPU_FP32 = 0,      /* activations only */
+    NEXUS_GPU_FP16 = 1,
+    NEXUS_GPU_BF16 = 2,      /* activations only */
+    NEXUS_GPU_GGUF_Q4_0 = 7,
+    NEXUS_GPU_GGUF_Q8_0 = 9,
+    NEXUS_GPU_GGUF_Q5_K = 11,
+    NEXUS_GPU_GGUF_Q6_K = 12
+};
+
+/* NexusStatus (include/nexus_common.hpp:329-340) */
+enum {
+    NEXUS_GPU_SUCCESS = 0,
+    NEXUS_GPU_ERROR_OUT_OF_HOST_MEMORY = -1,
+    NEXUS_GPU_ERROR_OUT_OF_TIER0_MEMORY = -2, /* cudaMalloc failed */
+    NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED = -3,
+    NEXUS_GPU_ERROR_SHAPE_MISMATCH = -5,      /* cols not a whole number of blocks */
+    NEXUS_GPU_ERROR_INVALID_ARGUMENT = -9,
+    /* no NexusStatus equivalent: */
+    NEXUS_GPU_ERROR_CUDA = -100,              /* a CUDA runtime call failed */
+    NEXUS_GPU_ERROR_NO_DEVICE = -101,
+    NEXUS_GPU_ERROR_WORKSPACE = -102,         /* workspace too small (and cannot grow now) */
+    NEXUS_GPU_ERROR_TIMEOUT = -103            /* a bounded device-side wait expired */
+};
+
+/* ---------------------------------------------------------------- layer 1 */
+
+/* QuantizationKernel::fused_gemv_q4_0 (include/quantization.hpp:116-120):
+ * y[rows] = W[rows, cols] . x[cols]; W is rows*cols/32 BlockQ4_0 (18 B). */
+NEXUS_GPU_API void nexus_fused_gemv_q4_0(const void* W_q4, const float* x, float* y, size_t rows, size_t cols);
+/* QuantizationKernel::fused_gemv_q8_0 (include/quantization.hpp:122-126); BlockQ8_0 (34 B). */
+NEXUS_GPU_API void nexus_fused_gemv_q8_0(const void* W_q8, const float* x, float* y, size_t rows, size_t cols);
+/* QuantizationKernel::fused_gemv_fp16 (include/quantization.hpp:128-132); W is rows*cols halves,
+ * decoded with the reference's fp16_to_fp32 (include/quantization.hpp:59-70). */
+NEXUS_GPU_API void nexus_fused_gemv_fp16(const uint16_t* W_fp16, const float* x, float* y, size_t rows,
+                                         size_t cols);
+/* QuantizationKernel::fused_gemv_q5_k (include/quantization.hpp:143-147); BlockQ5_K (176 B). */
+NEXUS_GPU_API void nexus_fused_gemv_q5_k(const void* W_q5_k, const float* x, float* y, size_t rows, size_t cols);
+/* QuantizationKernel::fused_gemv_q6_k (include/quantization.hpp:149-153); BlockQ6_K (210 B). */
+NEXUS_GPU_API void nexus_fused_gemv_q6_k(const void* W_q6_k, const float* x, float* y, size_t rows, size_t cols);
+
+/* QuantizationKernel::dequantize_gguf_q4_0 / _q5_k / _q6_k (include/quantization.hpp:80-83,135-141):
+ * host blocks in, host floats out (32 or 256 per block), bit-exact. */
+NEXUS_GPU_API void nexus_dequantize_gguf_q4_0(const void* blocks, float* output, size_t num_blocks);
+NEXUS_GPU_API void nexus_dequantize_gguf_q5_k(const void* blocks, float* output, size_t num_blocks);
+NEXUS_GPU_API void nexus_dequantize_gguf_q6_k(const void* blocks, float* output, size_t num_blocks);
+
+/* ---------------------------------------------------------------- layer 2 */
+
+/* INexusComputeBackend::gemv_dispatch (include/nexus_backend.hpp:55-62) on the
+ * CUDA device: host W (cached on the device), host x and y, synchronous.
+ * W == NULL is a no-op returning SUCCESS, like TransformerOps::matmul_vec_dispatch
+ * (include/transformer_ops.hpp:158).  FP32 weights are not handled here
+ * (FORMAT_UNSUPPORTED): the reference's FP32 path is TransformerOps::matmul_vec. */
+NEXUS_GPU_API int32_t nexus_gpu_gemv_dispatch(const void* W, uint32_t dtype, const float* x, float* y, size_t rows,
+                                              size_t cols);
+
+/* INexusComputeBackend::allocate_device_memory / free_device_memory /
+ * copy_host_to_device_async / copy_device_to_host_async / synchronize
+ * (include/nexus_backend.hpp:46-52) for the current CUDA device. */
+NEXUS_GPU_API void* nexus_gpu_allocate_device_memory(size_t bytes);
+NEXUS_GPU_API void nexus_gpu_free_device_memory(void* ptr);
+NEXUS_GPU_API int32_t nexus_gpu_copy_host_to_device_async(void* dst_device, const void* src_host, size_t bytes,
+                                                           void* stream);
+NEXUS_GPU_API int32_t nexus_gpu_copy_device_to_host_async(void* dst_host, const void* src_device, size_t bytes,
+                                                           void* stream);
+NEXUS_GPU_API int32_t nexus_gpu_synchronize(void* stream);
+
+/* Drop the cached device copy of a host weight buffer (call when the host
+ * buffer is reused for another tensor, e.g. a recycled tier-0 slot,
+ * src/memory_tier.cpp:341-356).  NULL drops every cached weight of the
+ * current device.  The cache also re-uploads by itself when a sampled
+ * fingerprint of the host bytes changes, but only this call is a guarantee. */
+NEXUS_GPU_API int32_t nexus_gpu_weight_cache_invalidate(const void* host_W);
+/* Bytes of device memory currently held by the weight cache. */
+NEXUS_GPU_API size_t nexus_gpu_weight_cache_bytes(void);
+
+/* ---------------------------------------------------------------- layer 3 */
+
+/* Exact weight bytes of a rows x cols matrix in `dtype` (0 if unsupported). */
+NEXUS_GPU_API size_t nexus_gpu_weight_bytes(uint32_t dtype, size_t rows, size_t cols);
+
+/* Y[M, rows] = X[M, cols] . W[rows, cols]^T on the device, asynchronous on
+ * `stream`.  dW, dX, dY are device pointers; X and Y are row-major with
+ * leading dimensions cols and rows.  x_dtype is NEXUS_GPU_FP32 or
+ * NEXUS_GPU_BF16.  Scratch space comes from a per-(device, stream) workspace
+ * that the library grows with cudaMalloc when needed; it never grows while
+ * the stream is capturing a CUDA graph (WORKSPACE is returned instead: make
+ * one uncaptured call with the same shapes first, or use nexus_gpu_gemv_ws). */
+NEXUS_GPU_API int32_t nexus_gpu_gemv(const void* dW, uint32_t dtype, const void* dX, uint32_t x_dtype, float* dY,
+                                     size_t M, size_t rows, size_t cols, void* stream);
+
+/* Scratch bytes nexus_gpu_gemv_ws needs for these shapes. */
+NEXUS_GPU_API size_t nexus_gpu_gemv_workspace_size(uint32_t dtype, size_t M, size_t rows, size_t cols);
+
+/* nexus_gpu_gemv with caller-owned scratch (device memory, 256-byte aligned,
+ * at least nexus_gpu_gemv_workspace_size bytes).  Never allocates. */
+NEXUS_GPU_API int32_t nexus_gpu_gemv_ws(const void* dW, uint32_t dtype, const void* dX, uint32_t x_dtype, float* dY,
+                                        size_t M, size_t rows, size_t cols, void* workspace,
+                                        size_t workspace_bytes, void* stream);
+
+/* Bit-exact dequantization of `count` elements (a whole number of blocks)
+ * from device blocks to device floats, asynchronous on `stream`. */
+NEXUS_GPU_API int32_t nexus_gpu_dequantize(const void* dW, uint32_t dtype, float* dOut, size_t count, void* stream);
+
+/* ------------------------------------------------------------- diagnostics */
+
+/* Message of the last error on the calling thread ("" if none). */
+NEXUS_GPU_API const char* nexus_gpu_last_error(void);
+/* Reads and clears the device-side status word of the current device
+ * (bit 0: a bounded wait expired).  Synchronizes the device. */
+NEXUS_GPU_API int32_t nexus_gpu_device_status(uint32_t* out_bits);
+/* Name of the device, SM count and compute capability of the current device. */
+NEXUS_GPU_API int32_t nexus_gpu_device_info(char* name, size_t name_len, int* sm_count, int* cc_major,
+                                            int* cc_minor);
+/* Library version string. */
+NEXUS_GPU_API const char* nexus_gpu_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NEXUS_GPU_H */

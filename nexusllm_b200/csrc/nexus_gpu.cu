@@ -1,0 +1,591 @@
+// nexus_gpu.cu -- host side of libnexus_gpu.so: the C ABI declared in
+// include/nexus_gpu.h, per-device contexts (stream, workspace, weight cache)
+// and kernel launchers.  Device code lives in gemv_kernels.cuh.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/nexus_gpu.h"
+#include "gemv_kernels.cuh"
+
+namespace nexus_gpu {
+namespace {
+
+thread_local std::string t_last_error;
+
+int32_t fail(int32_t code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return code;
+}
+
+#define CUDA_TRY(expr)                                                                               \
+    do {                                                                                             \
+        cudaError_t e_ = (expr);                                                                     \
+        if (e_ != cudaSuccess)                                                                       \
+            return fail(e_ == cudaErrorMemoryAllocation ? NEXUS_GPU_ERROR_OUT_OF_TIER0_MEMORY       \
+                                                        : NEXUS_GPU_ERROR_CUDA,                     \
+                        "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, __LINE__); \
+    } while (0)
+
+// ---------------------------------------------------------------- formats
+struct FormatInfo {
+    int elems;      // elements per block
+    int bytes;      // bytes per block
+};
+
+bool format_info(uint32_t dtype, FormatInfo& f) {
+    switch (dtype) {
+        case NEXUS_GPU_FP16: f = {1, 2}; return true;
+        case NEXUS_GPU_GGUF_Q4_0: f = {32, 18}; return true;
+        case NEXUS_GPU_GGUF_Q8_0: f = {32, 34}; return true;
+        case NEXUS_GPU_GGUF_Q5_K: f = {256, 176}; return true;
+        case NEXUS_GPU_GGUF_Q6_K: f = {256, 210}; return true;
+        default: return false;
+    }
+}
+
+int32_t check_shape(uint32_t dtype, size_t rows, size_t cols, FormatInfo& f) {
+    if (!format_info(dtype, f)) return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "unsupported weight dtype %u", dtype);
+    if (cols % (size_t)f.elems != 0)
+        return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "cols=%zu is not a multiple of the block size %d", cols, f.elems);
+    if (rows > (size_t)INT32_MAX || cols > (size_t)INT32_MAX)
+        return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "rows/cols exceed 2^31-1");
+    return NEXUS_GPU_SUCCESS;
+}
+
+size_t row_bytes_of(const FormatInfo& f, size_t cols) { return cols / (size_t)f.elems * (size_t)f.bytes; }
+
+bool is_int_format(uint32_t dtype) { return dtype != NEXUS_GPU_FP16; }
+
+size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// workspace: xq limbs [M][K/32][64] then meta [M][K/32][16 B]
+size_t xq_bytes(uint32_t dtype, size_t M, size_t cols) {
+    if (!is_int_format(dtype)) return 0;
+    const size_t nxb = cols / 32;
+    return align256(M * nxb * kXQLimbBytes) + align256(M * nxb * kXQMetaBytes);
+}
+
+// --------------------------------------------------------------- contexts
+struct CachedWeight {
+    void* dptr = nullptr;
+    size_t bytes = 0;
+    uint64_t fingerprint = 0;
+};
+
+struct Workspace {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+
+struct Device {
+    int id = -1;
+    int sms = 0;
+    int smem_optin = 0;
+    cudaStream_t stream = nullptr;  // stream of the synchronous host-pointer API
+    std::mutex mu;
+    std::unordered_map<std::string, CachedWeight> cache;
+    size_t cache_bytes = 0;
+    std::unordered_map<cudaStream_t, Workspace> ws;
+    void* dx = nullptr;
+    size_t dx_cap = 0;
+    void* dy = nullptr;
+    size_t dy_cap = 0;
+    bool smem_attr_set = false;
+};
+
+std::mutex g_devices_mu;
+std::vector<std::unique_ptr<Device>> g_devices;
+
+int32_t get_device(Device** out) {
+    int id = 0;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return fail(NEXUS_GPU_ERROR_NO_DEVICE, "no CUDA device");
+    }
+    CUDA_TRY(cudaGetDevice(&id));
+    std::lock_guard<std::mutex> lk(g_devices_mu);
+    if ((int)g_devices.size() < n) g_devices.resize(n);
+    if (!g_devices[id]) {
+        auto d = std::make_unique<Device>();
+        d->id = id;
+        CUDA_TRY(cudaDeviceGetAttribute(&d->sms, cudaDevAttrMultiProcessorCount, id));
+        CUDA_TRY(cudaDeviceGetAttribute(&d->smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, id));
+        CUDA_TRY(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
+        g_devices[id] = std::move(d);
+    }
+    *out = g_devices[id].get();
+    return NEXUS_GPU_SUCCESS;
+}
+
+template <class F>
+int32_t set_smem_attr(int bytes) {
+    CUDA_TRY(cudaFuncSetAttribute(gemv_m1_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    return NEXUS_GPU_SUCCESS;
+}
+
+int32_t ensure_attrs(Device& d) {
+    if (d.smem_attr_set) return NEXUS_GPU_SUCCESS;
+    int32_t rc;
+    if ((rc = set_smem_attr<FmtQ4_0>(d.smem_optin))) return rc;
+    if ((rc = set_smem_attr<FmtQ8_0>(d.smem_optin))) return rc;
+    if ((rc = set_smem_attr<FmtQ5_K>(d.smem_optin))) return rc;
+    if ((rc = set_smem_attr<FmtQ6_K>(d.smem_optin))) return rc;
+    if ((rc = set_smem_attr<FmtF16>(d.smem_optin))) return rc;
+    d.smem_attr_set = true;
+    return NEXUS_GPU_SUCCESS;
+}
+
+// ---------------------------------------------------------------- launches
+template <class Kern, class... Args>
+int32_t launch(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, args...));
+    return NEXUS_GPU_SUCCESS;
+}
+
+template <class F>
+int32_t launch_fast(Device& d, const GemvParams& p, cudaStream_t st) {
+    const size_t smem = Layout<F>::smem_bytes(p.K);
+    const int grid = std::min(d.sms, p.N);
+    return launch(gemv_m1_kernel<F>, dim3(grid), dim3(kGemvThreads), smem, st, p);
+}
+
+template <class F>
+bool fast_fits(const Device& d, int K) {
+    return Layout<F>::smem_bytes(K) <= (size_t)d.smem_optin;
+}
+
+// One GEMV of M rows of x.  `ws` holds at least xq_bytes(dtype, M, cols).
+int32_t run_gemv(Device& d, const void* dW, uint32_t dtype, const void* dX, uint32_t x_dtype, float* dY, size_t M,
+                 size_t rows, size_t cols, uint8_t* ws, cudaStream_t st) {
+    FormatInfo f;
+    int32_t rc = check_shape(dtype, rows, cols, f);
+    if (rc) return rc;
+    if (x_dtype != NEXUS_GPU_FP32 && x_dtype != NEXUS_GPU_BF16)
+        return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "unsupported activation dtype %u", x_dtype);
+    if (M == 0 || rows == 0) return NEXUS_GPU_SUCCESS;
+    if (cols == 0) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "cols == 0");
+    if (!dW || !dX || !dY) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null device pointer");
+    if ((rc = ensure_attrs(d))) return rc;
+    const int K = (int)cols, N = (int)rows;
+    const size_t rb = row_bytes_of(f, cols);
+    const bool w16 = ((uintptr_t)dW & 15) == 0;
+    const int xbf = x_dtype == NEXUS_GPU_BF16;
+    const size_t xes = xbf ? 2 : 4;
+    const size_t nxb = cols / 32;
+    uint8_t* limbs = ws;
+    int4* meta = is_int_format(dtype) ? reinterpret_cast<int4*>(ws + align256(M * nxb * kXQLimbBytes)) : nullptr;
+
+    bool fast = w16;
+    switch (dtype) {
+        case NEXUS_GPU_GGUF_Q4_0: fast = fast && fast_fits<FmtQ4_0>(d, K); break;
+        case NEXUS_GPU_GGUF_Q8_0: fast = fast && fast_fits<FmtQ8_0>(d, K); break;
+        case NEXUS_GPU_GGUF_Q5_K: fast = fast && fast_fits<FmtQ5_K>(d, K); break;
+        case NEXUS_GPU_GGUF_Q6_K: fast = fast && fast_fits<FmtQ6_K>(d, K); break;
+        default: fast = fast && (K % 16 == 0) && fast_fits<FmtF16>(d, K); break;
+    }
+    if (fast && is_int_format(dtype)) {
+        dim3 g((unsigned)((nxb + 7) / 8), (unsigned)M);
+        if ((rc = launch(xquant_kernel, g, dim3(256), 0, st, dX, xbf, K, K, limbs, meta))) return rc;
+    }
+    for (size_t m = 0; m < M; ++m) {
+        const uint8_t* xm = static_cast<const uint8_t*>(dX) + m * cols * xes;
+        float* ym = dY + m * rows;
+        if (!fast) {
+            const int blocks = (N + 7) / 8;
+            if ((rc = launch(gemv_generic_kernel, dim3(blocks), dim3(256), 0, st, (int)dtype,
+                             static_cast<const uint8_t*>(dW), (uint64_t)rb, N, K, (const void*)xm, xbf, ym)))
+                return rc;
+            continue;
+        }
+        GemvParams p{};
+        p.W = static_cast<const uint8_t*>(dW);
+        p.total_bytes = (uint64_t)rb * rows;
+        p.row_bytes = rb;
+        p.N = N;
+        p.K = K;
+        p.y = ym;
+        p.x = xm;
+        p.x_bf16 = xbf;
+        p.xq_limbs = limbs + m * nxb * kXQLimbBytes;
+        p.xq_meta = meta ? meta + m * nxb : nullptr;
+        switch (dtype) {
+            case NEXUS_GPU_GGUF_Q4_0: p.nwi = K / 32; rc = launch_fast<FmtQ4_0>(d, p, st); break;
+            case NEXUS_GPU_GGUF_Q8_0: p.nwi = K / 32; rc = launch_fast<FmtQ8_0>(d, p, st); break;
+            case NEXUS_GPU_GGUF_Q5_K: p.nwi = K / 32; rc = launch_fast<FmtQ5_K>(d, p, st); break;
+            case NEXUS_GPU_GGUF_Q6_K: p.nwi = K / 32; rc = launch_fast<FmtQ6_K>(d, p, st); break;
+            default: p.nwi = K / 16; rc = launch_fast<FmtF16>(d, p, st); break;
+        }
+        if (rc) return rc;
+    }
+    return NEXUS_GPU_SUCCESS;
+}
+
+// ----------------------------------------------------------- dequantization
+__global__ void dequant_kernel(int dtype, const uint8_t* __restrict__ W, float* __restrict__ out, uint64_t count) {
+    const uint64_t i0 = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (i0 >= count) return;
+    float v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) v[k] = (i0 + k < count) ? deq_elem(dtype, W, i0 + k) : 0.f;
+    if (i0 + 4 <= count && ((uintptr_t)(out + i0) & 15) == 0) {
+        *reinterpret_cast<float4*>(out + i0) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+        for (int k = 0; k < 4 && i0 + k < count; ++k) out[i0 + k] = v[k];
+    }
+}
+
+int32_t run_dequant(const void* dW, uint32_t dtype, float* dOut, size_t count, cudaStream_t st) {
+    FormatInfo f;
+    if (!format_info(dtype, f)) return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "unsupported dtype %u", dtype);
+    if (count % (size_t)f.elems) return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "count not a whole number of blocks");
+    if (count == 0) return NEXUS_GPU_SUCCESS;
+    if (!dW || !dOut) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null pointer");
+    const uint64_t threads = (count + 3) / 4;
+    const unsigned blocks = (unsigned)((threads + 255) / 256);
+    dequant_kernel<<<blocks, 256, 0, st>>>((int)dtype, static_cast<const uint8_t*>(dW), dOut, (uint64_t)count);
+    CUDA_TRY(cudaGetLastError());
+    return NEXUS_GPU_SUCCESS;
+}
+
+// ------------------------------------------------------------ workspace
+int32_t get_workspace(Device& d, cudaStream_t st, size_t need, uint8_t** out) {
+    if (need == 0) {
+        *out = nullptr;
+        return NEXUS_GPU_SUCCESS;
+    }
+    std::lock_guard<std::mutex> lk(d.mu);
+    Workspace& w = d.ws[st];
+    if (w.bytes < need) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        CUDA_TRY(cudaStreamIsCapturing(st, &cs));
+        if (cs != cudaStreamCaptureStatusNone)
+            return fail(NEXUS_GPU_ERROR_WORKSPACE,
+                        "workspace of %zu bytes needed while the stream is capturing; make one uncaptured call "
+                        "with these shapes first or pass a workspace to nexus_gpu_gemv_ws",
+                        need);
+        if (w.ptr) {
+            CUDA_TRY(cudaStreamSynchronize(st));
+            CUDA_TRY(cudaFree(w.ptr));
+            w.ptr = nullptr;
+            w.bytes = 0;
+        }
+        const size_t sz = align256(need + need / 4);
+        CUDA_TRY(cudaMalloc(&w.ptr, sz));
+        w.bytes = sz;
+    }
+    *out = static_cast<uint8_t*>(w.ptr);
+    return NEXUS_GPU_SUCCESS;
+}
+
+// ---------------------------------------------------------- weight cache
+uint64_t fnv1a(uint64_t h, const uint8_t* p, size_t n) {
+    for (size_t i = 0; i < n; ++i) {
+        h ^= p[i];
+        h *= 0x100000001b3ull;
+    }
+    return h;
+}
+
+// Sampled fingerprint of a host buffer: head, tail and 16 evenly spaced
+// 8-byte probes.  Detects a buffer reused for another tensor; it is not a
+// full content hash.
+uint64_t fingerprint(const void* p, size_t n) {
+    const uint8_t* b = static_cast<const uint8_t*>(p);
+    uint64_t h = 0xcbf29ce484222325ull ^ n;
+    h = fnv1a(h, b, std::min<size_t>(n, 64));
+    if (n > 64) h = fnv1a(h, b + n - 64, 64);
+    if (n > 256)
+        for (int k = 1; k < 16; ++k) h = fnv1a(h, b + (n - 8) * k / 16, 8);
+    return h;
+}
+
+std::string cache_key(const void* W, uint32_t dtype, size_t rows, size_t cols) {
+    char buf[96];
+    snprintf(buf, sizeof(buf), "%p/%u/%zu/%zu", W, dtype, rows, cols);
+    return buf;
+}
+
+int32_t cached_weight(Device& d, const void* W, uint32_t dtype, size_t rows, size_t cols, size_t bytes,
+                      const void** out) {
+    const std::string key = cache_key(W, dtype, rows, cols);
+    const uint64_t fp = fingerprint(W, bytes);
+    auto it = d.cache.find(key);
+    if (it != d.cache.end() && it->second.fingerprint == fp) {
+        *out = it->second.dptr;
+        return NEXUS_GPU_SUCCESS;
+    }
+    if (it != d.cache.end()) {
+        CUDA_TRY(cudaStreamSynchronize(d.stream));
+        CUDA_TRY(cudaFree(it->second.dptr));
+        d.cache_bytes -= it->second.bytes;
+        d.cache.erase(it);
+    }
+    CachedWeight cw;
+    CUDA_TRY(cudaMalloc(&cw.dptr, align256(bytes)));
+    cw.bytes = align256(bytes);
+    cw.fingerprint = fp;
+    cudaError_t e = cudaMemcpy(cw.dptr, W, bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(cw.dptr);
+        return fail(NEXUS_GPU_ERROR_CUDA, "weight upload failed: %s", cudaGetErrorString(e));
+    }
+    d.cache_bytes += cw.bytes;
+    d.cache.emplace(key, cw);
+    *out = cw.dptr;
+    return NEXUS_GPU_SUCCESS;
+}
+
+int32_t grow(void** p, size_t* cap, size_t need) {
+    if (*cap >= need) return NEXUS_GPU_SUCCESS;
+    if (*p) CUDA_TRY(cudaFree(*p));
+    *p = nullptr;
+    *cap = 0;
+    const size_t sz = align256(std::max<size_t>(need, 4096));
+    CUDA_TRY(cudaMalloc(p, sz));
+    *cap = sz;
+    return NEXUS_GPU_SUCCESS;
+}
+
+// The synchronous host-pointer GEMV behind layers 1 and 2.
+int32_t host_gemv(const void* W, uint32_t dtype, const float* x, float* y, size_t rows, size_t cols) {
+    if (!W) return NEXUS_GPU_SUCCESS;  // transformer_ops.hpp:158
+    FormatInfo f;
+    int32_t rc = check_shape(dtype, rows, cols, f);
+    if (rc) return rc;
+    if (rows == 0) return NEXUS_GPU_SUCCESS;
+    if (!x || !y) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null x or y");
+    Device* d = nullptr;
+    if ((rc = get_device(&d))) return rc;
+    std::lock_guard<std::mutex> lk(d->mu);
+    const void* dW = nullptr;
+    if ((rc = cached_weight(*d, W, dtype, rows, cols, rows * row_bytes_of(f, cols), &dW))) return rc;
+    if ((rc = grow(&d->dx, &d->dx_cap, cols * 4 + xq_bytes(dtype, 1, cols) + 256))) return rc;
+    if ((rc = grow(&d->dy, &d->dy_cap, rows * 4))) return rc;
+    uint8_t* ws = static_cast<uint8_t*>(d->dx) + align256(cols * 4);
+    CUDA_TRY(cudaMemcpyAsync(d->dx, x, cols * 4, cudaMemcpyHostToDevice, d->stream));
+    if ((rc = run_gemv(*d, dW, dtype, d->dx, NEXUS_GPU_FP32, static_cast<float*>(d->dy), 1, rows, cols, ws,
+                       d->stream)))
+        return rc;
+    CUDA_TRY(cudaMemcpyAsync(y, d->dy, rows * 4, cudaMemcpyDeviceToHost, d->stream));
+    CUDA_TRY(cudaStreamSynchronize(d->stream));
+    return NEXUS_GPU_SUCCESS;
+}
+
+int32_t host_dequant(const void* blocks, uint32_t dtype, float* out, size_t num_blocks) {
+    FormatInfo f;
+    if (!format_info(dtype, f)) return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "unsupported dtype %u", dtype);
+    if (num_blocks == 0) return NEXUS_GPU_SUCCESS;
+    if (!blocks || !out) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null pointer");
+    Device* d = nullptr;
+    int32_t rc = get_device(&d);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(d->mu);
+    const size_t in_bytes = num_blocks * (size_t)f.bytes, count = num_blocks * (size_t)f.elems;
+    if ((rc = grow(&d->dx, &d->dx_cap, in_bytes))) return rc;
+    if ((rc = grow(&d->dy, &d->dy_cap, count * 4))) return rc;
+    CUDA_TRY(cudaMemcpyAsync(d->dx, blocks, in_bytes, cudaMemcpyHostToDevice, d->stream));
+    if ((rc = run_dequant(d->dx, dtype, static_cast<float*>(d->dy), count, d->stream))) return rc;
+    CUDA_TRY(cudaMemcpyAsync(out, d->dy, count * 4, cudaMemcpyDeviceToHost, d->stream));
+    CUDA_TRY(cudaStreamSynchronize(d->stream));
+    return NEXUS_GPU_SUCCESS;
+}
+
+void report_void(const char* fn, int32_t rc) {
+    if (rc != NEXUS_GPU_SUCCESS) fprintf(stderr, "[nexus_gpu] %s: %s (status %d)\n", fn, t_last_error.c_str(), rc);
+}
+
+}  // namespace
+}  // namespace nexus_gpu
+
+using namespace nexus_gpu;
+
+// ================================================================ C ABI
+extern "C" {
+
+NEXUS_GPU_API void nexus_fused_gemv_q4_0(const void* W, const float* x, float* y, size_t rows, size_t cols) {
+    report_void(__func__, host_gemv(W, NEXUS_GPU_GGUF_Q4_0, x, y, rows, cols));
+}
+NEXUS_GPU_API void nexus_fused_gemv_q8_0(const void* W, const float* x, float* y, size_t rows, size_t cols) {
+    report_void(__func__, host_gemv(W, NEXUS_GPU_GGUF_Q8_0, x, y, rows, cols));
+}
+NEXUS_GPU_API void nexus_fused_gemv_fp16(const uint16_t* W, const float* x, float* y, size_t rows, size_t cols) {
+    report_void(__func__, host_gemv(W, NEXUS_GPU_FP16, x, y, rows, cols));
+}
+NEXUS_GPU_API void nexus_fused_gemv_q5_k(const void* W, const float* x, float* y, size_t rows, size_t cols) {
+    report_void(__func__, host_gemv(W, NEXUS_GPU_GGUF_Q5_K, x, y, rows, cols));
+}
+NEXUS_GPU_API void nexus_fused_gemv_q6_k(const void* W, const float* x, float* y, size_t rows, size_t cols) {
+    report_void(__func__, host_gemv(W, NEXUS_GPU_GGUF_Q6_K, x, y, rows, cols));
+}
+
+NEXUS_GPU_API void nexus_dequantize_gguf_q4_0(const void* blocks, float* out, size_t nb) {
+    report_void(__func__, host_dequant(blocks, NEXUS_GPU_GGUF_Q4_0, out, nb));
+}
+NEXUS_GPU_API void nexus_dequantize_gguf_q5_k(const void* blocks, float* out, size_t nb) {
+    report_void(__func__, host_dequant(blocks, NEXUS_GPU_GGUF_Q5_K, out, nb));
+}
+NEXUS_GPU_API void nexus_dequantize_gguf_q6_k(const void* blocks, float* out, size_t nb) {
+    report_void(__func__, host_dequant(blocks, NEXUS_GPU_GGUF_Q6_K, out, nb));
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_gemv_dispatch(const void* W, uint32_t dtype, const float* x, float* y, size_t rows,
+                                              size_t cols) {
+    t_last_error.clear();
+    return host_gemv(W, dtype, x, y, rows, cols);
+}
+
+NEXUS_GPU_API void* nexus_gpu_allocate_device_memory(size_t bytes) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        fail(NEXUS_GPU_ERROR_OUT_OF_TIER0_MEMORY, "cudaMalloc(%zu) failed", bytes);
+        return nullptr;
+    }
+    return p;
+}
+NEXUS_GPU_API void nexus_gpu_free_device_memory(void* ptr) {
+    if (ptr) cudaFree(ptr);
+}
+NEXUS_GPU_API int32_t nexus_gpu_copy_host_to_device_async(void* dst, const void* src, size_t bytes, void* stream) {
+    CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream)));
+    return NEXUS_GPU_SUCCESS;
+}
+NEXUS_GPU_API int32_t nexus_gpu_copy_device_to_host_async(void* dst, const void* src, size_t bytes, void* stream) {
+    CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream)));
+    return NEXUS_GPU_SUCCESS;
+}
+NEXUS_GPU_API int32_t nexus_gpu_synchronize(void* stream) {
+    CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+    return NEXUS_GPU_SUCCESS;
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_weight_cache_invalidate(const void* host_W) {
+    Device* d = nullptr;
+    int32_t rc = get_device(&d);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(d->mu);
+    CUDA_TRY(cudaStreamSynchronize(d->stream));
+    char prefix[32];
+    snprintf(prefix, sizeof(prefix), "%p/", host_W);
+    for (auto it = d->cache.begin(); it != d->cache.end();) {
+        if (host_W == nullptr || it->first.rfind(prefix, 0) == 0) {
+            CUDA_TRY(cudaFree(it->second.dptr));
+            d->cache_bytes -= it->second.bytes;
+            it = d->cache.erase(it);
+        } else {
+            ++it;
+        }
+    }
+    return NEXUS_GPU_SUCCESS;
+}
+
+NEXUS_GPU_API size_t nexus_gpu_weight_cache_bytes(void) {
+    Device* d = nullptr;
+    if (get_device(&d)) return 0;
+    std::lock_guard<std::mutex> lk(d->mu);
+    return d->cache_bytes;
+}
+
+NEXUS_GPU_API size_t nexus_gpu_weight_bytes(uint32_t dtype, size_t rows, size_t cols) {
+    FormatInfo f;
+    if (!format_info(dtype, f) || cols % (size_t)f.elems) return 0;
+    return rows * row_bytes_of(f, cols);
+}
+
+NEXUS_GPU_API size_t nexus_gpu_gemv_workspace_size(uint32_t dtype, size_t M, size_t rows, size_t cols) {
+    (void)rows;
+    return xq_bytes(dtype, M, cols);
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_gemv_ws(const void* dW, uint32_t dtype, const void* dX, uint32_t x_dtype, float* dY,
+                                        size_t M, size_t rows, size_t cols, void* workspace, size_t workspace_bytes,
+                                        void* stream) {
+    t_last_error.clear();
+    Device* d = nullptr;
+    int32_t rc = get_device(&d);
+    if (rc) return rc;
+    const size_t need = xq_bytes(dtype, M, cols);
+    if (workspace_bytes < need || (need && !workspace))
+        return fail(NEXUS_GPU_ERROR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+    if (need && ((uintptr_t)workspace & 255))
+        return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+    return run_gemv(*d, dW, dtype, dX, x_dtype, dY, M, rows, cols, static_cast<uint8_t*>(workspace),
+                    static_cast<cudaStream_t>(stream));
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_gemv(const void* dW, uint32_t dtype, const void* dX, uint32_t x_dtype, float* dY,
+                                     size_t M, size_t rows, size_t cols, void* stream) {
+    t_last_error.clear();
+    Device* d = nullptr;
+    int32_t rc = get_device(&d);
+    if (rc) return rc;
+    FormatInfo f;
+    if ((rc = check_shape(dtype, rows, cols, f))) return rc;
+    uint8_t* ws = nullptr;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((rc = get_workspace(*d, st, xq_bytes(dtype, M, cols), &ws))) return rc;
+    return run_gemv(*d, dW, dtype, dX, x_dtype, dY, M, rows, cols, ws, st);
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_dequantize(const void* dW, uint32_t dtype, float* dOut, size_t count, void* stream) {
+    t_last_error.clear();
+    return run_dequant(dW, dtype, dOut, count, static_cast<cudaStream_t>(stream));
+}
+
+NEXUS_GPU_API const char* nexus_gpu_last_error(void) { return t_last_error.c_str(); }
+
+NEXUS_GPU_API int32_t nexus_gpu_device_status(uint32_t* out_bits) {
+    if (!out_bits) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null out_bits");
+    CUDA_TRY(cudaDeviceSynchronize());
+    unsigned v = 0, zero = 0;
+    CUDA_TRY(cudaMemcpyFromSymbol(&v, g_device_status, sizeof(v)));
+    CUDA_TRY(cudaMemcpyToSymbol(g_device_status, &zero, sizeof(zero)));
+    *out_bits = v;
+    return NEXUS_GPU_SUCCESS;
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_device_info(char* name, size_t name_len, int* sm_count, int* cc_major,
+                                            int* cc_minor) {
+    int id = 0;
+    CUDA_TRY(cudaGetDevice(&id));
+    cudaDeviceProp prop;
+    CUDA_TRY(cudaGetDeviceProperties(&prop, id));
+    if (name && name_len) {
+        strncpy(name, prop.name, name_len - 1);
+        name[name_len - 1] = '\0';
+    }
+    if (sm_count) *sm_count = prop.multiProcessorCount;
+    if (cc_major) *cc_major = prop.major;
+    if (cc_minor) *cc_minor = prop.minor;
+    return NEXUS_GPU_SUCCESS;
+}
+
+NEXUS_GPU_API const char* nexus_gpu_version(void) { return "nexus_gpu 0.1.0 (sm_100a)"; }
+
+}  // extern "C"
