@@ -59,11 +59,11 @@ def q4_bytes(rows, cols):
     return rows * (cols // 32) * 18
 
 
-def step_bytes(include_head=True):
+def step_bytes(include_head=True, layers=None):
     b = 0
     for _, n, k in LAYER_SHAPES:
         b += q4_bytes(n, k) + 4 * k + 4 * n
-    b *= LAYERS
+    b *= LAYERS if layers is None else layers
     if include_head:
         b += q4_bytes(VOCAB, HIDDEN) + 4 * HIDDEN + 4 * VOCAB
     return b
@@ -232,12 +232,12 @@ def workload_config(args, reference=False):
 
 
 # -------------------------------------------------------------- our arm
-def build_stack(torch, rank, world):
+def build_stack(torch, rank, world, n_layers):
     """Weights for this rank: every matrix's row slice [rank*n/W, (rank+1)*n/W)."""
     from nexusllm_b200 import synth
 
     layers = []
-    for l in range(LAYERS):
+    for l in range(n_layers):
         mats = {}
         for i, (name, n, k) in enumerate(LAYER_SHAPES):
             nl = n // world
@@ -250,11 +250,14 @@ def build_stack(torch, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="decoder layers in the stack (32 = the configuration; fewer only for profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -281,7 +284,7 @@ def main():
     be = CUDABackend()
     L = _native.lib()
     dev = torch.device("cuda", local)
-    layers, head = build_stack(torch, rank, world)
+    layers, head = build_stack(torch, rank, world, args.layers)
     stream = torch.cuda.Stream(dev)
     h0 = torch.randn(HIDDEN, generator=torch.Generator(device=dev).manual_seed(5), device=dev)
 
@@ -334,13 +337,16 @@ def main():
             dist.barrier(device_ids=[local])
 
     def timed(fn, iters):
+        # graph.replay() launches on torch's current stream: make that `stream`
+        # and record the events on it
         barrier()
         torch.cuda.synchronize(dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(iters):
-            fn()
-        e1.record(stream)
+        with torch.cuda.stream(stream):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(iters):
+                fn()
+            e1.record()
         torch.cuda.synchronize(dev)
         barrier()
         ms = e0.elapsed_time(e1)
@@ -350,12 +356,14 @@ def main():
             ms = float(t.item())
         return ms
 
-    for _ in range(args.warmup):
-        graph.replay()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
     with Clocks(gpu_uuid(torch, local)) as clk:
         ms = timed(graph.replay, args.steps)
     clocks = clk.summary()
-    sb = step_bytes()
+    verify_head(torch, be, head, h0, out["head"], world, rank)
+    sb = step_bytes(layers=args.layers)
     value = sb * args.steps / (ms / 1e3) / 1e9
     ms_step = ms / args.steps
 
@@ -371,8 +379,9 @@ def main():
                 L.nexus_gpu_gemv_ws(W.data_ptr(), DTYPE, xin[name].data_ptr(), 0, part[name].data_ptr(), 1,
                                     part[name].numel(), k, ws.data_ptr(), ws.numel(),
                                     torch.cuda.current_stream(dev).cuda_stream)
-    for _ in range(3):
-        g2.replay()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g2.replay()
     reps = max(3, args.steps // 5)
     ms_ffn = timed(g2.replay, reps)
     launches = len(ffn) * reps
@@ -388,7 +397,9 @@ def main():
 
     # ---- e2e
     e2e = None
-    if world == 1:
+    if args.no_e2e:
+        pass
+    elif world == 1:
         e2e = e2e_host_api(torch, L, layers, head, h0, args)
     else:
         e2e = e2e_resident(torch, graph, h0, full, stream, dev, args, timed, sb)
@@ -398,7 +409,7 @@ def main():
         gbs, sec, kind, sample = time_reference_layer(3, cpu_threads(), min_seconds=10.0)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cpu_threads(), "kind": kind, "sample": sample}
 
-    launches_per_step = 2 * (7 * LAYERS + 1)  # xquant + fused GEMV per call
+    launches_per_step = 2 * (7 * args.layers + 1)  # xquant + fused GEMV per call
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
@@ -406,15 +417,16 @@ def main():
         "dtype_note": "Q4_0 codes x 16-bit fixed-point x in int8 dp4a limbs, fp32 accumulation",
         "data": "synthetic (seeded GGUF Q4_0 blocks, x ~ N(0,1))",
         "config": workload_config(args),
+        "layers": args.layers,
         "pct_of_8tbs": round(100 * value / NOMINAL_HBM_GBS, 2),
         "pct_of_measured_hbm": round(100 * value / peak, 2),
         "tokens_per_s": round(1e3 / ms_step, 2),
-        "gemv_calls_per_s": round((7 * LAYERS + 1) * 1e3 / ms_step, 1),
+        "gemv_calls_per_s": round((7 * args.layers + 1) * 1e3 / ms_step, 1),
         "bytes_per_step": sb,
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
         "gpu_launches": launches_per_step * args.steps,
         "gpu_launches_note": f"{launches_per_step} per step (xquant + gemv per GEMV) x {args.steps} steps"
-                             + (f"; plus {7 * LAYERS + 1} NCCL all-gathers per step" if world > 1 else ""),
+                             + (f"; plus {7 * args.layers + 1} NCCL all-gathers per step" if world > 1 else ""),
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -427,6 +439,17 @@ def main():
 # bytes read + written by one FFN launch in an ncu capture (profiles/); None
 # until a capture has been summarised there
 TRAFFIC_PER_FFN_LAUNCH = None
+
+
+def verify_head(torch, be, head, h0, y_graph, world, rank):
+    """The replayed graph must have computed the LM head: compare this rank's
+    slice (or, at N > 1, the gathered vector's slice) with an eager call."""
+    torch.cuda.synchronize()
+    y_eager = be.gemv(head, 7, h0)
+    n = y_eager.numel()
+    got = y_graph[rank * n:(rank + 1) * n] if world > 1 else y_graph[:n]
+    if not torch.equal(got, y_eager):
+        raise RuntimeError("graph replay did not reproduce the eager LM-head GEMV")
 
 
 def e2e_host_api(torch, L, layers, head, h0, args):
@@ -451,8 +474,8 @@ def e2e_host_api(torch, L, layers, head, h0, args):
     for _, n, k in LAYER_SHAPES:
         h2d += 4 * k
         d2h += 4 * n
-    h2d = h2d * LAYERS + 4 * HIDDEN
-    d2h = d2h * LAYERS + 4 * VOCAB
+    h2d = h2d * len(layers) + 4 * HIDDEN
+    d2h = d2h * len(layers) + 4 * VOCAB
 
     def step():
         for hm in host_layers:
@@ -474,7 +497,7 @@ def e2e_host_api(torch, L, layers, head, h0, args):
     sec = (time.perf_counter() - t0) / args.e2e_steps
     L.nexus_gpu_weight_cache_invalidate(None)
     del host_layers, host_head
-    return {"value": round(step_bytes() / sec / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+    return {"value": round(step_bytes(layers=len(layers)) / sec / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": round(sec * 1e3, 3), "tokens_per_s": round(1 / sec, 2),
             "api": "nexus_gpu_gemv_dispatch (host pointers, synchronous, weights cached on device)",
             "steps": args.e2e_steps}

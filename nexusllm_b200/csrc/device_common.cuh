@@ -116,13 +116,13 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far beyond any legal w
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
-    while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    for (uint32_t k = 1;; ++k) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((k & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {  // the clock is read rarely
             atomicOr(&g_device_status, kStatusWaitTimeout);
             return false;
         }
     }
-    return true;
 }
 
 // 1-D bulk copy global -> shared through the TMA engine, completing on an

@@ -4,21 +4,27 @@
 // QuantizationKernel::fused_gemv_{q4_0,q8_0,q5_k,q6_k,fp16},
 // src/quantization.cpp:264-722).
 //
-// Data path (one CTA per SM, 8 consumer warps + 1 producer warp):
-//  * The CTA owns a contiguous range of rows.  Rows are processed in groups
-//    of up to 8*R rows (R rows per consumer warp) and, inside a group, in
-//    K-chunks of 32 "work items" (a work item = 32 weights; 16 for FP16).
-//  * The producer warp streams each (row group, K-chunk) tile from HBM into a
-//    ring of shared-memory stages with 1-D bulk copies (cp.async.bulk on the
-//    TMA engine), one copy per row segment, completing on a "full" mbarrier.
-//    Row segments start on 16-byte boundaries rounded down from the true
-//    start, so blocks of any size (18, 34, 176, 210 bytes) land at a known
-//    2-byte offset and are realigned with byte permutes in registers.
-//  * Consumer lane l takes work item l of each row segment, loads that work
-//    item's slice of x once and reuses it for the warp's R rows, dequantizes
-//    in registers and accumulates.  The stage is released on an "empty"
-//    mbarrier; at the end of a row group each warp reduces its R partial
-//    sums with shuffles and writes y.
+// Data path (one CTA per SM: 15 consumer warps + 1 producer warp):
+//  * The CTA owns a contiguous range of rows.  Consecutive rows of a GGUF
+//    matrix are contiguous in memory, so the CTA's weights are one contiguous
+//    byte range, streamed in stages of R whole rows (about 16 KB).  Each stage
+//    is ONE 1-D bulk copy (cp.async.bulk on the TMA engine) into a ring of
+//    shared-memory buffers, completing on a "full" mbarrier; consumers release
+//    it on an "empty" mbarrier.  One large copy per stage matters: the cost of
+//    a bulk copy is dominated by its issue, not by its size.
+//  * The copy starts on the 16-byte boundary at or below the first row, so
+//    blocks of any size (18, 34, 176, 210 bytes) land at a known 2-byte offset
+//    and are realigned in registers with byte permutes.
+//  * x is stationary: a row is cut into S K-segments (S in {1, 3, 5, 15}),
+//    each owned by one warp whose lanes keep that segment's slice of x in
+//    registers (up to 4 work items of 32 weights -- 16 for FP16 -- per lane).
+//    The warps form 15/S row groups; rows are dealt to the groups
+//    round-robin, so each stage is worked on by several warps at once.
+//  * A warp reduces its row partial with shuffles.  With S == 1 it writes y
+//    directly; otherwise the S partials meet in shared slots and the last
+//    warp to arrive (shared atomic counter) sums them in segment order.
+//    Results are deterministic and do not depend on how rows are spread over
+//    CTAs or GPUs.
 //
 // Arithmetic.  For the integer formats the activation is first turned into
 // a 16-bit fixed-point vector by xquant_kernel (per 32-element block: scale
@@ -34,15 +40,27 @@
 // ggml's) Q5_K / Q6_K bit orders (src/quantization.cpp:418-509).
 #pragma once
 
+#include <type_traits>
+
 #include "device_common.cuh"
 
 namespace nexus_gpu {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
-constexpr int kXQLimbBytes = 64;   // Xh[32] then Xl[32], int8
-constexpr int kXQMetaBytes = 16;   // {float s, int sum X[0:16), int sum X[16:32), pad}
-constexpr float kXQMax = 32639.0f;  // largest |X| whose high limb fits int8
+constexpr int kConsumerWarps = 15;   // + 1 producer warp = 16 warps: 128 registers per thread
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kGemvThreads = kConsumers + 32;
+constexpr int kXQLimbBytes = 64;     // Xh[32] then Xl[32], int8
+constexpr int kXQMetaBytes = 16;     // {float s, int sum X[0:16), int sum X[16:32), int sum X[0:32)}
+constexpr float kXQMax = 32639.0f;   // largest |X| whose high limb fits int8
+constexpr int kMaxJ = 4;             // work items (x slices in registers) per lane
+constexpr int kMaxSegments = 15;     // K segments per row (one warp each); a divisor of kConsumerWarps
+constexpr int kMaxStageRows = 64;
+constexpr int kMaxStages = 12;
+constexpr int kMaxSlots = 1024;      // n_stages * stage_rows * segments partial sums
+constexpr int kBarBytes = 256;       // 2 x kMaxStages mbarriers
+constexpr int kSmemHeader = kBarBytes + kMaxSlots * 4 + kMaxStages * kMaxStageRows * 4;  // + slots + counters
+constexpr int kStageTargetBytes = 32768;
+constexpr int kStageMaxBytes = 49152;
 
 struct GemvParams {
     const uint8_t* W;        // weight blocks, 16-byte aligned
@@ -50,6 +68,12 @@ struct GemvParams {
     uint64_t row_bytes;
     int N, K;
     int nwi;                 // work items per row
+    int segments;            // S: K segments per row, one warp each (divides kConsumerWarps)
+    int seg_wi;              // work items per segment
+    int wi_per_lane;         // J = ceil(seg_wi / 32)
+    int stage_rows;          // R
+    int stage_bytes;         // shared bytes per stage buffer (multiple of 16)
+    int n_stages;
     const uint8_t* xq_limbs; // [K/32][64]      (integer formats)
     const int4* xq_meta;     // [K/32]          (integer formats)
     const void* x;           // fp32 or bf16 [K] (FP16 weights)
@@ -58,66 +82,77 @@ struct GemvParams {
 };
 
 // ------------------------------------------------------------------ formats
+// kBlockBytes: bytes of one storage block; kWIPerBlock: work items per block;
+// kWIElems: weights per work item.
 struct FmtQ4_0 {
     static constexpr int kBlockBytes = 18, kWIPerBlock = 1, kWIElems = 32;
-    static constexpr int kRows = 4, kChunkWI = 32, kStages = 6;
     static constexpr bool kIntX = true;
 };
 struct FmtQ8_0 {
     static constexpr int kBlockBytes = 34, kWIPerBlock = 1, kWIElems = 32;
-    static constexpr int kRows = 2, kChunkWI = 32, kStages = 6;
     static constexpr bool kIntX = true;
 };
 struct FmtQ5_K {
     static constexpr int kBlockBytes = 176, kWIPerBlock = 8, kWIElems = 32;
-    static constexpr int kRows = 4, kChunkWI = 32, kStages = 5;
     static constexpr bool kIntX = true;
 };
 struct FmtQ6_K {
     static constexpr int kBlockBytes = 210, kWIPerBlock = 8, kWIElems = 32;
-    static constexpr int kRows = 2, kChunkWI = 32, kStages = 7;
     static constexpr bool kIntX = true;
 };
 struct FmtF16 {
     static constexpr int kBlockBytes = 32, kWIPerBlock = 1, kWIElems = 16;  // 16 halves per work item
-    static constexpr int kRows = 2, kChunkWI = 32, kStages = 6;
     static constexpr bool kIntX = false;
-};
-
-template <class F>
-struct Layout {
-    static constexpr int kRG = kConsumerWarps * F::kRows;                         // rows per group
-    static constexpr int kChunkBytes = F::kChunkWI / F::kWIPerBlock * F::kBlockBytes;
-    static constexpr int kRowStride = (kChunkBytes + 32 + 15) / 16 * 16;           // room for 16-B rounding
-    static constexpr int kStageBytes = kRG * kRowStride;
-    static constexpr int kBarBytes = 128;
-    __host__ __device__ static size_t x_bytes(int K) {
-        size_t b = F::kIntX ? (size_t)(K / 32) * (kXQLimbBytes + kXQMetaBytes) : (size_t)K * 4;
-        return (b + 127) / 128 * 128;
-    }
-    __host__ __device__ static size_t smem_bytes(int K) { return kBarBytes + x_bytes(K) + (size_t)F::kStages * kStageBytes + 128; }
 };
 
 // x slice of one work item, integer formats
 struct XInt {
     uint32_t h[8], l[8];
     float s;
-    int sa, sb;
+    int sa, sb, sx;  // sums of X over [0,16), [16,32), [0,32)
 };
 
-__device__ __forceinline__ void load_xint(uint32_t limbs, uint32_t meta, int gj, XInt& X) {
-    const uint32_t a = limbs + gj * kXQLimbBytes;
+__device__ __forceinline__ void load_xint(const uint8_t* limbs, const int4* meta, int gj, XInt& X) {
+    const int4* a = reinterpret_cast<const int4*>(limbs + (size_t)gj * kXQLimbBytes);
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
-        uint4 v = lds128(a + 16 * q);
+        const int4 v = __ldg(a + q);
         X.h[4 * q + 0] = v.x; X.h[4 * q + 1] = v.y; X.h[4 * q + 2] = v.z; X.h[4 * q + 3] = v.w;
-        uint4 u = lds128(a + 32 + 16 * q);
+        const int4 u = __ldg(a + 2 + q);
         X.l[4 * q + 0] = u.x; X.l[4 * q + 1] = u.y; X.l[4 * q + 2] = u.z; X.l[4 * q + 3] = u.w;
     }
-    uint4 m = lds128(meta + gj * kXQMetaBytes);
-    X.s = __uint_as_float(m.x);
-    X.sa = (int)m.y;
-    X.sb = (int)m.z;
+    const int4 m = __ldg(meta + gj);
+    X.s = __int_as_float(m.x);
+    X.sa = m.y;
+    X.sb = m.z;
+    X.sx = m.w;
+}
+
+struct XF16 {
+    float v[16];
+};
+
+__device__ __forceinline__ void load_xf16(const void* x, int x_bf16, int gj, XF16& X) {
+    if (x_bf16) {
+        const uint4* a = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + (size_t)gj * 16);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const uint4 w = __ldg(a + q);
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                X.v[8 * q + 2 * k] = __uint_as_float(ws[k] << 16);
+                X.v[8 * q + 2 * k + 1] = __uint_as_float(ws[k] & 0xffff0000u);
+            }
+        }
+    } else {
+        const float4* a = reinterpret_cast<const float4*>(static_cast<const float*>(x) + (size_t)gj * 16);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 f = __ldg(a + q);
+            X.v[4 * q] = f.x; X.v[4 * q + 1] = f.y; X.v[4 * q + 2] = f.z; X.v[4 * q + 3] = f.w;
+        }
+    }
 }
 
 // Q4_0 (include/quantization.hpp:8-11; src/quantization.cpp:264-330).
@@ -137,7 +172,7 @@ __device__ __forceinline__ float dot_q4_0(uint32_t p, const XInt& X) {
         slh = dp4a_us(hi, X.l[4 + k], slh);
     }
     // 16 * sum((q - 8) * X), exact in int32
-    const int t16 = ((shl * 16 + shh) << 8) + sll * 16 + slh - 128 * (X.sa + X.sb);
+    const int t16 = ((shl * 16 + shh) << 8) + sll * 16 + slh - 128 * X.sx;
     return (d * X.s) * (0.0625f * (float)t16);
 }
 
@@ -189,7 +224,7 @@ __device__ __forceinline__ float dot_q5_k(uint32_t o, int sub, const XInt& X) {
     }
     const float scale = d * (float)sc;
     const float minv = dmin * (float)mn;
-    return X.s * (scale * (float)((sh << 8) + sl) - minv * (float)(X.sa + X.sb));
+    return X.s * (scale * (float)((sh << 8) + sl) - minv * (float)X.sx);
 }
 
 // Q6_K sub-blocks 2*pair and 2*pair+1 (16 weights each) of the 210-byte
@@ -232,18 +267,15 @@ __device__ __forceinline__ float dot_q6_k(uint32_t o, int pair, const XInt& X) {
     return X.s * r;
 }
 
-// FP16: 16 halves at p (2-byte aligned) against fp32 x at xs (16-B aligned).
-__device__ __forceinline__ float dot_f16(uint32_t p, uint32_t xs) {
+// FP16: 16 halves at p (2-byte aligned) against x held in registers.
+__device__ __forceinline__ float dot_f16(uint32_t p, const XF16& X) {
     uint32_t w[8];
     lds_words_2a<8>(p, w);
     float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const float4 xv = lds128f(xs + 16 * q);
-        a0 = fmaf(nexus_fp16(w[2 * q] & 0xffffu), xv.x, a0);
-        a1 = fmaf(nexus_fp16_hi(w[2 * q]), xv.y, a1);
-        a0 = fmaf(nexus_fp16(w[2 * q + 1] & 0xffffu), xv.z, a0);
-        a1 = fmaf(nexus_fp16_hi(w[2 * q + 1]), xv.w, a1);
+    for (int q = 0; q < 8; ++q) {
+        a0 = fmaf(nexus_fp16(w[q] & 0xffffu), X.v[2 * q], a0);
+        a1 = fmaf(nexus_fp16_hi(w[q]), X.v[2 * q + 1], a1);
     }
     return a0 + a1;
 }
@@ -254,31 +286,54 @@ __device__ __forceinline__ uint32_t wi_offset(int j) {
     else return (uint32_t)(j / F::kWIPerBlock) * F::kBlockBytes;
 }
 
+template <class F, class X>
+__device__ __forceinline__ float dot_wi(uint32_t row, int wi, const X& x) {
+    const uint32_t b = row + wi_offset<F>(wi);
+    if constexpr (F::kIntX) {
+        if constexpr (F::kBlockBytes == 18) return dot_q4_0(b, x);
+        else if constexpr (F::kBlockBytes == 34) return dot_q8_0(b, x);
+        else if constexpr (F::kBlockBytes == 176) return dot_q5_k(b, wi & 7, x);
+        else return dot_q6_k(b, wi & 7, x);
+    } else {
+        return dot_f16(b, x);
+    }
+}
+
 // ------------------------------------------------------------------- kernel
+// Warp w of the 15 consumer warps owns K segment (w % S) and row group
+// (w / S), S in {1, 3, 5, 15}; the CTA's rows are dealt to the 15/S row
+// groups round-robin (row q of the CTA -> group q % (15/S)).  A warp keeps the x slices of its
+// segment in registers (J work items per lane), so per row it only reads
+// weights from shared memory.  With S == 1 a warp covers whole rows and writes
+// y itself; with S > 1 each warp leaves its row partial in a shared slot and
+// bumps the row's arrival counter, and the last of the S warps sums the slots
+// in segment order and writes y -- deterministic, no CTA-wide barrier.
 template <class F>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_m1_kernel(const GemvParams p) {
-    using L = Layout<F>;
+    using XT = typename std::conditional<F::kIntX, XInt, XF16>::type;
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t full_bar = sbase;                          // kStages x 8 B
-    const uint32_t empty_bar = sbase + 8 * F::kStages;        // kStages x 8 B
-    const uint32_t xs = sbase + L::kBarBytes;                 // x region
-    const uint32_t stage0 = xs + (uint32_t)L::x_bytes(p.K);  // stage ring
+    const uint32_t full_bar = sbase;                     // kMaxStages x 8 B
+    const uint32_t empty_bar = sbase + 8 * kMaxStages;  // kMaxStages x 8 B
+    float* slots = reinterpret_cast<float*>(smem + kBarBytes);            // [n_stages][R][S]
+    int* counters = reinterpret_cast<int*>(smem + kBarBytes + kMaxSlots * 4);  // [n_stages][R]
+    const uint32_t stage0 = sbase + kSmemHeader;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, c = blockIdx.x;
     const int row_begin = (int)((int64_t)p.N * c / G);
     const int row_end = (int)((int64_t)p.N * (c + 1) / G);
-    const int n_groups = (row_end - row_begin + L::kRG - 1) / L::kRG;
-    const int n_chunks = (p.nwi + F::kChunkWI - 1) / F::kChunkWI;
+    const int R = p.stage_rows;
+    const int n_st = (row_end - row_begin + R - 1) / R;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < F::kStages; ++s) {
+        for (int s = 0; s < p.n_stages; ++s) {
             mbar_init(full_bar + 8 * s, 1);
             mbar_init(empty_bar + 8 * s, kConsumerWarps);
         }
         fence_mbar_init();
     }
+    for (int i = threadIdx.x; i < p.n_stages * R; i += blockDim.x) counters[i] = 0;
     __syncthreads();
     pdl_launch_dependents();
 
@@ -286,151 +341,111 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_m1_kernel(const GemvPara
         // ------------------------------------------------------- producer
         if (lane != 0) return;
         const uint64_t floor16 = p.total_bytes & ~(uint64_t)15;
-        int it = 0;
+        const uint64_t stage_span = (uint64_t)R * p.row_bytes;
+        uint64_t start = (uint64_t)row_begin * p.row_bytes;
+        const uint64_t cta_end = (uint64_t)row_end * p.row_bytes;
         bool ok = true;
-        for (int g = 0; g < n_groups && ok; ++g) {
-            const int r0 = row_begin + g * L::kRG;
-            const int nr = min(L::kRG, row_end - r0);
-            for (int ch = 0; ch < n_chunks; ++ch, ++it) {
-                const int s = it % F::kStages, use = it / F::kStages;
-                if (use > 0 && !mbar_wait_bounded(empty_bar + 8 * s, (use - 1) & 1)) { ok = false; break; }
-                const int nwi_c = min(F::kChunkWI, p.nwi - ch * F::kChunkWI);
-                const uint64_t cbytes = (uint64_t)(nwi_c / F::kWIPerBlock) * F::kBlockBytes;
-                const uint64_t coff = (uint64_t)ch * L::kChunkBytes;
-                const uint32_t dst0 = stage0 + (uint32_t)s * L::kStageBytes;
-                uint32_t tx = 0;
-                bool tail = false;
-                for (int rl = 0; rl < nr; ++rl) {
-                    const uint64_t start = (uint64_t)(r0 + rl) * p.row_bytes + coff;
-                    const uint64_t end = start + cbytes;
-                    const uint64_t a = start & ~(uint64_t)15;
-                    const uint64_t bend = min((end + 15) & ~(uint64_t)15, floor16);
-                    if (bend > a) tx += (uint32_t)(bend - a);
-                    // bytes past the last 16-byte boundary of the matrix
-                    for (uint64_t pos = (bend > a ? bend : a); pos < end; pos += 2) {
-                        const uint16_t v = *reinterpret_cast<const uint16_t*>(p.W + pos);
-                        sts16(dst0 + rl * L::kRowStride + (uint32_t)(pos - a), v);
-                        tail = true;
-                    }
-                }
-                if (tail) fence_proxy_async_smem();
-                mbar_arrive_expect_tx(full_bar + 8 * s, tx);
-                for (int rl = 0; rl < nr; ++rl) {
-                    const uint64_t start = (uint64_t)(r0 + rl) * p.row_bytes + coff;
-                    const uint64_t end = start + cbytes;
-                    const uint64_t a = start & ~(uint64_t)15;
-                    const uint64_t bend = min((end + 15) & ~(uint64_t)15, floor16);
-                    if (bend > a) bulk_g2s(dst0 + rl * L::kRowStride, p.W + a, (uint32_t)(bend - a), full_bar + 8 * s);
-                }
+        int i = 0, s = 0;
+        uint32_t phase = 0;  // parity of the empty-barrier phase to wait for
+        for (; i < n_st; ++i) {
+            if (i >= p.n_stages && !mbar_wait_bounded(empty_bar + 8 * s, phase)) {
+                ok = false;
+                break;
+            }
+            const uint64_t end = min(start + stage_span, cta_end);
+            const uint64_t a = start & ~(uint64_t)15;
+            const uint64_t bend = min((end + 15) & ~(uint64_t)15, floor16);
+            const uint32_t dst = stage0 + (uint32_t)(s * p.stage_bytes);
+            // bytes past the last 16-byte boundary of the matrix: plain copies
+            if (bend < end) {
+                for (uint64_t pos = (bend > a ? bend : a); pos < end; pos += 2)
+                    sts16(dst + (uint32_t)(pos - a), *reinterpret_cast<const uint16_t*>(p.W + pos));
+                fence_proxy_async_smem();
+            }
+            const uint32_t n = bend > a ? (uint32_t)(bend - a) : 0u;
+            mbar_arrive_expect_tx(full_bar + 8 * s, n);
+            if (n) bulk_g2s(dst, p.W + a, n, full_bar + 8 * s);
+            start = end;
+            if (++s == p.n_stages) {
+                s = 0;
+                if (i >= p.n_stages) phase ^= 1;  // passes 1, 2, ... wait parities 0, 1, ...
             }
         }
-        // Leave no copy in flight: wait (bounded) for every stage issued but
-        // not consumed when something went wrong.
-        if (!ok) {
-            for (int k = 0; k < F::kStages && k < it; ++k) {
-                const int j = it - 1 - k, s = j % F::kStages;
-                mbar_wait_bounded(full_bar + 8 * s, (j / F::kStages) & 1);
+        if (!ok) {  // leave no copy in flight
+            for (int k = 0; k < p.n_stages && k < i; ++k) {
+                const int j = i - 1 - k;
+                mbar_wait_bounded(full_bar + 8 * (j % p.n_stages), (j / p.n_stages) & 1);
             }
         }
         return;
     }
 
     // ----------------------------------------------------------- consumers
+    const int S = p.segments, NW = p.nwi, SW = p.seg_wi, J = p.wi_per_lane;
+    const int sg = warp % S, grp = warp / S, n_grp = kConsumerWarps / S;
+    int wi[kMaxJ];
+    bool has[kMaxJ];
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j) {
+        const int o = lane + 32 * j;
+        wi[j] = sg * SW + o;
+        has[j] = j < J && o < SW && wi[j] < NW;
+    }
+
     // x depends on the previous kernel in the stream (x quantization or the
-    // GEMV that produced x); weights do not, so the producer never waits.
+    // GEMV that produced x); the weights do not, so the producer never waits.
     pdl_wait();
-    if constexpr (F::kIntX) {
-        const int nxb = p.K / 32;
-        const int4* lsrc = reinterpret_cast<const int4*>(p.xq_limbs);
-        for (int i = threadIdx.x; i < nxb * (kXQLimbBytes / 16); i += kConsumerWarps * 32) {
-            const int4 v = __ldg(lsrc + i);
-            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(xs + 16 * i), "r"(v.x), "r"(v.y), "r"(v.z),
-                         "r"(v.w)
-                         : "memory");
-        }
-        const uint32_t ms = xs + nxb * kXQLimbBytes;
-        for (int i = threadIdx.x; i < nxb; i += kConsumerWarps * 32) {
-            const int4 v = __ldg(p.xq_meta + i);
-            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(ms + 16 * i), "r"(v.x), "r"(v.y), "r"(v.z),
-                         "r"(v.w)
-                         : "memory");
-        }
-    } else {
-        if (p.x_bf16) {
-            const uint16_t* xb = static_cast<const uint16_t*>(p.x);
-            for (int i = threadIdx.x; i < p.K; i += kConsumerWarps * 32) {
-                const float v = __uint_as_float((uint32_t)xb[i] << 16);
-                asm volatile("st.shared.f32 [%0], %1;" ::"r"(xs + 4 * i), "f"(v) : "memory");
-            }
-        } else {
-            const float* xf = static_cast<const float*>(p.x);
-            for (int i = threadIdx.x; i < p.K; i += kConsumerWarps * 32)
-                asm volatile("st.shared.f32 [%0], %1;" ::"r"(xs + 4 * i), "f"(__ldg(xf + i)) : "memory");
+    XT X[kMaxJ];
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j) {
+        if (has[j]) {
+            if constexpr (F::kIntX) load_xint(p.xq_limbs, p.xq_meta, wi[j], X[j]);
+            else load_xf16(p.x, p.x_bf16, wi[j], X[j]);
         }
     }
-    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
 
-    const uint32_t xlimbs = xs;
-    const uint32_t xmeta = xs + (uint32_t)(p.K / 32) * kXQLimbBytes;
-    int it = 0;
-    bool ok = true;
-    for (int g = 0; g < n_groups && ok; ++g) {
-        const int r0 = row_begin + g * L::kRG;
-        const int nr = min(L::kRG, row_end - r0);
-        const int reff = (nr + kConsumerWarps - 1) / kConsumerWarps;
-        const int my0 = warp * reff;
-        const int mynr = max(0, min(reff, nr - my0));
-        float acc[F::kRows];
+    int s = 0, rot = 0;  // stage buffer, (i * R) % n_grp
+    uint32_t phase = 0;  // parity of the full-barrier phase to wait for
+    for (int i = 0; i < n_st; ++i) {
+        const int r0 = row_begin + i * R;
+        const int nr = min(R, row_end - r0);
+        if (!mbar_wait_bounded(full_bar + 8 * s, phase)) break;
+        const uint32_t base = stage0 + (uint32_t)(s * p.stage_bytes) + (uint32_t)(((uint64_t)r0 * p.row_bytes) & 15);
+        // first local row of this warp's group in this stage
+        int rl = grp - rot;
+        if (rl < 0) rl += n_grp;
+        for (; rl < nr; rl += n_grp) {
+            const uint32_t row = base + (uint32_t)(rl * p.row_bytes);
+            float acc = 0.f;
 #pragma unroll
-        for (int r = 0; r < F::kRows; ++r) acc[r] = 0.f;
-        for (int ch = 0; ch < n_chunks; ++ch, ++it) {
-            const int s = it % F::kStages, use = it / F::kStages;
-            if (!mbar_wait_bounded(full_bar + 8 * s, use & 1)) { ok = false; break; }
-            const int nwi_c = min(F::kChunkWI, p.nwi - ch * F::kChunkWI);
-            const uint32_t st = stage0 + (uint32_t)s * L::kStageBytes;
-            const uint64_t coff = (uint64_t)ch * L::kChunkBytes;
-            for (int j = lane; j < nwi_c; j += 32) {
-                const int gj = ch * F::kChunkWI + j;  // global work item = x block
-                if constexpr (F::kIntX) {
-                    XInt X;
-                    load_xint(xlimbs, xmeta, gj, X);
+            for (int j = 0; j < kMaxJ; ++j)
+                if (has[j]) acc += dot_wi<F>(row, wi[j], X[j]);
 #pragma unroll
-                    for (int r = 0; r < F::kRows; ++r) {
-                        if (r < mynr) {
-                            const int rl = my0 + r;
-                            const uint32_t delta =
-                                (uint32_t)(((uint64_t)(r0 + rl) * p.row_bytes + coff) & 15);
-                            const uint32_t base = st + rl * L::kRowStride + delta + wi_offset<F>(j);
-                            if constexpr (F::kBlockBytes == 18) acc[r] += dot_q4_0(base, X);
-                            else if constexpr (F::kBlockBytes == 34) acc[r] += dot_q8_0(base, X);
-                            else if constexpr (F::kBlockBytes == 176) acc[r] += dot_q5_k(base, j & 7, X);
-                            else acc[r] += dot_q6_k(base, j & 7, X);
-                        }
-                    }
-                } else {
-#pragma unroll
-                    for (int r = 0; r < F::kRows; ++r) {
-                        if (r < mynr) {
-                            const int rl = my0 + r;
-                            const uint32_t delta =
-                                (uint32_t)(((uint64_t)(r0 + rl) * p.row_bytes + coff) & 15);
-                            const uint32_t base = st + rl * L::kRowStride + delta + wi_offset<F>(j);
-                            acc[r] += dot_f16(base, xs + 64u * gj);
-                        }
-                    }
+            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (S == 1) {
+                if (lane == 0) p.y[r0 + rl] = acc;
+            } else if (lane == 0) {
+                float* sl = slots + (s * R + rl) * S;
+                sl[sg] = acc;
+                __threadfence_block();
+                const int prev = atomicAdd(&counters[s * R + rl], 1);
+                if (prev == S - 1) {  // last segment of this row: sum in segment order
+                    __threadfence_block();
+                    float y = 0.f;
+                    for (int k = 0; k < S; ++k) y += *(volatile float*)(sl + k);
+                    p.y[r0 + rl] = y;
+                    counters[s * R + rl] = 0;
                 }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(empty_bar + 8 * s);
         }
-        if (!ok) break;
-#pragma unroll
-        for (int r = 0; r < F::kRows; ++r) {
-            float v = acc[r];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0 && r < mynr) p.y[r0 + my0 + r] = v;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_bar + 8 * s);
+        if (++s == p.n_stages) {
+            s = 0;
+            phase ^= 1;
         }
+        rot += R % n_grp;
+        if (rot >= n_grp) rot -= n_grp;
     }
 }
 
@@ -469,7 +484,7 @@ __global__ void __launch_bounds__(256) xquant_kernel(const void* __restrict__ x,
     limbs[bidx * kXQLimbBytes + 32 + lane] = (uint8_t)(int8_t)xl;
     const int sa = __reduce_add_sync(0xffffffffu, lane < 16 ? X : 0);
     const int sb = __reduce_add_sync(0xffffffffu, lane < 16 ? 0 : X);
-    if (lane == 0) meta[bidx] = make_int4((int)__float_as_uint(s), sa, sb, 0);
+    if (lane == 0) meta[bidx] = make_int4((int)__float_as_uint(s), sa, sb, sa + sb);
 }
 
 // ------------------------------------------------------ generic fallback

@@ -168,16 +168,64 @@ int32_t launch(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st,
     return NEXUS_GPU_SUCCESS;
 }
 
+// Fast-path geometry for a weight format and shape (see gemv_kernels.cuh).
+// Returns false when the shape is outside the fast kernel's limits.
 template <class F>
-int32_t launch_fast(Device& d, const GemvParams& p, cudaStream_t st) {
-    const size_t smem = Layout<F>::smem_bytes(p.K);
+bool plan_fast(const Device& d, int N, int K, uint64_t row_bytes, GemvParams& p, size_t& smem) {
+    const int NW = K / F::kWIElems;
+    if (NW < 32) return false;
+    // K segments: the smallest divisor S of kConsumerWarps that leaves at most
+    // 32*kMaxJ work items (x slices held in registers) per warp and lets a
+    // stage hold one row for each of the 15/S row groups within
+    // kStageMaxBytes.  A stage then holds m rows per group, so every warp has
+    // work in every stage.
+    int S = 0;
+    for (int cand = 1; cand <= kMaxSegments; ++cand) {
+        if (kConsumerWarps % cand) continue;
+        if ((NW + cand - 1) / cand > 32 * kMaxJ) continue;
+        if ((uint64_t)(kConsumerWarps / cand) * row_bytes > (uint64_t)kStageMaxBytes && cand < kMaxSegments) continue;
+        S = cand;
+        break;
+    }
+    if (S == 0) return false;
+    const int SW = (NW + S - 1) / S;
+    const int J = (SW + 31) / 32;
+    if (J > kMaxJ) return false;
+    const int n_grp = kConsumerWarps / S;
+    const uint64_t grp_bytes = (uint64_t)n_grp * row_bytes;
+    const int m = (int)std::max<uint64_t>(1, std::min<uint64_t>(4, kStageTargetBytes / grp_bytes));
+    const int R = std::min(n_grp * m, kMaxStageRows);
+    const uint64_t sb = (R * row_bytes + 32 + 15) / 16 * 16;
+    const uint64_t avail = (uint64_t)d.smem_optin - kSmemHeader - 128;
+    int ns = (int)std::min<uint64_t>(kMaxStages, avail / sb);
+    while (ns > 2 && ns * R * S > kMaxSlots) --ns;
+    if (ns < 2 || ns * R * S > kMaxSlots) return false;
+    p.nwi = NW;
+    p.segments = S;
+    p.seg_wi = SW;
+    p.wi_per_lane = J;
+    p.stage_rows = R;
+    p.stage_bytes = (int)sb;
+    p.n_stages = ns;
+    smem = kSmemHeader + (size_t)ns * sb;
+    (void)N;
+    return true;
+}
+
+template <class F>
+int32_t launch_fast(Device& d, const GemvParams& p, size_t smem, cudaStream_t st) {
     const int grid = std::min(d.sms, p.N);
     return launch(gemv_m1_kernel<F>, dim3(grid), dim3(kGemvThreads), smem, st, p);
 }
 
-template <class F>
-bool fast_fits(const Device& d, int K) {
-    return Layout<F>::smem_bytes(K) <= (size_t)d.smem_optin;
+bool plan_for(uint32_t dtype, const Device& d, int N, int K, uint64_t rb, GemvParams& p, size_t& smem) {
+    switch (dtype) {
+        case NEXUS_GPU_GGUF_Q4_0: return plan_fast<FmtQ4_0>(d, N, K, rb, p, smem);
+        case NEXUS_GPU_GGUF_Q8_0: return plan_fast<FmtQ8_0>(d, N, K, rb, p, smem);
+        case NEXUS_GPU_GGUF_Q5_K: return plan_fast<FmtQ5_K>(d, N, K, rb, p, smem);
+        case NEXUS_GPU_GGUF_Q6_K: return plan_fast<FmtQ6_K>(d, N, K, rb, p, smem);
+        default: return (K % 16 == 0) && plan_fast<FmtF16>(d, N, K, rb, p, smem);
+    }
 }
 
 // One GEMV of M rows of x.  `ws` holds at least xq_bytes(dtype, M, cols).
@@ -201,14 +249,9 @@ int32_t run_gemv(Device& d, const void* dW, uint32_t dtype, const void* dX, uint
     uint8_t* limbs = ws;
     int4* meta = is_int_format(dtype) ? reinterpret_cast<int4*>(ws + align256(M * nxb * kXQLimbBytes)) : nullptr;
 
-    bool fast = w16;
-    switch (dtype) {
-        case NEXUS_GPU_GGUF_Q4_0: fast = fast && fast_fits<FmtQ4_0>(d, K); break;
-        case NEXUS_GPU_GGUF_Q8_0: fast = fast && fast_fits<FmtQ8_0>(d, K); break;
-        case NEXUS_GPU_GGUF_Q5_K: fast = fast && fast_fits<FmtQ5_K>(d, K); break;
-        case NEXUS_GPU_GGUF_Q6_K: fast = fast && fast_fits<FmtQ6_K>(d, K); break;
-        default: fast = fast && (K % 16 == 0) && fast_fits<FmtF16>(d, K); break;
-    }
+    GemvParams plan{};
+    size_t smem = 0;
+    const bool fast = w16 && plan_for(dtype, d, N, K, rb, plan, smem);
     if (fast && is_int_format(dtype)) {
         dim3 g((unsigned)((nxb + 7) / 8), (unsigned)M);
         if ((rc = launch(xquant_kernel, g, dim3(256), 0, st, dX, xbf, K, K, limbs, meta))) return rc;
@@ -223,7 +266,7 @@ int32_t run_gemv(Device& d, const void* dW, uint32_t dtype, const void* dX, uint
                 return rc;
             continue;
         }
-        GemvParams p{};
+        GemvParams p = plan;
         p.W = static_cast<const uint8_t*>(dW);
         p.total_bytes = (uint64_t)rb * rows;
         p.row_bytes = rb;
@@ -235,11 +278,11 @@ int32_t run_gemv(Device& d, const void* dW, uint32_t dtype, const void* dX, uint
         p.xq_limbs = limbs + m * nxb * kXQLimbBytes;
         p.xq_meta = meta ? meta + m * nxb : nullptr;
         switch (dtype) {
-            case NEXUS_GPU_GGUF_Q4_0: p.nwi = K / 32; rc = launch_fast<FmtQ4_0>(d, p, st); break;
-            case NEXUS_GPU_GGUF_Q8_0: p.nwi = K / 32; rc = launch_fast<FmtQ8_0>(d, p, st); break;
-            case NEXUS_GPU_GGUF_Q5_K: p.nwi = K / 32; rc = launch_fast<FmtQ5_K>(d, p, st); break;
-            case NEXUS_GPU_GGUF_Q6_K: p.nwi = K / 32; rc = launch_fast<FmtQ6_K>(d, p, st); break;
-            default: p.nwi = K / 16; rc = launch_fast<FmtF16>(d, p, st); break;
+            case NEXUS_GPU_GGUF_Q4_0: rc = launch_fast<FmtQ4_0>(d, p, smem, st); break;
+            case NEXUS_GPU_GGUF_Q8_0: rc = launch_fast<FmtQ8_0>(d, p, smem, st); break;
+            case NEXUS_GPU_GGUF_Q5_K: rc = launch_fast<FmtQ5_K>(d, p, smem, st); break;
+            case NEXUS_GPU_GGUF_Q6_K: rc = launch_fast<FmtQ6_K>(d, p, smem, st); break;
+            default: rc = launch_fast<FmtF16>(d, p, smem, st); break;
         }
         if (rc) return rc;
     }

@@ -1,15 +1,17 @@
-"""CPU check of gemv_m1_kernel's index arithmetic (nexusllm_b200/csrc/gemv_kernels.cuh).
+"""CPU check of gemv_m1_kernel's index arithmetic (nexusllm_b200/csrc/gemv_kernels.cuh)
+and of the host plan that sizes it (plan_fast in nexusllm_b200/csrc/nexus_gpu.cu).
 
-Restates, in Python, how the kernel splits rows over CTAs, row groups and
-K-chunks, which byte ranges the producer warp bulk-copies (and tail-copies)
-from global memory into each shared-memory stage, and which shared-memory
-bytes the consumer decoders read.  For every configuration shape and a set of
-ragged ones it asserts that every global read stays inside the weight matrix,
-every bulk copy is 16-byte aligned with a size that is a multiple of 16, every
-shared-memory write and read stays inside its row slot and the dynamic
-shared-memory allocation, and the decoders read exactly the bytes the copies
-delivered.  The format constants are parsed from the kernel header, so the
-check follows the kernel when they change.
+Restates, in Python, how the kernel splits rows over CTAs and stages, which
+byte range the producer bulk-copies (and tail-copies) into each shared-memory
+stage buffer, which shared bytes the consumer decoders read, and which x
+slices and y rows each thread touches.  For every configuration shape and a
+set of ragged ones it asserts that every global read stays inside the weight
+matrix and x, every bulk copy is 16-byte aligned with a size that is a
+multiple of 16, every shared write and read stays inside its stage buffer and
+the allocation, the decoders read only bytes the copies delivered, every row
+slot and y index is in range, and every row gets exactly the warps of its
+phase.  Constants are parsed from the kernel header so the check follows the
+kernel when they change.
 """
 import os
 import re
@@ -22,149 +24,190 @@ SMS = 148
 SMEM_OPTIN = 232448  # B200 max dynamic shared memory per block (227 KB)
 
 
-def _fmt_constants():
+def _constants():
     text = open(HDR).read()
-    out = {}
+    glob = {k: int(v) for k, v in re.findall(r"constexpr int (k\w+) = (\d+);", text)}
+    glob["kConsumers"] = glob["kConsumerWarps"] * 32
+    glob["kSmemHeader"] = glob["kBarBytes"] + glob["kMaxSlots"] * 4 + glob["kMaxStages"] * glob["kMaxStageRows"] * 4
+    fmts = {}
     for name in ("FmtQ4_0", "FmtQ8_0", "FmtQ5_K", "FmtQ6_K", "FmtF16"):
         body = re.search(r"struct %s \{(.*?)\};" % name, text, re.S).group(1)
         vals = dict(re.findall(r"(k\w+) = (\w+)", body))
-        out[name] = {k: (v == "true") if v in ("true", "false") else int(v) for k, v in vals.items()}
-    return out
+        fmts[name] = {k: (v == "true") if v in ("true", "false") else int(v) for k, v in vals.items()}
+    return glob, fmts
 
 
-FMT = _fmt_constants()
-CONSUMER_WARPS = 8
+C, FMT = _constants()
 
 
-def c16(v):
-    return (v + 15) // 16 * 16
+def plan(name, K, rb):
+    """Mirror of plan_fast<F> (nexus_gpu.cu); None when the generic kernel runs."""
+    f = FMT[name]
+    NW = K // f["kWIElems"]
+    if NW < 32:
+        return None
+    W = C["kConsumerWarps"]
+    S = next((c for c in range(1, C["kMaxSegments"] + 1)
+              if W % c == 0 and -(-NW // c) <= 32 * C["kMaxJ"]
+              and ((W // c) * rb <= C["kStageMaxBytes"] or c == C["kMaxSegments"])), 0)
+    if S == 0:
+        return None
+    SW = -(-NW // S)
+    J = -(-SW // 32)
+    if J > C["kMaxJ"]:
+        return None
+    n_grp = W // S
+    m = max(1, min(4, C["kStageTargetBytes"] // (n_grp * rb)))
+    R = min(n_grp * m, C["kMaxStageRows"])
+    sb = (R * rb + 32 + 15) // 16 * 16
+    avail = SMEM_OPTIN - C["kSmemHeader"] - 128
+    ns = min(C["kMaxStages"], avail // sb)
+    while ns > 2 and ns * R * S > C["kMaxSlots"]:
+        ns -= 1
+    if ns < 2 or ns * R * S > C["kMaxSlots"]:
+        return None
+    return dict(NW=NW, S=S, SW=SW, J=J, R=R, sb=sb, ns=ns, smem=C["kSmemHeader"] + ns * sb)
 
 
-def layout(f, K):
-    rg = CONSUMER_WARPS * f["kRows"]
-    chunk = f["kChunkWI"] // f["kWIPerBlock"] * f["kBlockBytes"]
-    stride = c16(chunk + 32)
-    stage = rg * stride
-    xb = (K // 32) * 80 if f["kIntX"] else K * 4
-    xb = (xb + 127) // 128 * 128
-    smem = 128 + xb + f["kStages"] * stage + 128
-    return rg, chunk, stride, stage, xb, smem
-
-
-def reads(name, base, j):
-    """(first, last) shared byte offsets a decoder touches for work item j
-    whose data starts at `base` (block base for Q4_0/Q8_0/FP16, super-block
-    base for the K-quants); plus the used byte range."""
+def reads(name, base, wi):
+    """Shared byte ranges (inclusive) a decoder touches for work item wi of a
+    row whose data starts at `base`, and the used byte range."""
     if name == "FmtQ4_0":
-        q = base + 2
-        return [(base, base + 1), (q & ~3, (q & ~3) + 19)], (base, base + 17)
+        b = base + 18 * wi
+        q = b + 2
+        return [(b, b + 1), (q & ~3, (q & ~3) + 19)], (b, b + 17)
     if name == "FmtQ8_0":
-        q = base + 2
-        return [(base, base + 1), (q & ~3, (q & ~3) + 35)], (base, base + 33)
+        b = base + 34 * wi
+        q = b + 2
+        return [(b, b + 1), (q & ~3, (q & ~3) + 35)], (b, b + 33)
     if name == "FmtQ5_K":
-        sub = j & 7
-        return [(base, base + 15), (base + 16 + 4 * sub, base + 19 + 4 * sub),
-                (base + 48 + 16 * sub, base + 63 + 16 * sub)], (base, base + 175)
+        o, sub = base + 176 * (wi // 8), wi & 7
+        assert o % 16 == 0
+        return [(o, o + 15), (o + 16 + 4 * sub, o + 19 + 4 * sub), (o + 48 + 16 * sub, o + 63 + 16 * sub)], \
+            (o, o + 175)
     if name == "FmtQ6_K":
-        p = j & 7
-        a, b = base + 16 * p, base + 128 + 8 * p
-        return [((a & ~3), (a & ~3) + 19), ((b & ~3), (b & ~3) + 11), (base + 192 + 2 * p, base + 193 + 2 * p),
-                (base + 208, base + 209)], (base, base + 209)
-    return [((base & ~3), (base & ~3) + 35)], (base, base + 31)
+        o, pr = base + 210 * (wi // 8), wi & 7
+        a, b = o + 16 * pr, o + 128 + 8 * pr
+        return [(a & ~3, (a & ~3) + 19), (b & ~3, (b & ~3) + 11), (o + 192 + 2 * pr, o + 193 + 2 * pr),
+                (o + 208, o + 209)], (o, o + 209)
+    b = base + 32 * wi
+    return [(b & ~3, (b & ~3) + 35)], (b, b + 31)
+
+
+ROW_BYTES = {"FmtQ4_0": lambda K: K // 32 * 18, "FmtQ8_0": lambda K: K // 32 * 34,
+             "FmtQ5_K": lambda K: K // 256 * 176, "FmtQ6_K": lambda K: K // 256 * 210,
+             "FmtF16": lambda K: K * 2}
 
 
 def simulate(name, N, K, ctas=None):
     f = FMT[name]
-    rg, chunk, stride, stage, xb, smem = layout(f, K)
-    assert smem <= SMEM_OPTIN, (name, K, smem)
-    per = 16 if name == "FmtF16" else 32
-    nwi = K // per
-    rb = {"FmtQ4_0": K // 32 * 18, "FmtQ8_0": K // 32 * 34, "FmtQ5_K": K // 256 * 176,
-          "FmtQ6_K": K // 256 * 210, "FmtF16": K * 2}[name]
+    rb = ROW_BYTES[name](K)
+    pl = plan(name, K, rb)
+    if pl is None:
+        return False
+    W15 = C["kConsumerWarps"]
+    assert pl["smem"] <= SMEM_OPTIN
+    NW, S, SW, J, R, sb, ns = pl["NW"], pl["S"], pl["SW"], pl["J"], pl["R"], pl["sb"], pl["ns"]
+    n_grp = W15 // S
+    assert n_grp * S == W15
     total = N * rb
     floor16 = total & ~15
     G = min(SMS, N)
-    nchunks = (nwi + f["kChunkWI"] - 1) // f["kChunkWI"]
+    # (segment, lane, j) -> work item: every work item of a row covered exactly once
+    cover = set()
+    for sg in range(S):
+        for lane in range(32):
+            for j in range(C["kMaxJ"]):
+                o = lane + 32 * j
+                wi = sg * SW + o
+                if j < J and o < SW and wi < NW:
+                    assert wi not in cover
+                    cover.add(wi)
+                    if f["kIntX"]:
+                        assert wi * 64 + 63 < (K // 32) * 64 and wi < K // 32
+                    else:
+                        assert wi * 16 + 15 < K
+    assert cover == set(range(NW))
     for c in (ctas if ctas is not None else range(G)):
         if c >= G:
             continue
         rb0, re0 = N * c // G, N * (c + 1) // G
         assert re0 > rb0
-        ngroups = (re0 - rb0 + rg - 1) // rg
-        for g in range(ngroups):
-            r0 = rb0 + g * rg
-            nr = min(rg, re0 - r0)
-            reff = (nr + CONSUMER_WARPS - 1) // CONSUMER_WARPS
-            assert reff <= f["kRows"]
-            for ch in range(nchunks):
-                nwi_c = min(f["kChunkWI"], nwi - ch * f["kChunkWI"])
-                cbytes = nwi_c // f["kWIPerBlock"] * f["kBlockBytes"]
-                coff = ch * chunk
-                tx = 0
-                for rl in range(nr):
-                    start = (r0 + rl) * rb + coff
-                    end = start + cbytes
-                    assert end <= (r0 + rl + 1) * rb <= total
-                    a = start & ~15
-                    bend = min((end + 15) & ~15, floor16)
-                    slot_lo, slot_hi = rl * stride, (rl + 1) * stride
-                    if bend > a:
-                        n = bend - a
-                        assert a % 16 == 0 and n % 16 == 0 and 0 <= a and bend <= total
-                        assert slot_lo + n <= slot_hi
-                        tx += n
-                    covered_hi = max(bend, a)
-                    for pos in range(max(a, bend), end, 2):
-                        assert pos % 2 == 0 and pos + 2 <= total
-                        assert slot_lo + (pos - a) + 2 <= slot_hi
-                        covered_hi = pos + 2
-                    delivered = (slot_lo, slot_lo + (covered_hi - a))  # bytes present in smem
-                    delta = start & 15
-                    if name == "FmtQ5_K":
-                        assert delta == 0
-                    for j in range(nwi_c):
-                        off = j * f["kBlockBytes"] if f["kWIPerBlock"] == 1 else (j // 8) * f["kBlockBytes"]
-                        base = slot_lo + delta + off
-                        rr, used = reads(name, base, j)
-                        for lo, hi in rr:
-                            assert slot_lo <= lo and hi < slot_hi, (name, N, K, c, g, ch, rl, j)
-                        assert delivered[0] <= used[0] and used[1] < delivered[1], (name, N, K, rl, j)
-                        if name == "FmtQ5_K":
-                            assert (base + 48) % 16 == 0
-                        gj = ch * f["kChunkWI"] + j
-                        if f["kIntX"]:
-                            assert gj * 64 + 63 < (K // 32) * 64
-                            assert (K // 32) * 64 + gj * 16 + 15 < xb
-                        else:
-                            assert gj * 64 + 63 < xb
-                assert tx < (1 << 20)
+        n_st = (re0 - rb0 + R - 1) // R
+        for i in range(n_st):
+            r0 = rb0 + i * R
+            nr = min(R, re0 - r0)
+            start, end = r0 * rb, r0 * rb + nr * rb
+            a = start & ~15
+            bend = min((end + 15) & ~15, floor16)
+            n = bend - a if bend > a else 0
+            assert a % 16 == 0 and n % 16 == 0 and n <= sb and bend <= total and n < (1 << 20)
+            hi = a + n
+            for pos in range(max(a, bend), end, 2):
+                assert pos + 2 <= total and (pos - a) + 2 <= sb
+                hi = pos + 2
+            delivered = hi - a
+            delta = start & 15
+            if name == "FmtQ5_K":
+                assert delta == 0
+            # every row of the stage goes to exactly one row group, the one
+            # q % n_grp of its CTA-local index q; slot and counter indices in range
+            seen = []
+            for grp in range(n_grp):
+                rl = grp - (i * R) % n_grp
+                if rl < 0:
+                    rl += n_grp
+                while rl < nr:
+                    assert (i * R + rl) % n_grp == grp
+                    seen.append(rl)
+                    st = i % ns
+                    assert (st * R + rl) * S + (S - 1) < C["kMaxSlots"]
+                    assert st * R + rl < C["kMaxStages"] * C["kMaxStageRows"]
+                    assert r0 + rl < re0
+                    rl += n_grp
+            assert sorted(seen) == list(range(nr))
+            for rl in range(nr):
+                rowbase = delta + rl * rb
+                for wi in range(NW):
+                    rr, used = reads(name, rowbase, wi)
+                    for lo, hi2 in rr:
+                        assert 0 <= lo and hi2 < sb, (name, N, K, c, i, rl, wi)
+                    assert used[1] < delivered, (name, N, K, c, i, rl, wi)
     return True
 
 
 CONFIG_SHAPES = [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336), (11008, 4096), (4096, 11008),
                  (8192, 8192), (1024, 8192), (28672, 8192), (8192, 28672), (128256, 4096), (128256, 8192)]
-RAGGED = [(1, 256), (3, 512), (7, 768), (37, 1024), (149, 2048), (150, 256), (300, 4096), (4097, 4096),
-          (513, 11008), (64, 2816)]
+RAGGED = [(1, 1024), (3, 1024), (37, 1024), (149, 2048), (150, 4096), (300, 4096), (4097, 4096),
+          (513, 11008), (64, 2816), (5, 28672)]
 
 
 @pytest.mark.parametrize("name", sorted(FMT))
 def test_config_shapes_in_bounds(name):
+    ran = 0
     for N, K in CONFIG_SHAPES:
         G = min(SMS, N)
-        simulate(name, N, K, ctas=sorted({0, 1, G // 2, G - 2, G - 1}))
+        ran += simulate(name, N, K, ctas=sorted({0, 1, G // 2, G - 2, G - 1}))
+    assert ran >= 8
 
 
 @pytest.mark.parametrize("name", sorted(FMT))
 def test_ragged_shapes_in_bounds(name):
     for N, K in RAGGED:
-        if name != "FmtF16" and K % 256 and name in ("FmtQ5_K", "FmtQ6_K"):
+        if name in ("FmtQ5_K", "FmtQ6_K") and K % 256:
             continue
-        simulate(name, N, K)
+        G = min(SMS, N)
+        simulate(name, N, K, ctas=sorted({0, G // 2, G - 1}))
 
 
-def test_q6_k_unaligned_rows_exercise_the_tail_copy():
-    # K=256*3: rows of 630 bytes; with 3 rows the matrix is 1890 bytes, not a
-    # multiple of 16, so the last row's last chunk needs the 2-byte tail path
-    simulate("FmtQ6_K", 3, 768)
-    simulate("FmtQ4_0", 1, 32)   # 18-byte matrix
-    simulate("FmtQ8_0", 1, 96)   # 102-byte matrix
+def test_fast_path_covers_the_configurations():
+    for name in ("FmtQ4_0", "FmtQ8_0", "FmtQ5_K", "FmtQ6_K"):
+        for N, K in CONFIG_SHAPES:
+            assert plan(name, K, ROW_BYTES[name](K)) is not None, (name, K)
+
+
+def test_unaligned_totals_exercise_the_tail_copy():
+    # Q6_K K=1024*... rows of 840 B; N=3 -> 2520 B total, not a multiple of 16
+    assert simulate("FmtQ6_K", 3, 1024)
+    assert simulate("FmtQ8_0", 1, 1024)   # 1088-byte matrix
+    assert simulate("FmtQ4_0", 3, 1024)   # 1728 = 108*16 -> no tail; still in bounds
