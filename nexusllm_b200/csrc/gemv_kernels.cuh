@@ -60,7 +60,7 @@ constexpr int kMaxSlots = 1024;      // n_stages * stage_rows * segments partial
 constexpr int kBarBytes = 256;       // 2 x kMaxStages mbarriers
 constexpr int kSmemHeader = kBarBytes + kMaxSlots * 4 + kMaxStages * kMaxStageRows * 4;  // + slots + counters
 constexpr int kStageTargetBytes = 32768;
-constexpr int kStageMaxBytes = 49152;
+constexpr int kStageMaxBytes = 73728;
 
 struct GemvParams {
     const uint8_t* W;        // weight blocks, 16-byte aligned
@@ -70,7 +70,8 @@ struct GemvParams {
     int nwi;                 // work items per row
     int segments;            // S: K segments per row, one warp each (divides kConsumerWarps)
     int seg_wi;              // work items per segment
-    int wi_per_lane;         // J = ceil(seg_wi / 32)
+    int wi_per_lane;         // J: work items per lane (a multiple of group)
+    int group;               // consecutive work items per lane (1 or the format's kGroup)
     int stage_rows;          // R
     int stage_bytes;         // shared bytes per stage buffer (multiple of 16)
     int n_stages;
@@ -84,24 +85,27 @@ struct GemvParams {
 // ------------------------------------------------------------------ formats
 // kBlockBytes: bytes of one storage block; kWIPerBlock: work items per block;
 // kWIElems: weights per work item.
+// kGroup: consecutive work items one lane decodes together when the shape
+// allows (a block pair for Q4_0/Q8_0, half a super-block for Q5_K/Q6_K), so
+// that block headers are decoded and bytes realigned once per group.
 struct FmtQ4_0 {
-    static constexpr int kBlockBytes = 18, kWIPerBlock = 1, kWIElems = 32;
+    static constexpr int kBlockBytes = 18, kWIPerBlock = 1, kWIElems = 32, kGroup = 2;
     static constexpr bool kIntX = true;
 };
 struct FmtQ8_0 {
-    static constexpr int kBlockBytes = 34, kWIPerBlock = 1, kWIElems = 32;
+    static constexpr int kBlockBytes = 34, kWIPerBlock = 1, kWIElems = 32, kGroup = 2;
     static constexpr bool kIntX = true;
 };
 struct FmtQ5_K {
-    static constexpr int kBlockBytes = 176, kWIPerBlock = 8, kWIElems = 32;
+    static constexpr int kBlockBytes = 176, kWIPerBlock = 8, kWIElems = 32, kGroup = 4;
     static constexpr bool kIntX = true;
 };
 struct FmtQ6_K {
-    static constexpr int kBlockBytes = 210, kWIPerBlock = 8, kWIElems = 32;
+    static constexpr int kBlockBytes = 210, kWIPerBlock = 8, kWIElems = 32, kGroup = 4;
     static constexpr bool kIntX = true;
 };
 struct FmtF16 {
-    static constexpr int kBlockBytes = 32, kWIPerBlock = 1, kWIElems = 16;  // 16 halves per work item
+    static constexpr int kBlockBytes = 32, kWIPerBlock = 1, kWIElems = 16, kGroup = 1;  // 16 halves per work item
     static constexpr bool kIntX = false;
 };
 
@@ -267,6 +271,145 @@ __device__ __forceinline__ float dot_q6_k(uint32_t o, int pair, const XInt& X) {
     return X.s * r;
 }
 
+// ------------------------------------------------------- grouped decoders
+// 32 Q4_0 weights already in registers (4 words of nibble pairs) against x.
+__device__ __forceinline__ float q4_0_block(float d, const uint32_t (&q)[4], const XInt& X) {
+    int shl = 0, shh = 0, sll = 0, slh = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint32_t lo = q[k] & 0x0F0F0F0Fu;  // weights 4k..4k+3
+        const uint32_t hi = q[k] & 0xF0F0F0F0u;  // 16 * weights 16+4k..
+        shl = dp4a_us(lo, X.h[k], shl);
+        shh = dp4a_us(hi, X.h[4 + k], shh);
+        sll = dp4a_us(lo, X.l[k], sll);
+        slh = dp4a_us(hi, X.l[4 + k], slh);
+    }
+    // sum((q - 8) * X), exact: the high-nibble sums carry a factor 16
+    const int t = ((shl + (shh >> 4)) << 8) + sll + (slh >> 4) - 8 * X.sx;
+    return (d * X.s) * (float)t;
+}
+
+// Two consecutive Q4_0 blocks (36 bytes) at a 4-byte-aligned shared address.
+__device__ __forceinline__ float dot_q4_0_x2(uint32_t p, const XInt& X0, const XInt& X1) {
+    uint32_t w[9];
+#pragma unroll
+    for (int k = 0; k < 9; ++k) w[k] = lds32(p + 4 * k);
+    uint32_t q0[4], q1[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        q0[k] = __byte_perm(w[k], w[k + 1], 0x5432);  // bytes 2..17
+        q1[k] = w[5 + k];                             // bytes 20..35
+    }
+    return q4_0_block(nexus_fp16(w[0] & 0xffffu), q0, X0) + q4_0_block(nexus_fp16_hi(w[4]), q1, X1);
+}
+
+__device__ __forceinline__ float q8_0_block(float d, const uint32_t (&q)[8], const XInt& X) {
+    int sh = 0, sl = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        sh = dp4a_ss(q[k], X.h[k], sh);
+        sl = dp4a_ss(q[k], X.l[k], sl);
+    }
+    return (d * X.s) * (float)((sh << 8) + sl);
+}
+
+// Two consecutive Q8_0 blocks (68 bytes) at a 4-byte-aligned shared address.
+__device__ __forceinline__ float dot_q8_0_x2(uint32_t p, const XInt& X0, const XInt& X1) {
+    uint32_t w[17];
+#pragma unroll
+    for (int k = 0; k < 17; ++k) w[k] = lds32(p + 4 * k);
+    uint32_t q0[8], q1[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        q0[k] = __byte_perm(w[k], w[k + 1], 0x5432);  // bytes 2..33
+        q1[k] = w[9 + k];                             // bytes 36..67
+    }
+    return q8_0_block(nexus_fp16(w[0] & 0xffffu), q0, X0) + q8_0_block(nexus_fp16_hi(w[8]), q1, X1);
+}
+
+// Q5_K sub-block: 16 qs bytes (4 words), its qh word, against x.
+__device__ __forceinline__ int q5_k_sub(const uint4& qv, uint32_t qhw, const XInt& X) {
+    const uint32_t qs[4] = {qv.x, qv.y, qv.z, qv.w};
+    int sh = 0, sl = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint32_t hb = (qhw >> (8 * k)) & 0xffu;
+        const uint32_t he = ((hb & 0x55u) * 0x00410410u) & 0x10101010u;
+        const uint32_t ho = (((hb >> 1) & 0x55u) * 0x00410410u) & 0x10101010u;
+        const uint32_t ulo = (qs[k] & 0x0F0F0F0Fu) | he;
+        const uint32_t uhi = ((qs[k] >> 4) & 0x0F0F0F0Fu) | ho;
+        sh = dp4a_us(ulo, X.h[k], sh);
+        sh = dp4a_us(uhi, X.h[4 + k], sh);
+        sl = dp4a_us(ulo, X.l[k], sl);
+        sl = dp4a_us(uhi, X.l[4 + k], sl);
+    }
+    return (sh << 8) + sl;
+}
+
+// Sub-blocks 4h..4h+3 (half h of the 176-byte super-block at 16-byte-aligned
+// o).  Scales and mins of the four sub-blocks come out of the 12 packed bytes
+// four at a time (src/quantization.cpp:418-430).
+__device__ __forceinline__ float dot_q5_k_x4(uint32_t o, int h, const XInt (&X)[4]) {
+    const uint32_t dd = lds32(o);
+    const float d = nexus_fp16(dd & 0xffffu);
+    const float dmin = nexus_fp16_hi(dd);
+    const uint32_t s0 = lds32(o + 4), s1 = lds32(o + 8), s2 = lds32(o + 12);
+    const uint32_t scw = h ? ((s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u)) : (s0 & 0x3F3F3F3Fu);
+    const uint32_t mnw = h ? (((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u)) : (s1 & 0x3F3F3F3Fu);
+    const uint4 qh = lds128(o + 16 + 16 * h);
+    const uint32_t qhw[4] = {qh.x, qh.y, qh.z, qh.w};
+    float r = 0.f;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const uint4 qv = lds128(o + 48 + 64 * h + 16 * t);
+        const int u = q5_k_sub(qv, qhw[t], X[t]);
+        const float scale = d * (float)((scw >> (8 * t)) & 0xffu);
+        const float minv = dmin * (float)((mnw >> (8 * t)) & 0xffu);
+        r = fmaf(X[t].s, scale * (float)u - minv * (float)X[t].sx, r);
+    }
+    return r;
+}
+
+// Q6_K: 16 weights of one sub-block from 2 ql words and 1 qh word.
+__device__ __forceinline__ int q6_k_sub(uint32_t l0, uint32_t l1, uint32_t hw, const uint32_t* xh,
+                                        const uint32_t* xl) {
+    const uint32_t pa = __byte_perm(hw, 0, 0x1100);  // qh bytes 0,0,1,1
+    const uint32_t pb = __byte_perm(hw, 0, 0x3322);  // qh bytes 2,2,3,3
+    const uint32_t u0 = (l0 & 0x0F0F0F0Fu) | (((pa << 4) & 0x00300030u) | (pa & 0x30003000u));
+    const uint32_t u1 = (l1 & 0x0F0F0F0Fu) | (((pb << 4) & 0x00300030u) | (pb & 0x30003000u));
+    const uint32_t u2 = ((l0 >> 4) & 0x0F0F0F0Fu) | (((pa << 2) & 0x00300030u) | ((pa >> 2) & 0x30003000u));
+    const uint32_t u3 = ((l1 >> 4) & 0x0F0F0F0Fu) | (((pb << 2) & 0x00300030u) | ((pb >> 2) & 0x30003000u));
+    int sh = dp4a_us(u0, xh[0], 0);
+    sh = dp4a_us(u1, xh[1], sh);
+    sh = dp4a_us(u2, xh[2], sh);
+    sh = dp4a_us(u3, xh[3], sh);
+    int sl = dp4a_us(u0, xl[0], 0);
+    sl = dp4a_us(u1, xl[1], sl);
+    sl = dp4a_us(u2, xl[2], sl);
+    sl = dp4a_us(u3, xl[3], sl);
+    return (sh << 8) + sl;
+}
+
+// Work items 4h..4h+3 (sub-blocks 8h..8h+7) of the 210-byte super-block at
+// 2-byte-aligned o.
+__device__ __forceinline__ float dot_q6_k_x4(uint32_t o, int h, const XInt (&X)[4]) {
+    uint32_t L[16], H[8], SC[2];
+    lds_words_2a<16>(o + 64 * h, L);
+    lds_words_2a<8>(o + 128 + 32 * h, H);
+    lds_words_2a<2>(o + 192 + 8 * h, SC);
+    const float d = nexus_fp16(lds16(o + 208));
+    float r = 0.f;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const int sc0 = (int)(int8_t)((SC[t >> 1] >> (16 * (t & 1))) & 0xffu);
+        const int sc1 = (int)(int8_t)((SC[t >> 1] >> (16 * (t & 1) + 8)) & 0xffu);
+        const int v0 = q6_k_sub(L[4 * t], L[4 * t + 1], H[2 * t], X[t].h, X[t].l) - 32 * X[t].sa;
+        const int v1 = q6_k_sub(L[4 * t + 2], L[4 * t + 3], H[2 * t + 1], X[t].h + 4, X[t].l + 4) - 32 * X[t].sb;
+        r = fmaf(X[t].s, d * ((float)sc0 * (float)v0 + (float)sc1 * (float)v1), r);
+    }
+    return r;
+}
+
 // FP16: 16 halves at p (2-byte aligned) against x held in registers.
 __device__ __forceinline__ float dot_f16(uint32_t p, const XF16& X) {
     uint32_t w[8];
@@ -308,7 +451,7 @@ __device__ __forceinline__ float dot_wi(uint32_t row, int wi, const X& x) {
 // y itself; with S > 1 each warp leaves its row partial in a shared slot and
 // bumps the row's arrival counter, and the last of the S warps sums the slots
 // in segment order and writes y -- deterministic, no CTA-wide barrier.
-template <class F>
+template <class F, int G>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_m1_kernel(const GemvParams p) {
     using XT = typename std::conditional<F::kIntX, XInt, XF16>::type;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -320,9 +463,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_m1_kernel(const GemvPara
     const uint32_t stage0 = sbase + kSmemHeader;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int G = gridDim.x, c = blockIdx.x;
-    const int row_begin = (int)((int64_t)p.N * c / G);
-    const int row_end = (int)((int64_t)p.N * (c + 1) / G);
+    const int n_cta = gridDim.x, c = blockIdx.x;
+    const int row_begin = (int)((int64_t)p.N * c / n_cta);
+    const int row_end = (int)((int64_t)p.N * (c + 1) / n_cta);
     const int R = p.stage_rows;
     const int n_st = (row_end - row_begin + R - 1) / R;
 
@@ -383,11 +526,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_m1_kernel(const GemvPara
     // ----------------------------------------------------------- consumers
     const int S = p.segments, NW = p.nwi, SW = p.seg_wi, J = p.wi_per_lane;
     const int sg = warp % S, grp = warp / S, n_grp = kConsumerWarps / S;
+    // lane -> work items: G consecutive items per lane per round of 32*G
     int wi[kMaxJ];
     bool has[kMaxJ];
 #pragma unroll
     for (int j = 0; j < kMaxJ; ++j) {
-        const int o = lane + 32 * j;
+        const int o = G * (lane + 32 * (j / G)) + (j % G);
         wi[j] = sg * SW + o;
         has[j] = j < J && o < SW && wi[j] < NW;
     }
@@ -417,9 +561,26 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_m1_kernel(const GemvPara
         for (; rl < nr; rl += n_grp) {
             const uint32_t row = base + (uint32_t)(rl * p.row_bytes);
             float acc = 0.f;
+            if constexpr (G == 1) {
 #pragma unroll
-            for (int j = 0; j < kMaxJ; ++j)
-                if (has[j]) acc += dot_wi<F>(row, wi[j], X[j]);
+                for (int j = 0; j < kMaxJ; ++j)
+                    if (has[j]) acc += dot_wi<F>(row, wi[j], X[j]);
+            } else {
+                // groups are whole: the host only picks G > 1 when segments
+                // and rows hold whole groups
+#pragma unroll
+                for (int jj = 0; jj < kMaxJ / G; ++jj) {
+                    const int j = jj * G;
+                    if (!has[j]) continue;
+                    const uint32_t b = row + wi_offset<F>(wi[j]);
+                    if constexpr (F::kBlockBytes == 18) acc += dot_q4_0_x2(b, X[j], X[j + 1]);
+                    else if constexpr (F::kBlockBytes == 34) acc += dot_q8_0_x2(b, X[j], X[j + 1]);
+                    else if constexpr (F::kBlockBytes == 176)
+                        acc += dot_q5_k_x4(b, (wi[j] >> 2) & 1, *reinterpret_cast<const XInt(*)[4]>(&X[j]));
+                    else
+                        acc += dot_q6_k_x4(b, (wi[j] >> 2) & 1, *reinterpret_cast<const XInt(*)[4]>(&X[j]));
+                }
+            }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
             if (S == 1) {

@@ -135,7 +135,10 @@ int32_t get_device(Device** out) {
 
 template <class F>
 int32_t set_smem_attr(int bytes) {
-    CUDA_TRY(cudaFuncSetAttribute(gemv_m1_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    CUDA_TRY(cudaFuncSetAttribute(gemv_m1_kernel<F, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    if (F::kGroup > 1)
+        CUDA_TRY(cudaFuncSetAttribute(gemv_m1_kernel<F, F::kGroup>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      bytes));
     return NEXUS_GPU_SUCCESS;
 }
 
@@ -188,9 +191,12 @@ bool plan_fast(const Device& d, int N, int K, uint64_t row_bytes, GemvParams& p,
         break;
     }
     if (S == 0) return false;
-    const int SW = (NW + S - 1) / S;
-    const int J = (SW + 31) / 32;
+    // grouped lanes need whole groups in every segment and row
+    const int Gp = (NW % F::kGroup == 0) ? F::kGroup : 1;
+    const int SW = ((NW + S - 1) / S + Gp - 1) / Gp * Gp;
+    const int J = (SW + 32 * Gp - 1) / (32 * Gp) * Gp;
     if (J > kMaxJ) return false;
+    p.group = Gp;
     const int n_grp = kConsumerWarps / S;
     const uint64_t grp_bytes = (uint64_t)n_grp * row_bytes;
     const int m = (int)std::max<uint64_t>(1, std::min<uint64_t>(4, kStageTargetBytes / grp_bytes));
@@ -215,7 +221,9 @@ bool plan_fast(const Device& d, int N, int K, uint64_t row_bytes, GemvParams& p,
 template <class F>
 int32_t launch_fast(Device& d, const GemvParams& p, size_t smem, cudaStream_t st) {
     const int grid = std::min(d.sms, p.N);
-    return launch(gemv_m1_kernel<F>, dim3(grid), dim3(kGemvThreads), smem, st, p);
+    if (F::kGroup > 1 && p.group == F::kGroup)
+        return launch(gemv_m1_kernel<F, F::kGroup>, dim3(grid), dim3(kGemvThreads), smem, st, p);
+    return launch(gemv_m1_kernel<F, 1>, dim3(grid), dim3(kGemvThreads), smem, st, p);
 }
 
 bool plan_for(uint32_t dtype, const Device& d, int N, int K, uint64_t rb, GemvParams& p, size_t& smem) {

@@ -82,12 +82,14 @@ def test_golden_dequant_bit_exact(L, be, golden):
 
 # ------------------------------------------------------------ seeded parity
 SHAPES = [(4096, 4096), (1024, 4096), (11008, 4096), (4096, 11008), (300, 14336), (1, 4096), (7, 256),
-          (149, 512), (4097, 1024), (64, 28672)]
+          (149, 512), (4097, 1024), (64, 28672), (300, 1056), (45, 3104)]
 
 
 @pytest.mark.parametrize("dt", FORMATS, ids=lambda d: d.name)
 def test_parity_vs_oracle(be, port, dt):
     for i, (rows, cols) in enumerate(SHAPES):
+        if cols % BLOCK[dt][0]:
+            continue  # odd block counts (ungrouped lanes) exist only for the 32-element formats
         W = synth.blocks_numpy(dt, rows, cols, 1000 * int(dt) + i)
         x = synth.activations_numpy(1, cols, 7000 + i)[0]
         want = port.gemv(int(dt), W, x, rows, cols)

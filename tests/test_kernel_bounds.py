@@ -52,8 +52,9 @@ def plan(name, K, rb):
               and ((W // c) * rb <= C["kStageMaxBytes"] or c == C["kMaxSegments"])), 0)
     if S == 0:
         return None
-    SW = -(-NW // S)
-    J = -(-SW // 32)
+    Gp = f["kGroup"] if NW % f["kGroup"] == 0 else 1
+    SW = -(-(-(-NW // S)) // Gp) * Gp
+    J = -(-SW // (32 * Gp)) * Gp
     if J > C["kMaxJ"]:
         return None
     n_grp = W // S
@@ -66,7 +67,29 @@ def plan(name, K, rb):
         ns -= 1
     if ns < 2 or ns * R * S > C["kMaxSlots"]:
         return None
-    return dict(NW=NW, S=S, SW=SW, J=J, R=R, sb=sb, ns=ns, smem=C["kSmemHeader"] + ns * sb)
+    return dict(NW=NW, S=S, SW=SW, J=J, G=Gp, R=R, sb=sb, ns=ns, smem=C["kSmemHeader"] + ns * sb)
+
+
+def reads_group(name, base, wi):
+    """Grouped decoders (dot_*_x2 / dot_*_x4): ranges read for the group that
+    starts at work item wi, and the used byte range."""
+    if name == "FmtQ4_0":
+        b = base + 18 * wi
+        assert b % 4 == 0
+        return [(b, b + 35)], (b, b + 35)
+    if name == "FmtQ8_0":
+        b = base + 34 * wi
+        assert b % 4 == 0
+        return [(b, b + 67)], (b, b + 67)
+    if name == "FmtQ5_K":
+        o, h = base + 176 * (wi // 8), (wi >> 2) & 1
+        assert o % 16 == 0 and wi % 4 == 0
+        return [(o, o + 15), (o + 16 + 16 * h, o + 31 + 16 * h), (o + 48 + 64 * h, o + 111 + 64 * h)], (o, o + 175)
+    o, h = base + 210 * (wi // 8), (wi >> 2) & 1
+    assert wi % 4 == 0
+    a, b, c = o + 64 * h, o + 128 + 32 * h, o + 192 + 8 * h
+    return [(a & ~3, (a & ~3) + 67), (b & ~3, (b & ~3) + 35), (c & ~3, (c & ~3) + 11), (o + 208, o + 209)], \
+        (o, o + 209)
 
 
 def reads(name, base, wi):
@@ -107,7 +130,7 @@ def simulate(name, N, K, ctas=None):
         return False
     W15 = C["kConsumerWarps"]
     assert pl["smem"] <= SMEM_OPTIN
-    NW, S, SW, J, R, sb, ns = pl["NW"], pl["S"], pl["SW"], pl["J"], pl["R"], pl["sb"], pl["ns"]
+    NW, S, SW, J, Gp, R, sb, ns = pl["NW"], pl["S"], pl["SW"], pl["J"], pl["G"], pl["R"], pl["sb"], pl["ns"]
     n_grp = W15 // S
     assert n_grp * S == W15
     total = N * rb
@@ -115,19 +138,26 @@ def simulate(name, N, K, ctas=None):
     G = min(SMS, N)
     # (segment, lane, j) -> work item: every work item of a row covered exactly once
     cover = set()
+    starts = set()   # first work item of each lane group
     for sg in range(S):
         for lane in range(32):
             for j in range(C["kMaxJ"]):
-                o = lane + 32 * j
+                o = Gp * (lane + 32 * (j // Gp)) + (j % Gp)
                 wi = sg * SW + o
                 if j < J and o < SW and wi < NW:
                     assert wi not in cover
                     cover.add(wi)
+                    if j % Gp == 0:
+                        starts.add(wi)
+                        # a group is whole whenever its first item is valid
+                        assert all(o + t < SW and wi + t < NW for t in range(Gp))
                     if f["kIntX"]:
                         assert wi * 64 + 63 < (K // 32) * 64 and wi < K // 32
                     else:
                         assert wi * 16 + 15 < K
     assert cover == set(range(NW))
+    if Gp > 1 and name in ("FmtQ4_0", "FmtQ8_0"):
+        assert rb % 4 == 0  # block pairs start 4-byte aligned
     for c in (ctas if ctas is not None else range(G)):
         if c >= G:
             continue
@@ -168,8 +198,8 @@ def simulate(name, N, K, ctas=None):
             assert sorted(seen) == list(range(nr))
             for rl in range(nr):
                 rowbase = delta + rl * rb
-                for wi in range(NW):
-                    rr, used = reads(name, rowbase, wi)
+                for wi in (sorted(starts) if Gp > 1 else range(NW)):
+                    rr, used = reads_group(name, rowbase, wi) if Gp > 1 else reads(name, rowbase, wi)
                     for lo, hi2 in rr:
                         assert 0 <= lo and hi2 < sb, (name, N, K, c, i, rl, wi)
                     assert used[1] < delivered, (name, N, K, c, i, rl, wi)
@@ -179,7 +209,7 @@ def simulate(name, N, K, ctas=None):
 CONFIG_SHAPES = [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336), (11008, 4096), (4096, 11008),
                  (8192, 8192), (1024, 8192), (28672, 8192), (8192, 28672), (128256, 4096), (128256, 8192)]
 RAGGED = [(1, 1024), (3, 1024), (37, 1024), (149, 2048), (150, 4096), (300, 4096), (4097, 4096),
-          (513, 11008), (64, 2816), (5, 28672)]
+          (513, 11008), (64, 2816), (5, 28672), (7, 1056), (9, 3104)]
 
 
 @pytest.mark.parametrize("name", sorted(FMT))
