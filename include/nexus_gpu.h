@@ -148,6 +148,28 @@ NEXUS_GPU_API int32_t nexus_gpu_gemv_ws(const void* dW, uint32_t dtype, const vo
                                         size_t M, size_t rows, size_t cols, void* workspace,
                                         size_t workspace_bytes, void* stream);
 
+/* nexus_gpu_gemv without any allocation.  No counterpart in the reference.
+ *
+ * For callers that cannot call cudaMalloc: engines that assign all device
+ * memory to weights and KV cache at start-up and forbid allocations on the
+ * decode path, code that must not trigger the device-wide synchronisation a
+ * cudaMalloc/cudaFree can cause, and callers with no workspace of their own to
+ * hand to nexus_gpu_gemv_ws.  Same arguments and results as nexus_gpu_gemv.
+ *
+ * Its scratch (the quantized activations) is a fixed 1 MiB array inside the
+ * library, held by every GPU that loads the library until the process exits.
+ * Shapes needing more than that -- M * cols / 32 * 80 bytes (plus alignment)
+ * above 1 MiB, e.g. M = 1 with cols above about 409,000 -- are rejected with
+ * NEXUS_GPU_ERROR_WORKSPACE and a message naming the limit.  FP16 weights need
+ * no scratch.  The first call on a device looks up the array's device address
+ * for that device (cudaGetSymbolAddress, with the device current); make that
+ * first call before any stream capture.  All calls share the one array and
+ * every call rewrites the part it reads, so nothing needs clearing between
+ * calls, but calls that overlap on the GPU (different streams, no ordering
+ * between them) race on it: serialise them. */
+NEXUS_GPU_API int32_t nexus_gpu_gemv_noalloc(const void* dW, uint32_t dtype, const void* dX, uint32_t x_dtype,
+                                             float* dY, size_t M, size_t rows, size_t cols, void* stream);
+
 /* Bit-exact dequantization of `count` elements (a whole number of blocks)
  * from device blocks to device floats, asynchronous on `stream`. */
 NEXUS_GPU_API int32_t nexus_gpu_dequantize(const void* dW, uint32_t dtype, float* dOut, size_t count, void* stream);

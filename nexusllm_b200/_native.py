@@ -39,6 +39,7 @@ SIGNATURES = {
     "nexus_gpu_gemv": (_I32, [_VP, _U32, _VP, _U32, _VP, _SZ, _SZ, _SZ, _VP]),
     "nexus_gpu_gemv_workspace_size": (_SZ, [_U32, _SZ, _SZ, _SZ]),
     "nexus_gpu_gemv_ws": (_I32, [_VP, _U32, _VP, _U32, _VP, _SZ, _SZ, _SZ, _VP, _SZ, _VP]),
+    "nexus_gpu_gemv_noalloc": (_I32, [_VP, _U32, _VP, _U32, _VP, _SZ, _SZ, _SZ, _VP]),
     "nexus_gpu_dequantize": (_I32, [_VP, _U32, _VP, _SZ, _VP]),
     "nexus_gpu_last_error": (ctypes.c_char_p, []),
     "nexus_gpu_device_status": (_I32, [ctypes.POINTER(ctypes.c_uint32)]),

@@ -18,6 +18,10 @@
 #include "gemv_kernels.cuh"
 
 namespace nexus_gpu {
+
+// Fixed scratch of the no-allocation GEMV entry point (see nexus_gpu_gemv_noalloc).
+static __device__ __align__(256) uint8_t g_noalloc_scratch[size_t(1) << 20];
+
 namespace {
 
 thread_local std::string t_last_error;
@@ -471,6 +475,56 @@ void report_void(const char* fn, int32_t rc) {
     if (rc != NEXUS_GPU_SUCCESS) fprintf(stderr, "[nexus_gpu] %s: %s (status %d)\n", fn, t_last_error.c_str(), rc);
 }
 
+// ------------------------------------------------ no-allocation entry point
+// Scratch of nexus_gpu_gemv_noalloc: the quantized activations (limbs and
+// block metadata) that xquant_kernel writes and the GEMV kernel reads.  It is
+// part of the loaded module, so every GPU that loads the library holds these
+// kNoAllocScratchBytes until the process exits, and no call ever allocates.
+// In host code the array's name is only a host-side stand-in: the device
+// address comes from cudaGetSymbolAddress, once per device.
+constexpr size_t kNoAllocScratchBytes = size_t(1) << 20;  // 1 MiB
+constexpr int kNoAllocMaxDevices = 64;
+static_assert(sizeof(g_noalloc_scratch) == kNoAllocScratchBytes, "scratch array and its stated limit differ");
+
+struct NoAllocDevice {
+    bool ready = false;
+    uint8_t* scratch = nullptr;  // device address of g_noalloc_scratch on this device
+    Device dev;                  // geometry and kernel attributes only; no stream, no memory
+};
+std::mutex g_noalloc_mu;
+NoAllocDevice g_noalloc[kNoAllocMaxDevices];  // constructed at load time: calls never allocate
+
+// First call on a device (with that device current): resolve the scratch
+// array's device address and read the device geometry.
+int32_t noalloc_device(Device** out_dev, uint8_t** out_scratch) {
+    int id = 0, n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return fail(NEXUS_GPU_ERROR_NO_DEVICE, "no CUDA device");
+    }
+    CUDA_TRY(cudaGetDevice(&id));
+    if (id < 0 || id >= kNoAllocMaxDevices)
+        return fail(NEXUS_GPU_ERROR_NO_DEVICE, "device %d beyond the %d devices the no-allocation path serves", id,
+                    kNoAllocMaxDevices);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    NoAllocDevice& e = g_noalloc[id];
+    if (!e.ready) {
+        void* ptr = nullptr;
+        const cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (err != cudaSuccess)
+            return fail(NEXUS_GPU_ERROR_CUDA, "cudaGetSymbolAddress(no-allocation scratch) failed: %s",
+                        cudaGetErrorString(err));
+        e.dev.id = id;
+        CUDA_TRY(cudaDeviceGetAttribute(&e.dev.sms, cudaDevAttrMultiProcessorCount, id));
+        CUDA_TRY(cudaDeviceGetAttribute(&e.dev.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, id));
+        e.scratch = static_cast<uint8_t*>(ptr);
+        e.ready = true;
+    }
+    *out_dev = &e.dev;
+    *out_scratch = e.scratch;
+    return NEXUS_GPU_SUCCESS;
+}
+
 }  // namespace
 }  // namespace nexus_gpu
 
@@ -602,6 +656,24 @@ NEXUS_GPU_API int32_t nexus_gpu_gemv(const void* dW, uint32_t dtype, const void*
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     if ((rc = get_workspace(*d, st, xq_bytes(dtype, M, cols), &ws))) return rc;
     return run_gemv(*d, dW, dtype, dX, x_dtype, dY, M, rows, cols, ws, st);
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_gemv_noalloc(const void* dW, uint32_t dtype, const void* dX, uint32_t x_dtype,
+                                             float* dY, size_t M, size_t rows, size_t cols, void* stream) {
+    t_last_error.clear();
+    FormatInfo f;
+    int32_t rc = check_shape(dtype, rows, cols, f);
+    if (rc) return rc;
+    const size_t need = xq_bytes(dtype, M, cols);
+    if (need > kNoAllocScratchBytes)
+        return fail(NEXUS_GPU_ERROR_WORKSPACE,
+                    "nexus_gpu_gemv_noalloc: M=%zu x cols=%zu needs %zu bytes of scratch, above its fixed %zu-byte "
+                    "array (M * cols / 32 * 80 bytes must fit); use nexus_gpu_gemv_ws for larger shapes",
+                    M, cols, need, kNoAllocScratchBytes);
+    Device* d = nullptr;
+    uint8_t* scratch = nullptr;
+    if ((rc = noalloc_device(&d, &scratch))) return rc;
+    return run_gemv(*d, dW, dtype, dX, x_dtype, dY, M, rows, cols, scratch, static_cast<cudaStream_t>(stream));
 }
 
 NEXUS_GPU_API int32_t nexus_gpu_dequantize(const void* dW, uint32_t dtype, float* dOut, size_t count, void* stream) {
