@@ -436,9 +436,10 @@ def main():
         dist.destroy_process_group()
 
 
-# bytes read + written by one FFN launch in an ncu capture (profiles/); None
-# until a capture has been summarised there
-TRAFFIC_PER_FFN_LAUNCH = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one FFN launch of the fused
+# GEMV (mean of gate/up/down), from the ncu capture summarised in
+# profiles/gemv_q4_0_llama3_8b_decode_stack.md
+TRAFFIC_PER_FFN_LAUNCH = 33071445
 
 
 def verify_head(torch, be, head, h0, y_graph, world, rank):
