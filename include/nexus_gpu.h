@@ -170,6 +170,34 @@ NEXUS_GPU_API int32_t nexus_gpu_gemv_ws(const void* dW, uint32_t dtype, const vo
 NEXUS_GPU_API int32_t nexus_gpu_gemv_noalloc(const void* dW, uint32_t dtype, const void* dX, uint32_t x_dtype,
                                              float* dY, size_t M, size_t rows, size_t cols, void* stream);
 
+/* ------------------------------------------------------------ GEMV stacks */
+
+/* One GEMV of a stack: y[rows] = W[rows, cols] . x (device pointers).  x is
+ * the stack input (x_source = -1) or the y of an earlier task x_source.
+ * `after` (-1 for none) names an earlier task that must have completed before
+ * this one starts -- the ordering a decode step has between layers even when
+ * the data does not flow directly. */
+typedef struct {
+    const void* W;
+    uint64_t rows, cols;
+    float* y;
+    int32_t x_source;
+    int32_t after;
+} NexusGpuStackTask;
+
+/* A sequence of GEMVs run by ONE persistent, cooperative kernel launch: the
+ * GEMVs of a decode step (src/forward_pass.cpp:504-585 runs them one call at a
+ * time).  Weights stream through the SMs back to back across tasks; each task
+ * waits only for its own input.  Results equal nexus_gpu_gemv on the same
+ * inputs bit for bit.  Integer GGUF formats; every task's shape must be inside
+ * the fast kernel's limits.  No counterpart in the reference. */
+NEXUS_GPU_API int32_t nexus_gpu_stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n_tasks,
+                                             uint64_t input_cols, void** out_stack);
+/* Run the stack on `stream` with input dX (fp32, input_cols).  Graph-capturable:
+ * a counter reset and one kernel launch.  Runs of one stack must not overlap. */
+NEXUS_GPU_API int32_t nexus_gpu_stack_run(void* stack, const float* dX, void* stream);
+NEXUS_GPU_API int32_t nexus_gpu_stack_destroy(void* stack);
+
 /* Bit-exact dequantization of `count` elements (a whole number of blocks)
  * from device blocks to device floats, asynchronous on `stream`. */
 NEXUS_GPU_API int32_t nexus_gpu_dequantize(const void* dW, uint32_t dtype, float* dOut, size_t count, void* stream);

@@ -40,6 +40,9 @@ SIGNATURES = {
     "nexus_gpu_gemv_workspace_size": (_SZ, [_U32, _SZ, _SZ, _SZ]),
     "nexus_gpu_gemv_ws": (_I32, [_VP, _U32, _VP, _U32, _VP, _SZ, _SZ, _SZ, _VP, _SZ, _VP]),
     "nexus_gpu_gemv_noalloc": (_I32, [_VP, _U32, _VP, _U32, _VP, _SZ, _SZ, _SZ, _VP]),
+    "nexus_gpu_stack_create": (_I32, [_U32, _VP, _U32, ctypes.c_uint64, ctypes.POINTER(_VP)]),
+    "nexus_gpu_stack_run": (_I32, [_VP, _VP, _VP]),
+    "nexus_gpu_stack_destroy": (_I32, [_VP]),
     "nexus_gpu_dequantize": (_I32, [_VP, _U32, _VP, _SZ, _VP]),
     "nexus_gpu_last_error": (ctypes.c_char_p, []),
     "nexus_gpu_device_status": (_I32, [ctypes.POINTER(ctypes.c_uint32)]),
@@ -47,6 +50,12 @@ SIGNATURES = {
                                      ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
     "nexus_gpu_version": (ctypes.c_char_p, []),
 }
+
+class StackTask(ctypes.Structure):
+    """NexusGpuStackTask (include/nexus_gpu.h)."""
+    _fields_ = [("W", _VP), ("rows", ctypes.c_uint64), ("cols", ctypes.c_uint64), ("y", _VP),
+                ("x_source", ctypes.c_int32), ("after", ctypes.c_int32)]
+
 
 _lib = None
 

@@ -116,16 +116,19 @@ struct XInt {
     int sa, sb, sx;  // sums of X over [0,16), [16,32), [0,32)
 };
 
+// kCoherent: read through L2 (ld.global.cg) -- needed when the quantized x was
+// written by other CTAs of the same kernel; otherwise the read-only path.
+template <bool kCoherent = false>
 __device__ __forceinline__ void load_xint(const uint8_t* limbs, const int4* meta, int gj, XInt& X) {
     const int4* a = reinterpret_cast<const int4*>(limbs + (size_t)gj * kXQLimbBytes);
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
-        const int4 v = __ldg(a + q);
+        const int4 v = kCoherent ? __ldcg(a + q) : __ldg(a + q);
         X.h[4 * q + 0] = v.x; X.h[4 * q + 1] = v.y; X.h[4 * q + 2] = v.z; X.h[4 * q + 3] = v.w;
-        const int4 u = __ldg(a + 2 + q);
+        const int4 u = kCoherent ? __ldcg(a + 2 + q) : __ldg(a + 2 + q);
         X.l[4 * q + 0] = u.x; X.l[4 * q + 1] = u.y; X.l[4 * q + 2] = u.z; X.l[4 * q + 3] = u.w;
     }
-    const int4 m = __ldg(meta + gj);
+    const int4 m = kCoherent ? __ldcg(meta + gj) : __ldg(meta + gj);
     X.s = __int_as_float(m.x);
     X.sa = m.y;
     X.sb = m.z;
@@ -442,6 +445,47 @@ __device__ __forceinline__ float dot_wi(uint32_t row, int wi, const X& x) {
     }
 }
 
+// This lane's partial dot product of one row (shared address `row`) over its
+// work items; G consecutive items per lane when grouped.  Groups are whole:
+// the host only picks G > 1 when segments and rows hold whole groups.
+template <class F, int G, class XT>
+__device__ __forceinline__ float row_partial(uint32_t row, const int (&wi)[kMaxJ], const bool (&has)[kMaxJ],
+                                             const XT (&X)[kMaxJ]) {
+    float acc = 0.f;
+    if constexpr (G == 1) {
+#pragma unroll
+        for (int j = 0; j < kMaxJ; ++j)
+            if (has[j]) acc += dot_wi<F>(row, wi[j], X[j]);
+    } else {
+#pragma unroll
+        for (int jj = 0; jj < kMaxJ / G; ++jj) {
+            const int j = jj * G;
+            if (!has[j]) continue;
+            const uint32_t b = row + wi_offset<F>(wi[j]);
+            if constexpr (F::kBlockBytes == 18) acc += dot_q4_0_x2(b, X[j], X[j + 1]);
+            else if constexpr (F::kBlockBytes == 34) acc += dot_q8_0_x2(b, X[j], X[j + 1]);
+            else if constexpr (F::kBlockBytes == 176)
+                acc += dot_q5_k_x4(b, (wi[j] >> 2) & 1, *reinterpret_cast<const XInt(*)[4]>(&X[j]));
+            else
+                acc += dot_q6_k_x4(b, (wi[j] >> 2) & 1, *reinterpret_cast<const XInt(*)[4]>(&X[j]));
+        }
+    }
+    return acc;
+}
+
+// Lane -> work items of segment sg: G consecutive items per lane per round of
+// 32*G; has[j] is false past the segment or the row.
+template <int G>
+__device__ __forceinline__ void lane_items(int lane, int sg, int SW, int J, int NW, int (&wi)[kMaxJ],
+                                           bool (&has)[kMaxJ]) {
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j) {
+        const int o = G * (lane + 32 * (j / G)) + (j % G);
+        wi[j] = sg * SW + o;
+        has[j] = j < J && o < SW && wi[j] < NW;
+    }
+}
+
 // ------------------------------------------------------------------- kernel
 // Warp w of the 15 consumer warps owns K segment (w % S) and row group
 // (w / S), S in {1, 3, 5, 15}; the CTA's rows are dealt to the 15/S row
@@ -526,15 +570,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_m1_kernel(const GemvPara
     // ----------------------------------------------------------- consumers
     const int S = p.segments, NW = p.nwi, SW = p.seg_wi, J = p.wi_per_lane;
     const int sg = warp % S, grp = warp / S, n_grp = kConsumerWarps / S;
-    // lane -> work items: G consecutive items per lane per round of 32*G
     int wi[kMaxJ];
     bool has[kMaxJ];
-#pragma unroll
-    for (int j = 0; j < kMaxJ; ++j) {
-        const int o = G * (lane + 32 * (j / G)) + (j % G);
-        wi[j] = sg * SW + o;
-        has[j] = j < J && o < SW && wi[j] < NW;
-    }
+    lane_items<G>(lane, sg, SW, J, NW, wi, has);
 
     // x depends on the previous kernel in the stream (x quantization or the
     // GEMV that produced x); the weights do not, so the producer never waits.
@@ -560,27 +598,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_m1_kernel(const GemvPara
         if (rl < 0) rl += n_grp;
         for (; rl < nr; rl += n_grp) {
             const uint32_t row = base + (uint32_t)(rl * p.row_bytes);
-            float acc = 0.f;
-            if constexpr (G == 1) {
-#pragma unroll
-                for (int j = 0; j < kMaxJ; ++j)
-                    if (has[j]) acc += dot_wi<F>(row, wi[j], X[j]);
-            } else {
-                // groups are whole: the host only picks G > 1 when segments
-                // and rows hold whole groups
-#pragma unroll
-                for (int jj = 0; jj < kMaxJ / G; ++jj) {
-                    const int j = jj * G;
-                    if (!has[j]) continue;
-                    const uint32_t b = row + wi_offset<F>(wi[j]);
-                    if constexpr (F::kBlockBytes == 18) acc += dot_q4_0_x2(b, X[j], X[j + 1]);
-                    else if constexpr (F::kBlockBytes == 34) acc += dot_q8_0_x2(b, X[j], X[j + 1]);
-                    else if constexpr (F::kBlockBytes == 176)
-                        acc += dot_q5_k_x4(b, (wi[j] >> 2) & 1, *reinterpret_cast<const XInt(*)[4]>(&X[j]));
-                    else
-                        acc += dot_q6_k_x4(b, (wi[j] >> 2) & 1, *reinterpret_cast<const XInt(*)[4]>(&X[j]));
-                }
-            }
+            float acc = row_partial<F, G>(row, wi, has, X);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
             if (S == 1) {
@@ -611,6 +629,31 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_m1_kernel(const GemvPara
 }
 
 // -------------------------------------------------------- x quantization
+// One 32-element block of x, one element per lane: writes the two int8 limbs
+// of X = rint(x / s), s = amax / 32639, and {s, sum X[0:16), sum X[16:32),
+// sum X}.  Non-finite blocks get s = amax (Inf/NaN) and X = 0.
+__device__ __forceinline__ void quantize_x_block(float v, int lane, uint8_t* limbs, int4* meta) {
+    const uint32_t abits = __float_as_uint(v) & 0x7fffffffu;
+    const uint32_t mbits = __reduce_max_sync(0xffffffffu, abits);
+    const float amax = __uint_as_float(mbits);
+    int X = 0;
+    float s = 0.0f;
+    if (mbits >= 0x7f800000u) {
+        s = amax;  // Inf or NaN
+    } else if (mbits != 0) {
+        X = __float2int_rn(__fmul_rn(__fdiv_rn(v, amax), kXQMax));
+        X = max(-32639, min(32639, X));
+        s = __fdiv_rn(amax, kXQMax);
+    }
+    const int xh = (X + 128) >> 8;
+    const int xl = X - (xh << 8);
+    limbs[lane] = (uint8_t)(int8_t)xh;
+    limbs[32 + lane] = (uint8_t)(int8_t)xl;
+    const int sa = __reduce_add_sync(0xffffffffu, lane < 16 ? X : 0);
+    const int sb = __reduce_add_sync(0xffffffffu, lane < 16 ? 0 : X);
+    if (lane == 0) *meta = make_int4((int)__float_as_uint(s), sa, sb, sa + sb);
+}
+
 // One warp per 32-element block of x (row m of M).  Writes limbs [M][K/32][64]
 // and meta [M][K/32].  Non-finite blocks get s = amax (Inf/NaN) and X = 0, so
 // every row that touches them comes out non-finite, as in fp32 arithmetic.
@@ -626,26 +669,8 @@ __global__ void __launch_bounds__(256) xquant_kernel(const void* __restrict__ x,
     const size_t e = (size_t)m * ldx + (size_t)xb * 32 + lane;
     const float v = x_bf16 ? __uint_as_float((uint32_t)static_cast<const uint16_t*>(x)[e] << 16)
                            : static_cast<const float*>(x)[e];
-    const uint32_t abits = __float_as_uint(v) & 0x7fffffffu;
-    const uint32_t mbits = __reduce_max_sync(0xffffffffu, abits);
-    const float amax = __uint_as_float(mbits);
-    int X = 0;
-    float s = 0.0f;
-    if (mbits >= 0x7f800000u) {
-        s = amax;  // Inf or NaN
-    } else if (mbits != 0) {
-        X = __float2int_rn(__fmul_rn(__fdiv_rn(v, amax), kXQMax));
-        X = max(-32639, min(32639, X));
-        s = __fdiv_rn(amax, kXQMax);
-    }
-    const int xh = (X + 128) >> 8;
-    const int xl = X - (xh << 8);
     const size_t bidx = (size_t)m * nxb + xb;
-    limbs[bidx * kXQLimbBytes + lane] = (uint8_t)(int8_t)xh;
-    limbs[bidx * kXQLimbBytes + 32 + lane] = (uint8_t)(int8_t)xl;
-    const int sa = __reduce_add_sync(0xffffffffu, lane < 16 ? X : 0);
-    const int sb = __reduce_add_sync(0xffffffffu, lane < 16 ? 0 : X);
-    if (lane == 0) meta[bidx] = make_int4((int)__float_as_uint(s), sa, sb, sa + sb);
+    quantize_x_block(v, lane, limbs + bidx * kXQLimbBytes, meta + bidx);
 }
 
 // ------------------------------------------------------ generic fallback

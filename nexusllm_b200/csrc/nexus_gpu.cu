@@ -16,6 +16,7 @@
 
 #include "../../include/nexus_gpu.h"
 #include "gemv_kernels.cuh"
+#include "stack_kernels.cuh"
 
 namespace nexus_gpu {
 
@@ -475,6 +476,244 @@ void report_void(const char* fn, int32_t rc) {
     if (rc != NEXUS_GPU_SUCCESS) fprintf(stderr, "[nexus_gpu] %s: %s (status %d)\n", fn, t_last_error.c_str(), rc);
 }
 
+
+// ------------------------------------------------------------ GEMV stacks
+struct StackHandle {
+    int dev = -1;
+    uint32_t dtype = 0;
+    int group = 1;
+    int grid = 0;
+    size_t smem = 0;
+    int n_tasks = 0;
+    StackParams params{};
+    StackTask* d_tasks = nullptr;
+    unsigned* d_counters = nullptr;  // done[(n + 1) * kCounterStride] | abort
+    size_t counter_bytes = 0;
+    uint8_t* d_xq = nullptr;         // quantized-x buffers of every source
+};
+
+template <class F, int G>
+int32_t stack_kernel_attrs(const Device& d, size_t smem) {
+    CUDA_TRY(cudaFuncSetAttribute(gemv_stack_kernel<F, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, d.smem_optin));
+    int per_sm = 0;
+    CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_stack_kernel<F, G>, kGemvThreads, smem));
+    if (per_sm < 1) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "stack kernel cannot be resident (smem %zu)", smem);
+    return NEXUS_GPU_SUCCESS;
+}
+
+template <class F>
+int32_t stack_attrs_for(int group, const Device& d, size_t smem) {
+    if (F::kGroup > 1 && group == F::kGroup) return stack_kernel_attrs<F, F::kGroup>(d, smem);
+    return stack_kernel_attrs<F, 1>(d, smem);
+}
+
+template <class F>
+int32_t stack_launch_for(const StackHandle& h, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(h.grid);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = h.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // CTAs wait on one another: all must be resident
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (F::kGroup > 1 && h.group == F::kGroup)
+        CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stack_kernel<F, F::kGroup>, h.params));
+    else
+        CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stack_kernel<F, 1>, h.params));
+    return NEXUS_GPU_SUCCESS;
+}
+
+void stack_free(StackHandle* h) {
+    if (!h) return;
+    if (h->d_tasks) cudaFree(h->d_tasks);
+    if (h->d_counters) cudaFree(h->d_counters);
+    if (h->d_xq) cudaFree(h->d_xq);
+    delete h;
+}
+
+int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n, uint64_t input_cols,
+                     void** out) {
+    if (!out || (!tasks && n)) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    if (dtype == NEXUS_GPU_FP16)
+        return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "GEMV stacks serve the integer GGUF formats");
+    FormatInfo f;
+    if (!format_info(dtype, f)) return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "unsupported weight dtype %u", dtype);
+    if (n == 0 || n > 100000) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task count %u", n);
+    if (input_cols == 0 || input_cols % 32 || input_cols > (uint64_t)INT32_MAX)
+        return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "stack input length %llu is not a positive multiple of 32",
+                    (unsigned long long)input_cols);
+    Device* d = nullptr;
+    int32_t rc = get_device(&d);
+    if (rc) return rc;
+    if ((rc = ensure_attrs(*d))) return rc;
+
+    std::vector<StackTask> ht(n);
+    std::vector<char> is_src(n, 0);
+    int group = -1;
+    size_t slot = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        const NexusGpuStackTask& u = tasks[i];
+        if ((rc = check_shape(dtype, u.rows, u.cols, f))) return fail(rc, "task %u: %s", i, t_last_error.c_str());
+        if (!u.W || !u.y || u.rows == 0) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u: null W/y or no rows", i);
+        if (((uintptr_t)u.W & 15) != 0) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u: W not 16-byte aligned", i);
+        const uint64_t xlen = u.x_source < 0 ? input_cols : (u.x_source < (int32_t)i ? tasks[u.x_source].rows : 0);
+        if (u.x_source >= (int32_t)i || xlen != u.cols)
+            return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "task %u: x_source %d does not give a vector of %llu", i,
+                        u.x_source, (unsigned long long)u.cols);
+        if (u.after >= (int32_t)i || u.after < -1)
+            return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u: after=%d is not an earlier task", i, u.after);
+        if (u.x_source >= 0) {
+            if (tasks[u.x_source].rows % 32)
+                return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "task %d feeds x but has %llu rows (not a multiple of 32)",
+                            u.x_source, (unsigned long long)tasks[u.x_source].rows);
+            is_src[u.x_source] = 1;
+        }
+        GemvParams gp{};
+        size_t sm = 0;
+        const uint64_t rb = row_bytes_of(f, u.cols);
+        if (!plan_for(dtype, *d, (int)u.rows, (int)u.cols, rb, gp, sm))
+            return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "task %u (%llux%llu) is outside the fast kernel's limits", i,
+                        (unsigned long long)u.rows, (unsigned long long)u.cols);
+        if (group < 0) group = gp.group;
+        if (gp.group != group)
+            return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "task %u: mixed block-grouping in one stack", i);
+        StackTask& T = ht[i];
+        T.W = static_cast<const uint8_t*>(u.W);
+        T.row_bytes = rb;
+        T.total_bytes = rb * u.rows;
+        T.N = (int)u.rows;
+        T.K = (int)u.cols;
+        T.nwi = gp.nwi;
+        T.segments = gp.segments;
+        T.seg_wi = gp.seg_wi;
+        T.wi_per_lane = gp.wi_per_lane;
+        T.stage_rows = gp.stage_rows;
+        T.stage_bytes = gp.stage_bytes;
+        T.y = u.y;
+        T.src = u.x_source < 0 ? (int)n : u.x_source;
+        T.after = u.after;
+        slot = std::max(slot, (size_t)gp.stage_bytes);
+    }
+    size_t x_smem = 0;
+    for (const StackTask& T : ht) x_smem = std::max(x_smem, (size_t)(T.K / 32) * (kXQLimbBytes + kXQMetaBytes));
+    x_smem = (x_smem + 127) / 128 * 128;
+    if ((uint64_t)d->smem_optin < kStackSmemHeader + x_smem + 128 + 2 * slot)
+        return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "stack stages do not fit shared memory");
+    const uint64_t avail = (uint64_t)d->smem_optin - kStackSmemHeader - x_smem - 128;
+    int ns = (int)std::min<uint64_t>(kMaxStages, avail / slot);
+    auto fits = [&](int k) {
+        for (const StackTask& T : ht)
+            if (T.stage_rows * T.segments > kMaxSlots / k) return false;
+        return true;
+    };
+    while (ns > 2 && !fits(ns)) --ns;
+    if (ns < 2 || !fits(ns)) return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "stack stages do not fit shared memory");
+
+    auto h = new StackHandle();
+    h->dev = d->id;
+    h->dtype = dtype;
+    h->group = group;
+    h->grid = d->sms;
+    h->n_tasks = (int)n;
+    h->smem = kStackSmemHeader + x_smem + (size_t)ns * slot;
+
+    // quantized-x buffers: the input, then every task that feeds a later task
+    size_t xq_total = 0;
+    auto xq_size = [](uint64_t len) { return align256(len / 32 * kXQLimbBytes) + align256(len / 32 * kXQMetaBytes); };
+    xq_total += xq_size(input_cols);
+    for (uint32_t i = 0; i < n; ++i)
+        if (is_src[i]) xq_total += xq_size(tasks[i].rows);
+    cudaError_t e = cudaMalloc(&h->d_xq, xq_total);
+    if (e == cudaSuccess) e = cudaMalloc(&h->d_tasks, n * sizeof(StackTask));
+    h->counter_bytes = (size_t)((n + 1) * kCounterStride + 1) * sizeof(unsigned);
+    if (e == cudaSuccess) e = cudaMalloc(&h->d_counters, h->counter_bytes);
+    if (e != cudaSuccess) {
+        stack_free(h);
+        cudaGetLastError();
+        return fail(NEXUS_GPU_ERROR_OUT_OF_TIER0_MEMORY, "stack allocation failed: %s", cudaGetErrorString(e));
+    }
+    std::vector<uint8_t*> limbs(n + 1, nullptr);
+    std::vector<int4*> meta(n + 1, nullptr);
+    uint8_t* cur = h->d_xq;
+    auto carve = [&](uint32_t idx, uint64_t len) {
+        limbs[idx] = cur;
+        cur += align256(len / 32 * kXQLimbBytes);
+        meta[idx] = reinterpret_cast<int4*>(cur);
+        cur += align256(len / 32 * kXQMetaBytes);
+    };
+    carve(n, input_cols);
+    for (uint32_t i = 0; i < n; ++i)
+        if (is_src[i]) carve(i, tasks[i].rows);
+    std::vector<char> waited_for(n, 0);
+    for (uint32_t i = 0; i < n; ++i) {
+        if (tasks[i].after >= 0) waited_for[tasks[i].after] = 1;
+        if (tasks[i].x_source >= 0) waited_for[tasks[i].x_source] = 1;
+    }
+    for (uint32_t i = 0; i < n; ++i) {
+        StackTask& T = ht[i];
+        T.signal = waited_for[i];
+        // same input, same plan (same cols), and no new ordering dependency:
+        // keep the previous task's x slices and skip the wait and the staging
+        T.reuse_x = i > 0 && tasks[i].x_source == tasks[i - 1].x_source && tasks[i].cols == tasks[i - 1].cols &&
+                    (tasks[i].after == -1 || tasks[i].after == tasks[i - 1].after);
+        T.x_limbs = limbs[T.src];
+        T.x_meta = meta[T.src];
+        T.q_limbs = is_src[i] ? limbs[i] : nullptr;
+        T.q_meta = is_src[i] ? meta[i] : nullptr;
+    }
+    e = cudaMemcpy(h->d_tasks, ht.data(), n * sizeof(StackTask), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        stack_free(h);
+        return fail(NEXUS_GPU_ERROR_CUDA, "stack upload failed: %s", cudaGetErrorString(e));
+    }
+    StackParams& P = h->params;
+    P.tasks = h->d_tasks;
+    P.n_tasks = (int)n;
+    P.n_stages = ns;
+    P.stage_slot = (int)slot;
+    P.x_smem = (int)x_smem;
+    P.slot_stride = kMaxSlots / ns;
+    P.x_in = nullptr;
+    P.in_K = (int)input_cols;
+    P.in_limbs = limbs[n];
+    P.in_meta = meta[n];
+    P.done = h->d_counters;
+    P.abort_flag = h->d_counters + (size_t)(n + 1) * kCounterStride;
+
+    switch (dtype) {
+        case NEXUS_GPU_GGUF_Q4_0: rc = stack_attrs_for<FmtQ4_0>(group, *d, h->smem); break;
+        case NEXUS_GPU_GGUF_Q8_0: rc = stack_attrs_for<FmtQ8_0>(group, *d, h->smem); break;
+        case NEXUS_GPU_GGUF_Q5_K: rc = stack_attrs_for<FmtQ5_K>(group, *d, h->smem); break;
+        default: rc = stack_attrs_for<FmtQ6_K>(group, *d, h->smem); break;
+    }
+    if (rc) {
+        stack_free(h);
+        return rc;
+    }
+    *out = h;
+    return NEXUS_GPU_SUCCESS;
+}
+
+int32_t stack_run(void* handle, const float* x_in, cudaStream_t st) {
+    StackHandle* h = static_cast<StackHandle*>(handle);
+    if (!h || !x_in) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null handle or input");
+    int cur = -1;
+    CUDA_TRY(cudaGetDevice(&cur));
+    if (cur != h->dev) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "stack belongs to device %d, current is %d", h->dev, cur);
+    h->params.x_in = x_in;
+    CUDA_TRY(cudaMemsetAsync(h->d_counters, 0, h->counter_bytes, st));
+    switch (h->dtype) {
+        case NEXUS_GPU_GGUF_Q4_0: return stack_launch_for<FmtQ4_0>(*h, st);
+        case NEXUS_GPU_GGUF_Q8_0: return stack_launch_for<FmtQ8_0>(*h, st);
+        case NEXUS_GPU_GGUF_Q5_K: return stack_launch_for<FmtQ5_K>(*h, st);
+        default: return stack_launch_for<FmtQ6_K>(*h, st);
+    }
+}
+
 // ------------------------------------------------ no-allocation entry point
 // Scratch of nexus_gpu_gemv_noalloc: the quantized activations (limbs and
 // block metadata) that xquant_kernel writes and the GEMV kernel reads.  It is
@@ -674,6 +913,22 @@ NEXUS_GPU_API int32_t nexus_gpu_gemv_noalloc(const void* dW, uint32_t dtype, con
     uint8_t* scratch = nullptr;
     if ((rc = noalloc_device(&d, &scratch))) return rc;
     return run_gemv(*d, dW, dtype, dX, x_dtype, dY, M, rows, cols, scratch, static_cast<cudaStream_t>(stream));
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n_tasks,
+                                             uint64_t input_cols, void** out_stack) {
+    t_last_error.clear();
+    return stack_create(dtype, tasks, n_tasks, input_cols, out_stack);
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_stack_run(void* stack, const float* dX, void* stream) {
+    t_last_error.clear();
+    return stack_run(stack, dX, static_cast<cudaStream_t>(stream));
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_stack_destroy(void* stack) {
+    stack_free(static_cast<StackHandle*>(stack));
+    return NEXUS_GPU_SUCCESS;
 }
 
 NEXUS_GPU_API int32_t nexus_gpu_dequantize(const void* dW, uint32_t dtype, float* dOut, size_t count, void* stream) {
