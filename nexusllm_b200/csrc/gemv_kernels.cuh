@@ -629,9 +629,22 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_m1_kernel(const GemvPara
 }
 
 // -------------------------------------------------------- x quantization
+// Element rule shared by every x quantizer (so all paths give the same bits):
+// X = rint(x * (32639 / amax)), one IEEE division per block.  Blocks whose
+// amax is below 2^-100 (where 32639 / amax could overflow) divide element by
+// element instead: X = rint((x / amax) * 32639).  Called for finite amax > 0.
+constexpr float kXQTiny = 0x1p-100f;
+__device__ __forceinline__ float xq_inv(float amax) { return __fdiv_rn(kXQMax, amax); }
+__device__ __forceinline__ int xq_clamp(float q) { return max(-32639, min(32639, __float2int_rn(q))); }
+__device__ __forceinline__ int xq_elem_fast(float v, float inv) { return xq_clamp(__fmul_rn(v, inv)); }  // amax >= kXQTiny
+__device__ __forceinline__ int xq_elem_tiny(float v, float amax) { return xq_clamp(__fmul_rn(__fdiv_rn(v, amax), kXQMax)); }
+__device__ __forceinline__ int xq_elem(float v, float amax, float inv) {
+    return amax >= kXQTiny ? xq_elem_fast(v, inv) : xq_elem_tiny(v, amax);
+}
+
 // One 32-element block of x, one element per lane: writes the two int8 limbs
-// of X = rint(x / s), s = amax / 32639, and {s, sum X[0:16), sum X[16:32),
-// sum X}.  Non-finite blocks get s = amax (Inf/NaN) and X = 0.
+// of X (xq_elem), s = amax / 32639, and {s, sum X[0:16), sum X[16:32), sum X}.
+// Non-finite blocks get s = amax (Inf/NaN) and X = 0.
 __device__ __forceinline__ void quantize_x_block(float v, int lane, uint8_t* limbs, int4* meta) {
     const uint32_t abits = __float_as_uint(v) & 0x7fffffffu;
     const uint32_t mbits = __reduce_max_sync(0xffffffffu, abits);
@@ -641,8 +654,7 @@ __device__ __forceinline__ void quantize_x_block(float v, int lane, uint8_t* lim
     if (mbits >= 0x7f800000u) {
         s = amax;  // Inf or NaN
     } else if (mbits != 0) {
-        X = __float2int_rn(__fmul_rn(__fdiv_rn(v, amax), kXQMax));
-        X = max(-32639, min(32639, X));
+        X = xq_elem(v, amax, xq_inv(amax));
         s = __fdiv_rn(amax, kXQMax);
     }
     const int xh = (X + 128) >> 8;

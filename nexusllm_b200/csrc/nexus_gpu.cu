@@ -487,9 +487,8 @@ struct StackHandle {
     int n_tasks = 0;
     StackParams params{};
     StackTask* d_tasks = nullptr;
-    unsigned* d_counters = nullptr;  // done[(n + 1) * kCounterStride] | abort
+    unsigned* d_counters = nullptr;  // done[n * kCounterStride] | abort
     size_t counter_bytes = 0;
-    uint8_t* d_xq = nullptr;         // quantized-x buffers of every source
 };
 
 template <class F, int G>
@@ -530,7 +529,6 @@ void stack_free(StackHandle* h) {
     if (!h) return;
     if (h->d_tasks) cudaFree(h->d_tasks);
     if (h->d_counters) cudaFree(h->d_counters);
-    if (h->d_xq) cudaFree(h->d_xq);
     delete h;
 }
 
@@ -552,7 +550,6 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n,
     if ((rc = ensure_attrs(*d))) return rc;
 
     std::vector<StackTask> ht(n);
-    std::vector<char> is_src(n, 0);
     int group = -1;
     size_t slot = 0;
     for (uint32_t i = 0; i < n; ++i) {
@@ -566,12 +563,9 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n,
                         u.x_source, (unsigned long long)u.cols);
         if (u.after >= (int32_t)i || u.after < -1)
             return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u: after=%d is not an earlier task", i, u.after);
-        if (u.x_source >= 0) {
-            if (tasks[u.x_source].rows % 32)
-                return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "task %d feeds x but has %llu rows (not a multiple of 32)",
-                            u.x_source, (unsigned long long)tasks[u.x_source].rows);
-            is_src[u.x_source] = 1;
-        }
+        if (u.x_source >= 0 && ((uintptr_t)tasks[u.x_source].y & 15) != 0)
+            return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %d feeds x but its y is not 16-byte aligned",
+                        u.x_source);
         GemvParams gp{};
         size_t sm = 0;
         const uint64_t rb = row_bytes_of(f, u.cols);
@@ -594,12 +588,13 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n,
         T.stage_rows = gp.stage_rows;
         T.stage_bytes = gp.stage_bytes;
         T.y = u.y;
-        T.src = u.x_source < 0 ? (int)n : u.x_source;
+        T.x = u.x_source < 0 ? nullptr : tasks[u.x_source].y;
+        T.src = u.x_source < 0 ? -1 : u.x_source;
         T.after = u.after;
         slot = std::max(slot, (size_t)gp.stage_bytes);
     }
     size_t x_smem = 0;
-    for (const StackTask& T : ht) x_smem = std::max(x_smem, (size_t)(T.K / 32) * (kXQLimbBytes + kXQMetaBytes));
+    for (const StackTask& T : ht) x_smem = std::max(x_smem, (size_t)x_stage_planes_len(T.K) * (kXQLimbBytes + kXQMetaBytes));
     x_smem = (x_smem + 127) / 128 * 128;
     if ((uint64_t)d->smem_optin < kStackSmemHeader + x_smem + 128 + 2 * slot)
         return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "stack stages do not fit shared memory");
@@ -621,33 +616,14 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n,
     h->n_tasks = (int)n;
     h->smem = kStackSmemHeader + x_smem + (size_t)ns * slot;
 
-    // quantized-x buffers: the input, then every task that feeds a later task
-    size_t xq_total = 0;
-    auto xq_size = [](uint64_t len) { return align256(len / 32 * kXQLimbBytes) + align256(len / 32 * kXQMetaBytes); };
-    xq_total += xq_size(input_cols);
-    for (uint32_t i = 0; i < n; ++i)
-        if (is_src[i]) xq_total += xq_size(tasks[i].rows);
-    cudaError_t e = cudaMalloc(&h->d_xq, xq_total);
-    if (e == cudaSuccess) e = cudaMalloc(&h->d_tasks, n * sizeof(StackTask));
-    h->counter_bytes = (size_t)((n + 1) * kCounterStride + 1) * sizeof(unsigned);
+    cudaError_t e = cudaMalloc(&h->d_tasks, n * sizeof(StackTask));
+    h->counter_bytes = (size_t)(n * kCounterStride + 1) * sizeof(unsigned);
     if (e == cudaSuccess) e = cudaMalloc(&h->d_counters, h->counter_bytes);
     if (e != cudaSuccess) {
         stack_free(h);
         cudaGetLastError();
         return fail(NEXUS_GPU_ERROR_OUT_OF_TIER0_MEMORY, "stack allocation failed: %s", cudaGetErrorString(e));
     }
-    std::vector<uint8_t*> limbs(n + 1, nullptr);
-    std::vector<int4*> meta(n + 1, nullptr);
-    uint8_t* cur = h->d_xq;
-    auto carve = [&](uint32_t idx, uint64_t len) {
-        limbs[idx] = cur;
-        cur += align256(len / 32 * kXQLimbBytes);
-        meta[idx] = reinterpret_cast<int4*>(cur);
-        cur += align256(len / 32 * kXQMetaBytes);
-    };
-    carve(n, input_cols);
-    for (uint32_t i = 0; i < n; ++i)
-        if (is_src[i]) carve(i, tasks[i].rows);
     std::vector<char> waited_for(n, 0);
     for (uint32_t i = 0; i < n; ++i) {
         if (tasks[i].after >= 0) waited_for[tasks[i].after] = 1;
@@ -660,10 +636,6 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n,
         // keep the previous task's x slices and skip the wait and the staging
         T.reuse_x = i > 0 && tasks[i].x_source == tasks[i - 1].x_source && tasks[i].cols == tasks[i - 1].cols &&
                     (tasks[i].after == -1 || tasks[i].after == tasks[i - 1].after);
-        T.x_limbs = limbs[T.src];
-        T.x_meta = meta[T.src];
-        T.q_limbs = is_src[i] ? limbs[i] : nullptr;
-        T.q_meta = is_src[i] ? meta[i] : nullptr;
     }
     e = cudaMemcpy(h->d_tasks, ht.data(), n * sizeof(StackTask), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
@@ -678,11 +650,8 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n,
     P.x_smem = (int)x_smem;
     P.slot_stride = kMaxSlots / ns;
     P.x_in = nullptr;
-    P.in_K = (int)input_cols;
-    P.in_limbs = limbs[n];
-    P.in_meta = meta[n];
     P.done = h->d_counters;
-    P.abort_flag = h->d_counters + (size_t)(n + 1) * kCounterStride;
+    P.abort_flag = h->d_counters + (size_t)n * kCounterStride;
 
     switch (dtype) {
         case NEXUS_GPU_GGUF_Q4_0: rc = stack_attrs_for<FmtQ4_0>(group, *d, h->smem); break;
@@ -701,6 +670,7 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n,
 int32_t stack_run(void* handle, const float* x_in, cudaStream_t st) {
     StackHandle* h = static_cast<StackHandle*>(handle);
     if (!h || !x_in) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null handle or input");
+    if (((uintptr_t)x_in & 15) != 0) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "stack input not 16-byte aligned");
     int cur = -1;
     CUDA_TRY(cudaGetDevice(&cur));
     if (cur != h->dev) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "stack belongs to device %d, current is %d", h->dev, cur);

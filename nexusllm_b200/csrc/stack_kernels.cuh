@@ -12,19 +12,16 @@
 //    consumers wait for a task's input.
 //  * Each task's consumer work is the single-GEMV kernel's (same plan, same
 //    per-row arithmetic, so results are bit-identical to nexus_gpu_gemv).
-//  * A task's x is either the stack input or the y of an earlier task.  A task
-//    whose y feeds a later task splits its rows over the CTAs in whole 32-row
-//    blocks, so each 32-element block of y is computed by one CTA: when a CTA's
-//    warps have finished the task, the last of them quantizes the CTA's own
-//    blocks of y into the 16-bit fixed-point form consumers load
-//    (quantize_x_block) and only then bumps the task's global completion
-//    counter.  One counter per task therefore means "y written and quantized";
-//    a task starts when its source's counter and, optionally, another task's
-//    counter (the ordering a real decode has between layers) reach the CTA
-//    count.  The consumer warps of a CTA step through the tasks together:
-//    one thread polls the grid counters, and the task's quantized x is staged
-//    once per CTA in shared memory.  The stack input is quantized the same way
-//    at kernel start.
+//  * A task's x is either the stack input or the y of an earlier task.  Rows
+//    are balanced over the CTAs.  When a CTA has written its rows of a task
+//    that a later task waits for, one thread counts the CTA on the task's
+//    global counter; a task starts when its source's counter and, optionally,
+//    another task's counter (the ordering a real decode has between layers)
+//    reach the CTA count.  The consumer warps of a CTA step through the tasks
+//    together: one thread polls the grid counters, then the CTA reads the
+//    task's fp32 x from L2 and quantizes it into shared memory itself
+//    (quantize_x_pair, the same bits as xquant_kernel), so a finished task
+//    only has to be counted, never converted, before its dependants start.
 //  * All CTAs must be resident at once (they wait on one another): the host
 //    launches the kernel cooperatively with one CTA per SM.  Every wait is
 //    bounded; an expired wait raises a global abort flag that ends every CTA's
@@ -41,12 +38,9 @@ struct StackTask {
     int N, K;
     int nwi, segments, seg_wi, wi_per_lane, stage_rows, stage_bytes;
     float* y;
-    const uint8_t* x_limbs;  // quantized x of this task's source
-    const int4* x_meta;
-    int src;                 // counter index of the source: a task index, or n_tasks (the stack input)
+    const float* x;          // fp32 x: the source task's y, or null for the stack input
+    int src;                 // the source task, or -1 (the stack input: nothing to wait for)
     int after;               // -1, or a task that must complete before this one starts
-    uint8_t* q_limbs;        // non-null when y is some later task's x: quantize y here, and
-    int4* q_meta;            // split rows over CTAs in whole 32-row blocks
     int signal;              // some later task waits for this one: count CTAs when done
     int reuse_x;             // same input and plan as the previous task: keep its x, skip the wait
 };
@@ -58,28 +52,17 @@ struct StackParams {
     int stage_slot;          // bytes per ring slot (>= every task's stage_bytes)
     int x_smem;              // bytes of the shared x staging buffer (>= every task's K/32 * 80)
     int slot_stride;         // partial-sum floats per ring slot (>= R * S of every task)
-    const float* x_in;       // stack input, fp32 [in_K]
-    int in_K;
-    uint8_t* in_limbs;
-    int4* in_meta;
-    unsigned* done;          // [(n_tasks + 1) * kCounterStride]: CTAs that finished (and quantized)
-                             // each task; slot n_tasks counts the quantized stack input
+    const float* x_in;       // stack input, fp32, 16-byte aligned
+    unsigned* done;          // [n_tasks * kCounterStride]: CTAs that finished each task
     unsigned* abort_flag;
 };
 
 constexpr int kCounterStride = 32;  // one 128-byte line per counter
 
-// Rows [rb, re) of an N-row task for CTA c of n_cta: balanced, or in whole
-// 32-row blocks for tasks whose y is quantized by the CTAs that computed it.
-__device__ __forceinline__ void cta_rows(int N, bool blocks32, int c, int n_cta, int& rb, int& re) {
-    if (blocks32) {
-        const int nb = N / 32;
-        rb = 32 * (int)((int64_t)nb * c / n_cta);
-        re = 32 * (int)((int64_t)nb * (c + 1) / n_cta);
-    } else {
-        rb = (int)((int64_t)N * c / n_cta);
-        re = (int)((int64_t)N * (c + 1) / n_cta);
-    }
+// Rows [rb, re) of an N-row task for CTA c of n_cta, balanced.
+__device__ __forceinline__ void cta_rows(int N, int c, int n_cta, int& rb, int& re) {
+    rb = (int)((int64_t)N * c / n_cta);
+    re = (int)((int64_t)N * (c + 1) / n_cta);
 }
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
@@ -126,17 +109,75 @@ __device__ __forceinline__ bool consumer_bar_any(bool v) {
     return r != 0;
 }
 
-// x slice of work item gj from the shared staging buffer (limbs at xl, meta at xm).
-__device__ __forceinline__ void load_xint_smem(uint32_t xl, uint32_t xm, int gj, XInt& X) {
-    const uint32_t a = xl + (uint32_t)gj * kXQLimbBytes;
+// Shared staging layout of a task's quantized x.  The 64 limb bytes of block b
+// are four 16-byte chunks (Xh 0-15, Xh 16-31, Xl 0-15, Xl 16-31); chunk q of
+// every block sits in plane q, planes of nxbp = K/32 rounded up to 8 chunks:
+// chunk (q, b) at 16 * (q * nxbp + xsw(b)), then the metadata plane, block b at
+// 16 * (4 * nxbp + xsw(b)).  Lanes read blocks G apart (G = 1, 2, 4); the swizzle
+// xsw(b) = b ^ ((b >> 3) & 7) maps any 8 such lanes to 8 distinct 16-byte bank
+// groups, so the 128-bit loads of a quarter warp never conflict.
+__device__ __forceinline__ uint32_t xsw(int b) { return (uint32_t)(b ^ ((b >> 3) & 7)); }
+__host__ __device__ constexpr int x_stage_planes_len(int K) { return (K / 32 + 7) / 8 * 8; }
+
+// quantize_x_block with two lanes per block: lane half hf (0 or 1) of the
+// pair holds elements 16*hf .. 16*hf+15 in e.  Same element rule and sums as
+// quantize_x_block, so the limbs and metadata are the same bits.  Stores
+// block b into the staging layout at xs when `store`; every lane must call it.
+__device__ __forceinline__ void quantize_x_pair(const float (&e)[16], int hf, bool store, uint32_t xs, int nxbp,
+                                                int b) {
+    uint32_t mbits = 0;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) mbits = max(mbits, __float_as_uint(e[k]) & 0x7fffffffu);
+    mbits = max(mbits, __shfl_xor_sync(0xffffffffu, mbits, 1));
+    const float amax = __uint_as_float(mbits);
+    const bool nz = mbits < 0x7f800000u && mbits != 0;
+    const bool fast = amax >= kXQTiny;
+    const float s = mbits >= 0x7f800000u ? amax : (nz ? __fdiv_rn(amax, kXQMax) : 0.0f);
+    const float inv = nz && fast ? xq_inv(amax) : 0.0f;
+    uint32_t h[4], l[4];
+    int sum = 0;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        h[w] = 0;
+        l[w] = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float v = e[4 * w + k];
+            const int x = !nz ? 0 : (fast ? xq_elem_fast(v, inv) : xq_elem_tiny(v, amax));
+            const int xh = (x + 128) >> 8;
+            const int xl = x - (xh << 8);
+            h[w] |= ((uint32_t)xh & 0xffu) << (8 * k);
+            l[w] |= ((uint32_t)xl & 0xffu) << (8 * k);
+            sum += x;
+        }
+    }
+    const int other = __shfl_xor_sync(0xffffffffu, sum, 1);
+    if (store) {
+        const uint32_t col = 16 * xsw(b), plane = 16u * (uint32_t)nxbp;
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(xs + (uint32_t)hf * plane + col), "r"(h[0]),
+                     "r"(h[1]), "r"(h[2]), "r"(h[3])
+                     : "memory");
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(xs + (uint32_t)(2 + hf) * plane + col), "r"(l[0]),
+                     "r"(l[1]), "r"(l[2]), "r"(l[3])
+                     : "memory");
+        if (hf == 0)
+            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(xs + 4 * plane + col), "r"(__float_as_uint(s)),
+                         "r"(sum), "r"(other), "r"(sum + other)
+                         : "memory");
+    }
+}
+
+// x slice of work item gj (block gj) from the staging layout at xs.
+__device__ __forceinline__ void load_xint_smem(uint32_t xs, int nxbp, int gj, XInt& X) {
+    const uint32_t col = 16 * xsw(gj), plane = 16u * (uint32_t)nxbp;
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
-        const uint4 v = lds128(a + 16 * q);
+        const uint4 v = lds128(xs + (uint32_t)q * plane + col);
         X.h[4 * q + 0] = v.x; X.h[4 * q + 1] = v.y; X.h[4 * q + 2] = v.z; X.h[4 * q + 3] = v.w;
-        const uint4 u = lds128(a + 32 + 16 * q);
+        const uint4 u = lds128(xs + (uint32_t)(2 + q) * plane + col);
         X.l[4 * q + 0] = u.x; X.l[4 * q + 1] = u.y; X.l[4 * q + 2] = u.z; X.l[4 * q + 3] = u.w;
     }
-    const uint4 m = lds128(xm + (uint32_t)gj * kXQMetaBytes);
+    const uint4 m = lds128(xs + 4 * plane + col);
     X.s = __uint_as_float(m.x);
     X.sa = (int)m.y;
     X.sb = (int)m.z;
@@ -184,8 +225,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
             const uint8_t* W = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.W)));
             const int N = __ldg(&T.N), R = __ldg(&T.stage_rows);
             int row_begin, row_end;
-            cta_rows(N, __ldg(reinterpret_cast<const unsigned long long*>(&T.q_limbs)) != 0ull, c, n_cta, row_begin,
-                     row_end);
+            cta_rows(N, c, n_cta, row_begin, row_end);
             const uint64_t floor16 = total & ~(uint64_t)15;
             const uint64_t span = (uint64_t)R * rb, cta_end = (uint64_t)row_end * rb;
             for (uint64_t start = (uint64_t)row_begin * rb; start < cta_end; ++it) {
@@ -222,143 +262,133 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
     }
 
     // ----------------------------------------------------------- consumers
-    // Consumer warps step through the tasks together: at each task start the
-    // CTA loads the task's quantized x once into shared memory (every warp
-    // reading it from L2 on its own multiplied the L2 traffic by the warp count
-    // and stalled behind the weight stream), then each warp copies its slices
-    // into registers.  Warp 0 polls the grid counters for the CTA.
+    // Consumer warps step through the tasks together, one x group at a time
+    // (a task and the tasks after it that read the same x with the same plan):
+    // warp 0 polls the grid counters for the CTA, the CTA reads the group's
+    // fp32 x from L2 once, quantizes it into shared memory, and each warp
+    // copies its slices into registers, which then serve every task of the
+    // group.  Staging from L2 once per CTA (not once per warp) keeps x off the
+    // L2 path the weight stream saturates; the x registers live only inside a
+    // group, so the staging loads can all be in flight at once.
     const int tid = threadIdx.x;  // 0 .. kConsumers-1
-    const uint32_t xs = sbase + kStackSmemHeader;  // x staging: limbs [nxb][64] then meta [nxb][16]
-    bool alive = true;
-    // this CTA's 32-element blocks of the stack input
-    {
-        int b0, b1;
-        cta_rows(P.in_K, true, c, n_cta, b0, b1);
-        for (int b = b0 / 32 + warp; b < b1 / 32; b += kConsumerWarps)
-            quantize_x_block(__ldcg(P.x_in + 32 * b + lane), lane, P.in_limbs + (size_t)b * kXQLimbBytes,
-                             P.in_meta + b);
-        __threadfence();
-    }
-    consumer_bar();
-    if (tid == 0) atomicAdd(&P.done[P.n_tasks * kCounterStride], 1u);
-
+    const uint32_t xs = sbase + kStackSmemHeader;  // x staging (xsw layout)
+    bool alive = true, stop = false;
     int s = 0;
     uint32_t phase = 0;
-    XT X[kMaxJ];
-    for (int t = 0; t < P.n_tasks; ++t) {
-        const StackTask& T = P.tasks[t];
-        const int N = __ldg(&T.N), K = __ldg(&T.K), R = __ldg(&T.stage_rows), S = __ldg(&T.segments);
-        const int NW = __ldg(&T.nwi), SW = __ldg(&T.seg_wi), J = __ldg(&T.wi_per_lane);
-        const uint64_t rbytes = __ldg(&T.row_bytes);
-        float* y = reinterpret_cast<float*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.y)));
-        uint8_t* ql = reinterpret_cast<uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.q_limbs)));
-        const bool reuse = __ldg(&T.reuse_x) != 0;
+    for (int t = 0; t < P.n_tasks && !stop;) {
+        // ---- group head: wait for the input, stage it, load the x slices
+        const StackTask& H = P.tasks[t];
+        const int K = __ldg(&H.K), S = __ldg(&H.segments);
+        const int NW = __ldg(&H.nwi), SW = __ldg(&H.seg_wi), J = __ldg(&H.wi_per_lane);
         const int sg = warp % S, grp = warp / S, n_grp = kConsumerWarps / S;
         int wi[kMaxJ];
         bool has[kMaxJ];
         lane_items<G>(lane, sg, SW, J, NW, wi, has);
-        if (!reuse) {
-        // the task's input must be written and quantized, and its ordering dependency done
-        int ok = 1;
-        if (tid == 0) {
-            const int after = __ldg(&T.after);
-            ok = wait_count_bounded(&P.done[__ldg(&T.src) * kCounterStride], (unsigned)n_cta, P.abort_flag);
+        if (tid == 0) {  // the input must be written, and the ordering dependency done
+            const int src = __ldg(&H.src), after = __ldg(&H.after);
+            int ok = 1;
+            if (src >= 0) ok = wait_count_bounded(&P.done[src * kCounterStride], (unsigned)n_cta, P.abort_flag);
             if (ok && after >= 0) ok = wait_count_bounded(&P.done[after * kCounterStride], (unsigned)n_cta, P.abort_flag);
+            __threadfence();
             s_flag[0] = ok;
         }
-        consumer_bar();  // also: every warp is done with the previous task's x staging
+        consumer_bar();  // also: every warp is done with the previous group's x staging
         if (!s_flag[0]) break;
-        __threadfence();
-        {   // stage x: limbs and meta, 16 bytes per thread per step
-            const int nxb = K / 32;
-            const int4* gl = reinterpret_cast<const int4*>(
-                __ldg(reinterpret_cast<const unsigned long long*>(&T.x_limbs)));
-            const int4* gm = reinterpret_cast<const int4*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.x_meta)));
-            for (int i = tid; i < nxb * (kXQLimbBytes / 16); i += kConsumers) {
-                const int4 v = __ldcg(gl + i);
-                asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(xs + 16 * i), "r"(v.x), "r"(v.y),
-                             "r"(v.z), "r"(v.w)
-                             : "memory");
-            }
-            const uint32_t xm = xs + (uint32_t)nxb * kXQLimbBytes;
-            for (int i = tid; i < nxb; i += kConsumers) {
-                const int4 v = __ldcg(gm + i);
-                asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(xm + 16 * i), "r"(v.x), "r"(v.y),
-                             "r"(v.z), "r"(v.w)
-                             : "memory");
+        {   // read x (L2) and quantize it into the staging buffer, two lanes
+            // per 32-element block, kConsumers / 2 blocks per pass
+            const float4* xv = reinterpret_cast<const float4*>(__ldg(reinterpret_cast<const unsigned long long*>(&H.x)));
+            if (xv == nullptr) xv = reinterpret_cast<const float4*>(P.x_in);
+            const int nxb = K / 32, nxbp = x_stage_planes_len(K), hf = lane & 1;
+            for (int base = 0; base < nxb; base += kConsumers / 2) {
+                const int b = base + (tid >> 1);
+                float e[16];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float4 v = b < nxb ? __ldcg(xv + 8 * b + 4 * hf + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    e[4 * q + 0] = v.x;
+                    e[4 * q + 1] = v.y;
+                    e[4 * q + 2] = v.z;
+                    e[4 * q + 3] = v.w;
+                }
+                quantize_x_pair(e, hf, b < nxb, xs, nxbp, b);
             }
         }
         consumer_bar();
+        XT X[kMaxJ];
         {
-            const uint32_t xm = xs + (uint32_t)(K / 32) * kXQLimbBytes;
+            const int nxbp = x_stage_planes_len(K);
 #pragma unroll
             for (int j = 0; j < kMaxJ; ++j)
-                if (has[j]) load_xint_smem(xs, xm, wi[j], X[j]);
+                if (has[j]) load_xint_smem(xs, nxbp, wi[j], X[j]);
         }
-        }  // !reuse
 
-        int row_begin, row_end;
-        cta_rows(N, ql != nullptr, c, n_cta, row_begin, row_end);
-        const int n_st = (row_end - row_begin + R - 1) / R;
-        int rot = 0;
-        for (int i = 0; i < n_st; ++i) {
-            const int r0 = row_begin + i * R;
-            const int nr = min(R, row_end - r0);
-            if (alive && !mbar_wait_bounded(full_bar + 8 * s, phase)) {
-                atomicExch(P.abort_flag, 1u);
-                alive = false;  // no more waits; the loop ends at the next reducing barrier
-            }
-            if (alive) {
-                const uint32_t base =
-                    stage0 + (uint32_t)(s * P.stage_slot) + (uint32_t)(((uint64_t)r0 * rbytes) & 15);
-                int rl = grp - rot;
-                if (rl < 0) rl += n_grp;
-                for (; rl < nr; rl += n_grp) {
-                    const uint32_t row = base + (uint32_t)(rl * rbytes);
-                    float acc = row_partial<F, G>(row, wi, has, X);
+        // ---- the group's tasks
+        for (;;) {
+            const StackTask& T = P.tasks[t];
+            const int N = __ldg(&T.N), R = __ldg(&T.stage_rows);
+            const uint64_t rbytes = __ldg(&T.row_bytes);
+            float* y = reinterpret_cast<float*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.y)));
+            int row_begin, row_end;
+            cta_rows(N, c, n_cta, row_begin, row_end);
+            const int n_st = (row_end - row_begin + R - 1) / R;
+            int rot = 0;
+            for (int i = 0; i < n_st; ++i) {
+                const int r0 = row_begin + i * R;
+                const int nr = min(R, row_end - r0);
+                if (alive && !mbar_wait_bounded(full_bar + 8 * s, phase)) {
+                    atomicExch(P.abort_flag, 1u);
+                    alive = false;  // no more waits; the loop ends at the next reducing barrier
+                }
+                if (alive) {
+                    const uint32_t base =
+                        stage0 + (uint32_t)(s * P.stage_slot) + (uint32_t)(((uint64_t)r0 * rbytes) & 15);
+                    int rl = grp - rot;
+                    if (rl < 0) rl += n_grp;
+                    for (; rl < nr; rl += n_grp) {
+                        const uint32_t row = base + (uint32_t)(rl * rbytes);
+                        float acc = row_partial<F, G>(row, wi, has, X);
 #pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-                    if (S == 1) {
-                        if (lane == 0) y[r0 + rl] = acc;
-                    } else if (lane == 0) {
-                        float* sl = slots + s * P.slot_stride + rl * S;
-                        sl[sg] = acc;
-                        __threadfence_block();
-                        const int prev = atomicAdd(&counters[s * kMaxStageRows + rl], 1);
-                        if (prev == S - 1) {  // last segment of this row: sum in segment order
+                        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                        if (S == 1) {
+                            if (lane == 0) y[r0 + rl] = acc;
+                        } else if (lane == 0) {
+                            float* sl = slots + s * P.slot_stride + rl * S;
+                            sl[sg] = acc;
                             __threadfence_block();
-                            float v = 0.f;
-                            for (int k = 0; k < S; ++k) v += *(volatile float*)(sl + k);
-                            y[r0 + rl] = v;
-                            counters[s * kMaxStageRows + rl] = 0;
+                            const int prev = atomicAdd(&counters[s * kMaxStageRows + rl], 1);
+                            if (prev == S - 1) {  // last segment of this row: sum in segment order
+                                __threadfence_block();
+                                float v = 0.f;
+                                for (int k = 0; k < S; ++k) v += *(volatile float*)(sl + k);
+                                y[r0 + rl] = v;
+                                counters[s * kMaxStageRows + rl] = 0;
+                            }
                         }
                     }
                 }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(empty_bar + 8 * s);
-            if (++s == P.n_stages) {
-                s = 0;
-                phase ^= 1;
-            }
-            rot += R % n_grp;
-            if (rot >= n_grp) rot -= n_grp;
-        }
-        // this CTA's rows of task t are written; when a later task waits for
-        // it, warp 0 quantizes the CTA's blocks of y (when y feeds a later
-        // task) and counts the CTA
-        if (!__ldg(&T.signal)) continue;  // a failed wait ends the loop at the next reducing barrier
-        __threadfence();
-        if (consumer_bar_any(!alive)) break;  // every consumer leaves together after a failed wait
-        if (warp == 0) {
-            if (ql != nullptr) {
-                int4* qm = reinterpret_cast<int4*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.q_meta)));
-                for (int b = row_begin / 32; b < row_end / 32; ++b)
-                    quantize_x_block(__ldcg(y + 32 * b + lane), lane, ql + (size_t)b * kXQLimbBytes, qm + b);
-                __threadfence();
                 __syncwarp();
+                if (lane == 0) mbar_arrive(empty_bar + 8 * s);
+                if (++s == P.n_stages) {
+                    s = 0;
+                    phase ^= 1;
+                }
+                rot += R % n_grp;
+                if (rot >= n_grp) rot -= n_grp;
             }
-            if (lane == 0) atomicAdd(&P.done[t * kCounterStride], 1u);
+            // this CTA's rows of task t are written; when a later task waits
+            // for it, one thread counts the CTA once every consumer is past its
+            // stores.  A failed wait ends the loops at the next reducing barrier.
+            if (__ldg(&T.signal)) {
+                if (consumer_bar_any(!alive)) {  // every consumer leaves together after a failed wait
+                    stop = true;
+                    break;
+                }
+                if (tid == 0) {
+                    __threadfence();
+                    atomicAdd(&P.done[t * kCounterStride], 1u);
+                }
+            }
+            if (++t >= P.n_tasks || !__ldg(&P.tasks[t].reuse_x)) break;
         }
     }
 }
