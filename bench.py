@@ -356,18 +356,186 @@ def main():
             ms = float(t.item())
         return ms
 
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            graph.replay()
-    with Clocks(gpu_uuid(torch, local)) as clk:
-        ms = timed(graph.replay, args.steps)
-    clocks = clk.summary()
-    verify_head(torch, be, head, h0, out["head"], world, rank)
     sb = step_bytes(layers=args.layers)
-    value = sb * args.steps / (ms / 1e3) / 1e9
-    ms_step = ms / args.steps
+    peak, peak_kind = load_peaks()
+    n_gemvs = 7 * args.layers + 1
 
-    # ---- roofline: the fused Q4_0 GEMV alone on the 96 FFN matrices
+    if world == 1:
+        # ---- headline: the whole step in ONE persistent kernel (GEMV stack)
+        stack, stack_graph, ys = build_stack_graph(torch, L, _native, layers, head, h0, stream, dev)
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                stack_graph.replay()
+        with Clocks(gpu_uuid(torch, local)) as clk:
+            ms = timed(stack_graph.replay, args.steps)
+        clocks = clk.summary()
+        check_status(L)
+        # the stack must reproduce the per-GEMV path bit for bit (LM head and last layer)
+        with torch.cuda.stream(stream):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+        for name, y in (("head", ys[-1]), ("down", ys[-2]), ("gate", ys[-4])):
+            if not torch.equal(y, out[name]):
+                raise RuntimeError(f"stack output of {name} differs from the per-GEMV path")
+        verify_head(torch, be, head, h0, ys[-1], world, rank)
+        ms_step = ms / args.steps
+        value = sb * args.steps / (ms / 1e3) / 1e9
+        # secondary: the same step as 225 separately launched GEMVs in a CUDA graph
+        reps = max(10, args.steps // 5)
+        ms_graph = timed(graph.replay, reps) / reps
+        per_gemv = {"ms_per_step": round(ms_graph, 4), "value": round(sb / (ms_graph / 1e3) / 1e9, 1),
+                    "unit": "GB/s", "tokens_per_s": round(1e3 / ms_graph, 2),
+                    "launches_per_step": 2 * n_gemvs}
+        roofline = {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
+                    "frac": round(value / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                    "kernel": "gemv_stack_kernel<FmtQ4_0,2>: the step's 225 GEMVs in one cooperative launch",
+                    "bytes_per_launch": sb, "avg_launch_us": round(ms_step * 1e3, 2),
+                    "launch_note": "one launch per step, after a 28 KB counter reset (cudaMemsetAsync)",
+                    "traffic": round(STACK_TRAFFIC_PER_ALG_BYTE * sb)}
+        e2e = None if args.no_e2e else e2e_stack_host(torch, L, stack, h0, ys[-1], stream, dev, args, timed, sb)
+        e2e_dispatch = None if args.no_e2e else e2e_host_api(torch, L, layers, head, h0, args)
+        launches = args.steps
+        launches_note = f"1 gemv_stack_kernel per step x {args.steps} steps (plus one counter memset per step)"
+        extra = {"per_gemv_graph": per_gemv, "e2e_per_gemv_dispatch": e2e_dispatch}
+        del stack_graph
+        L.nexus_gpu_stack_destroy(stack)
+    else:
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                graph.replay()
+        with Clocks(gpu_uuid(torch, local)) as clk:
+            ms = timed(graph.replay, args.steps)
+        clocks = clk.summary()
+        verify_head(torch, be, head, h0, out["head"], world, rank)
+        ms_step = ms / args.steps
+        value = sb * args.steps / (ms / 1e3) / 1e9
+        roofline = ffn_roofline(torch, L, layers, h0, out, part, ws, stream, dev, timed, args, peak, peak_kind)
+        e2e = None if args.no_e2e else e2e_resident(torch, graph, h0, full, stream, dev, args, timed, sb)
+        launches = 2 * n_gemvs * args.steps
+        launches_note = (f"{2 * n_gemvs} per step (xquant + gemv per GEMV) x {args.steps} steps; "
+                         f"plus {n_gemvs} NCCL all-gathers per step")
+        extra = {}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        gbs, sec, kind, sample = time_reference_layer(3, cpu_threads(), min_seconds=10.0)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cpu_threads(), "kind": kind, "sample": sample}
+
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8+fp32",
+        "dtype_note": "Q4_0 codes x 16-bit fixed-point x in int8 dp4a limbs, fp32 accumulation",
+        "data": "synthetic (seeded GGUF Q4_0 blocks, x ~ N(0,1))",
+        "config": workload_config(args),
+        "layers": args.layers,
+        "pct_of_8tbs": round(100 * value / NOMINAL_HBM_GBS, 2),
+        "pct_of_measured_hbm": round(100 * value / peak, 2),
+        "tokens_per_s": round(1e3 / ms_step, 2),
+        "gemv_calls_per_s": round(n_gemvs * 1e3 / ms_step, 1),
+        "bytes_per_step": sb,
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
+        "gpu_launches": launches, "gpu_launches_note": launches_note,
+    }
+    line.update(extra)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def check_status(L):
+    import ctypes
+
+    bits = ctypes.c_uint32(0)
+    L.nexus_gpu_device_status(ctypes.byref(bits))
+    if bits.value:
+        raise RuntimeError(f"device status word {bits.value:#x} (a bounded wait expired)")
+
+
+def build_stack_graph(torch, L, _native, layers, head, h0, stream, dev):
+    """The step as one GEMV stack: per layer q, k, v (x = the hidden state,
+    after the previous layer's down), o (x = q), gate, up (x = o), down
+    (x = gate); then the LM head (x = the hidden state, after the last down).
+    Captured once in a CUDA graph (counter reset + one launch)."""
+    import ctypes
+
+    tasks, ys = [], []
+    inputs_of = {"q": -1, "k": -1, "v": -1, "o": 0, "gate": 3, "up": 3, "down": 4}
+    last_down = -1
+    for mats in layers:
+        base = len(tasks)
+        for i, (name, n, k) in enumerate(LAYER_SHAPES):
+            y = torch.empty(n, dtype=torch.float32, device=dev)
+            src = inputs_of[name]
+            after = last_down if src < 0 else -1
+            tasks.append(_native.StackTask(mats[name].data_ptr(), n, k, y.data_ptr(), src if src < 0 else base + src,
+                                           after))
+            ys.append(y)
+        last_down = base + 6
+    y = torch.empty(VOCAB, dtype=torch.float32, device=dev)
+    tasks.append(_native.StackTask(head.data_ptr(), VOCAB, HIDDEN, y.data_ptr(), -1, last_down))
+    ys.append(y)
+    arr = (_native.StackTask * len(tasks))(*tasks)
+    h = ctypes.c_void_p()
+    _native.check(L.nexus_gpu_stack_create(DTYPE, arr, len(tasks), HIDDEN, ctypes.byref(h)))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        _native.check(L.nexus_gpu_stack_run(h, h0.data_ptr(), stream.cuda_stream))  # uncaptured warm run
+        torch.cuda.synchronize(dev)
+        with torch.cuda.graph(g, stream=stream):
+            _native.check(L.nexus_gpu_stack_run(h, h0.data_ptr(), stream.cuda_stream))
+    torch.cuda.synchronize(dev)
+    return h, g, ys
+
+
+def e2e_stack_host(torch, L, stack, h0, y_head, stream, dev, args, timed, sb):
+    """The step through the library's public C ABI with host buffers: the
+    token's hidden state is copied from pinned host memory
+    (nexus_gpu_copy_host_to_device_async), the stack runs
+    (nexus_gpu_stack_run), the logits are copied back to pinned host memory
+    (nexus_gpu_copy_device_to_host_async), then the stream is synchronised --
+    every step, inside the timed region."""
+    import ctypes
+
+    hin = torch.empty(HIDDEN, dtype=torch.float32, pin_memory=True)
+    hin.copy_(h0.cpu())
+    hout = torch.empty(VOCAB, dtype=torch.float32, pin_memory=True)
+    xdev = torch.empty(HIDDEN, dtype=torch.float32, device=dev)
+    st = ctypes.c_void_p(stream.cuda_stream)
+
+    def one():
+        _native_check(L.nexus_gpu_copy_host_to_device_async(xdev.data_ptr(), hin.data_ptr(), 4 * HIDDEN, st))
+        _native_check(L.nexus_gpu_stack_run(stack, xdev.data_ptr(), st))
+        _native_check(L.nexus_gpu_copy_device_to_host_async(hout.data_ptr(), y_head.data_ptr(), 4 * VOCAB, st))
+        _native_check(L.nexus_gpu_synchronize(st))
+
+    for _ in range(3):
+        one()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        one()
+    sec = (time.perf_counter() - t0) / args.e2e_steps
+    torch.cuda.synchronize(dev)
+    if not torch.equal(hout, y_head.cpu()):
+        raise RuntimeError("host logits differ from the device result")
+    return {"value": round(sb / sec / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": 4 * HIDDEN,
+            "d2h_bytes_per_step": 4 * VOCAB, "ms_per_step": round(sec * 1e3, 4), "tokens_per_s": round(1 / sec, 2),
+            "api": "nexus_gpu_copy_host_to_device_async + nexus_gpu_stack_run + "
+                   "nexus_gpu_copy_device_to_host_async + nexus_gpu_synchronize, host wall clock per step",
+            "steps": args.e2e_steps}
+
+
+def _native_check(rc):
+    from nexusllm_b200 import _native
+
+    _native.check(rc)
+
+
+def ffn_roofline(torch, L, layers, h0, out, part, ws, stream, dev, timed, args, peak, peak_kind):
+    """N > 1 path: the fused Q4_0 GEMV alone on the 96 FFN matrices."""
     ffn = [(mats[name], name) for mats in layers for name in ("gate", "up", "down")]
     g2 = torch.cuda.CUDAGraph()
     xin = {"gate": h0, "up": h0, "down": out["gate"]}
@@ -387,59 +555,20 @@ def main():
     launches = len(ffn) * reps
     ffn_bytes = sum(W.numel() + 4 * (FFN if n == "down" else HIDDEN) + 4 * part[n].numel() for W, n in ffn)
     avg_launch_us = ms_ffn * 1e3 / launches
-    peak, peak_kind = load_peaks()
     achieved = ffn_bytes / len(ffn) / (avg_launch_us * 1e-6) / 1e9
-    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                "kernel": "gemv_m1_kernel<FmtQ4_0> (+ xquant_kernel), FFN 14336x4096 / 4096x14336",
-                "bytes_per_launch": int(ffn_bytes / len(ffn)), "avg_launch_us": round(avg_launch_us, 3),
-                "traffic": TRAFFIC_PER_FFN_LAUNCH}
-
-    # ---- e2e
-    e2e = None
-    if args.no_e2e:
-        pass
-    elif world == 1:
-        e2e = e2e_host_api(torch, L, layers, head, h0, args)
-    else:
-        e2e = e2e_resident(torch, graph, h0, full, stream, dev, args, timed, sb)
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        gbs, sec, kind, sample = time_reference_layer(3, cpu_threads(), min_seconds=10.0)
-        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cpu_threads(), "kind": kind, "sample": sample}
-
-    launches_per_step = 2 * (7 * args.layers + 1)  # xquant + fused GEMV per call
-    line = {
-        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "int8+fp32",
-        "dtype_note": "Q4_0 codes x 16-bit fixed-point x in int8 dp4a limbs, fp32 accumulation",
-        "data": "synthetic (seeded GGUF Q4_0 blocks, x ~ N(0,1))",
-        "config": workload_config(args),
-        "layers": args.layers,
-        "pct_of_8tbs": round(100 * value / NOMINAL_HBM_GBS, 2),
-        "pct_of_measured_hbm": round(100 * value / peak, 2),
-        "tokens_per_s": round(1e3 / ms_step, 2),
-        "gemv_calls_per_s": round((7 * args.layers + 1) * 1e3 / ms_step, 1),
-        "bytes_per_step": sb,
-        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
-        "gpu_launches": launches_per_step * args.steps,
-        "gpu_launches_note": f"{launches_per_step} per step (xquant + gemv per GEMV) x {args.steps} steps"
-                             + (f"; plus {7 * args.layers + 1} NCCL all-gathers per step" if world > 1 else ""),
-    }
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    del graph, g2
-    if world > 1:
-        dist.barrier(device_ids=[local])
-        dist.destroy_process_group()
+    del g2
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+            "kernel": "gemv_m1_kernel<FmtQ4_0> (+ xquant_kernel), FFN 14336x4096 / 4096x14336 row slices",
+            "bytes_per_launch": int(ffn_bytes / len(ffn)), "avg_launch_us": round(avg_launch_us, 3),
+            "traffic": None}
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one FFN launch of the fused
-# GEMV (mean of gate/up/down), from the ncu capture summarised in
-# profiles/gemv_q4_0_llama3_8b_decode_stack.md
-TRAFFIC_PER_FFN_LAUNCH = 33071445
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per algorithmic
+# byte of the stack kernel, from the ncu capture of a 4-layer Llama-3-8B Q4_0
+# stack summarised in profiles/gemv_stack_q4_0_llama3_8b.md (traffic grows in
+# proportion to the layers a launch processes).
+STACK_TRAFFIC_PER_ALG_BYTE = 495263744 / 492044288  # 4 layers: 490.91 MB read + 4.35 MB written
 
 
 def verify_head(torch, be, head, h0, y_graph, world, rank):
