@@ -568,7 +568,7 @@ def ffn_roofline(torch, L, layers, h0, out, part, ws, stream, dev, timed, args, 
 # byte of the stack kernel, from the ncu capture of a 4-layer Llama-3-8B Q4_0
 # stack summarised in profiles/gemv_stack_q4_0_llama3_8b.md (traffic grows in
 # proportion to the layers a launch processes).
-STACK_TRAFFIC_PER_ALG_BYTE = 495263744 / 492044288  # 4 layers: 490.91 MB read + 4.35 MB written
+STACK_TRAFFIC_PER_ALG_BYTE = (786439424 + 6302976) / 788075520  # 4 layers + LM head: read + written / algorithmic
 
 
 def verify_head(torch, be, head, h0, y_graph, world, rank):
