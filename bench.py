@@ -11,19 +11,24 @@ starts from the same resident hidden state.  Weights are seeded synthetic
 GGUF blocks with the configuration's distributions (nexusllm_b200/synth.py),
 generated on the device.
 
-A step = one token = the 225 GEMVs, captured once in a CUDA graph and
-replayed.  With --gpus N > 1 (torchrun, one rank per GPU) every matrix is
-row-sharded over the ranks and each GEMV's output slices are all-gathered with
-NCCL (strong scaling: the same model at every N).
+A step = one token = the 225 GEMVs as ONE persistent GEMV-stack launch
+(nexus_gpu_stack_run), captured once in a CUDA graph and replayed.  With
+--gpus N > 1 (torchrun, one rank per GPU) every matrix is row-sharded over the
+ranks and the stack kernel stores each rank's output rows straight into every
+peer's output over NVLink (the all-gather fused into the GEMV; strong
+scaling: the same model at every N).  The same step as 225 separate GEMV
+launches (+ NCCL all-gathers at N > 1) is timed as a secondary figure and
+must agree bit for bit.
 
 Reported (one JSON line on rank 0):
   value     whole-job algorithmic GB/s = (weight + x + y bytes per step) x
             steps / device time (max over ranks)
-  e2e       same metric through the reference-facing C ABI with host
-            buffers (N=1: nexus_gpu_gemv_dispatch per GEMV, pinned host x/y,
-            copies and syncs inside the timed region)
-  roofline  the fused Q4_0 GEMV on the FFN matrices (81% of the step's
-            bytes), timed alone with CUDA events, against MEASURED_PEAKS.json
+  e2e       same metric through the library's C ABI with host buffers:
+            pinned host hidden state in, host logits out, every step
+            (N=1 also reports the reference-facing nexus_gpu_gemv_dispatch
+            path, one synchronous host-pointer call per GEMV)
+  roofline  the stack kernel (the only kernel of the step), algorithmic
+            bytes per launch / CUDA-event time, against MEASURED_PEAKS.json
   cpu_baseline  NexusLLM's own AVX2 GEMV (oracle/_ref) on this host's cores
             over one decode layer
 
@@ -400,21 +405,44 @@ def main():
         del stack_graph
         L.nexus_gpu_stack_destroy(stack)
     else:
+        # ---- headline: the row-sharded stack, all-gather fused into the kernel
+        sst, sgraph, souts = build_sharded_stack_graph(torch, L, layers, head, h0, stream, dev, world, rank)
         with torch.cuda.stream(stream):
             for _ in range(args.warmup):
-                graph.replay()
+                sgraph.replay()
         with Clocks(gpu_uuid(torch, local)) as clk:
-            ms = timed(graph.replay, args.steps)
+            ms = timed(sgraph.replay, args.steps)
         clocks = clk.summary()
-        verify_head(torch, be, head, h0, out["head"], world, rank)
+        check_status(L)
+        # bit-exact against the per-GEMV path with NCCL all-gathers
+        with torch.cuda.stream(stream):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+        for name, idx in (("head", -1), ("down", -2), ("gate", -4)):
+            if not torch.equal(souts[idx], out[name]):
+                raise RuntimeError(f"sharded stack output of {name} differs from the per-GEMV NCCL path")
         ms_step = ms / args.steps
         value = sb * args.steps / (ms / 1e3) / 1e9
-        roofline = ffn_roofline(torch, L, layers, h0, out, part, ws, stream, dev, timed, args, peak, peak_kind)
-        e2e = None if args.no_e2e else e2e_resident(torch, graph, h0, full, stream, dev, args, timed, sb)
-        launches = 2 * n_gemvs * args.steps
-        launches_note = (f"{2 * n_gemvs} per step (xquant + gemv per GEMV) x {args.steps} steps; "
-                         f"plus {n_gemvs} NCCL all-gathers per step")
-        extra = {}
+        reps = max(10, args.steps // 5)
+        ms_graph = timed(graph.replay, reps) / reps
+        per_gemv = {"ms_per_step": round(ms_graph, 4), "value": round(sb / (ms_graph / 1e3) / 1e9, 1),
+                    "unit": "GB/s", "tokens_per_s": round(1e3 / ms_graph, 2),
+                    "launches_per_step": 2 * n_gemvs, "nccl_all_gathers_per_step": n_gemvs}
+        per_gpu = sb / world
+        roofline = {"bound": "hbm", "achieved": round(per_gpu / (ms_step * 1e-3) / 1e9, 1), "peak": peak,
+                    "unit": "GB/s", "frac": round(per_gpu / (ms_step * 1e-3) / 1e9 / peak, 4),
+                    "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                    "kernel": f"gemv_stack_kernel<FmtQ4_0,2>, rank's 1/{world} row slice of every GEMV, "
+                              "output rows stored into every peer over NVLink",
+                    "bytes_per_launch": int(per_gpu), "avg_launch_us": round(ms_step * 1e3, 2),
+                    "traffic": round(STACK_TRAFFIC_PER_ALG_BYTE * per_gpu)}
+        e2e = None if args.no_e2e else e2e_sharded(torch, sst, sgraph, h0, souts[-1], stream, dev, args, timed, sb)
+        launches = args.steps
+        launches_note = (f"1 gemv_stack_kernel per step per GPU x {args.steps} steps; no NCCL in the step "
+                         "(peer stores + peer counters inside the kernel)")
+        extra = {"per_gemv_graph_nccl": per_gemv}
+        del sgraph
+        sst.close()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -491,6 +519,67 @@ def build_stack_graph(torch, L, _native, layers, head, h0, stream, dev):
     return h, g, ys
 
 
+def build_sharded_stack_graph(torch, L, layers, head, h0, stream, dev, world, rank):
+    """This rank's row slices of the step's GEMVs as one sharded stack (same
+    task order and dependencies as build_stack_graph); outputs are
+    full-length on every rank.  Captured once in a CUDA graph."""
+    from nexusllm_b200.sharded import ShardedStack
+
+    tasks = []
+    inputs_of = {"q": -1, "k": -1, "v": -1, "o": 0, "gate": 3, "up": 3, "down": 4}
+    last_down = -1
+    for mats in layers:
+        base = len(tasks)
+        for name, n, k in LAYER_SHAPES:
+            src = inputs_of[name]
+            tasks.append((mats[name].data_ptr(), n, k, src if src < 0 else base + src, last_down if src < 0 else -1))
+        last_down = base + 6
+    tasks.append((head.data_ptr(), VOCAB, HIDDEN, -1, last_down))
+    st = ShardedStack(DTYPE, tasks, HIDDEN, world, rank)
+    outs = []
+    for i, (_, n, *_r) in enumerate(tasks):
+        outs.append(torch.as_tensor(_DeviceVec(st.output(i), n), device=dev))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        st.run(h0.data_ptr(), stream.cuda_stream)  # uncaptured warm run (every rank runs it)
+        torch.cuda.synchronize(dev)
+        with torch.cuda.graph(g, stream=stream):
+            st.run(h0.data_ptr(), stream.cuda_stream)
+    torch.cuda.synchronize(dev)
+    return st, g, outs
+
+
+class _DeviceVec:
+    """A library-owned fp32 device vector seen through __cuda_array_interface__."""
+
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 2}
+
+
+def e2e_sharded(torch, st, sgraph, h0, y_head, stream, dev, args, timed, sb):
+    """N > 1: per step, every rank copies the token's hidden state from pinned
+    host memory, replays its sharded-stack graph, and copies the full logits
+    back to pinned host memory (device-timed, max over ranks)."""
+    hin = torch.empty(HIDDEN, dtype=torch.float32, pin_memory=True)
+    hin.copy_(h0.cpu())
+    hout = torch.empty(VOCAB, dtype=torch.float32, pin_memory=True)
+
+    def one():
+        h0.copy_(hin, non_blocking=True)
+        sgraph.replay()
+        hout.copy_(y_head, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            one()
+        ms = timed(one, args.e2e_steps)
+    return {"value": round(sb * args.e2e_steps / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
+            "h2d_bytes_per_step": 4 * HIDDEN, "d2h_bytes_per_step": 4 * VOCAB,
+            "ms_per_step": round(ms / args.e2e_steps, 4),
+            "api": "sharded GEMV stack (nexus_gpu_stack_run) per rank; host hidden state in, host logits out "
+                   "per step (device-timed, max over ranks)"}
+
+
 def e2e_stack_host(torch, L, stack, h0, y_head, stream, dev, args, timed, sb):
     """The step through the library's public C ABI with host buffers: the
     token's hidden state is copied from pinned host memory
@@ -532,36 +621,6 @@ def _native_check(rc):
     from nexusllm_b200 import _native
 
     _native.check(rc)
-
-
-def ffn_roofline(torch, L, layers, h0, out, part, ws, stream, dev, timed, args, peak, peak_kind):
-    """N > 1 path: the fused Q4_0 GEMV alone on the 96 FFN matrices."""
-    ffn = [(mats[name], name) for mats in layers for name in ("gate", "up", "down")]
-    g2 = torch.cuda.CUDAGraph()
-    xin = {"gate": h0, "up": h0, "down": out["gate"]}
-    with torch.cuda.stream(stream):
-        torch.cuda.synchronize(dev)
-        with torch.cuda.graph(g2, stream=stream):
-            for W, name in ffn:
-                k = xin[name].numel()
-                L.nexus_gpu_gemv_ws(W.data_ptr(), DTYPE, xin[name].data_ptr(), 0, part[name].data_ptr(), 1,
-                                    part[name].numel(), k, ws.data_ptr(), ws.numel(),
-                                    torch.cuda.current_stream(dev).cuda_stream)
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            g2.replay()
-    reps = max(3, args.steps // 5)
-    ms_ffn = timed(g2.replay, reps)
-    launches = len(ffn) * reps
-    ffn_bytes = sum(W.numel() + 4 * (FFN if n == "down" else HIDDEN) + 4 * part[n].numel() for W, n in ffn)
-    avg_launch_us = ms_ffn * 1e3 / launches
-    achieved = ffn_bytes / len(ffn) / (avg_launch_us * 1e-6) / 1e9
-    del g2
-    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-            "kernel": "gemv_m1_kernel<FmtQ4_0> (+ xquant_kernel), FFN 14336x4096 / 4096x14336 row slices",
-            "bytes_per_launch": int(ffn_bytes / len(ffn)), "avg_launch_us": round(avg_launch_us, 3),
-            "traffic": None}
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per algorithmic
@@ -631,25 +690,6 @@ def e2e_host_api(torch, L, layers, head, h0, args):
             "d2h_bytes_per_step": d2h, "ms_per_step": round(sec * 1e3, 3), "tokens_per_s": round(1 / sec, 2),
             "api": "nexus_gpu_gemv_dispatch (host pointers, synchronous, weights cached on device)",
             "steps": args.e2e_steps}
-
-
-def e2e_resident(torch, graph, h0, full, stream, dev, args, timed, sb):
-    """N > 1: per step, the token's hidden state comes from pinned host memory
-    and the logits go back to pinned host memory around the graph replay."""
-    hin = torch.empty(HIDDEN, dtype=torch.float32, pin_memory=True)
-    hin.copy_(h0.cpu())
-    hout = torch.empty(VOCAB, dtype=torch.float32, pin_memory=True)
-
-    def one():
-        h0.copy_(hin, non_blocking=True)
-        graph.replay()
-        hout.copy_(full["head"], non_blocking=True)
-
-    with torch.cuda.stream(stream):
-        ms = timed(one, args.e2e_steps)
-    return {"value": round(sb * args.e2e_steps / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
-            "h2d_bytes_per_step": 4 * HIDDEN, "d2h_bytes_per_step": 4 * VOCAB,
-            "api": "device-resident stack; host hidden state in, host logits out per step"}
 
 
 if __name__ == "__main__":

@@ -193,10 +193,39 @@ typedef struct {
  * the fast kernel's limits.  No counterpart in the reference. */
 NEXUS_GPU_API int32_t nexus_gpu_stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n_tasks,
                                              uint64_t input_cols, void** out_stack);
-/* Run the stack on `stream` with input dX (fp32, input_cols).  Graph-capturable:
- * a counter reset and one kernel launch.  Runs of one stack must not overlap. */
+/* Run the stack on `stream` with input dX (fp32, input_cols, 16-byte aligned).
+ * Graph-capturable: one kernel launch.  Runs of one stack must not overlap.
+ * Counters are cumulative over runs (a device-side run counter sets each
+ * run's targets), so a run needs no reset.  After a run reported a timeout
+ * through nexus_gpu_device_status the stack is poisoned: destroy it. */
 NEXUS_GPU_API int32_t nexus_gpu_stack_run(void* stack, const float* dX, void* stream);
 NEXUS_GPU_API int32_t nexus_gpu_stack_destroy(void* stack);
+
+/* Row-sharded GEMV stacks over `world` GPUs (2..8) of one node, one process
+ * (or thread) per GPU, each holding the full x.  SURVEY-style row sharding of
+ * the reference's GEMVs (src/forward_pass.cpp:504-585) with the all-gather
+ * fused into the kernel: rank r computes rows [rows*r/world, rows*(r+1)/world)
+ * of every task and writes them straight into every peer's copy of the
+ * output over NVLink (peer stores), then counts itself on every peer's
+ * counter; each task waits for all ranks' CTAs.  No counterpart in the
+ * reference.
+ *   tasks[i].rows = the FULL row count; tasks[i].W = this rank's row slice
+ *   (contiguous GGUF rows); tasks[i].y must be NULL: outputs belong to the
+ *   stack (full-length on every rank, nexus_gpu_stack_output).
+ * Every rank builds the same task list, then:
+ *   nexus_gpu_stack_export  -> this rank's blob (CUDA IPC handle + checks);
+ *   exchange the blobs between ranks (any host channel);
+ *   nexus_gpu_stack_connect -> all `world` blobs in rank order.
+ * Every rank must run the stack the same number of times. */
+NEXUS_GPU_API int32_t nexus_gpu_stack_create_sharded(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n_tasks,
+                                                     uint64_t input_cols, uint32_t world, uint32_t rank,
+                                                     void** out_stack);
+/* Blob size when blob == NULL; else writes *blob_bytes (>= that size) bytes. */
+NEXUS_GPU_API int32_t nexus_gpu_stack_export(void* stack, void* blob, uint64_t* blob_bytes);
+NEXUS_GPU_API int32_t nexus_gpu_stack_connect(void* stack, const void* blobs, uint64_t blobs_bytes);
+/* Device pointer to task `task`'s output on this rank (the caller's y for an
+ * unsharded stack). */
+NEXUS_GPU_API int32_t nexus_gpu_stack_output(void* stack, uint32_t task, float** y);
 
 /* Bit-exact dequantization of `count` elements (a whole number of blocks)
  * from device blocks to device floats, asynchronous on `stream`. */

@@ -478,6 +478,14 @@ void report_void(const char* fn, int32_t rc) {
 
 
 // ------------------------------------------------------------ GEMV stacks
+// Device block of a stack: the control area (per-task counters, abort flag,
+// run epoch, CTA-exit count, end-of-run count), then -- sharded stacks only --
+// every task's full-length output.  Peers map this block through CUDA IPC.
+struct StackLayout {
+    size_t done = 0, abort = 0, epoch = 0, fin = 0, end = 0, ctrl = 0, total = 0;
+    std::vector<uint64_t> out_off;  // sharded: output of task i at float offset out_off[i]
+};
+
 struct StackHandle {
     int dev = -1;
     uint32_t dtype = 0;
@@ -485,11 +493,24 @@ struct StackHandle {
     int grid = 0;
     size_t smem = 0;
     int n_tasks = 0;
+    int world = 1, rank = 0;
+    bool connected = true;  // sharded stacks need nexus_gpu_stack_connect first
+    uint64_t fingerprint = 0;
     StackParams params{};
     StackTask* d_tasks = nullptr;
-    unsigned* d_counters = nullptr;  // done[n * kCounterStride] | abort
-    size_t counter_bytes = 0;
+    uint8_t* d_block = nullptr;
+    StackLayout lay;
+    std::vector<float*> outputs;        // this rank's output of each task
+    std::vector<void*> peer_mappings;   // IPC mappings opened by connect
 };
+
+// What a rank publishes to its peers (nexus_gpu_stack_export).
+struct StackBlob {
+    uint32_t magic, version, world, rank, n_tasks, grid;
+    uint64_t fingerprint, block_bytes;
+    cudaIpcMemHandle_t handle;
+};
+constexpr uint32_t kStackBlobMagic = 0x4e535442u;  // "NSTB"
 
 template <class F, int G>
 int32_t stack_kernel_attrs(const Device& d, size_t smem) {
@@ -527,15 +548,51 @@ int32_t stack_launch_for(const StackHandle& h, cudaStream_t st) {
 
 void stack_free(StackHandle* h) {
     if (!h) return;
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (h->dev >= 0 && cur != h->dev) cudaSetDevice(h->dev);
+    for (void* m : h->peer_mappings)
+        if (m) cudaIpcCloseMemHandle(m);
     if (h->d_tasks) cudaFree(h->d_tasks);
-    if (h->d_counters) cudaFree(h->d_counters);
+    if (h->d_block) cudaFree(h->d_block);
+    if (h->dev >= 0 && cur >= 0 && cur != h->dev) cudaSetDevice(cur);
     delete h;
 }
 
-int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n, uint64_t input_cols,
-                     void** out) {
+// Rows [r0, r1) of an N-row matrix that rank `rank` of `world` owns.
+inline void shard_rows(uint64_t N, int world, int rank, uint64_t& r0, uint64_t& r1) {
+    r0 = N * (uint64_t)rank / (uint64_t)world;
+    r1 = N * (uint64_t)(rank + 1) / (uint64_t)world;
+}
+
+uint64_t stack_fingerprint(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n, uint64_t input_cols, int world) {
+    uint64_t h = 1469598103934665603ull;
+    auto mix = [&](uint64_t v) {
+        for (int i = 0; i < 8; ++i) {
+            h ^= (v >> (8 * i)) & 0xffu;
+            h *= 1099511628211ull;
+        }
+    };
+    mix(dtype);
+    mix(n);
+    mix(input_cols);
+    mix((uint64_t)world);
+    for (uint32_t i = 0; i < n; ++i) {
+        mix(tasks[i].rows);
+        mix(tasks[i].cols);
+        mix((uint64_t)(int64_t)tasks[i].x_source);
+        mix((uint64_t)(int64_t)tasks[i].after);
+    }
+    return h;
+}
+
+int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n, uint64_t input_cols, int world,
+                     int rank, void** out) {
     if (!out || (!tasks && n)) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null argument");
     *out = nullptr;
+    if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world)
+        return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "rank %d of world %d (1..%d GPUs)", rank, world, kMaxWorld);
+    const bool sharded = world > 1;
     if (dtype == NEXUS_GPU_FP16)
         return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "GEMV stacks serve the integer GGUF formats");
     FormatInfo f;
@@ -550,12 +607,17 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n,
     if ((rc = ensure_attrs(*d))) return rc;
 
     std::vector<StackTask> ht(n);
+    std::vector<uint64_t> local_rows(n), row_off(n);
     int group = -1;
     size_t slot = 0;
     for (uint32_t i = 0; i < n; ++i) {
         const NexusGpuStackTask& u = tasks[i];
         if ((rc = check_shape(dtype, u.rows, u.cols, f))) return fail(rc, "task %u: %s", i, t_last_error.c_str());
-        if (!u.W || !u.y || u.rows == 0) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u: null W/y or no rows", i);
+        if (!u.W || u.rows == 0) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u: null W or no rows", i);
+        if (sharded ? u.y != nullptr : u.y == nullptr)
+            return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT,
+                        sharded ? "task %u: y must be NULL in a sharded stack (outputs belong to the stack)"
+                                : "task %u: null y", i);
         if (((uintptr_t)u.W & 15) != 0) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u: W not 16-byte aligned", i);
         const uint64_t xlen = u.x_source < 0 ? input_cols : (u.x_source < (int32_t)i ? tasks[u.x_source].rows : 0);
         if (u.x_source >= (int32_t)i || xlen != u.cols)
@@ -563,23 +625,30 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n,
                         u.x_source, (unsigned long long)u.cols);
         if (u.after >= (int32_t)i || u.after < -1)
             return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u: after=%d is not an earlier task", i, u.after);
-        if (u.x_source >= 0 && ((uintptr_t)tasks[u.x_source].y & 15) != 0)
+        if (!sharded && u.x_source >= 0 && ((uintptr_t)tasks[u.x_source].y & 15) != 0)
             return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %d feeds x but its y is not 16-byte aligned",
                         u.x_source);
+        uint64_t r0 = 0, r1 = u.rows;
+        if (sharded) shard_rows(u.rows, world, rank, r0, r1);
+        if (r1 <= r0 || u.rows > (uint64_t)INT32_MAX)
+            return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "task %u: %llu rows leave rank %d of %d no rows", i,
+                        (unsigned long long)u.rows, rank, world);
+        local_rows[i] = r1 - r0;
+        row_off[i] = r0;
         GemvParams gp{};
         size_t sm = 0;
         const uint64_t rb = row_bytes_of(f, u.cols);
-        if (!plan_for(dtype, *d, (int)u.rows, (int)u.cols, rb, gp, sm))
+        if (!plan_for(dtype, *d, (int)local_rows[i], (int)u.cols, rb, gp, sm))
             return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "task %u (%llux%llu) is outside the fast kernel's limits", i,
-                        (unsigned long long)u.rows, (unsigned long long)u.cols);
+                        (unsigned long long)local_rows[i], (unsigned long long)u.cols);
         if (group < 0) group = gp.group;
         if (gp.group != group)
             return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "task %u: mixed block-grouping in one stack", i);
         StackTask& T = ht[i];
         T.W = static_cast<const uint8_t*>(u.W);
         T.row_bytes = rb;
-        T.total_bytes = rb * u.rows;
-        T.N = (int)u.rows;
+        T.total_bytes = rb * local_rows[i];
+        T.N = (int)local_rows[i];
         T.K = (int)u.cols;
         T.nwi = gp.nwi;
         T.segments = gp.segments;
@@ -587,10 +656,7 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n,
         T.wi_per_lane = gp.wi_per_lane;
         T.stage_rows = gp.stage_rows;
         T.stage_bytes = gp.stage_bytes;
-        T.y = u.y;
-        T.x = u.x_source < 0 ? nullptr : tasks[u.x_source].y;
-        T.src = u.x_source < 0 ? -1 : u.x_source;
-        T.after = u.after;
+        T.row_off = (int)row_off[i];
         slot = std::max(slot, (size_t)gp.stage_bytes);
     }
     size_t x_smem = 0;
@@ -614,28 +680,69 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n,
     h->group = group;
     h->grid = d->sms;
     h->n_tasks = (int)n;
+    h->world = world;
+    h->rank = rank;
+    h->connected = !sharded;
+    h->fingerprint = stack_fingerprint(dtype, tasks, n, input_cols, world);
     h->smem = kStackSmemHeader + x_smem + (size_t)ns * slot;
 
-    cudaError_t e = cudaMalloc(&h->d_tasks, n * sizeof(StackTask));
-    h->counter_bytes = (size_t)(n * kCounterStride + 1) * sizeof(unsigned);
-    if (e == cudaSuccess) e = cudaMalloc(&h->d_counters, h->counter_bytes);
-    if (e != cudaSuccess) {
-        stack_free(h);
-        cudaGetLastError();
-        return fail(NEXUS_GPU_ERROR_OUT_OF_TIER0_MEMORY, "stack allocation failed: %s", cudaGetErrorString(e));
-    }
     std::vector<char> waited_for(n, 0);
     for (uint32_t i = 0; i < n; ++i) {
         if (tasks[i].after >= 0) waited_for[tasks[i].after] = 1;
         if (tasks[i].x_source >= 0) waited_for[tasks[i].x_source] = 1;
     }
+    StackLayout& lay = h->lay;
+    lay.done = 0;
+    lay.abort = (size_t)n * kCounterStride * sizeof(unsigned long long);
+    lay.epoch = lay.abort + 128;
+    lay.fin = lay.epoch + 128;
+    lay.end = lay.fin + 128;
+    lay.ctrl = align256(lay.end + 128);
+    lay.total = lay.ctrl;
+    if (sharded) {
+        lay.out_off.resize(n);
+        for (uint32_t i = 0; i < n; ++i) {
+            lay.out_off[i] = lay.total / sizeof(float);
+            lay.total += align256(tasks[i].rows * sizeof(float));
+        }
+    }
+
+    cudaError_t e = cudaMalloc(&h->d_tasks, n * sizeof(StackTask));
+    if (e == cudaSuccess) e = cudaMalloc(&h->d_block, lay.total);
+    if (e == cudaSuccess) e = cudaMemset(h->d_block, 0, lay.total);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        stack_free(h);
+        cudaGetLastError();
+        return fail(NEXUS_GPU_ERROR_OUT_OF_TIER0_MEMORY, "stack allocation failed: %s", cudaGetErrorString(e));
+    }
+    h->outputs.resize(n);
+    for (uint32_t i = 0; i < n; ++i)
+        h->outputs[i] = sharded ? reinterpret_cast<float*>(h->d_block) + lay.out_off[i] : tasks[i].y;
+    int n_signal = 0, sig_in_group = 0;
     for (uint32_t i = 0; i < n; ++i) {
         StackTask& T = ht[i];
+        T.y = h->outputs[i];
+        T.y_off = sharded ? lay.out_off[i] : 0;
+        T.x = tasks[i].x_source < 0 ? nullptr : h->outputs[tasks[i].x_source];
+        T.src = tasks[i].x_source < 0 ? -1 : tasks[i].x_source;
+        T.after = tasks[i].after;
         T.signal = waited_for[i];
+        T.sig_ord = T.signal ? n_signal++ : -1;
         // same input, same plan (same cols), and no new ordering dependency:
         // keep the previous task's x slices and skip the wait and the staging
         T.reuse_x = i > 0 && tasks[i].x_source == tasks[i - 1].x_source && tasks[i].cols == tasks[i - 1].cols &&
                     (tasks[i].after == -1 || tasks[i].after == tasks[i - 1].after);
+        // Consumer warps drift apart only within an x group (they meet at every
+        // group head), so a group holds fewer signalled tasks than there are
+        // shared completion slots: warps never post to a slot's next round
+        // before every warp has posted the current one.
+        if (!T.reuse_x) sig_in_group = 0;
+        if (T.signal && sig_in_group == kSigSlots / 2) {
+            T.reuse_x = 0;
+            sig_in_group = 0;
+        }
+        if (T.signal) ++sig_in_group;
     }
     e = cudaMemcpy(h->d_tasks, ht.data(), n * sizeof(StackTask), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
@@ -650,8 +757,16 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n,
     P.x_smem = (int)x_smem;
     P.slot_stride = kMaxSlots / ns;
     P.x_in = nullptr;
-    P.done = h->d_counters;
-    P.abort_flag = h->d_counters + (size_t)n * kCounterStride;
+    P.done = reinterpret_cast<unsigned long long*>(h->d_block + lay.done);
+    P.abort_flag = reinterpret_cast<unsigned*>(h->d_block + lay.abort);
+    P.epoch = reinterpret_cast<unsigned long long*>(h->d_block + lay.epoch);
+    P.fin = reinterpret_cast<unsigned long long*>(h->d_block + lay.fin);
+    P.end_done = reinterpret_cast<unsigned long long*>(h->d_block + lay.end);
+    P.world = world;
+    P.rank = rank;
+    P.peer_done[rank] = P.done;
+    P.peer_end[rank] = P.end_done;
+    P.peer_block[rank] = h->d_block;
 
     switch (dtype) {
         case NEXUS_GPU_GGUF_Q4_0: rc = stack_attrs_for<FmtQ4_0>(group, *d, h->smem); break;
@@ -667,15 +782,102 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n,
     return NEXUS_GPU_SUCCESS;
 }
 
+int32_t stack_current_device(const StackHandle* h) {
+    int cur = -1;
+    CUDA_TRY(cudaGetDevice(&cur));
+    if (cur != h->dev) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "stack belongs to device %d, current is %d", h->dev, cur);
+    return NEXUS_GPU_SUCCESS;
+}
+
+int32_t stack_export(void* handle, void* blob, uint64_t* bytes) {
+    StackHandle* h = static_cast<StackHandle*>(handle);
+    if (!h || !bytes) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null handle or size");
+    if (!blob) {
+        *bytes = sizeof(StackBlob);
+        return NEXUS_GPU_SUCCESS;
+    }
+    if (*bytes < sizeof(StackBlob)) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "blob buffer of %llu bytes, need %zu",
+                                                (unsigned long long)*bytes, sizeof(StackBlob));
+    if (h->world < 2) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "not a sharded stack");
+    int32_t rc = stack_current_device(h);
+    if (rc) return rc;
+    StackBlob b{};
+    b.magic = kStackBlobMagic;
+    b.version = 1;
+    b.world = (uint32_t)h->world;
+    b.rank = (uint32_t)h->rank;
+    b.n_tasks = (uint32_t)h->n_tasks;
+    b.grid = (uint32_t)h->grid;
+    b.fingerprint = h->fingerprint;
+    b.block_bytes = h->lay.total;
+    CUDA_TRY(cudaIpcGetMemHandle(&b.handle, h->d_block));
+    std::memcpy(blob, &b, sizeof(b));
+    *bytes = sizeof(StackBlob);
+    return NEXUS_GPU_SUCCESS;
+}
+
+int32_t stack_connect(void* handle, const void* blobs, uint64_t bytes) {
+    StackHandle* h = static_cast<StackHandle*>(handle);
+    if (!h || !blobs) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null handle or blobs");
+    if (h->world < 2) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "not a sharded stack");
+    if (!h->peer_mappings.empty()) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "stack already connected");
+    if (bytes != (uint64_t)h->world * sizeof(StackBlob))
+        return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "%llu blob bytes, need %d x %zu", (unsigned long long)bytes,
+                    h->world, sizeof(StackBlob));
+    int32_t rc = stack_current_device(h);
+    if (rc) return rc;
+    std::vector<StackBlob> b(h->world);
+    std::memcpy(b.data(), blobs, bytes);
+    for (int p = 0; p < h->world; ++p) {
+        if (b[p].magic != kStackBlobMagic || b[p].version != 1 || b[p].world != (uint32_t)h->world ||
+            b[p].rank != (uint32_t)p)
+            return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "blob %d is not rank %d's stack export", p, p);
+        if (b[p].fingerprint != h->fingerprint || b[p].n_tasks != (uint32_t)h->n_tasks ||
+            b[p].block_bytes != h->lay.total)
+            return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "rank %d built a different task list", p);
+        if (b[p].grid != (uint32_t)h->grid)
+            return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "rank %d runs %u CTAs, this rank %d", p, b[p].grid, h->grid);
+    }
+    std::vector<void*> maps(h->world, nullptr);
+    for (int p = 0; p < h->world; ++p) {
+        if (p == h->rank) continue;
+        cudaError_t e = cudaIpcOpenMemHandle(&maps[p], b[p].handle, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (void* m : maps)
+                if (m) cudaIpcCloseMemHandle(m);
+            cudaGetLastError();
+            return fail(NEXUS_GPU_ERROR_CUDA, "opening rank %d's stack memory: %s", p, cudaGetErrorString(e));
+        }
+    }
+    StackParams& P = h->params;
+    for (int p = 0; p < h->world; ++p) {
+        if (p == h->rank) continue;
+        uint8_t* base = static_cast<uint8_t*>(maps[p]);
+        P.peer_done[p] = reinterpret_cast<unsigned long long*>(base + h->lay.done);
+        P.peer_end[p] = reinterpret_cast<unsigned long long*>(base + h->lay.end);
+        P.peer_block[p] = base;
+    }
+    h->peer_mappings = maps;
+    h->connected = true;
+    return NEXUS_GPU_SUCCESS;
+}
+
+int32_t stack_output(void* handle, uint32_t task, float** y) {
+    StackHandle* h = static_cast<StackHandle*>(handle);
+    if (!h || !y) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null handle or output pointer");
+    if (task >= (uint32_t)h->n_tasks) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u of %d", task, h->n_tasks);
+    *y = h->outputs[task];
+    return NEXUS_GPU_SUCCESS;
+}
+
 int32_t stack_run(void* handle, const float* x_in, cudaStream_t st) {
     StackHandle* h = static_cast<StackHandle*>(handle);
     if (!h || !x_in) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null handle or input");
     if (((uintptr_t)x_in & 15) != 0) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "stack input not 16-byte aligned");
-    int cur = -1;
-    CUDA_TRY(cudaGetDevice(&cur));
-    if (cur != h->dev) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "stack belongs to device %d, current is %d", h->dev, cur);
+    if (!h->connected) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "sharded stack not connected to its peers");
+    int32_t rc = stack_current_device(h);
+    if (rc) return rc;
     h->params.x_in = x_in;
-    CUDA_TRY(cudaMemsetAsync(h->d_counters, 0, h->counter_bytes, st));
     switch (h->dtype) {
         case NEXUS_GPU_GGUF_Q4_0: return stack_launch_for<FmtQ4_0>(*h, st);
         case NEXUS_GPU_GGUF_Q8_0: return stack_launch_for<FmtQ8_0>(*h, st);
@@ -888,7 +1090,32 @@ NEXUS_GPU_API int32_t nexus_gpu_gemv_noalloc(const void* dW, uint32_t dtype, con
 NEXUS_GPU_API int32_t nexus_gpu_stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n_tasks,
                                              uint64_t input_cols, void** out_stack) {
     t_last_error.clear();
-    return stack_create(dtype, tasks, n_tasks, input_cols, out_stack);
+    return stack_create(dtype, tasks, n_tasks, input_cols, 1, 0, out_stack);
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_stack_create_sharded(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n_tasks,
+                                                     uint64_t input_cols, uint32_t world, uint32_t rank,
+                                                     void** out_stack) {
+    t_last_error.clear();
+    if (world < 2) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "a sharded stack needs 2..%d ranks", kMaxWorld);
+    if (world > (uint32_t)kMaxWorld || rank >= world)
+        return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "rank %u of world %u (2..%d GPUs)", rank, world, kMaxWorld);
+    return stack_create(dtype, tasks, n_tasks, input_cols, (int)world, (int)rank, out_stack);
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_stack_export(void* stack, void* blob, uint64_t* blob_bytes) {
+    t_last_error.clear();
+    return stack_export(stack, blob, blob_bytes);
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_stack_connect(void* stack, const void* blobs, uint64_t blobs_bytes) {
+    t_last_error.clear();
+    return stack_connect(stack, blobs, blobs_bytes);
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_stack_output(void* stack, uint32_t task, float** y) {
+    t_last_error.clear();
+    return stack_output(stack, task, y);
 }
 
 NEXUS_GPU_API int32_t nexus_gpu_stack_run(void* stack, const float* dX, void* stream) {

@@ -12,16 +12,25 @@
 //    consumers wait for a task's input.
 //  * Each task's consumer work is the single-GEMV kernel's (same plan, same
 //    per-row arithmetic, so results are bit-identical to nexus_gpu_gemv).
-//  * A task's x is either the stack input or the y of an earlier task.  Rows
-//    are balanced over the CTAs.  When a CTA has written its rows of a task
-//    that a later task waits for, one thread counts the CTA on the task's
-//    global counter; a task starts when its source's counter and, optionally,
-//    another task's counter (the ordering a real decode has between layers)
-//    reach the CTA count.  The consumer warps of a CTA step through the tasks
-//    together: one thread polls the grid counters, then the CTA reads the
-//    task's fp32 x from L2 and quantizes it into shared memory itself
-//    (quantize_x_pair, the same bits as xquant_kernel), so a finished task
-//    only has to be counted, never converted, before its dependants start.
+//    Rows are balanced over the CTAs.
+//  * A task's x is either the stack input or the y of an earlier task.  Each
+//    task that a later task reads or waits for has a counter, cumulative over
+//    runs.  When all consumer warps of a CTA have posted a task done (shared
+//    memory, release), the CTA's producer thread -- between weight copies --
+//    makes one release fence for every task finished since its last look and
+//    adds 1 to each one's counter on every rank; the consumers never wait for
+//    a fence or an atomic.  A dependent task's CTA waits (one thread) until
+//    the counter reaches every CTA of every rank, then reads x.
+//  * The consumer warps of a CTA step through the tasks together, one x group
+//    (a task and the following tasks with the same input and plan) at a time:
+//    the CTA reads the group's x once, quantizes it into shared memory itself
+//    (quantize_x_pair, the same bits as xquant_kernel), and each warp copies
+//    its slices into registers for every task of the group.
+//  * Sharded over GPUs, a rank computes its row slice of every task and
+//    stores each output row into every peer as well (plain stores).  The
+//    run ends when every rank's rows of every task have landed everywhere:
+//    each CTA posts its end to every rank after a system-scope release, and
+//    one thread per rank waits for all of them.
 //  * All CTAs must be resident at once (they wait on one another): the host
 //    launches the kernel cooperatively with one CTA per SM.  Every wait is
 //    bounded; an expired wait raises a global abort flag that ends every CTA's
@@ -32,32 +41,47 @@
 
 namespace nexus_gpu {
 
+constexpr int kMaxWorld = 8;
+
 struct StackTask {
     const uint8_t* W;
     uint64_t row_bytes, total_bytes;
     int N, K;
     int nwi, segments, seg_wi, wi_per_lane, stage_rows, stage_bytes;
-    float* y;
-    const float* x;          // fp32 x: the source task's y, or null for the stack input
-    int src;                 // the source task, or -1 (the stack input: nothing to wait for)
-    int after;               // -1, or a task that must complete before this one starts
-    int signal;              // some later task waits for this one: count CTAs when done
-    int reuse_x;             // same input and plan as the previous task: keep its x, skip the wait
+    float* y;                            // this rank's full-length output (slice written at row_off)
+    uint64_t y_off;                      // sharded: y's float offset in every rank's block
+    const float* x;                      // fp32 x: the source task's y, or null for the stack input
+    int src;                             // the source task, or -1 (the stack input)
+    int after;                           // -1, or a task that must complete before this one starts
+    int row_off;                         // first global row of this rank's slice (0 unless sharded)
+    int reuse_x;                         // same input and plan as the previous task: keep its x
+    int signal;                          // a later task waits for this one: count it on the counters
+    int sig_ord;                         // ordinal among the signalled tasks (shared completion slot)
 };
 
 struct StackParams {
     const StackTask* tasks;
     int n_tasks;
     int n_stages;
-    int stage_slot;          // bytes per ring slot (>= every task's stage_bytes)
-    int x_smem;              // bytes of the shared x staging buffer (>= every task's K/32 * 80)
-    int slot_stride;         // partial-sum floats per ring slot (>= R * S of every task)
-    const float* x_in;       // stack input, fp32, 16-byte aligned
-    unsigned* done;          // [n_tasks * kCounterStride]: CTAs that finished each task
-    unsigned* abort_flag;
+    int stage_slot;                      // bytes per ring slot (>= every task's stage_bytes)
+    int x_smem;                          // bytes of the shared x staging buffer
+    int slot_stride;                     // partial-sum floats per ring slot (>= R * S of every task)
+    const float* x_in;                   // stack input, fp32, 16-byte aligned
+    unsigned long long* done;            // [n_tasks * kCounterStride]: CTAs (of every rank) that
+                                         // finished each task, summed over all runs of the stack
+    unsigned* abort_flag;                // sticky: an expired wait poisons the stack
+    unsigned long long* epoch;           // runs completed on this rank
+    unsigned long long* fin;             // CTAs of this rank that left, summed over all runs
+    unsigned long long* end_done;        // sharded: CTAs of all ranks whose rows all landed here, all runs
+    int world, rank;                     // row sharding over `world` GPUs (1, rank 0: unsharded)
+    unsigned long long* peer_done[kMaxWorld]; // every rank's `done` (own included)
+    unsigned long long* peer_end[kMaxWorld];  // every rank's end_done (own included)
+    uint8_t* peer_block[kMaxWorld];           // every rank's stack block (own included)
 };
 
-constexpr int kCounterStride = 32;  // one 128-byte line per counter
+// One 128-byte line per counter.  Counters are never reset: run e of a stack
+// (e = 0, 1, ...) waits for (e + 1) * world * n_cta.
+constexpr int kCounterStride = 16;
 
 // Rows [rb, re) of an N-row task for CTA c of n_cta, balanced.
 __device__ __forceinline__ void cta_rows(int N, int c, int n_cta, int& rb, int& re) {
@@ -65,20 +89,26 @@ __device__ __forceinline__ void cta_rows(int N, int c, int n_cta, int& rb, int& 
     re = (int)((int64_t)N * (c + 1) / n_cta);
 }
 
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p, bool sys) {
+    unsigned long long v;
+    if (sys) asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    else asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
-
+// Add 1 to a counter, on this GPU or (sys) on a peer, after the caller's fence.
+__device__ __forceinline__ void red_add_u64(unsigned long long* p, bool sys) {
+    if (sys) asm volatile("red.relaxed.sys.global.add.u64 [%0], 1;" ::"l"(p) : "memory");
+    else asm volatile("red.relaxed.gpu.global.add.u64 [%0], 1;" ::"l"(p) : "memory");
+}
 // Wait (one thread) until *ctr >= target.  Bounded: gives up when another CTA
 // raised the abort flag or after kWaitLimitNs, raising it itself.
-__device__ __noinline__ bool wait_count_bounded(const unsigned* ctr, unsigned target, unsigned* abort_flag) {
-    if (ld_acquire_u32(ctr) >= target) return true;
+__device__ __noinline__ bool wait_count_bounded(const unsigned long long* ctr, unsigned long long target,
+                                                unsigned* abort_flag, bool sys) {
+    if (ld_acquire_u64(ctr, sys) >= target) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t k = 1;; ++k) {
         __nanosleep(64);
-        if (ld_acquire_u32(ctr) >= target) return true;
+        if (ld_acquire_u64(ctr, sys) >= target) return true;
         if ((k & 15u) == 0) {
             if (*reinterpret_cast<volatile unsigned*>(abort_flag)) return false;
             if (globaltimer_ns() - t0 > kWaitLimitNs) {
@@ -90,8 +120,24 @@ __device__ __noinline__ bool wait_count_bounded(const unsigned* ctr, unsigned ta
     }
 }
 
-constexpr int kStackBarBytes = 16 * kMaxStages + 16;  // mbarriers + a broadcast flag
+constexpr int kSigSlots = 16;  // shared per-task completion counters (cumulative, by signal ordinal)
+// mbarriers, a broadcast flag, the end-of-run post count, the completion slots
+constexpr int kStackBarBytes = 16 * kMaxStages + 32 + 4 * kSigSlots;
 constexpr int kStackSmemHeader = ((kStackBarBytes + 127) / 128) * 128 + kSmemHeader - kBarBytes;
+
+__device__ __forceinline__ void red_release_shared_add(uint32_t addr, uint32_t v) {
+    asm volatile("red.release.cta.shared::cta.add.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_shared(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+// Release fences (the counters that follow are relaxed atomics).
+__device__ __forceinline__ void fence_release(bool sys) {
+    if (sys) asm volatile("fence.acq_rel.sys;" ::: "memory");
+    else asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
 
 // Named barrier of the consumer warps (the producer warp never joins it).
 __device__ __forceinline__ void consumer_bar() {
@@ -184,6 +230,32 @@ __device__ __forceinline__ void load_xint_smem(uint32_t xs, int nxbp, int gj, XI
     X.sx = (int)m.w;
 }
 
+// Task fields read at the point of use (lane 0, once per output row): volatile
+// loads keep the compiler from holding them in registers across the hot loop.
+__device__ __forceinline__ uint64_t ld_task_u64(const void* p) {
+    uint64_t v;
+    asm volatile("ld.global.nc.u64 %0, [%1];" : "=l"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ int ld_task_i32(const int* p) {
+    int v;
+    asm volatile("ld.global.nc.s32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+
+// Write row r (of this rank's slice) of task T: this rank's output and --
+// sharded -- every peer's copy (plain stores over NVLink).
+__device__ __forceinline__ void put_row(const StackParams& P, const StackTask* T, int r, float v) {
+    const uint64_t g = (uint64_t)ld_task_i32(&T->row_off) + (uint64_t)r;  // global row
+    reinterpret_cast<float*>(ld_task_u64(&T->y))[g] = v;
+    if (P.world > 1) {
+        const uint64_t y_off = ld_task_u64(&T->y_off);
+#pragma unroll 1
+        for (int p = 0; p < P.world; ++p)
+            if (p != P.rank) reinterpret_cast<float*>(P.peer_block[p])[y_off + g] = v;
+    }
+}
+
 template <class F, int G>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const StackParams P) {
     using XT = typename std::conditional<F::kIntX, XInt, XF16>::type;
@@ -193,6 +265,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
     const uint32_t full_bar = sbase;
     const uint32_t empty_bar = sbase + 8 * kMaxStages;
     volatile int* s_flag = reinterpret_cast<volatile int*>(smem + 16 * kMaxStages);  // warp-0 verdicts
+    const uint32_t tend = sbase + 16 * kMaxStages + 16;  // consumer warps done with every task
+    const uint32_t tdone = tend + 16;                     // [kSigSlots] u32 task completion posts
     constexpr int kHdr = ((kStackBarBytes + 127) / 128) * 128;
     float* slots = reinterpret_cast<float*>(smem + kHdr);
     int* counters = reinterpret_cast<int*>(smem + kHdr + kMaxSlots * 4);  // [kMaxStages][kMaxStageRows]
@@ -201,6 +275,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_cta = gridDim.x, c = blockIdx.x;
     const int NS = P.n_stages;
+    const bool sys = P.world > 1;  // outputs shared with peer GPUs
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
@@ -208,6 +283,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
             mbar_init(empty_bar + 8 * s, kConsumerWarps);
         }
         s_flag[0] = 1;
+        for (int k = 0; k < 4 + kSigSlots; ++k) reinterpret_cast<volatile uint32_t*>(smem + 16 * kMaxStages + 16)[k] = 0;
         fence_mbar_init();
     }
     for (int i = threadIdx.x; i < kMaxStages * kMaxStageRows; i += blockDim.x) counters[i] = 0;
@@ -215,10 +291,43 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
 
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------- producer
+        // Lane 0 streams weights and, between copies, releases the tasks this
+        // CTA's consumer warps have all posted done: one release fence (system
+        // scope when sharded), then this CTA is counted on every rank's counter.
         if (lane != 0) return;
         int it = 0, s = 0;
         uint32_t phase = 0;
         bool ok = true;
+        int st = 0, sk = 0;  // next task to count, its signal ordinal
+        while (st < P.n_tasks && !__ldg(&P.tasks[st].signal)) ++st;
+        auto poll = [&]() -> bool {  // true when tasks were released
+            // every consecutive finished task goes out under ONE release fence
+            int e = st, ek = sk;
+            while (e < P.n_tasks) {
+                const uint32_t need = (uint32_t)kConsumerWarps * (uint32_t)(ek / kSigSlots + 1);
+                if (ld_acquire_shared(tdone + 4 * (ek % kSigSlots)) < need) break;
+                ++ek;
+                ++e;
+                while (e < P.n_tasks && !__ldg(&P.tasks[e].signal)) ++e;
+            }
+            if (e == st) return false;
+            fence_release(sys);
+            for (int t = st; t < e; ++t) {
+                if (!__ldg(&P.tasks[t].signal)) continue;
+                if (sys)
+                    for (int p = 0; p < P.world; ++p) red_add_u64(P.peer_done[p] + t * kCounterStride, true);
+                else
+                    red_add_u64(P.done + t * kCounterStride, false);
+            }
+            st = e;
+            sk = ek;
+            return true;
+        };
+        auto give_up = [&]() {
+            atomicOr(&g_device_status, kStatusWaitTimeout);
+            atomicExch(P.abort_flag, 1u);
+            ok = false;
+        };
         for (int t = 0; t < P.n_tasks && ok; ++t) {
             const StackTask& T = P.tasks[t];
             const uint64_t rb = __ldg(&T.row_bytes), total = __ldg(&T.total_bytes);
@@ -229,9 +338,24 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
             const uint64_t floor16 = total & ~(uint64_t)15;
             const uint64_t span = (uint64_t)R * rb, cta_end = (uint64_t)row_end * rb;
             for (uint64_t start = (uint64_t)row_begin * rb; start < cta_end; ++it) {
-                if (it >= NS && !mbar_wait_bounded(empty_bar + 8 * s, phase)) {
-                    ok = false;
-                    break;
+                poll();
+                if (it >= NS && !mbar_test_wait(empty_bar + 8 * s, phase)) {
+                    // ring full: keep counting finished tasks while the slot drains
+                    uint64_t t0 = globaltimer_ns();
+                    for (uint32_t k = 1; !mbar_test_wait(empty_bar + 8 * s, phase); ++k) {
+                        if (poll()) t0 = globaltimer_ns();
+                        if ((k & 255u) == 0) {
+                            if (*reinterpret_cast<volatile unsigned*>(P.abort_flag)) {
+                                ok = false;
+                                break;
+                            }
+                            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                                give_up();
+                                break;
+                            }
+                        }
+                    }
+                    if (!ok) break;
                 }
                 const uint64_t end = min(start + span, cta_end);
                 const uint64_t a = start & ~(uint64_t)15;
@@ -252,6 +376,33 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                 }
             }
         }
+        // every copy issued: count the remaining tasks as the consumers finish
+        // them; sharded, then tell every rank that this CTA's rows of every
+        // task have been stored (one system-scope release per run)
+        if (ok) {
+            uint64_t t0 = globaltimer_ns();
+            for (uint32_t k = 1; st < P.n_tasks || (sys && ld_acquire_shared(tend) < (uint32_t)kConsumerWarps); ++k) {
+                if (poll()) {
+                    t0 = globaltimer_ns();
+                    continue;
+                }
+                __nanosleep(32);
+                if ((k & 63u) == 0) {
+                    if (*reinterpret_cast<volatile unsigned*>(P.abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                        give_up();
+                        break;
+                    }
+                }
+            }
+            if (ok && sys) {
+                asm volatile("fence.acq_rel.sys;" ::: "memory");
+                for (int p = 0; p < P.world; ++p) red_add_u64(P.peer_end[p], true);
+            }
+        }
         if (!ok) {  // leave no copy in flight
             for (int k = 0; k < NS && k < it; ++k) {
                 const int j = it - 1 - k;
@@ -262,16 +413,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
     }
 
     // ----------------------------------------------------------- consumers
-    // Consumer warps step through the tasks together, one x group at a time
-    // (a task and the tasks after it that read the same x with the same plan):
-    // warp 0 polls the grid counters for the CTA, the CTA reads the group's
-    // fp32 x from L2 once, quantizes it into shared memory, and each warp
+    // Consumer warps step through the tasks together, one x group at a time:
+    // the CTA reads the group's x once, quantizes it into shared memory, and each warp
     // copies its slices into registers, which then serve every task of the
     // group.  Staging from L2 once per CTA (not once per warp) keeps x off the
     // L2 path the weight stream saturates; the x registers live only inside a
     // group, so the staging loads can all be in flight at once.
     const int tid = threadIdx.x;  // 0 .. kConsumers-1
     const uint32_t xs = sbase + kStackSmemHeader;  // x staging (xsw layout)
+    // this run's number: counter targets sit on top of all earlier runs
+    const unsigned long long run = *reinterpret_cast<volatile unsigned long long*>(P.epoch);
     bool alive = true, stop = false;
     int s = 0;
     uint32_t phase = 0;
@@ -284,18 +435,18 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
         int wi[kMaxJ];
         bool has[kMaxJ];
         lane_items<G>(lane, sg, SW, J, NW, wi, has);
-        if (tid == 0) {  // the input must be written, and the ordering dependency done
+        if (tid == 0) {  // the input's CTAs (all ranks) are done, and the ordering dependency
             const int src = __ldg(&H.src), after = __ldg(&H.after);
-            int ok = 1;
-            if (src >= 0) ok = wait_count_bounded(&P.done[src * kCounterStride], (unsigned)n_cta, P.abort_flag);
-            if (ok && after >= 0) ok = wait_count_bounded(&P.done[after * kCounterStride], (unsigned)n_cta, P.abort_flag);
+            const unsigned long long target = (run + 1) * (unsigned long long)P.world * (unsigned long long)n_cta;
+            int ok = *reinterpret_cast<volatile unsigned*>(P.abort_flag) == 0;  // poisoned by an earlier run
+            if (ok && src >= 0) ok = wait_count_bounded(&P.done[src * kCounterStride], target, P.abort_flag, sys);
+            if (ok && after >= 0) ok = wait_count_bounded(&P.done[after * kCounterStride], target, P.abort_flag, sys);
             __threadfence();
             s_flag[0] = ok;
         }
         consumer_bar();  // also: every warp is done with the previous group's x staging
-        if (!s_flag[0]) break;
-        {   // read x (L2) and quantize it into the staging buffer, two lanes
-            // per 32-element block, kConsumers / 2 blocks per pass
+        bool failed = s_flag[0] == 0;
+        if (!failed) {   // read x (L2) and quantize it, two lanes per 32-element block
             const float4* xv = reinterpret_cast<const float4*>(__ldg(reinterpret_cast<const unsigned long long*>(&H.x)));
             if (xv == nullptr) xv = reinterpret_cast<const float4*>(P.x_in);
             const int nxb = K / 32, nxbp = x_stage_planes_len(K), hf = lane & 1;
@@ -313,7 +464,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                 quantize_x_pair(e, hf, b < nxb, xs, nxbp, b);
             }
         }
-        consumer_bar();
+        if (consumer_bar_any(failed)) {  // every consumer leaves together after a failed wait
+            stop = true;
+            break;
+        }
         XT X[kMaxJ];
         {
             const int nxbp = x_stage_planes_len(K);
@@ -327,7 +481,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
             const StackTask& T = P.tasks[t];
             const int N = __ldg(&T.N), R = __ldg(&T.stage_rows);
             const uint64_t rbytes = __ldg(&T.row_bytes);
-            float* y = reinterpret_cast<float*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.y)));
             int row_begin, row_end;
             cta_rows(N, c, n_cta, row_begin, row_end);
             const int n_st = (row_end - row_begin + R - 1) / R;
@@ -337,7 +490,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                 const int nr = min(R, row_end - r0);
                 if (alive && !mbar_wait_bounded(full_bar + 8 * s, phase)) {
                     atomicExch(P.abort_flag, 1u);
-                    alive = false;  // no more waits; the loop ends at the next reducing barrier
+                    alive = false;  // no more waits; the loop ends at the next group head
                 }
                 if (alive) {
                     const uint32_t base =
@@ -350,7 +503,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
 #pragma unroll
                         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
                         if (S == 1) {
-                            if (lane == 0) y[r0 + rl] = acc;
+                            if (lane == 0) put_row(P, &T, r0 + rl, acc);
                         } else if (lane == 0) {
                             float* sl = slots + s * P.slot_stride + rl * S;
                             sl[sg] = acc;
@@ -360,7 +513,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                                 __threadfence_block();
                                 float v = 0.f;
                                 for (int k = 0; k < S; ++k) v += *(volatile float*)(sl + k);
-                                y[r0 + rl] = v;
+                                put_row(P, &T, r0 + rl, v);
                                 counters[s * kMaxStageRows + rl] = 0;
                             }
                         }
@@ -375,21 +528,31 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                 rot += R % n_grp;
                 if (rot >= n_grp) rot -= n_grp;
             }
-            // this CTA's rows of task t are written; when a later task waits
-            // for it, one thread counts the CTA once every consumer is past its
-            // stores.  A failed wait ends the loops at the next reducing barrier.
+            // this warp's rows of task t are stored: post it for the producer thread
             if (__ldg(&T.signal)) {
-                if (consumer_bar_any(!alive)) {  // every consumer leaves together after a failed wait
-                    stop = true;
-                    break;
-                }
-                if (tid == 0) {
-                    __threadfence();
-                    atomicAdd(&P.done[t * kCounterStride], 1u);
-                }
+                __syncwarp();
+                if (lane == 0) red_release_shared_add(tdone + 4 * (__ldg(&T.sig_ord) % kSigSlots), 1u);
             }
             if (++t >= P.n_tasks || !__ldg(&P.tasks[t].reuse_x)) break;
         }
+    }
+    // A sharded run ends only when every rank's rows of every task have landed
+    // here: each warp posts that it is done, the producer thread then counts
+    // this CTA on every rank's end counter, and one thread of CTA 0 waits for
+    // all CTAs of all ranks (the kernel, and so the stream, completes after it).
+    if (sys) {
+        __syncwarp();
+        if (lane == 0) red_release_shared_add(tend, 1u);
+        if (c == 0 && tid == 0 && !stop)
+            wait_count_bounded(P.end_done, (run + 1) * (unsigned long long)P.world * (unsigned long long)n_cta,
+                               P.abort_flag, true);
+    }
+    // the last CTA of this rank to leave advances the epoch for the next run
+    consumer_bar();
+    if (tid == 0) {
+        __threadfence();
+        const unsigned long long left = atomicAdd(P.fin, 1ull) + 1;
+        if (left == (run + 1) * (unsigned long long)n_cta) atomicExch(P.epoch, run + 1);
     }
 }
 
