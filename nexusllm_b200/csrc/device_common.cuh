@@ -166,4 +166,20 @@ __device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
     return d;
 }
 
+// Four weight bytes w (elements e..e+3) against int16 x pairs v0 = (x[e],
+// x[e+1]) and v1 = (x[e+2], x[e+3]): two dp2a, full 16-bit x in one pass.
+// _u: unsigned weight bytes; _s: signed.
+__device__ __forceinline__ int dpx_u(uint32_t w, uint32_t v0, uint32_t v1, int c) {
+    int d;
+    asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(v0), "r"(w), "r"(c));
+    asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(v1), "r"(w), "r"(d));
+    return d;
+}
+__device__ __forceinline__ int dpx_s(uint32_t w, uint32_t v0, uint32_t v1, int c) {
+    int d;
+    asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(v0), "r"(w), "r"(c));
+    asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(v1), "r"(w), "r"(d));
+    return d;
+}
+
 }  // namespace nexus_gpu

@@ -28,9 +28,9 @@
 //
 // Arithmetic.  For the integer formats the activation is first turned into
 // a 16-bit fixed-point vector by xquant_kernel (per 32-element block: scale
-// s = amax/32639 and X = rint(x/s) split into two signed 8-bit limbs
-// X = 256*Xh + Xl, plus the block sums of X).  Each block's dot product is
-// then exact int32 dp4a arithmetic over (weight code, limb) pairs, scaled once
+// s = amax/32639 and int16 X = rint(x/s), plus the block sums of X).  Each
+// block's dot product is then exact int32 dp2a arithmetic (16-bit X against
+// 8-bit weight codes, two products per instruction), scaled once
 // per block by the block's fp16 scale(s) (as the reference does,
 // src/quantization.cpp:325,374) and by s.  The only rounding beyond fp32
 // accumulation is the fixed-point representation of x: |x - X*s| <= s/2 with
@@ -49,11 +49,11 @@ namespace nexus_gpu {
 constexpr int kConsumerWarps = 15;   // + 1 producer warp = 16 warps: 128 registers per thread
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kGemvThreads = kConsumers + 32;
-constexpr int kXQLimbBytes = 64;     // Xh[32] then Xl[32], int8
+constexpr int kXQLimbBytes = 64;     // X[32], int16
 constexpr int kXQMetaBytes = 16;     // {float s, int sum X[0:16), int sum X[16:32), int sum X[0:32)}
-constexpr float kXQMax = 32639.0f;   // largest |X| whose high limb fits int8
+constexpr float kXQMax = 32639.0f;   // largest |X|
 constexpr int kMaxJ = 4;             // work items (x slices in registers) per lane
-constexpr int kMaxSegments = 15;     // K segments per row (one warp each); a divisor of kConsumerWarps
+constexpr int kMaxSegments = 15;     // K segments per row (one warp each)
 constexpr int kMaxStageRows = 64;
 constexpr int kMaxStages = 12;
 constexpr int kMaxSlots = 1024;      // n_stages * stage_rows * segments partial sums
@@ -109,9 +109,10 @@ struct FmtF16 {
     static constexpr bool kIntX = false;
 };
 
-// x slice of one work item, integer formats
+// x slice of one work item, integer formats: the 32 X values as int16 pairs
+// (v[j] = X[2j] | X[2j+1] << 16), the block scale and the block sums.
 struct XInt {
-    uint32_t h[8], l[8];
+    uint32_t v[16];
     float s;
     int sa, sb, sx;  // sums of X over [0,16), [16,32), [0,32)
 };
@@ -122,11 +123,9 @@ template <bool kCoherent = false>
 __device__ __forceinline__ void load_xint(const uint8_t* limbs, const int4* meta, int gj, XInt& X) {
     const int4* a = reinterpret_cast<const int4*>(limbs + (size_t)gj * kXQLimbBytes);
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
+    for (int q = 0; q < 4; ++q) {
         const int4 v = kCoherent ? __ldcg(a + q) : __ldg(a + q);
-        X.h[4 * q + 0] = v.x; X.h[4 * q + 1] = v.y; X.h[4 * q + 2] = v.z; X.h[4 * q + 3] = v.w;
-        const int4 u = kCoherent ? __ldcg(a + 2 + q) : __ldg(a + 2 + q);
-        X.l[4 * q + 0] = u.x; X.l[4 * q + 1] = u.y; X.l[4 * q + 2] = u.z; X.l[4 * q + 3] = u.w;
+        X.v[4 * q + 0] = v.x; X.v[4 * q + 1] = v.y; X.v[4 * q + 2] = v.z; X.v[4 * q + 3] = v.w;
     }
     const int4 m = kCoherent ? __ldcg(meta + gj) : __ldg(meta + gj);
     X.s = __int_as_float(m.x);
@@ -168,19 +167,17 @@ __device__ __forceinline__ float dot_q4_0(uint32_t p, const XInt& X) {
     uint32_t q[4];
     lds_words_2a<4>(p + 2, q);
     const float d = nexus_fp16(lds16(p));
-    int shl = 0, shh = 0, sll = 0, slh = 0;
+    int al = 0, ah = 0;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const uint32_t lo = q[k] & 0x0F0F0F0Fu;  // weights 4k..4k+3
         const uint32_t hi = q[k] & 0xF0F0F0F0u;  // 16 * weights 16+4k..
-        shl = dp4a_us(lo, X.h[k], shl);
-        shh = dp4a_us(hi, X.h[4 + k], shh);
-        sll = dp4a_us(lo, X.l[k], sll);
-        slh = dp4a_us(hi, X.l[4 + k], slh);
+        al = dpx_u(lo, X.v[2 * k], X.v[2 * k + 1], al);
+        ah = dpx_u(hi, X.v[8 + 2 * k], X.v[9 + 2 * k], ah);
     }
-    // 16 * sum((q - 8) * X), exact in int32
-    const int t16 = ((shl * 16 + shh) << 8) + sll * 16 + slh - 128 * X.sx;
-    return (d * X.s) * (0.0625f * (float)t16);
+    // sum((q - 8) * X), exact in int32 (ah carries a factor 16)
+    const int t = al + (ah >> 4) - 8 * X.sx;
+    return (d * X.s) * (float)t;
 }
 
 // Q8_0 (include/quantization.hpp:14-17; src/quantization.cpp:332-379).
@@ -188,13 +185,13 @@ __device__ __forceinline__ float dot_q8_0(uint32_t p, const XInt& X) {
     uint32_t q[8];
     lds_words_2a<8>(p + 2, q);
     const float d = nexus_fp16(lds16(p));
-    int sh = 0, sl = 0;
+    int a0 = 0, a1 = 0;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        sh = dp4a_ss(q[k], X.h[k], sh);
-        sl = dp4a_ss(q[k], X.l[k], sl);
+    for (int k = 0; k < 8; k += 2) {
+        a0 = dpx_s(q[k], X.v[2 * k], X.v[2 * k + 1], a0);
+        a1 = dpx_s(q[k + 1], X.v[2 * k + 2], X.v[2 * k + 3], a1);
     }
-    return (d * X.s) * (float)((sh << 8) + sl);
+    return (d * X.s) * (float)(a0 + a1);
 }
 
 // Q5_K sub-block `sub` (32 weights) of the 176-byte super-block at o
@@ -224,14 +221,12 @@ __device__ __forceinline__ float dot_q5_k(uint32_t o, int sub, const XInt& X) {
         const uint32_t ho = (((hb >> 1) & 0x55u) * 0x00410410u) & 0x10101010u;
         const uint32_t ulo = (qs[k] & 0x0F0F0F0Fu) | he;
         const uint32_t uhi = ((qs[k] >> 4) & 0x0F0F0F0Fu) | ho;
-        sh = dp4a_us(ulo, X.h[k], sh);
-        sh = dp4a_us(uhi, X.h[4 + k], sh);
-        sl = dp4a_us(ulo, X.l[k], sl);
-        sl = dp4a_us(uhi, X.l[4 + k], sl);
+        sh = dpx_u(ulo, X.v[2 * k], X.v[2 * k + 1], sh);
+        sl = dpx_u(uhi, X.v[8 + 2 * k], X.v[9 + 2 * k], sl);
     }
     const float scale = d * (float)sc;
     const float minv = dmin * (float)mn;
-    return X.s * (scale * (float)((sh << 8) + sl) - minv * (float)X.sx);
+    return X.s * (scale * (float)(sh + sl) - minv * (float)X.sx);
 }
 
 // Q6_K sub-blocks 2*pair and 2*pair+1 (16 weights each) of the 210-byte
@@ -258,18 +253,15 @@ __device__ __forceinline__ float dot_q6_k(uint32_t o, int pair, const XInt& X) {
         const uint32_t u1 = (l1 & 0x0F0F0F0Fu) | h0b;         // 4..7
         const uint32_t u2 = ((l0 >> 4) & 0x0F0F0F0Fu) | h1a;  // 8..11
         const uint32_t u3 = ((l1 >> 4) & 0x0F0F0F0Fu) | h1b;  // 12..15
-        int sh = dp4a_us(u0, X.h[4 * t + 0], 0);
-        sh = dp4a_us(u1, X.h[4 * t + 1], sh);
-        sh = dp4a_us(u2, X.h[4 * t + 2], sh);
-        sh = dp4a_us(u3, X.h[4 * t + 3], sh);
-        int sl = dp4a_us(u0, X.l[4 * t + 0], 0);
-        sl = dp4a_us(u1, X.l[4 * t + 1], sl);
-        sl = dp4a_us(u2, X.l[4 * t + 2], sl);
-        sl = dp4a_us(u3, X.l[4 * t + 3], sl);
+        const uint32_t* v = X.v + 8 * t;  // elements 16t .. 16t+15
+        int sh = dpx_u(u0, v[0], v[1], 0);
+        int sl = dpx_u(u1, v[2], v[3], 0);
+        sh = dpx_u(u2, v[4], v[5], sh);
+        sl = dpx_u(u3, v[6], v[7], sl);
         const int sx = t == 0 ? X.sa : X.sb;
         const int sc = (int)(int8_t)((scw >> (8 * t)) & 0xffu);
         const float scale = d * (float)sc;
-        r = fmaf(scale, (float)((sh << 8) + sl - 32 * sx), r);
+        r = fmaf(scale, (float)(sh + sl - 32 * sx), r);
     }
     return X.s * r;
 }
@@ -277,18 +269,16 @@ __device__ __forceinline__ float dot_q6_k(uint32_t o, int pair, const XInt& X) {
 // ------------------------------------------------------- grouped decoders
 // 32 Q4_0 weights already in registers (4 words of nibble pairs) against x.
 __device__ __forceinline__ float q4_0_block(float d, const uint32_t (&q)[4], const XInt& X) {
-    int shl = 0, shh = 0, sll = 0, slh = 0;
+    int al = 0, ah = 0;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const uint32_t lo = q[k] & 0x0F0F0F0Fu;  // weights 4k..4k+3
         const uint32_t hi = q[k] & 0xF0F0F0F0u;  // 16 * weights 16+4k..
-        shl = dp4a_us(lo, X.h[k], shl);
-        shh = dp4a_us(hi, X.h[4 + k], shh);
-        sll = dp4a_us(lo, X.l[k], sll);
-        slh = dp4a_us(hi, X.l[4 + k], slh);
+        al = dpx_u(lo, X.v[2 * k], X.v[2 * k + 1], al);
+        ah = dpx_u(hi, X.v[8 + 2 * k], X.v[9 + 2 * k], ah);
     }
-    // sum((q - 8) * X), exact: the high-nibble sums carry a factor 16
-    const int t = ((shl + (shh >> 4)) << 8) + sll + (slh >> 4) - 8 * X.sx;
+    // sum((q - 8) * X), exact: the high-nibble sum carries a factor 16
+    const int t = al + (ah >> 4) - 8 * X.sx;
     return (d * X.s) * (float)t;
 }
 
@@ -307,13 +297,13 @@ __device__ __forceinline__ float dot_q4_0_x2(uint32_t p, const XInt& X0, const X
 }
 
 __device__ __forceinline__ float q8_0_block(float d, const uint32_t (&q)[8], const XInt& X) {
-    int sh = 0, sl = 0;
+    int a0 = 0, a1 = 0;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        sh = dp4a_ss(q[k], X.h[k], sh);
-        sl = dp4a_ss(q[k], X.l[k], sl);
+    for (int k = 0; k < 8; k += 2) {
+        a0 = dpx_s(q[k], X.v[2 * k], X.v[2 * k + 1], a0);
+        a1 = dpx_s(q[k + 1], X.v[2 * k + 2], X.v[2 * k + 3], a1);
     }
-    return (d * X.s) * (float)((sh << 8) + sl);
+    return (d * X.s) * (float)(a0 + a1);
 }
 
 // Two consecutive Q8_0 blocks (68 bytes) at a 4-byte-aligned shared address.
@@ -341,12 +331,10 @@ __device__ __forceinline__ int q5_k_sub(const uint4& qv, uint32_t qhw, const XIn
         const uint32_t ho = (((hb >> 1) & 0x55u) * 0x00410410u) & 0x10101010u;
         const uint32_t ulo = (qs[k] & 0x0F0F0F0Fu) | he;
         const uint32_t uhi = ((qs[k] >> 4) & 0x0F0F0F0Fu) | ho;
-        sh = dp4a_us(ulo, X.h[k], sh);
-        sh = dp4a_us(uhi, X.h[4 + k], sh);
-        sl = dp4a_us(ulo, X.l[k], sl);
-        sl = dp4a_us(uhi, X.l[4 + k], sl);
+        sh = dpx_u(ulo, X.v[2 * k], X.v[2 * k + 1], sh);
+        sl = dpx_u(uhi, X.v[8 + 2 * k], X.v[9 + 2 * k], sl);
     }
-    return (sh << 8) + sl;
+    return sh + sl;
 }
 
 // Sub-blocks 4h..4h+3 (half h of the 176-byte super-block at 16-byte-aligned
@@ -374,23 +362,19 @@ __device__ __forceinline__ float dot_q5_k_x4(uint32_t o, int h, const XInt (&X)[
 }
 
 // Q6_K: 16 weights of one sub-block from 2 ql words and 1 qh word.
-__device__ __forceinline__ int q6_k_sub(uint32_t l0, uint32_t l1, uint32_t hw, const uint32_t* xh,
-                                        const uint32_t* xl) {
+// v: the 8 int16 x pairs of the sub-block's 16 elements.
+__device__ __forceinline__ int q6_k_sub(uint32_t l0, uint32_t l1, uint32_t hw, const uint32_t* v) {
     const uint32_t pa = __byte_perm(hw, 0, 0x1100);  // qh bytes 0,0,1,1
     const uint32_t pb = __byte_perm(hw, 0, 0x3322);  // qh bytes 2,2,3,3
     const uint32_t u0 = (l0 & 0x0F0F0F0Fu) | (((pa << 4) & 0x00300030u) | (pa & 0x30003000u));
     const uint32_t u1 = (l1 & 0x0F0F0F0Fu) | (((pb << 4) & 0x00300030u) | (pb & 0x30003000u));
     const uint32_t u2 = ((l0 >> 4) & 0x0F0F0F0Fu) | (((pa << 2) & 0x00300030u) | ((pa >> 2) & 0x30003000u));
     const uint32_t u3 = ((l1 >> 4) & 0x0F0F0F0Fu) | (((pb << 2) & 0x00300030u) | ((pb >> 2) & 0x30003000u));
-    int sh = dp4a_us(u0, xh[0], 0);
-    sh = dp4a_us(u1, xh[1], sh);
-    sh = dp4a_us(u2, xh[2], sh);
-    sh = dp4a_us(u3, xh[3], sh);
-    int sl = dp4a_us(u0, xl[0], 0);
-    sl = dp4a_us(u1, xl[1], sl);
-    sl = dp4a_us(u2, xl[2], sl);
-    sl = dp4a_us(u3, xl[3], sl);
-    return (sh << 8) + sl;
+    int sh = dpx_u(u0, v[0], v[1], 0);
+    int sl = dpx_u(u1, v[2], v[3], 0);
+    sh = dpx_u(u2, v[4], v[5], sh);
+    sl = dpx_u(u3, v[6], v[7], sl);
+    return sh + sl;
 }
 
 // Work items 4h..4h+3 (sub-blocks 8h..8h+7) of the 210-byte super-block at
@@ -406,8 +390,8 @@ __device__ __forceinline__ float dot_q6_k_x4(uint32_t o, int h, const XInt (&X)[
     for (int t = 0; t < 4; ++t) {
         const int sc0 = (int)(int8_t)((SC[t >> 1] >> (16 * (t & 1))) & 0xffu);
         const int sc1 = (int)(int8_t)((SC[t >> 1] >> (16 * (t & 1) + 8)) & 0xffu);
-        const int v0 = q6_k_sub(L[4 * t], L[4 * t + 1], H[2 * t], X[t].h, X[t].l) - 32 * X[t].sa;
-        const int v1 = q6_k_sub(L[4 * t + 2], L[4 * t + 3], H[2 * t + 1], X[t].h + 4, X[t].l + 4) - 32 * X[t].sb;
+        const int v0 = q6_k_sub(L[4 * t], L[4 * t + 1], H[2 * t], X[t].v) - 32 * X[t].sa;
+        const int v1 = q6_k_sub(L[4 * t + 2], L[4 * t + 3], H[2 * t + 1], X[t].v + 8) - 32 * X[t].sb;
         r = fmaf(X[t].s, d * ((float)sc0 * (float)v0 + (float)sc1 * (float)v1), r);
     }
     return r;
@@ -488,8 +472,9 @@ __device__ __forceinline__ void lane_items(int lane, int sg, int SW, int J, int 
 
 // ------------------------------------------------------------------- kernel
 // Warp w of the 15 consumer warps owns K segment (w % S) and row group
-// (w / S), S in {1, 3, 5, 15}; the CTA's rows are dealt to the 15/S row
-// groups round-robin (row q of the CTA -> group q % (15/S)).  A warp keeps the x slices of its
+// (w / S), S in 1..15; the CTA's rows are dealt to the n_grp = 15/S row
+// groups round-robin (row q of the CTA -> group q % n_grp), and the
+// 15 - S*n_grp warps past the last group idle.  A warp keeps the x slices of its
 // segment in registers (J work items per lane), so per row it only reads
 // weights from shared memory.  With S == 1 a warp covers whole rows and writes
 // y itself; with S > 1 each warp leaves its row partial in a shared slot and
@@ -596,6 +581,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_m1_kernel(const GemvPara
         // first local row of this warp's group in this stage
         int rl = grp - rot;
         if (rl < 0) rl += n_grp;
+        if (grp >= n_grp) rl = nr;  // the 15 - S*n_grp warps past the last row group idle
         for (; rl < nr; rl += n_grp) {
             const uint32_t row = base + (uint32_t)(rl * p.row_bytes);
             float acc = row_partial<F, G>(row, wi, has, X);
@@ -642,8 +628,8 @@ __device__ __forceinline__ int xq_elem(float v, float amax, float inv) {
     return amax >= kXQTiny ? xq_elem_fast(v, inv) : xq_elem_tiny(v, amax);
 }
 
-// One 32-element block of x, one element per lane: writes the two int8 limbs
-// of X (xq_elem), s = amax / 32639, and {s, sum X[0:16), sum X[16:32), sum X}.
+// One 32-element block of x, one element per lane: writes X (xq_elem) as
+// int16, s = amax / 32639, and {s, sum X[0:16), sum X[16:32), sum X}.
 // Non-finite blocks get s = amax (Inf/NaN) and X = 0.
 __device__ __forceinline__ void quantize_x_block(float v, int lane, uint8_t* limbs, int4* meta) {
     const uint32_t abits = __float_as_uint(v) & 0x7fffffffu;
@@ -657,10 +643,7 @@ __device__ __forceinline__ void quantize_x_block(float v, int lane, uint8_t* lim
         X = xq_elem(v, amax, xq_inv(amax));
         s = __fdiv_rn(amax, kXQMax);
     }
-    const int xh = (X + 128) >> 8;
-    const int xl = X - (xh << 8);
-    limbs[lane] = (uint8_t)(int8_t)xh;
-    limbs[32 + lane] = (uint8_t)(int8_t)xl;
+    reinterpret_cast<int16_t*>(limbs)[lane] = (int16_t)X;
     const int sa = __reduce_add_sync(0xffffffffu, lane < 16 ? X : 0);
     const int sb = __reduce_add_sync(0xffffffffu, lane < 16 ? 0 : X);
     if (lane == 0) *meta = make_int4((int)__float_as_uint(s), sa, sb, sa + sb);

@@ -182,25 +182,31 @@ template <class F>
 bool plan_fast(const Device& d, int N, int K, uint64_t row_bytes, GemvParams& p, size_t& smem) {
     const int NW = K / F::kWIElems;
     if (NW < 32) return false;
-    // K segments: the smallest divisor S of kConsumerWarps that leaves at most
-    // 32*kMaxJ work items (x slices held in registers) per warp and lets a
-    // stage hold one row for each of the 15/S row groups within
-    // kStageMaxBytes.  A stage then holds m rows per group, so every warp has
-    // work in every stage.
-    int S = 0;
+    // K segments S (1..15): S warps share a row, n_grp = 15/S row groups work
+    // in parallel (15 - S*n_grp warps idle).  A lane holds J x slices, J =
+    // its share of the SW = NW/S work items of a segment, so a row costs
+    // about J/n_grp lane-rounds: pick the S that minimises it (ties: fewer
+    // segments, less partial-sum traffic), with J <= kMaxJ and a stage that
+    // holds one row per group within kStageMaxBytes.  Segment boundaries fall
+    // on whole lane groups.
+    const int Gp = (NW % F::kGroup == 0) ? F::kGroup : 1;
+    int S = 0, SW = 0, J = 0;
+    double best = 1e30;
     for (int cand = 1; cand <= kMaxSegments; ++cand) {
-        if (kConsumerWarps % cand) continue;
-        if ((NW + cand - 1) / cand > 32 * kMaxJ) continue;
-        if ((uint64_t)(kConsumerWarps / cand) * row_bytes > (uint64_t)kStageMaxBytes && cand < kMaxSegments) continue;
-        S = cand;
-        break;
+        const int sw = ((NW + cand - 1) / cand + Gp - 1) / Gp * Gp;
+        const int j = (sw + 32 * Gp - 1) / (32 * Gp) * Gp;
+        const int groups = kConsumerWarps / cand;
+        if (j > kMaxJ || groups == 0) continue;
+        if ((uint64_t)groups * row_bytes > (uint64_t)kStageMaxBytes && cand < kMaxSegments) continue;
+        const double cost = (double)j / groups;
+        if (cost < best - 1e-9) {
+            best = cost;
+            S = cand;
+            SW = sw;
+            J = j;
+        }
     }
     if (S == 0) return false;
-    // grouped lanes need whole groups in every segment and row
-    const int Gp = (NW % F::kGroup == 0) ? F::kGroup : 1;
-    const int SW = ((NW + S - 1) / S + Gp - 1) / Gp * Gp;
-    const int J = (SW + 32 * Gp - 1) / (32 * Gp) * Gp;
-    if (J > kMaxJ) return false;
     p.group = Gp;
     const int n_grp = kConsumerWarps / S;
     const uint64_t grp_bytes = (uint64_t)n_grp * row_bytes;
@@ -887,7 +893,7 @@ int32_t stack_run(void* handle, const float* x_in, cudaStream_t st) {
 }
 
 // ------------------------------------------------ no-allocation entry point
-// Scratch of nexus_gpu_gemv_noalloc: the quantized activations (limbs and
+// Scratch of nexus_gpu_gemv_noalloc: the quantized activations (int16 X and
 // block metadata) that xquant_kernel writes and the GEMV kernel reads.  It is
 // part of the loaded module, so every GPU that loads the library holds these
 // kNoAllocScratchBytes until the process exits, and no call ever allocates.

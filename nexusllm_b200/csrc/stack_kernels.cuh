@@ -155,8 +155,8 @@ __device__ __forceinline__ bool consumer_bar_any(bool v) {
     return r != 0;
 }
 
-// Shared staging layout of a task's quantized x.  The 64 limb bytes of block b
-// are four 16-byte chunks (Xh 0-15, Xh 16-31, Xl 0-15, Xl 16-31); chunk q of
+// Shared staging layout of a task's quantized x.  The 64 bytes of block b's
+// int16 X are four 16-byte chunks (elements 8q .. 8q+7 in chunk q); chunk q of
 // every block sits in plane q, planes of nxbp = K/32 rounded up to 8 chunks:
 // chunk (q, b) at 16 * (q * nxbp + xsw(b)), then the metadata plane, block b at
 // 16 * (4 * nxbp + xsw(b)).  Lanes read blocks G apart (G = 1, 2, 4); the swizzle
@@ -167,7 +167,7 @@ __host__ __device__ constexpr int x_stage_planes_len(int K) { return (K / 32 + 7
 
 // quantize_x_block with two lanes per block: lane half hf (0 or 1) of the
 // pair holds elements 16*hf .. 16*hf+15 in e.  Same element rule and sums as
-// quantize_x_block, so the limbs and metadata are the same bits.  Stores
+// quantize_x_block, so X and the metadata are the same bits.  Stores
 // block b into the staging layout at xs when `store`; every lane must call it.
 __device__ __forceinline__ void quantize_x_pair(const float (&e)[16], int hf, bool store, uint32_t xs, int nxbp,
                                                 int b) {
@@ -180,31 +180,23 @@ __device__ __forceinline__ void quantize_x_pair(const float (&e)[16], int hf, bo
     const bool fast = amax >= kXQTiny;
     const float s = mbits >= 0x7f800000u ? amax : (nz ? __fdiv_rn(amax, kXQMax) : 0.0f);
     const float inv = nz && fast ? xq_inv(amax) : 0.0f;
-    uint32_t h[4], l[4];
+    uint32_t v[8];  // int16 pairs of elements 16hf .. 16hf+15
     int sum = 0;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
-        h[w] = 0;
-        l[w] = 0;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float v = e[4 * w + k];
-            const int x = !nz ? 0 : (fast ? xq_elem_fast(v, inv) : xq_elem_tiny(v, amax));
-            const int xh = (x + 128) >> 8;
-            const int xl = x - (xh << 8);
-            h[w] |= ((uint32_t)xh & 0xffu) << (8 * k);
-            l[w] |= ((uint32_t)xl & 0xffu) << (8 * k);
-            sum += x;
-        }
+    for (int w = 0; w < 8; ++w) {
+        const int x0 = !nz ? 0 : (fast ? xq_elem_fast(e[2 * w], inv) : xq_elem_tiny(e[2 * w], amax));
+        const int x1 = !nz ? 0 : (fast ? xq_elem_fast(e[2 * w + 1], inv) : xq_elem_tiny(e[2 * w + 1], amax));
+        v[w] = ((uint32_t)x0 & 0xffffu) | ((uint32_t)x1 << 16);
+        sum += x0 + x1;
     }
     const int other = __shfl_xor_sync(0xffffffffu, sum, 1);
     if (store) {
         const uint32_t col = 16 * xsw(b), plane = 16u * (uint32_t)nxbp;
-        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(xs + (uint32_t)hf * plane + col), "r"(h[0]),
-                     "r"(h[1]), "r"(h[2]), "r"(h[3])
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(xs + (uint32_t)(2 * hf) * plane + col), "r"(v[0]),
+                     "r"(v[1]), "r"(v[2]), "r"(v[3])
                      : "memory");
-        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(xs + (uint32_t)(2 + hf) * plane + col), "r"(l[0]),
-                     "r"(l[1]), "r"(l[2]), "r"(l[3])
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(xs + (uint32_t)(2 * hf + 1) * plane + col),
+                     "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
                      : "memory");
         if (hf == 0)
             asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(xs + 4 * plane + col), "r"(__float_as_uint(s)),
@@ -217,11 +209,9 @@ __device__ __forceinline__ void quantize_x_pair(const float (&e)[16], int hf, bo
 __device__ __forceinline__ void load_xint_smem(uint32_t xs, int nxbp, int gj, XInt& X) {
     const uint32_t col = 16 * xsw(gj), plane = 16u * (uint32_t)nxbp;
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
+    for (int q = 0; q < 4; ++q) {
         const uint4 v = lds128(xs + (uint32_t)q * plane + col);
-        X.h[4 * q + 0] = v.x; X.h[4 * q + 1] = v.y; X.h[4 * q + 2] = v.z; X.h[4 * q + 3] = v.w;
-        const uint4 u = lds128(xs + (uint32_t)(2 + q) * plane + col);
-        X.l[4 * q + 0] = u.x; X.l[4 * q + 1] = u.y; X.l[4 * q + 2] = u.z; X.l[4 * q + 3] = u.w;
+        X.v[4 * q + 0] = v.x; X.v[4 * q + 1] = v.y; X.v[4 * q + 2] = v.z; X.v[4 * q + 3] = v.w;
     }
     const uint4 m = lds128(xs + 4 * plane + col);
     X.s = __uint_as_float(m.x);
@@ -497,6 +487,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                         stage0 + (uint32_t)(s * P.stage_slot) + (uint32_t)(((uint64_t)r0 * rbytes) & 15);
                     int rl = grp - rot;
                     if (rl < 0) rl += n_grp;
+                    if (grp >= n_grp) rl = nr;  // the 15 - S*n_grp warps past the last row group idle
                     for (; rl < nr; rl += n_grp) {
                         const uint32_t row = base + (uint32_t)(rl * rbytes);
                         float acc = row_partial<F, G>(row, wi, has, X);

@@ -4,13 +4,14 @@ and of the host plan that sizes it (plan_fast in nexusllm_b200/csrc/nexus_gpu.cu
 Restates, in Python, how the kernel splits rows over CTAs and stages, which
 byte range the producer bulk-copies (and tail-copies) into each shared-memory
 stage buffer, which shared bytes the consumer decoders read, and which x
-slices and y rows each thread touches.  For every configuration shape and a
+slices and y rows each thread touches (including the plan's choice of K
+segments, which may leave warps past the last row group idle).  For every configuration shape and a
 set of ragged ones it asserts that every global read stays inside the weight
 matrix and x, every bulk copy is 16-byte aligned with a size that is a
 multiple of 16, every shared write and read stays inside its stage buffer and
 the allocation, the decoders read only bytes the copies delivered, every row
-slot and y index is in range, and every row gets exactly the warps of its
-phase.  Constants are parsed from the kernel header so the check follows the
+slot and y index is in range, and every row gets exactly the warps of
+its row group.  Constants are parsed from the kernel header so the check follows the
 kernel when they change.
 """
 import os
@@ -47,15 +48,20 @@ def plan(name, K, rb):
     if NW < 32:
         return None
     W = C["kConsumerWarps"]
-    S = next((c for c in range(1, C["kMaxSegments"] + 1)
-              if W % c == 0 and -(-NW // c) <= 32 * C["kMaxJ"]
-              and ((W // c) * rb <= C["kStageMaxBytes"] or c == C["kMaxSegments"])), 0)
-    if S == 0:
-        return None
     Gp = f["kGroup"] if NW % f["kGroup"] == 0 else 1
-    SW = -(-(-(-NW // S)) // Gp) * Gp
-    J = -(-SW // (32 * Gp)) * Gp
-    if J > C["kMaxJ"]:
+    S, best = 0, None
+    for c in range(1, C["kMaxSegments"] + 1):
+        sw = -(-(-(-NW // c)) // Gp) * Gp
+        j = -(-sw // (32 * Gp)) * Gp
+        groups = W // c
+        if j > C["kMaxJ"] or groups == 0:
+            continue
+        if groups * rb > C["kStageMaxBytes"] and c < C["kMaxSegments"]:
+            continue
+        cost = j / groups
+        if best is None or cost < best - 1e-9:
+            best, S, SW, J = cost, c, sw, j
+    if S == 0:
         return None
     n_grp = W // S
     m = max(1, min(4, C["kStageTargetBytes"] // (n_grp * rb)))
@@ -132,7 +138,7 @@ def simulate(name, N, K, ctas=None):
     assert pl["smem"] <= SMEM_OPTIN
     NW, S, SW, J, Gp, R, sb, ns = pl["NW"], pl["S"], pl["SW"], pl["J"], pl["G"], pl["R"], pl["sb"], pl["ns"]
     n_grp = W15 // S
-    assert n_grp * S == W15
+    assert 1 <= n_grp and n_grp * S <= W15  # warps past the last row group idle
     total = N * rb
     floor16 = total & ~15
     G = min(SMS, N)
