@@ -17,6 +17,7 @@
 #include "../../include/nexus_gpu.h"
 #include "gemv_kernels.cuh"
 #include "stack_kernels.cuh"
+#include "mma_kernels.cuh"
 
 namespace nexus_gpu {
 
@@ -83,6 +84,38 @@ size_t xq_bytes(uint32_t dtype, size_t M, size_t cols) {
     if (!is_int_format(dtype)) return 0;
     const size_t nxb = cols / 32;
     return align256(M * nxb * kXQLimbBytes) + align256(M * nxb * kXQMetaBytes);
+}
+
+// ---------------------------------------------------- batched (tensor cores)
+// Batched decode runs on the tcgen05 tensor cores for GGUF Q4_0 with
+// M >= kTcMinTokens activation rows and K a multiple of 256 (rows of whole
+// 144-byte chunks for the 2-D tensor copies), in groups of <= 64 tokens.
+constexpr size_t kTcMinTokens = 16;
+
+bool tc_eligible(uint32_t dtype, size_t M, size_t cols) {
+    return dtype == NEXUS_GPU_GGUF_Q4_0 && M >= kTcMinTokens && cols % kRawK == 0 && cols <= (size_t)INT32_MAX;
+}
+
+struct TcPlan {
+    int tiles, splits, chunks_per_split, n_chunks;
+};
+TcPlan tc_plan(int sms, size_t rows, size_t cols) {
+    TcPlan p;
+    p.n_chunks = (int)(cols / kRawK);
+    p.tiles = (int)((rows + kMmaRows - 1) / kMmaRows);
+    int s = std::max(1, std::min(p.n_chunks, sms / std::max(1, p.tiles)));
+    p.chunks_per_split = (p.n_chunks + s - 1) / s;
+    p.splits = (p.n_chunks + p.chunks_per_split - 1) / p.chunks_per_split;
+    return p;
+}
+// Workspace of one token group (<= kMaxTokens): the B operand (hi and lo fp16
+// rows), the per-token scales, and the split-K partial sums.
+size_t tc_group_bytes(int sms, size_t rows, size_t cols) {
+    const TcPlan pl = tc_plan(sms, rows, cols);
+    const size_t MP = kMaxTokens;
+    size_t b = align256(2 * MP * cols * sizeof(__half)) + align256(MP * sizeof(float));
+    if (pl.splits > 1) b += align256((size_t)pl.splits * kMaxTokens * rows * sizeof(float));
+    return b;
 }
 
 // --------------------------------------------------------------- contexts
@@ -247,9 +280,19 @@ bool plan_for(uint32_t dtype, const Device& d, int N, int K, uint64_t rb, GemvPa
     }
 }
 
-// One GEMV of M rows of x.  `ws` holds at least xq_bytes(dtype, M, cols).
+int32_t run_gemm_tc(Device& d, const void* dW, const void* dX, int xbf, float* dY, size_t M, size_t rows, size_t cols,
+                    uint8_t* ws, cudaStream_t st);
+
+// Workspace bytes of one GEMV call (gemv_ws_bytes with the tensor path allowed).
+size_t gemv_ws_bytes(int sms, uint32_t dtype, size_t M, size_t rows, size_t cols, bool allow_tc) {
+    if (allow_tc && tc_eligible(dtype, M, cols)) return tc_group_bytes(sms, rows, cols);
+    return xq_bytes(dtype, M, cols);
+}
+
+// One GEMV of M rows of x.  `ws` holds at least gemv_ws_bytes(d.sms, ...,
+// allow_tc).  Batched Q4_0 (M >= 16) goes to the tensor cores when allowed.
 int32_t run_gemv(Device& d, const void* dW, uint32_t dtype, const void* dX, uint32_t x_dtype, float* dY, size_t M,
-                 size_t rows, size_t cols, uint8_t* ws, cudaStream_t st) {
+                 size_t rows, size_t cols, uint8_t* ws, cudaStream_t st, bool allow_tc = true) {
     FormatInfo f;
     int32_t rc = check_shape(dtype, rows, cols, f);
     if (rc) return rc;
@@ -263,6 +306,7 @@ int32_t run_gemv(Device& d, const void* dW, uint32_t dtype, const void* dX, uint
     const size_t rb = row_bytes_of(f, cols);
     const bool w16 = ((uintptr_t)dW & 15) == 0;
     const int xbf = x_dtype == NEXUS_GPU_BF16;
+    if (allow_tc && w16 && tc_eligible(dtype, M, cols)) return run_gemm_tc(d, dW, dX, xbf, dY, M, rows, cols, ws, st);
     const size_t xes = xbf ? 2 : 4;
     const size_t nxb = cols / 32;
     uint8_t* limbs = ws;
@@ -304,6 +348,104 @@ int32_t run_gemv(Device& d, const void* dW, uint32_t dtype, const void* dX, uint
             default: rc = launch_fast<FmtF16>(d, p, smem, st); break;
         }
         if (rc) return rc;
+    }
+    return NEXUS_GPU_SUCCESS;
+}
+
+// ------------------------------------------------------------ tensor path
+using TensorMapEncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                          const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                          CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                          CUtensorMapFloatOOBfill);
+
+TensorMapEncodeTiled tensor_map_encoder() {
+    static std::once_flag once;
+    static TensorMapEncodeTiled fn = nullptr;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<TensorMapEncodeTiled>(p);
+        cudaGetLastError();
+    });
+    return fn;
+}
+
+int32_t mma_attrs(Device& d) {
+    static std::mutex mu;
+    static std::vector<int> done;
+    std::lock_guard<std::mutex> lk(mu);
+    if (std::find(done.begin(), done.end(), d.id) != done.end()) return NEXUS_GPU_SUCCESS;
+    if (d.smem_optin < kMmaSmemBytes)
+        return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "batched path needs %d bytes of shared memory", kMmaSmemBytes);
+    CUDA_TRY(cudaFuncSetAttribute(gemm_q4_0_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaSmemBytes));
+    done.push_back(d.id);
+    return NEXUS_GPU_SUCCESS;
+}
+
+// Batched Q4_0: token groups of <= 64, each one launch of x preparation, the
+// tensor-core GEMM and (split K) the partial-sum reduction.
+int32_t run_gemm_tc(Device& d, const void* dW, const void* dX, int xbf, float* dY, size_t M, size_t rows, size_t cols,
+                    uint8_t* ws, cudaStream_t st) {
+    int32_t rc = mma_attrs(d);
+    if (rc) return rc;
+    TensorMapEncodeTiled encode = tensor_map_encoder();
+    if (!encode) return fail(NEXUS_GPU_ERROR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const TcPlan pl = tc_plan(d.sms, rows, cols);
+    const size_t rb = cols / 32 * 18;
+    const size_t xes = xbf ? 2 : 4;
+    for (size_t g0 = 0; g0 < M; g0 += kMaxTokens) {
+        const int Mg = (int)std::min<size_t>(kMaxTokens, M - g0);
+        const int MP = (Mg + 7) / 8 * 8, NB = 2 * MP;
+        __half* xp = reinterpret_cast<__half*>(ws);
+        float* xscale = reinterpret_cast<float*>(ws + align256(2 * (size_t)kMaxTokens * cols * sizeof(__half)));
+        float* partial = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xscale) + align256(kMaxTokens * sizeof(float)));
+        CUtensorMap tmW, tmX;
+        {
+            const cuuint64_t dims[2] = {(cuuint64_t)rb, (cuuint64_t)rows};
+            const cuuint64_t strides[1] = {(cuuint64_t)rb};
+            const cuuint32_t box[2] = {(cuuint32_t)kRawRowBytes, (cuuint32_t)kMmaRows};
+            const cuuint32_t estr[2] = {1, 1};
+            if (encode(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(dW), dims, strides, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+                return fail(NEXUS_GPU_ERROR_CUDA, "weight tensor map rejected (%zu x %zu bytes)", rows, rb);
+        }
+        {
+            const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)NB};
+            const cuuint64_t strides[1] = {(cuuint64_t)cols * sizeof(__half)};
+            const cuuint32_t box[2] = {(cuuint32_t)kUnitK, (cuuint32_t)NB};
+            const cuuint32_t estr[2] = {1, 1};
+            if (encode(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xp, dims, strides, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+                return fail(NEXUS_GPU_ERROR_CUDA, "activation tensor map rejected (%d x %zu)", NB, cols);
+        }
+        const uint8_t* xg = static_cast<const uint8_t*>(dX) + g0 * cols * xes;
+        float* yg = dY + g0 * rows;
+        if ((rc = launch(mma_xprep_kernel, dim3(MP), dim3(256), 0, st, (const void*)xg, xbf, Mg, MP, (int)cols, xp,
+                         xscale)))
+            return rc;
+        MmaParams P;
+        P.N = (int)rows;
+        P.K = (int)cols;
+        P.M = Mg;
+        P.MP = MP;
+        P.chunks_per_split = pl.chunks_per_split;
+        P.n_chunks = pl.n_chunks;
+        P.splits = pl.splits;
+        P.out = pl.splits > 1 ? partial : yg;
+        P.xscale = xscale;
+        if ((rc = launch(gemm_q4_0_mma_kernel, dim3((unsigned)(pl.tiles * pl.splits)), dim3(kMmaThreads), kMmaSmemBytes,
+                         st, tmW, tmX, P)))
+            return rc;
+        if (pl.splits > 1) {
+            const size_t count = (size_t)Mg * rows;
+            if ((rc = launch(mma_splitk_reduce_kernel, dim3((unsigned)((count + 255) / 256)), dim3(256), 0, st,
+                             (const float*)partial, yg, pl.splits, count)))
+                return rc;
+        }
     }
     return NEXUS_GPU_SUCCESS;
 }
@@ -1040,9 +1182,19 @@ NEXUS_GPU_API size_t nexus_gpu_weight_bytes(uint32_t dtype, size_t rows, size_t 
     return rows * row_bytes_of(f, cols);
 }
 
+// SM count of the current device (148, a B200's, when there is none: sizes
+// then cover a B200).
+int current_sms() {
+    int id = 0, sms = 0;
+    if (cudaGetDevice(&id) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, id) != cudaSuccess) {
+        cudaGetLastError();
+        return 148;
+    }
+    return sms;
+}
+
 NEXUS_GPU_API size_t nexus_gpu_gemv_workspace_size(uint32_t dtype, size_t M, size_t rows, size_t cols) {
-    (void)rows;
-    return xq_bytes(dtype, M, cols);
+    return gemv_ws_bytes(current_sms(), dtype, M, rows, cols, true);
 }
 
 NEXUS_GPU_API int32_t nexus_gpu_gemv_ws(const void* dW, uint32_t dtype, const void* dX, uint32_t x_dtype, float* dY,
@@ -1052,7 +1204,7 @@ NEXUS_GPU_API int32_t nexus_gpu_gemv_ws(const void* dW, uint32_t dtype, const vo
     Device* d = nullptr;
     int32_t rc = get_device(&d);
     if (rc) return rc;
-    const size_t need = xq_bytes(dtype, M, cols);
+    const size_t need = gemv_ws_bytes(d->sms, dtype, M, rows, cols, true);
     if (workspace_bytes < need || (need && !workspace))
         return fail(NEXUS_GPU_ERROR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
     if (need && ((uintptr_t)workspace & 255))
@@ -1071,7 +1223,7 @@ NEXUS_GPU_API int32_t nexus_gpu_gemv(const void* dW, uint32_t dtype, const void*
     if ((rc = check_shape(dtype, rows, cols, f))) return rc;
     uint8_t* ws = nullptr;
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if ((rc = get_workspace(*d, st, xq_bytes(dtype, M, cols), &ws))) return rc;
+    if ((rc = get_workspace(*d, st, gemv_ws_bytes(d->sms, dtype, M, rows, cols, true), &ws))) return rc;
     return run_gemv(*d, dW, dtype, dX, x_dtype, dY, M, rows, cols, ws, st);
 }
 
@@ -1090,7 +1242,8 @@ NEXUS_GPU_API int32_t nexus_gpu_gemv_noalloc(const void* dW, uint32_t dtype, con
     Device* d = nullptr;
     uint8_t* scratch = nullptr;
     if ((rc = noalloc_device(&d, &scratch))) return rc;
-    return run_gemv(*d, dW, dtype, dX, x_dtype, dY, M, rows, cols, scratch, static_cast<cudaStream_t>(stream));
+    // the fixed scratch serves the CUDA-core path only (no tensor-core workspace)
+    return run_gemv(*d, dW, dtype, dX, x_dtype, dY, M, rows, cols, scratch, static_cast<cudaStream_t>(stream), false);
 }
 
 NEXUS_GPU_API int32_t nexus_gpu_stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n_tasks,
