@@ -261,6 +261,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-batched", action="store_true",
+                    help="skip the batched-decode points (M = 4, 16, 64 tokens per step)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="decoder layers in the stack (32 = the configuration; fewer only for profiling runs)")
     args = ap.parse_args()
@@ -402,6 +404,8 @@ def main():
         launches = args.steps
         launches_note = f"1 gemv_stack_kernel per step x {args.steps} steps (plus one counter memset per step)"
         extra = {"per_gemv_graph": per_gemv, "e2e_per_gemv_dispatch": e2e_dispatch}
+        if not args.no_batched:
+            extra["batched_decode"] = batched_decode(torch, L, layers, head, stream, dev, timed, args, peak)
         del stack_graph
         L.nexus_gpu_stack_destroy(stack)
     else:
@@ -481,6 +485,57 @@ def check_status(L):
     L.nexus_gpu_device_status(ctypes.byref(bits))
     if bits.value:
         raise RuntimeError(f"device status word {bits.value:#x} (a bounded wait expired)")
+
+
+def batched_decode(torch, L, layers, head, stream, dev, timed, args, peak):
+    """configs[3] at M = 4, 16, 64 tokens per step (N=1): the step's 225
+    GEMVs with M activation rows each, one nexus_gpu_gemv_ws call per GEMV,
+    captured in a CUDA graph.  M >= 16 runs on the tcgen05 tensor cores; M = 4
+    runs the batch-1 CUDA-core kernel once per token.  Same weights as the
+    headline; a step reads every weight once per call."""
+    out = []
+    ws_need = 0
+    for M in (4, 16, 64):
+        ws_need = max([ws_need] + [L.nexus_gpu_gemv_workspace_size(DTYPE, M, n, k) for _, n, k in LAYER_SHAPES]
+                      + [L.nexus_gpu_gemv_workspace_size(DTYPE, M, VOCAB, HIDDEN)])
+    ws = torch.empty(ws_need + 256, dtype=torch.uint8, device=dev)
+    for M in (4, 16, 64):
+        xs = {k: torch.randn(M, k, generator=torch.Generator(device=dev).manual_seed(11 + k), device=dev)
+              for k in (HIDDEN, FFN)}
+        ys = {n: torch.empty(M, n, dtype=torch.float32, device=dev) for n in (HIDDEN, KV, FFN, VOCAB)}
+
+        def step():
+            st = torch.cuda.current_stream(dev).cuda_stream
+            for mats in layers:
+                for name, n, k in LAYER_SHAPES:
+                    rc = L.nexus_gpu_gemv_ws(mats[name].data_ptr(), DTYPE, xs[k].data_ptr(), 0, ys[n].data_ptr(), M, n,
+                                             k, ws.data_ptr(), ws.numel(), st)
+                    if rc:
+                        raise RuntimeError(L.nexus_gpu_last_error())
+            rc = L.nexus_gpu_gemv_ws(head.data_ptr(), DTYPE, xs[HIDDEN].data_ptr(), 0, ys[VOCAB].data_ptr(), M, VOCAB,
+                                     HIDDEN, ws.data_ptr(), ws.numel(), st)
+            if rc:
+                raise RuntimeError(L.nexus_gpu_last_error())
+
+        with torch.cuda.stream(stream):
+            step()
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step()
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                g.replay()
+        reps = max(5, min(50, args.steps // 20))
+        ms = timed(g.replay, reps) / reps
+        sb = step_bytes(layers=len(layers))
+        gbs = sb / (ms * 1e-3) / 1e9
+        out.append({"M": M, "ms_per_step": round(ms, 4), "tokens_per_s": round(M * 1e3 / ms, 1),
+                    "value": round(gbs, 1), "unit": "GB/s", "pct_of_measured_hbm": round(100 * gbs / peak, 2),
+                    "path": "tcgen05 kind::f16 (gemm_q4_0_mma_kernel)" if M >= 16 else
+                            "batch-1 CUDA-core kernel per token", "steps": reps})
+        del g
+    return out
 
 
 def build_stack_graph(torch, L, _native, layers, head, h0, stream, dev):
