@@ -97,26 +97,35 @@ bool tc_eligible(uint32_t dtype, size_t M, size_t cols) {
 }
 
 struct TcPlan {
-    int tiles, splits, chunks_per_split, n_chunks;
+    int tiles, n_chunks, G;
+    long long total;
 };
+// One persistent CTA per SM over the tiles x chunks sequence (stream-K), at
+// least two chunks a CTA.
 TcPlan tc_plan(int sms, size_t rows, size_t cols) {
     TcPlan p;
     p.n_chunks = (int)(cols / kRawK);
     p.tiles = (int)((rows + kMmaRows - 1) / kMmaRows);
-    int s = std::max(1, std::min(p.n_chunks, sms / std::max(1, p.tiles)));
-    p.chunks_per_split = (p.n_chunks + s - 1) / s;
-    p.splits = (p.n_chunks + p.chunks_per_split - 1) / p.chunks_per_split;
+    p.total = (long long)p.tiles * p.n_chunks;
+    p.G = (int)std::max<long long>(1, std::min<long long>(sms, p.total / 2));
     return p;
 }
-// Workspace of one token group (<= kMaxTokens): the B operand (hi and lo fp16
-// rows), the per-token scales, and the split-K partial sums.
-size_t tc_group_bytes(int sms, size_t rows, size_t cols) {
+// Workspace of one token group (<= kMaxTokens): the B operand (fp16 rows),
+// the per-token scales, the per-tile arrival counters and the partial sums of
+// shared tiles (two slots a CTA).
+struct TcLayout {
+    size_t xscale, arrivals, partial, total;
+};
+TcLayout tc_layout(int sms, size_t rows, size_t cols) {
     const TcPlan pl = tc_plan(sms, rows, cols);
-    const size_t MP = kMaxTokens;
-    size_t b = align256(2 * MP * cols * sizeof(__half)) + align256(MP * sizeof(float));
-    if (pl.splits > 1) b += align256((size_t)pl.splits * kMaxTokens * rows * sizeof(float));
-    return b;
+    TcLayout l;
+    l.xscale = align256((size_t)kMaxTokens * cols * sizeof(__half));
+    l.arrivals = l.xscale + align256(kMaxTokens * sizeof(float));
+    l.partial = l.arrivals + align256((size_t)pl.tiles * sizeof(unsigned));
+    l.total = l.partial + align256((size_t)2 * pl.G * kMaxTokens * kMmaRows * sizeof(float));
+    return l;
 }
+size_t tc_group_bytes(int sms, size_t rows, size_t cols) { return tc_layout(sms, rows, cols).total; }
 
 // --------------------------------------------------------------- contexts
 struct CachedWeight {
@@ -380,12 +389,16 @@ int32_t mma_attrs(Device& d) {
     if (d.smem_optin < kMmaSmemBytes)
         return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "batched path needs %d bytes of shared memory", kMmaSmemBytes);
     CUDA_TRY(cudaFuncSetAttribute(gemm_q4_0_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaSmemBytes));
+    // both kernels of a batched GEMV on the same shared-memory carveout: no
+    // reconfiguration of the SMs between the x preparation and the GEMM
+    CUDA_TRY(cudaFuncSetAttribute(gemm_q4_0_mma_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    CUDA_TRY(cudaFuncSetAttribute(mma_xprep_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
     done.push_back(d.id);
     return NEXUS_GPU_SUCCESS;
 }
 
-// Batched Q4_0: token groups of <= 64, each one launch of x preparation, the
-// tensor-core GEMM and (split K) the partial-sum reduction.
+// Batched Q4_0: token groups of <= 64, each one launch of x preparation and
+// one of the persistent tensor-core GEMM.
 int32_t run_gemm_tc(Device& d, const void* dW, const void* dX, int xbf, float* dY, size_t M, size_t rows, size_t cols,
                     uint8_t* ws, cudaStream_t st) {
     int32_t rc = mma_attrs(d);
@@ -393,14 +406,16 @@ int32_t run_gemm_tc(Device& d, const void* dW, const void* dX, int xbf, float* d
     TensorMapEncodeTiled encode = tensor_map_encoder();
     if (!encode) return fail(NEXUS_GPU_ERROR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
     const TcPlan pl = tc_plan(d.sms, rows, cols);
+    const TcLayout lay = tc_layout(d.sms, rows, cols);
     const size_t rb = cols / 32 * 18;
     const size_t xes = xbf ? 2 : 4;
+    __half* xp = reinterpret_cast<__half*>(ws);
+    float* xscale = reinterpret_cast<float*>(ws + lay.xscale);
+    unsigned* arrivals = reinterpret_cast<unsigned*>(ws + lay.arrivals);
+    float* partial = reinterpret_cast<float*>(ws + lay.partial);
     for (size_t g0 = 0; g0 < M; g0 += kMaxTokens) {
         const int Mg = (int)std::min<size_t>(kMaxTokens, M - g0);
-        const int MP = (Mg + 7) / 8 * 8, NB = 2 * MP;
-        __half* xp = reinterpret_cast<__half*>(ws);
-        float* xscale = reinterpret_cast<float*>(ws + align256(2 * (size_t)kMaxTokens * cols * sizeof(__half)));
-        float* partial = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xscale) + align256(kMaxTokens * sizeof(float)));
+        const int NB = (Mg + 15) / 16 * 16;
         CUtensorMap tmW, tmX;
         {
             const cuuint64_t dims[2] = {(cuuint64_t)rb, (cuuint64_t)rows};
@@ -423,29 +438,27 @@ int32_t run_gemm_tc(Device& d, const void* dW, const void* dX, int xbf, float* d
                 return fail(NEXUS_GPU_ERROR_CUDA, "activation tensor map rejected (%d x %zu)", NB, cols);
         }
         const uint8_t* xg = static_cast<const uint8_t*>(dX) + g0 * cols * xes;
-        float* yg = dY + g0 * rows;
-        if ((rc = launch(mma_xprep_kernel, dim3(MP), dim3(256), 0, st, (const void*)xg, xbf, Mg, MP, (int)cols, xp,
-                         xscale)))
+        const int vec = ((uintptr_t)xg % (xbf ? 8 : 16)) == 0;  // rows start every cols * xes bytes: 1 KB multiples
+        if ((rc = launch(mma_xprep_kernel, dim3(NB), dim3(256), 0, st, (const void*)xg, xbf, vec, Mg, NB, (int)cols,
+                         xp, xscale, arrivals, pl.tiles)))
             return rc;
         MmaParams P;
         P.N = (int)rows;
         P.K = (int)cols;
         P.M = Mg;
-        P.MP = MP;
-        P.chunks_per_split = pl.chunks_per_split;
+        P.NB = NB;
+        P.tiles = pl.tiles;
         P.n_chunks = pl.n_chunks;
-        P.splits = pl.splits;
-        P.out = pl.splits > 1 ? partial : yg;
+        P.total = pl.total;
+        P.G = pl.G;
+        P.b_stages = std::min(kMaxBStages, kBRingBytes / (NB * 512));
+        P.y = dY + g0 * rows;
+        P.partial = partial;
+        P.arrivals = arrivals;
         P.xscale = xscale;
-        if ((rc = launch(gemm_q4_0_mma_kernel, dim3((unsigned)(pl.tiles * pl.splits)), dim3(kMmaThreads), kMmaSmemBytes,
-                         st, tmW, tmX, P)))
+        if ((rc = launch(gemm_q4_0_mma_kernel, dim3((unsigned)pl.G), dim3(kMmaThreads), kMmaSmemBytes, st, tmW, tmX,
+                         P)))
             return rc;
-        if (pl.splits > 1) {
-            const size_t count = (size_t)Mg * rows;
-            if ((rc = launch(mma_splitk_reduce_kernel, dim3((unsigned)((count + 255) / 256)), dim3(256), 0, st,
-                             (const float*)partial, yg, pl.splits, count)))
-                return rc;
-        }
     }
     return NEXUS_GPU_SUCCESS;
 }
