@@ -261,6 +261,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-formats", action="store_true",
+                    help="skip the INT4-AWQ / FP8-E4M3 per-shape GEMV timings")
     ap.add_argument("--no-batched", action="store_true",
                     help="skip the batched-decode points (M = 4, 16, 64 tokens per step)")
     ap.add_argument("--layers", type=int, default=LAYERS,
@@ -406,6 +408,8 @@ def main():
         extra = {"per_gemv_graph": per_gemv, "e2e_per_gemv_dispatch": e2e_dispatch}
         if not args.no_batched:
             extra["batched_decode"] = batched_decode(torch, L, layers, head, stream, dev, timed, args, peak)
+        if not args.no_formats:
+            extra["int4_awq_fp8"] = other_formats(torch, L, stream, dev, timed, peak)
         del stack_graph
         L.nexus_gpu_stack_destroy(stack)
     else:
@@ -535,6 +539,71 @@ def batched_decode(torch, L, layers, head, stream, dev, timed, args, peak):
                     "path": "tcgen05 kind::f16 (gemm_q4_0_mma_kernel)" if M >= 16 else
                             "batch-1 CUDA-core kernel per token", "steps": reps})
         del g
+    return out
+
+
+def other_formats(torch, L, stream, dev, timed, peak):
+    """INT4-AWQ (group 128, zeros) and FP8-E4M3 batch-1 GEMVs on the
+    Llama-3-8B shapes, through nexus_gpu_gemv_int4 / nexus_gpu_gemv_fp8 (the
+    reference's fused_gemv_int4 / fused_gemv_fp8).  Each shape cycles over
+    enough weight copies for >= 512 MB per graph pass (weights come from HBM);
+    GB/s counts weights, scales, zeros, x and y once per call."""
+    shapes = [(HIDDEN, HIDDEN), (FFN, HIDDEN), (HIDDEN, FFN), (VOCAB, HIDDEN)]
+    gs = 128
+    out = []
+    for fmt in ("int4_awq", "fp8_e4m3"):
+        for rows, cols in shapes:
+            if fmt == "int4_awq":
+                wbytes = rows * cols // 2
+                sbytes = 2 * rows * (cols // gs) * 4
+            else:
+                wbytes, sbytes = rows * cols, 0
+            alg = wbytes + sbytes + cols * 4 + rows * 4
+            n = max(1, -(-(512 << 20) // (wbytes + sbytes)))
+            gen = torch.Generator(device=dev).manual_seed(rows + cols)
+            if fmt == "int4_awq":
+                W = [torch.randint(-2**31, 2**31 - 1, (rows * cols // 8,), dtype=torch.int32, device=dev,
+                                   generator=gen) for _ in range(n)]
+                S = [torch.rand(rows * cols // gs, device=dev, generator=gen) * 0.02 for _ in range(n)]
+                Z = [torch.randint(0, 16, (rows * cols // gs,), device=dev, generator=gen).float() for _ in range(n)]
+            else:  # realistic E4M3 codes (no NaN encodings)
+                W = [(torch.randn(rows * cols, device=dev, generator=gen) * 0.5).to(torch.float8_e4m3fn).view(
+                    torch.uint8) for _ in range(n)]
+            x = torch.randn(cols, device=dev, generator=gen)
+            y = torch.empty(rows, device=dev)
+            calls = 2 * n
+
+            def run():
+                st = torch.cuda.current_stream(dev).cuda_stream
+                for i in range(calls):
+                    j = i % n
+                    if fmt == "int4_awq":
+                        rc = L.nexus_gpu_gemv_int4(W[j].data_ptr(), S[j].data_ptr(), Z[j].data_ptr(), x.data_ptr(),
+                                                   y.data_ptr(), rows, cols, gs, None, 0, st)
+                    else:
+                        rc = L.nexus_gpu_gemv_fp8(W[j].data_ptr(), x.data_ptr(), y.data_ptr(), rows, cols, 0.0625, st)
+                    if rc:
+                        raise RuntimeError(L.nexus_gpu_last_error())
+
+            with torch.cuda.stream(stream):
+                run()
+            torch.cuda.synchronize(dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                run()
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    g.replay()
+            reps = 5
+            ms = timed(g.replay, reps) / (reps * calls)
+            gbs = alg / (ms * 1e-3) / 1e9
+            out.append({"format": fmt, "rows": rows, "cols": cols, "group_size": gs if fmt == "int4_awq" else None,
+                        "us_per_call": round(ms * 1e3, 2), "value": round(gbs, 1), "unit": "GB/s",
+                        "pct_of_measured_hbm": round(100 * gbs / peak, 1), "bytes_per_call": alg,
+                        "weight_copies": n})
+            del g, W
+            if fmt == "int4_awq":
+                del S, Z
     return out
 
 

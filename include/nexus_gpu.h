@@ -94,6 +94,25 @@ NEXUS_GPU_API void nexus_dequantize_gguf_q4_0(const void* blocks, float* output,
 NEXUS_GPU_API void nexus_dequantize_gguf_q5_k(const void* blocks, float* output, size_t num_blocks);
 NEXUS_GPU_API void nexus_dequantize_gguf_q6_k(const void* blocks, float* output, size_t num_blocks);
 
+/* QuantizationKernel::fused_gemv_int4 (include/quantization.hpp:99-106; ABI
+ * nexus_fused_gemv_int4, include/nexus_abi.h:136-143): INT4-AWQ, W_packed is
+ * rows x cols/8 uint32 (column c = nibble c % 8 of word c / 8), scales and
+ * zeros are rows x cols/group_size floats (zeros may be NULL), w = (q - zero)
+ * * scale.  Needs cols % 8 == 0 and cols % group_size == 0 (the reference
+ * reads past a row otherwise). */
+NEXUS_GPU_API void nexus_fused_gemv_int4(const uint32_t* W_packed, const float* x, const float* scales,
+                                         const float* zeros, float* y, size_t rows, size_t cols, size_t group_size);
+/* QuantizationKernel::fused_gemv_fp8 (include/quantization.hpp:108-113; ABI
+ * nexus_fused_gemv_fp8, include/nexus_abi.h:145-150): FP8-E4M3 bytes, the
+ * reference's decoder (NaN codes 0x7F/0xFF -> 0) times one scale. */
+NEXUS_GPU_API void nexus_fused_gemv_fp8(const uint8_t* W_fp8, const float* x, float* y, size_t rows, size_t cols,
+                                        float scale);
+/* QuantizationKernel::dequantize_int4_awq / dequantize_fp8_e4m3
+ * (include/quantization.hpp:72-90): host in, host floats out, bit-exact. */
+NEXUS_GPU_API void nexus_dequantize_int4_awq(const uint32_t* packed, const float* scales, const float* zeros,
+                                             float* output, size_t count, size_t group_size);
+NEXUS_GPU_API void nexus_dequantize_fp8_e4m3(const uint8_t* input, float* output, size_t count, float scale);
+
 /* ---------------------------------------------------------------- layer 2 */
 
 /* INexusComputeBackend::gemv_dispatch (include/nexus_backend.hpp:55-62) on the
@@ -234,6 +253,22 @@ NEXUS_GPU_API int32_t nexus_gpu_dequantize(const void* dW, uint32_t dtype, float
 /* ------------------------------------------------------------- diagnostics */
 
 /* Message of the last error on the calling thread ("" if none). */
+/* INT4-AWQ / FP8-E4M3 on device pointers, stream-ordered (the layer-1 calls
+ * above on device memory).  nexus_gpu_gemv_int4 quantizes x into a workspace
+ * of nexus_gpu_gemv_int4_workspace_size(cols) bytes: the caller's (workspace,
+ * workspace_bytes), or the library's per-stream workspace when workspace is
+ * NULL.  Returns a NEXUS_GPU_* status. */
+NEXUS_GPU_API size_t nexus_gpu_gemv_int4_workspace_size(size_t cols);
+NEXUS_GPU_API int32_t nexus_gpu_gemv_int4(const void* dW, const float* dScales, const float* dZeros, const float* dX,
+                                          float* dY, size_t rows, size_t cols, size_t group_size, void* workspace,
+                                          size_t workspace_bytes, void* stream);
+NEXUS_GPU_API int32_t nexus_gpu_gemv_fp8(const void* dW, const float* dX, float* dY, size_t rows, size_t cols,
+                                         float scale, void* stream);
+NEXUS_GPU_API int32_t nexus_gpu_dequantize_int4_awq(const void* dPacked, const float* dScales, const float* dZeros,
+                                                    float* dOut, size_t count, size_t group_size, void* stream);
+NEXUS_GPU_API int32_t nexus_gpu_dequantize_fp8_e4m3(const void* dIn, float* dOut, size_t count, float scale,
+                                                    void* stream);
+
 NEXUS_GPU_API const char* nexus_gpu_last_error(void);
 /* Reads and clears the device-side status word of the current device
  * (bit 0: a bounded wait expired).  Synchronizes the device. */

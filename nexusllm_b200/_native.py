@@ -27,6 +27,15 @@ SIGNATURES = {
     "nexus_dequantize_gguf_q4_0": (None, [_VP, _VP, _SZ]),
     "nexus_dequantize_gguf_q5_k": (None, [_VP, _VP, _SZ]),
     "nexus_dequantize_gguf_q6_k": (None, [_VP, _VP, _SZ]),
+    "nexus_fused_gemv_int4": (None, [_VP, _VP, _VP, _VP, _VP, _SZ, _SZ, _SZ]),
+    "nexus_fused_gemv_fp8": (None, [_VP, _VP, _VP, _SZ, _SZ, ctypes.c_float]),
+    "nexus_dequantize_int4_awq": (None, [_VP, _VP, _VP, _VP, _SZ, _SZ]),
+    "nexus_dequantize_fp8_e4m3": (None, [_VP, _VP, _SZ, ctypes.c_float]),
+    "nexus_gpu_gemv_int4_workspace_size": (_SZ, [_SZ]),
+    "nexus_gpu_gemv_int4": (_I32, [_VP, _VP, _VP, _VP, _VP, _SZ, _SZ, _SZ, _VP, _SZ, _VP]),
+    "nexus_gpu_gemv_fp8": (_I32, [_VP, _VP, _VP, _SZ, _SZ, ctypes.c_float, _VP]),
+    "nexus_gpu_dequantize_int4_awq": (_I32, [_VP, _VP, _VP, _VP, _SZ, _SZ, _VP]),
+    "nexus_gpu_dequantize_fp8_e4m3": (_I32, [_VP, _VP, _SZ, ctypes.c_float, _VP]),
     "nexus_gpu_gemv_dispatch": (_I32, [_VP, _U32, _VP, _VP, _SZ, _SZ]),
     "nexus_gpu_allocate_device_memory": (_VP, [_SZ]),
     "nexus_gpu_free_device_memory": (None, [_VP]),

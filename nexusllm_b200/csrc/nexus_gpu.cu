@@ -17,6 +17,7 @@
 #include "../../include/nexus_gpu.h"
 #include "gemv_kernels.cuh"
 #include "stack_kernels.cuh"
+#include "awq_fp8_kernels.cuh"
 #include "mma_kernels.cuh"
 
 namespace nexus_gpu {
@@ -520,6 +521,124 @@ int32_t get_workspace(Device& d, cudaStream_t st, size_t need, uint8_t** out) {
     return NEXUS_GPU_SUCCESS;
 }
 
+// ------------------------------------------------- INT4-AWQ and FP8-E4M3
+bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+int32_t check_int4(size_t rows, size_t cols, size_t group_size) {
+    if (group_size == 0) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "group_size is 0");
+    if (cols % 8) return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "cols %zu not a multiple of 8 (whole packed words)", cols);
+    if (cols % group_size)
+        return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "cols %zu not a multiple of group_size %zu", cols, group_size);
+    if (rows > (size_t)INT32_MAX || cols > (size_t)INT32_MAX)
+        return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "rows or cols beyond 2^31");
+    return NEXUS_GPU_SUCCESS;
+}
+
+// Workspace of an INT4 GEMV: x quantized to 16-bit fixed point.
+size_t int4_ws_bytes(size_t cols) {
+    const size_t nxb = cols / 32;
+    return align256(nxb * kXQLimbBytes) + align256(nxb * kXQMetaBytes);
+}
+
+// Rows a warp streams together: 2 once every SM has at least 16 warps'
+// worth of 2-row tasks, else 1 (more warps busy on small matrices).
+int rows_per_warp(const Device& d, size_t rows) { return rows >= (size_t)d.sms * 16 * 2 ? 2 : 1; }
+
+int rows_grid(const Device& d, size_t rows, int rpw) {
+    const size_t per_cta = (kRowsThreads / 32) * (size_t)rpw;
+    return (int)std::max<size_t>(1, std::min<size_t>((size_t)d.sms * 4, (rows + per_cta - 1) / per_cta));
+}
+
+int32_t rows_attrs(Device& d) {
+    static std::mutex mu;
+    static std::vector<int> done;
+    std::lock_guard<std::mutex> lk(mu);
+    if (std::find(done.begin(), done.end(), d.id) != done.end()) return NEXUS_GPU_SUCCESS;
+    const int need = std::max(kInt4MaxCols / 32 * 72, kFp8MaxCols * 4);
+    if (d.smem_optin < need) return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "needs %d bytes of shared memory", need);
+    CUDA_TRY(cudaFuncSetAttribute(gemv_int4_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, need));
+    CUDA_TRY(cudaFuncSetAttribute(gemv_int4_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, need));
+    CUDA_TRY(cudaFuncSetAttribute(gemv_fp8_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, need));
+    CUDA_TRY(cudaFuncSetAttribute(gemv_fp8_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, need));
+    done.push_back(d.id);
+    return NEXUS_GPU_SUCCESS;
+}
+
+// y[rows] = W . x for INT4-AWQ weights (QuantizationKernel::fused_gemv_int4).
+// ws holds int4_ws_bytes(cols) (fast path only).
+int32_t run_gemv_int4(Device& d, const uint32_t* dW, const float* dS, const float* dZ, const float* dX, float* dY,
+                      size_t rows, size_t cols, size_t gs, uint8_t* ws, cudaStream_t st) {
+    int32_t rc = check_int4(rows, cols, gs);
+    if (rc) return rc;
+    if (rows == 0 || cols == 0) return NEXUS_GPU_SUCCESS;
+    if (!dW || !dS || !dX || !dY) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null pointer");
+    if ((rc = rows_attrs(d))) return rc;
+    const int rpw = rows_per_warp(d, rows), grid = rows_grid(d, rows, rpw);
+    if (cols % 32 == 0 && gs % 32 == 0 && cols <= (size_t)kInt4MaxCols && aligned16(dW) && ws) {
+        uint8_t* limbs = ws;
+        int4* meta = reinterpret_cast<int4*>(ws + align256(cols / 32 * kXQLimbBytes));
+        dim3 g((unsigned)((cols / 32 + 7) / 8), 1);
+        if ((rc = launch(xquant_kernel, g, dim3(256), 0, st, (const void*)dX, 0, (int)cols, (int)cols, limbs, meta)))
+            return rc;
+        Int4Params p;
+        p.W = dW;
+        p.scales = dS;
+        p.zeros = dZ;
+        p.limbs = limbs;
+        p.meta = meta;
+        p.y = dY;
+        p.rows = (int)rows;
+        p.cols = (int)cols;
+        p.group_size = (int)gs;
+        return rpw == 2 ? launch(gemv_int4_kernel<2>, dim3(grid), dim3(kRowsThreads), cols / 32 * 72, st, p)
+                        : launch(gemv_int4_kernel<1>, dim3(grid), dim3(kRowsThreads), cols / 32 * 72, st, p);
+    }
+    return launch(gemv_int4_generic_kernel, dim3(rows_grid(d, rows, 1)), dim3(256), 0, st, dW, dS, dZ, dX, dY,
+                  (int)rows, (int)cols, (int)gs);
+}
+
+// y[rows] = W . x for FP8-E4M3 weights (QuantizationKernel::fused_gemv_fp8).
+int32_t run_gemv_fp8(Device& d, const uint8_t* dW, const float* dX, float* dY, size_t rows, size_t cols, float scale,
+                     cudaStream_t st) {
+    if (rows > (size_t)INT32_MAX || cols > (size_t)INT32_MAX)
+        return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "rows or cols beyond 2^31");
+    if (rows == 0) return NEXUS_GPU_SUCCESS;
+    if (!dW || !dX || !dY) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null pointer");
+    int32_t rc = rows_attrs(d);
+    if (rc) return rc;
+    const int rpw = rows_per_warp(d, rows), grid = rows_grid(d, rows, rpw);
+    if (cols % 16 == 0 && cols > 0 && cols <= (size_t)kFp8MaxCols && aligned16(dW) && aligned16(dX)) {
+        Fp8Params p;
+        p.W = dW;
+        p.x = dX;
+        p.y = dY;
+        p.rows = (int)rows;
+        p.cols = (int)cols;
+        p.scale = scale;
+        return rpw == 2 ? launch(gemv_fp8_kernel<2>, dim3(grid), dim3(kRowsThreads), cols * 4, st, p)
+                        : launch(gemv_fp8_kernel<1>, dim3(grid), dim3(kRowsThreads), cols * 4, st, p);
+    }
+    return launch(gemv_fp8_generic_kernel, dim3(rows_grid(d, rows, 1)), dim3(256), 0, st, dW, dX, dY, (int)rows,
+                  (int)cols, scale);
+}
+
+int32_t run_dequant_int4(const uint32_t* dP, const float* dS, const float* dZ, float* dOut, size_t count, size_t gs,
+                         cudaStream_t st) {
+    if (gs == 0) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "group_size is 0");
+    if (count == 0) return NEXUS_GPU_SUCCESS;
+    if (!dP || !dS || !dOut) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null pointer");
+    const unsigned grid = (unsigned)std::min<uint64_t>((count + 255) / 256, 1u << 20);
+    return launch(dequant_int4_awq_kernel, dim3(grid), dim3(256), 0, st, dP, dS, dZ, dOut, (uint64_t)count,
+                  (uint64_t)gs);
+}
+
+int32_t run_dequant_fp8(const uint8_t* dIn, float* dOut, size_t count, float scale, cudaStream_t st) {
+    if (count == 0) return NEXUS_GPU_SUCCESS;
+    if (!dIn || !dOut) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null pointer");
+    const unsigned grid = (unsigned)std::min<uint64_t>((count + 255) / 256, 1u << 20);
+    return launch(dequant_fp8_kernel, dim3(grid), dim3(256), 0, st, dIn, dOut, (uint64_t)count, scale);
+}
+
 // ---------------------------------------------------------- weight cache
 uint64_t fnv1a(uint64_t h, const uint8_t* p, size_t n) {
     for (size_t i = 0; i < n; ++i) {
@@ -628,6 +747,102 @@ int32_t host_dequant(const void* blocks, uint32_t dtype, float* out, size_t num_
     if ((rc = grow(&d->dy, &d->dy_cap, count * 4))) return rc;
     CUDA_TRY(cudaMemcpyAsync(d->dx, blocks, in_bytes, cudaMemcpyHostToDevice, d->stream));
     if ((rc = run_dequant(d->dx, dtype, static_cast<float*>(d->dy), count, d->stream))) return rc;
+    CUDA_TRY(cudaMemcpyAsync(out, d->dy, count * 4, cudaMemcpyDeviceToHost, d->stream));
+    CUDA_TRY(cudaStreamSynchronize(d->stream));
+    return NEXUS_GPU_SUCCESS;
+}
+
+// Host-pointer INT4-AWQ / FP8 GEMV and dequantization (the reference's
+// signatures): weights, scales and zeros are cached on the device like the
+// GGUF weights (keyed by host pointer, shape and a sampled fingerprint).
+constexpr uint32_t kCacheInt4 = 5, kCacheInt4Scales = 0x10005, kCacheInt4Zeros = 0x20005, kCacheFp8 = 3;
+
+int32_t host_gemv_int4(const uint32_t* W, const float* x, const float* scales, const float* zeros, float* y,
+                       size_t rows, size_t cols, size_t gs) {
+    int32_t rc = check_int4(rows, cols, gs);
+    if (rc) return rc;
+    if (rows == 0 || cols == 0) return NEXUS_GPU_SUCCESS;
+    if (!W || !x || !scales || !y) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null pointer");
+    Device* d = nullptr;
+    if ((rc = get_device(&d))) return rc;
+    std::lock_guard<std::mutex> lk(d->mu);
+    const size_t ng = rows * (cols / gs);
+    const void *dW = nullptr, *dS = nullptr, *dZ = nullptr;
+    if ((rc = cached_weight(*d, W, kCacheInt4, rows, cols, rows * cols / 2, &dW))) return rc;
+    if ((rc = cached_weight(*d, scales, kCacheInt4Scales, rows, cols / gs, ng * 4, &dS))) return rc;
+    if (zeros && (rc = cached_weight(*d, zeros, kCacheInt4Zeros, rows, cols / gs, ng * 4, &dZ))) return rc;
+    if ((rc = grow(&d->dx, &d->dx_cap, align256(cols * 4) + int4_ws_bytes(cols) + 256))) return rc;
+    if ((rc = grow(&d->dy, &d->dy_cap, rows * 4))) return rc;
+    uint8_t* ws = static_cast<uint8_t*>(d->dx) + align256(cols * 4);
+    CUDA_TRY(cudaMemcpyAsync(d->dx, x, cols * 4, cudaMemcpyHostToDevice, d->stream));
+    if ((rc = run_gemv_int4(*d, static_cast<const uint32_t*>(dW), static_cast<const float*>(dS),
+                            static_cast<const float*>(dZ), static_cast<const float*>(d->dx),
+                            static_cast<float*>(d->dy), rows, cols, gs, ws, d->stream)))
+        return rc;
+    CUDA_TRY(cudaMemcpyAsync(y, d->dy, rows * 4, cudaMemcpyDeviceToHost, d->stream));
+    CUDA_TRY(cudaStreamSynchronize(d->stream));
+    return NEXUS_GPU_SUCCESS;
+}
+
+int32_t host_gemv_fp8(const uint8_t* W, const float* x, float* y, size_t rows, size_t cols, float scale) {
+    if (rows == 0 || cols == 0) return NEXUS_GPU_SUCCESS;
+    if (!W || !x || !y) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null pointer");
+    Device* d = nullptr;
+    int32_t rc = get_device(&d);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(d->mu);
+    const void* dW = nullptr;
+    if ((rc = cached_weight(*d, W, kCacheFp8, rows, cols, rows * cols, &dW))) return rc;
+    if ((rc = grow(&d->dx, &d->dx_cap, cols * 4))) return rc;
+    if ((rc = grow(&d->dy, &d->dy_cap, rows * 4))) return rc;
+    CUDA_TRY(cudaMemcpyAsync(d->dx, x, cols * 4, cudaMemcpyHostToDevice, d->stream));
+    if ((rc = run_gemv_fp8(*d, static_cast<const uint8_t*>(dW), static_cast<const float*>(d->dx),
+                           static_cast<float*>(d->dy), rows, cols, scale, d->stream)))
+        return rc;
+    CUDA_TRY(cudaMemcpyAsync(y, d->dy, rows * 4, cudaMemcpyDeviceToHost, d->stream));
+    CUDA_TRY(cudaStreamSynchronize(d->stream));
+    return NEXUS_GPU_SUCCESS;
+}
+
+int32_t host_dequant_int4(const uint32_t* packed, const float* scales, const float* zeros, float* out, size_t count,
+                          size_t gs) {
+    if (gs == 0) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "group_size is 0");
+    if (count == 0) return NEXUS_GPU_SUCCESS;
+    if (!packed || !scales || !out) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null pointer");
+    Device* d = nullptr;
+    int32_t rc = get_device(&d);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(d->mu);
+    const size_t words = (count + 7) / 8, ng = (count + gs - 1) / gs;
+    const size_t o_s = align256(words * 4), o_z = o_s + align256(ng * 4);
+    if ((rc = grow(&d->dx, &d->dx_cap, o_z + align256(ng * 4)))) return rc;
+    if ((rc = grow(&d->dy, &d->dy_cap, count * 4))) return rc;
+    uint8_t* base = static_cast<uint8_t*>(d->dx);
+    CUDA_TRY(cudaMemcpyAsync(base, packed, words * 4, cudaMemcpyHostToDevice, d->stream));
+    CUDA_TRY(cudaMemcpyAsync(base + o_s, scales, ng * 4, cudaMemcpyHostToDevice, d->stream));
+    if (zeros) CUDA_TRY(cudaMemcpyAsync(base + o_z, zeros, ng * 4, cudaMemcpyHostToDevice, d->stream));
+    if ((rc = run_dequant_int4(reinterpret_cast<const uint32_t*>(base), reinterpret_cast<const float*>(base + o_s),
+                               zeros ? reinterpret_cast<const float*>(base + o_z) : nullptr,
+                               static_cast<float*>(d->dy), count, gs, d->stream)))
+        return rc;
+    CUDA_TRY(cudaMemcpyAsync(out, d->dy, count * 4, cudaMemcpyDeviceToHost, d->stream));
+    CUDA_TRY(cudaStreamSynchronize(d->stream));
+    return NEXUS_GPU_SUCCESS;
+}
+
+int32_t host_dequant_fp8(const uint8_t* in, float* out, size_t count, float scale) {
+    if (count == 0) return NEXUS_GPU_SUCCESS;
+    if (!in || !out) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null pointer");
+    Device* d = nullptr;
+    int32_t rc = get_device(&d);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(d->mu);
+    if ((rc = grow(&d->dx, &d->dx_cap, count))) return rc;
+    if ((rc = grow(&d->dy, &d->dy_cap, count * 4))) return rc;
+    CUDA_TRY(cudaMemcpyAsync(d->dx, in, count, cudaMemcpyHostToDevice, d->stream));
+    if ((rc = run_dequant_fp8(static_cast<const uint8_t*>(d->dx), static_cast<float*>(d->dy), count, scale,
+                              d->stream)))
+        return rc;
     CUDA_TRY(cudaMemcpyAsync(out, d->dy, count * 4, cudaMemcpyDeviceToHost, d->stream));
     CUDA_TRY(cudaStreamSynchronize(d->stream));
     return NEXUS_GPU_SUCCESS;
@@ -1131,6 +1346,22 @@ NEXUS_GPU_API void nexus_dequantize_gguf_q6_k(const void* blocks, float* out, si
     report_void(__func__, host_dequant(blocks, NEXUS_GPU_GGUF_Q6_K, out, nb));
 }
 
+NEXUS_GPU_API void nexus_fused_gemv_int4(const uint32_t* W_packed, const float* x, const float* scales,
+                                         const float* zeros, float* y, size_t rows, size_t cols, size_t group_size) {
+    report_void(__func__, host_gemv_int4(W_packed, x, scales, zeros, y, rows, cols, group_size));
+}
+NEXUS_GPU_API void nexus_fused_gemv_fp8(const uint8_t* W_fp8, const float* x, float* y, size_t rows, size_t cols,
+                                        float scale) {
+    report_void(__func__, host_gemv_fp8(W_fp8, x, y, rows, cols, scale));
+}
+NEXUS_GPU_API void nexus_dequantize_int4_awq(const uint32_t* packed, const float* scales, const float* zeros,
+                                             float* output, size_t count, size_t group_size) {
+    report_void(__func__, host_dequant_int4(packed, scales, zeros, output, count, group_size));
+}
+NEXUS_GPU_API void nexus_dequantize_fp8_e4m3(const uint8_t* input, float* output, size_t count, float scale) {
+    report_void(__func__, host_dequant_fp8(input, output, count, scale));
+}
+
 NEXUS_GPU_API int32_t nexus_gpu_gemv_dispatch(const void* W, uint32_t dtype, const float* x, float* y, size_t rows,
                                               size_t cols) {
     t_last_error.clear();
@@ -1303,6 +1534,51 @@ NEXUS_GPU_API int32_t nexus_gpu_stack_destroy(void* stack) {
 NEXUS_GPU_API int32_t nexus_gpu_dequantize(const void* dW, uint32_t dtype, float* dOut, size_t count, void* stream) {
     t_last_error.clear();
     return run_dequant(dW, dtype, dOut, count, static_cast<cudaStream_t>(stream));
+}
+
+NEXUS_GPU_API size_t nexus_gpu_gemv_int4_workspace_size(size_t cols) { return int4_ws_bytes(cols); }
+
+NEXUS_GPU_API int32_t nexus_gpu_gemv_int4(const void* dW, const float* dScales, const float* dZeros, const float* dX,
+                                          float* dY, size_t rows, size_t cols, size_t group_size, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+    t_last_error.clear();
+    int32_t rc = check_int4(rows, cols, group_size);  // before touching a device
+    if (rc) return rc;
+    Device* d = nullptr;
+    if ((rc = get_device(&d))) return rc;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const size_t need = int4_ws_bytes(cols);
+    if (!ws) {
+        if ((rc = get_workspace(*d, st, need, &ws))) return rc;
+    } else if (workspace_bytes < need) {
+        return fail(NEXUS_GPU_ERROR_WORKSPACE, "workspace of %zu bytes given, %zu needed", workspace_bytes, need);
+    }
+    return run_gemv_int4(*d, static_cast<const uint32_t*>(dW), dScales, dZeros, dX, dY, rows, cols, group_size, ws,
+                         st);
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_gemv_fp8(const void* dW, const float* dX, float* dY, size_t rows, size_t cols,
+                                         float scale, void* stream) {
+    t_last_error.clear();
+    Device* d = nullptr;
+    int32_t rc = get_device(&d);
+    if (rc) return rc;
+    return run_gemv_fp8(*d, static_cast<const uint8_t*>(dW), dX, dY, rows, cols, scale,
+                        static_cast<cudaStream_t>(stream));
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_dequantize_int4_awq(const void* dPacked, const float* dScales, const float* dZeros,
+                                                    float* dOut, size_t count, size_t group_size, void* stream) {
+    t_last_error.clear();
+    return run_dequant_int4(static_cast<const uint32_t*>(dPacked), dScales, dZeros, dOut, count, group_size,
+                            static_cast<cudaStream_t>(stream));
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_dequantize_fp8_e4m3(const void* dIn, float* dOut, size_t count, float scale,
+                                                    void* stream) {
+    t_last_error.clear();
+    return run_dequant_fp8(static_cast<const uint8_t*>(dIn), dOut, count, scale, static_cast<cudaStream_t>(stream));
 }
 
 NEXUS_GPU_API const char* nexus_gpu_last_error(void) { return t_last_error.c_str(); }

@@ -95,6 +95,47 @@ class QuantizationKernel:
     def dequantize_gguf_q6_k(blocks, output, num_blocks: int) -> None:
         QuantizationKernel._deq(DataType.GGUF_Q6_K, blocks, output, num_blocks)
 
+    # ---------------------------------------------- INT4-AWQ and FP8-E4M3
+    @staticmethod
+    def fused_gemv_int4(W_packed, x, scales, zeros, y, rows: int, cols: int, group_size: int) -> None:
+        """src/quantization.cpp:102-200: W_packed uint32 [rows][cols/8] (column c
+        = nibble c % 8 of word c / 8), scales / zeros float32
+        [rows][cols/group_size] (zeros may be None), w = (q - zero) * scale."""
+        ng = rows * (cols // group_size) if group_size else 0
+        if W_packed.dtype != np.uint32 or W_packed.size < rows * (cols // 8):
+            raise ValueError("W_packed must be uint32 with rows * cols/8 words")
+        if scales.dtype != np.float32 or scales.size < ng or (zeros is not None and
+                                                              (zeros.dtype != np.float32 or zeros.size < ng)):
+            raise ValueError("scales/zeros must be float32 with rows * cols/group_size elements")
+        if x.dtype != np.float32 or x.size < cols or y.dtype != np.float32 or y.size < rows:
+            raise ValueError("x / y must be float32 of at least cols / rows elements")
+        _native.lib().nexus_fused_gemv_int4(_ptr(W_packed), _ptr(x), _ptr(scales),
+                                            None if zeros is None else _ptr(zeros), _ptr(y), rows, cols, group_size)
+
+    @staticmethod
+    def fused_gemv_fp8(W_fp8, x, y, rows: int, cols: int, scale: float) -> None:
+        """src/quantization.cpp:202-262: one E4M3 byte per weight times scale."""
+        if W_fp8.nbytes < rows * cols:
+            raise ValueError("W_fp8 holds fewer than rows * cols bytes")
+        if x.dtype != np.float32 or x.size < cols or y.dtype != np.float32 or y.size < rows:
+            raise ValueError("x / y must be float32 of at least cols / rows elements")
+        _native.lib().nexus_fused_gemv_fp8(_ptr(W_fp8), _ptr(x), _ptr(y), rows, cols, float(scale))
+
+    @staticmethod
+    def dequantize_int4_awq(packed, scales, zeros, output, count: int, group_size: int) -> None:
+        """src/quantization.cpp:28-46."""
+        if packed.dtype != np.uint32 or packed.size * 8 < count or output.dtype != np.float32 or output.size < count:
+            raise ValueError("buffer too small")
+        _native.lib().nexus_dequantize_int4_awq(_ptr(packed), _ptr(scales), None if zeros is None else _ptr(zeros),
+                                                _ptr(output), count, group_size)
+
+    @staticmethod
+    def dequantize_fp8_e4m3(input, output, count: int, scale: float) -> None:
+        """src/quantization.cpp:62-68."""
+        if input.nbytes < count or output.dtype != np.float32 or output.size < count:
+            raise ValueError("buffer too small")
+        _native.lib().nexus_dequantize_fp8_e4m3(_ptr(input), _ptr(output), count, float(scale))
+
 
 _NAME = {DataType.GGUF_Q4_0: "q4_0", DataType.GGUF_Q8_0: "q8_0", DataType.FP16: "fp16",
          DataType.GGUF_Q5_K: "q5_k", DataType.GGUF_Q6_K: "q6_k"}

@@ -65,6 +65,45 @@ class _Lib:
         X = np.ascontiguousarray(X, dtype=np.float32).reshape(-1, cols)
         return np.stack([self.gemv(dtype, W, X[m], rows, cols) for m in range(X.shape[0])])
 
+    # ------------------------------------ INT4-AWQ / FP8-E4M3 (the reference's
+    # QuantizationKernel::fused_gemv_int4 / fused_gemv_fp8 and dequantizers)
+    def _fn(self, name: str, argtypes):
+        f = getattr(self.lib, name)
+        f.restype = None
+        f.argtypes = argtypes
+        return f
+
+    def gemv_int4(self, W: np.ndarray, x: np.ndarray, scales: np.ndarray, zeros, rows: int, cols: int,
+                  group_size: int) -> np.ndarray:
+        """y[rows] = W . x; W uint32 [rows][cols/8] (nibble k of word j = column 8j+k),
+        scales/zeros float32 [rows][cols/group_size] (zeros may be None)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.zeros(rows, np.float32)
+        z = None if zeros is None else _ptr(np.ascontiguousarray(zeros, np.float32))
+        self._fn(self._g + "int4", [_VP, _VP, _VP, _VP, _VP, _SZ, _SZ, _SZ])(
+            _ptr(W), _ptr(x), _ptr(np.ascontiguousarray(scales, np.float32)), z, _ptr(y), rows, cols, group_size)
+        return y
+
+    def gemv_fp8(self, W: np.ndarray, x: np.ndarray, rows: int, cols: int, scale: float) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.zeros(rows, np.float32)
+        self._fn(self._g + "fp8", [_VP, _VP, _VP, _SZ, _SZ, ctypes.c_float])(_ptr(W), _ptr(x), _ptr(y), rows, cols,
+                                                                             scale)
+        return y
+
+    def dequantize_int4_awq(self, packed: np.ndarray, scales: np.ndarray, zeros, count: int,
+                            group_size: int) -> np.ndarray:
+        out = np.zeros(count, np.float32)
+        z = None if zeros is None else _ptr(np.ascontiguousarray(zeros, np.float32))
+        self._fn(self._d + "int4_awq", [_VP, _VP, _VP, _VP, _SZ, _SZ])(
+            _ptr(packed), _ptr(np.ascontiguousarray(scales, np.float32)), z, _ptr(out), count, group_size)
+        return out
+
+    def dequantize_fp8_e4m3(self, data: np.ndarray, count: int, scale: float) -> np.ndarray:
+        out = np.zeros(count, np.float32)
+        self._fn(self._d + "fp8_e4m3", [_VP, _VP, _SZ, ctypes.c_float])(_ptr(data), _ptr(out), count, scale)
+        return out
+
     def dequantize(self, dtype: int, W: np.ndarray, count: int) -> np.ndarray:
         name = _NAMES[int(dtype)]
         out = np.zeros(count, np.float32)

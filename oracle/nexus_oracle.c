@@ -324,6 +324,91 @@ void oracle_gemv_q6_k(const uint8_t* W, const float* x, float* y, size_t rows, s
     }
 }
 
+/* ------------------------------------------------ INT4-AWQ and FP8-E4M3 */
+
+/* src/quantization.cpp:12-26 (fp8_e4m3_to_fp32): sign, 4-bit exponent (bias
+ * 7), 3-bit mantissa; exponent 0 is subnormal mant * 2^-9; 0x7F and 0xFF
+ * (the E4M3 NaNs) decode to +0. */
+float oracle_fp8_e4m3_to_fp32(uint8_t v) {
+    if (v == 0x7F || v == 0xFF) return 0.0f;
+    const int sign = (v >> 7) & 1, exp = (v >> 3) & 0xF, mant = v & 0x7;
+    const float r = exp == 0 ? ldexpf((float)mant, -9) : ldexpf(1.0f + (float)mant / 8.0f, exp - 7);
+    return sign ? -r : r;
+}
+
+/* src/quantization.cpp:28-46 (dequantize_int4_awq): element i is nibble i % 8
+ * of word i / 8; w = ((float)q - zero) * scale (two roundings) with the group
+ * i / group_size; zeros may be NULL (zero 0). */
+void oracle_dequantize_int4_awq(const uint32_t* packed, const float* scales, const float* zeros, float* out,
+                                size_t count, size_t group_size) {
+    for (size_t i = 0; i < count; ++i) {
+        const size_t g = i / group_size;
+        const float scale = scales[g], zero = zeros ? zeros[g] : 0.0f;
+        const uint32_t q = (packed[i / 8] >> ((i % 8) * 4)) & 0x0Fu;
+        out[i] = ((float)q - zero) * scale;
+    }
+}
+
+/* src/quantization.cpp:62-68 (dequantize_fp8_e4m3): decoded value * scale. */
+void oracle_dequantize_fp8_e4m3(const uint8_t* in, float* out, size_t count, float scale) {
+    for (size_t i = 0; i < count; ++i) out[i] = oracle_fp8_e4m3_to_fp32(in[i]) * scale;
+}
+
+/* src/quantization.cpp:102-200, AVX2 branch :146-180.  Per 8-column step c
+ * (c + 8 <= cols): the group of column c supplies scale and zero for all 8
+ * columns (:149-151), w = ((float)q - zero) * scale, acc[k] = fma(w, x, acc[k]);
+ * horizontal sum; scalar tail with the group of each column, where the
+ * reference build keeps sum += w * x as a separate multiply and add (unlike
+ * the GGUF tails; checked against the reference build).  Row r reads words
+ * [r*(cols/8), ...) and groups [r*(cols/group_size), ...). */
+void oracle_gemv_int4(const uint32_t* W, const float* x, const float* scales, const float* zeros, float* y,
+                      size_t rows, size_t cols, size_t group_size) {
+    const size_t packed_cols = cols / 8;
+    for (size_t r = 0; r < rows; ++r) {
+        const uint32_t* row = W + r * packed_cols;
+        const size_t g_base = r * (cols / group_size);
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        size_t c = 0;
+        for (; c + 8 <= cols; c += 8) {
+            const size_t g = g_base + c / group_size;
+            const float scale = scales[g], zero = zeros ? zeros[g] : 0.0f;
+            const uint32_t word = row[c / 8];
+            for (int k = 0; k < 8; ++k) {
+                const float w = ((float)((word >> (k * 4)) & 0x0Fu) - zero) * scale;
+                acc[k] = fmaf(w, x[c + k], acc[k]);
+            }
+        }
+        float sum = hsum8(acc);
+        for (; c < cols; ++c) {
+            const size_t g = g_base + c / group_size;
+            const float scale = scales[g], zero = zeros ? zeros[g] : 0.0f;
+            const float w = ((float)((row[c / 8] >> ((c % 8) * 4)) & 0x0Fu) - zero) * scale;
+            const float p = w * x[c];
+            sum = sum + p;
+        }
+        y[r] = sum;
+    }
+}
+
+/* src/quantization.cpp:202-262, AVX2 branch :229-249: w = fp8(W) * scale,
+ * 8-lane fma accumulator, horizontal sum, scalar tail as a separate multiply
+ * and add (as the reference build compiles it). */
+void oracle_gemv_fp8(const uint8_t* W, const float* x, float* y, size_t rows, size_t cols, float scale) {
+    for (size_t r = 0; r < rows; ++r) {
+        const uint8_t* row = W + r * cols;
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        size_t c = 0;
+        for (; c + 8 <= cols; c += 8)
+            for (int k = 0; k < 8; ++k) acc[k] = fmaf(oracle_fp8_e4m3_to_fp32(row[c + k]) * scale, x[c + k], acc[k]);
+        float sum = hsum8(acc);
+        for (; c < cols; ++c) {
+            const float p = (oracle_fp8_e4m3_to_fp32(row[c]) * scale) * x[c];
+            sum = sum + p;
+        }
+        y[r] = sum;
+    }
+}
+
 /* Dispatch by NexusLLM DataType value (include/nexus_common.hpp:244-260), as
  * TransformerOps::matmul_vec_dispatch does (include/transformer_ops.hpp:157-173).
  * Returns 0 on success, -3 (ERROR_FORMAT_UNSUPPORTED) for other types. */

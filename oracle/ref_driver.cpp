@@ -85,6 +85,21 @@ REF_API void ref_fused_gemv_q6_k(const void* W, const float* x, float* y, size_t
     QuantizationKernel::fused_gemv_q6_k(static_cast<const BlockQ6_K*>(W), x, y, rows, cols);
 }
 
+REF_API void ref_fused_gemv_int4(const uint32_t* W, const float* x, const float* scales, const float* zeros,
+                                 float* y, size_t rows, size_t cols, size_t group_size) {
+    QuantizationKernel::fused_gemv_int4(W, x, scales, zeros, y, rows, cols, group_size);
+}
+REF_API void ref_fused_gemv_fp8(const uint8_t* W, const float* x, float* y, size_t rows, size_t cols, float scale) {
+    QuantizationKernel::fused_gemv_fp8(W, x, y, rows, cols, scale);
+}
+REF_API void ref_dequantize_int4_awq(const uint32_t* packed, const float* scales, const float* zeros, float* out,
+                                     size_t count, size_t group_size) {
+    QuantizationKernel::dequantize_int4_awq(packed, scales, zeros, out, count, group_size);
+}
+REF_API void ref_dequantize_fp8_e4m3(const uint8_t* in, float* out, size_t count, float scale) {
+    QuantizationKernel::dequantize_fp8_e4m3(in, out, count, scale);
+}
+
 // Bytes of one weight row for a NexusLLM DataType value (nexus_common.hpp:244-260).
 static size_t row_bytes(unsigned dtype, size_t cols) {
     switch (dtype) {

@@ -100,6 +100,49 @@ def edge_blocks(dt: DataType, seed: int) -> np.ndarray:
     return a.reshape(-1)
 
 
+# INT4-AWQ GEMV cases (rows, cols, group_size, with zeros) and FP8 shapes.
+INT4_SHAPES = [(1, 128, 128, True), (37, 256, 32, True), (16, 4096, 128, True), (5, 1000, 8, True),
+               (3, 96, 32, False), (4, 200, 40, True), (2, 64, 64, False)]
+FP8_SHAPES = [(1, 8), (37, 100), (24, 512), (16, 33), (3, 4096), (5, 16384)]
+
+
+def int4_fp8(ref, g) -> None:
+    """QuantizationKernel::fused_gemv_int4 / fused_gemv_fp8 and their
+    dequantizers (src/quantization.cpp:12-68,102-262), from the reference build."""
+    rng = np.random.default_rng(9500)
+    codes = np.arange(256, dtype=np.uint8)
+    g["fp8/codes"] = codes
+    g["fp8/codes_x1"] = ref.dequantize_fp8_e4m3(codes, 256, 1.0)
+    g["fp8/codes_x037"] = ref.dequantize_fp8_e4m3(codes, 256, 0.37)
+    packed = rng.integers(0, 2**32, size=125, dtype=np.uint64).astype(np.uint32)
+    sc = rng.uniform(0.001, 0.02, size=(1000 + 31) // 32).astype(np.float32)  # one scale per 32 elements
+    zr = rng.integers(0, 16, size=sc.size).astype(np.float32)
+    g["int4deq/packed"], g["int4deq/scales"], g["int4deq/zeros"] = packed, sc, zr
+    g["int4deq/out_g32"] = ref.dequantize_int4_awq(packed, sc, zr, 1000, 32)
+    s8 = np.random.default_rng(9501).uniform(-1, 1, 125).astype(np.float32)
+    g["int4deq/scales_g8"] = s8
+    g["int4deq/out_g8_nozero"] = ref.dequantize_int4_awq(packed, s8, None, 1000, 8)
+    for j, (rows, cols, gs, with_z) in enumerate(INT4_SHAPES):
+        r = np.random.default_rng(9600 + j)
+        W = r.integers(0, 2**32, size=rows * cols // 8, dtype=np.uint64).astype(np.uint32)
+        ng = rows * cols // gs
+        scales = r.uniform(0.001, 0.02, size=ng).astype(np.float32)
+        zeros = r.integers(0, 16, size=ng).astype(np.float32) if with_z else None
+        x = synth.activations_numpy(1, cols, 9700 + j)[0]
+        key = f"int4gemv/{rows}x{cols}g{gs}{'z' if with_z else ''}"
+        g[key + "/W"], g[key + "/x"], g[key + "/scales"] = W, x, scales
+        if with_z:
+            g[key + "/zeros"] = zeros
+        g[key + "/y"] = ref.gemv_int4(W, x, scales, zeros, rows, cols, gs)
+    for j, (rows, cols) in enumerate(FP8_SHAPES):
+        r = np.random.default_rng(9800 + j)
+        W = r.integers(0, 256, size=rows * cols, dtype=np.uint8)  # every code, NaN codes included
+        x = synth.activations_numpy(1, cols, 9900 + j)[0]
+        key = f"fp8gemv/{rows}x{cols}"
+        g[key + "/W"], g[key + "/x"] = W, x
+        g[key + "/y"] = ref.gemv_fp8(W, x, rows, cols, 0.0625)
+
+
 def main() -> None:
     ref = oracle.reference()
     g = {}
@@ -149,6 +192,7 @@ def main() -> None:
         g[key + "/x"] = x
         g[key + "/y"] = ref.gemv(int(dt), W, x, rows, cols)
 
+    int4_fp8(ref, g)
     np.savez_compressed(OUT, **g)
     print(f"wrote {OUT}: {len(g)} arrays, {os.path.getsize(OUT)} bytes")
 
