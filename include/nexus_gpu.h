@@ -252,7 +252,6 @@ NEXUS_GPU_API int32_t nexus_gpu_dequantize(const void* dW, uint32_t dtype, float
 
 /* ------------------------------------------------------------- diagnostics */
 
-/* Message of the last error on the calling thread ("" if none). */
 /* INT4-AWQ / FP8-E4M3 on device pointers, stream-ordered (the layer-1 calls
  * above on device memory).  nexus_gpu_gemv_int4 quantizes x into a workspace
  * of nexus_gpu_gemv_int4_workspace_size(cols) bytes: the caller's (workspace,
@@ -269,6 +268,7 @@ NEXUS_GPU_API int32_t nexus_gpu_dequantize_int4_awq(const void* dPacked, const f
 NEXUS_GPU_API int32_t nexus_gpu_dequantize_fp8_e4m3(const void* dIn, float* dOut, size_t count, float scale,
                                                     void* stream);
 
+/* Message of the last error on the calling thread ("" if none). */
 NEXUS_GPU_API const char* nexus_gpu_last_error(void);
 /* Reads and clears the device-side status word of the current device
  * (bit 0: a bounded wait expired).  Synchronizes the device. */
