@@ -49,8 +49,25 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 HIDDEN, KV, FFN, VOCAB, LAYERS = 4096, 1024, 14336, 128256, 32
-LAYER_SHAPES = [("q", HIDDEN, HIDDEN), ("k", KV, HIDDEN), ("v", KV, HIDDEN), ("o", HIDDEN, HIDDEN),
-                ("gate", FFN, HIDDEN), ("up", FFN, HIDDEN), ("down", HIDDEN, FFN)]
+MODEL = "8b"
+
+
+def layer_shapes():
+    return [("q", HIDDEN, HIDDEN), ("k", KV, HIDDEN), ("v", KV, HIDDEN), ("o", HIDDEN, HIDDEN),
+            ("gate", FFN, HIDDEN), ("up", FFN, HIDDEN), ("down", HIDDEN, FFN)]
+
+
+LAYER_SHAPES = layer_shapes()
+
+
+def set_model(name):
+    """--model 70b: BASELINE.json configs[4], Llama-3-70B shapes (hidden 8192,
+    GQA k/v 1024x8192, FFN 28672, 80 layers, LM head 128256x8192)."""
+    global HIDDEN, KV, FFN, VOCAB, LAYERS, LAYER_SHAPES, MODEL
+    MODEL = name
+    if name == "70b":
+        HIDDEN, KV, FFN, VOCAB, LAYERS = 8192, 1024, 28672, 128256, 80
+    LAYER_SHAPES = layer_shapes()
 DTYPE = 7  # GGUF_Q4_0
 NOMINAL_HBM_GBS = 8000.0
 
@@ -225,14 +242,21 @@ METRIC = "quant GEMV achieved HBM GB/s (% of 8 TB/s) & decode layer-stack tokens
 
 
 def workload_config(args, reference=False):
+    if MODEL == "70b":
+        head = {"workload": "configs[4]: Llama-3-70B Q4_0 decode stack (80 layers x q,k,v,o,gate,up,down + LM head "
+                            "128256x8192), batch M=1, fp32 activations",
+                "model": "Llama-3-70B shapes (hidden 8192, kv 1024, ffn 28672, vocab 128256)"}
+    else:
+        head = {"workload": "configs[3]: Llama-3-8B Q4_0 decode stack (32 layers x q,k,v,o,gate,up,down + LM head "
+                            "128256x4096), batch M=1, fp32 activations",
+                "model": "Llama-3-8B shapes (hidden 4096, kv 1024, ffn 14336, vocab 128256)"}
+    gb = step_bytes() / 1e9
     return {
-        "workload": "configs[3]: Llama-3-8B Q4_0 decode stack (32 layers x q,k,v,o,gate,up,down + LM head "
-                    "128256x4096), batch M=1, fp32 activations",
-        "model": "Llama-3-8B shapes (hidden 4096, kv 1024, ffn 14336, vocab 128256)",
+        **head,
         "weight_format": "GGUF Q4_0", "global_batch": 1, "gemvs_per_step": 7 * LAYERS + 1,
         "parallelism": "cpu" if reference else (f"row-shard x{args.gpus} + NCCL all-gather" if args.gpus > 1
                                                 else "single GPU"),
-        "l2": "working set 4.22 GB per step >> 126 MB L2 (no flush needed)",
+        "l2": f"working set {gb:.2f} GB per step >> 126 MB L2 (no flush needed)",
     }
 
 
@@ -263,11 +287,23 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-formats", action="store_true",
                     help="skip the INT4-AWQ / FP8-E4M3 per-shape GEMV timings")
+    ap.add_argument("--no-fused", action="store_true",
+                    help="skip the decode stack with RMSNorm / SwiGLU / residual fused in")
     ap.add_argument("--no-batched", action="store_true",
                     help="skip the batched-decode points (M = 4, 16, 64 tokens per step)")
-    ap.add_argument("--layers", type=int, default=LAYERS,
-                    help="decoder layers in the stack (32 = the configuration; fewer only for profiling runs)")
+    ap.add_argument("--model", default="8b", choices=["8b", "70b"],
+                    help="8b: configs[3] (the headline); 70b: configs[4], Llama-3-70B shapes")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="decoder layers in the stack (the configuration's count by default; fewer only for "
+                         "profiling runs)")
     args = ap.parse_args()
+    set_model(args.model)
+    if args.layers is None:
+        args.layers = LAYERS
+    if args.model == "70b":
+        # the 70B configuration is the batch-1 sharded stack; batched points,
+        # per-format timings and the host-weight path stay with the 8B headline
+        args.no_batched = args.no_formats = args.no_fused = True
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
@@ -402,7 +438,8 @@ def main():
                     "launch_note": "one launch per step, after a 28 KB counter reset (cudaMemsetAsync)",
                     "traffic": round(STACK_TRAFFIC_PER_ALG_BYTE * sb)}
         e2e = None if args.no_e2e else e2e_stack_host(torch, L, stack, h0, ys[-1], stream, dev, args, timed, sb)
-        e2e_dispatch = None if args.no_e2e else e2e_host_api(torch, L, layers, head, h0, args)
+        e2e_dispatch = None if (args.no_e2e or args.model == "70b") else e2e_host_api(torch, L, layers, head, h0,
+                                                                                      args)
         launches = args.steps
         launches_note = f"1 gemv_stack_kernel per step x {args.steps} steps (plus one counter memset per step)"
         extra = {"per_gemv_graph": per_gemv, "e2e_per_gemv_dispatch": e2e_dispatch}
@@ -410,6 +447,8 @@ def main():
             extra["batched_decode"] = batched_decode(torch, L, layers, head, stream, dev, timed, args, peak)
         if not args.no_formats:
             extra["int4_awq_fp8"] = other_formats(torch, L, stream, dev, timed, peak)
+        if not args.no_fused:
+            extra["fused_decode_stack"] = fused_decode_stack(torch, L, layers, head, h0, stream, dev, timed, args, peak)
         del stack_graph
         L.nexus_gpu_stack_destroy(stack)
     else:
@@ -605,6 +644,63 @@ def other_formats(torch, L, stream, dev, timed, peak):
             if fmt == "int4_awq":
                 del S, Z
     return out
+
+
+def fused_decode_stack(torch, L, layers, head, h0, stream, dev, timed, args, peak):
+    """The same weights as the headline, with the reference decode layer's
+    dataflow (src/forward_pass.cpp:504-562) fused into ONE stack launch:
+    RMSNorm -> q, k, v; o (x = q, standing in for attention) + residual;
+    RMSNorm -> gate, up; SwiGLU -> down + residual; final RMSNorm -> LM head
+    (nexus_gpu_stack_create_ex).  Norm weights ~ 1 + N(0, 0.1^2)."""
+    import ctypes
+
+    from nexusllm_b200 import _native
+
+    gen = torch.Generator(device=dev).manual_seed(77)
+    norm = lambda: 1.0 + 0.1 * torch.randn(HIDDEN, device=dev, generator=gen)  # noqa: E731
+    keep, tasks = [], []
+    prev = -1
+    eps = 1e-5
+    for mats in layers:
+        b = len(tasks)
+        na, nf = norm(), norm()
+        keep += [na, nf]
+        spec = [("q", prev, -1, -2, na), ("k", prev, -1, -2, na), ("v", prev, -1, -2, na), ("o", b, -1, prev, None),
+                ("gate", b + 3, -1, -2, nf), ("up", b + 3, -1, -2, nf), ("down", b + 4, b + 5, b + 3, None)]
+        for (name, src, src2, res, nw), (_, n, k) in zip(spec, LAYER_SHAPES):
+            y = torch.empty(n, dtype=torch.float32, device=dev)
+            keep.append(y)
+            tasks.append(_native.StackTaskEx(mats[name].data_ptr(), n, k, y.data_ptr(), src, -1, src2, res,
+                                             None if nw is None else nw.data_ptr(), eps))
+        prev = b + 6
+    no = norm()
+    y = torch.empty(VOCAB, dtype=torch.float32, device=dev)
+    keep += [no, y]
+    tasks.append(_native.StackTaskEx(head.data_ptr(), VOCAB, HIDDEN, y.data_ptr(), prev, -1, -1, -2, no.data_ptr(), eps))
+    arr = (_native.StackTaskEx * len(tasks))(*tasks)
+    h = ctypes.c_void_p()
+    _native.check(L.nexus_gpu_stack_create_ex(DTYPE, arr, len(tasks), HIDDEN, 1, 0, ctypes.byref(h)))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        _native.check(L.nexus_gpu_stack_run(h, h0.data_ptr(), stream.cuda_stream))
+        torch.cuda.synchronize(dev)
+        with torch.cuda.graph(g, stream=stream):
+            _native.check(L.nexus_gpu_stack_run(h, h0.data_ptr(), stream.cuda_stream))
+        for _ in range(3):
+            g.replay()
+    reps = max(20, min(300, args.steps))
+    ms = timed(g.replay, reps) / reps
+    check_status(L)
+    if not bool(torch.isfinite(y).all()):
+        raise RuntimeError("fused decode stack produced non-finite logits")
+    sb = step_bytes(layers=len(layers)) + 4 * HIDDEN * (2 * len(layers) + 1)  # + norm weights
+    gbs = sb / (ms * 1e-3) / 1e9
+    del g
+    L.nexus_gpu_stack_destroy(h)
+    return {"ms_per_step": round(ms, 4), "tokens_per_s": round(1e3 / ms, 2), "value": round(gbs, 1), "unit": "GB/s",
+            "pct_of_measured_hbm": round(100 * gbs / peak, 2), "steps": reps,
+            "dataflow": "RMSNorm->q,k,v; o(x=q)+residual; RMSNorm->gate,up; SwiGLU->down+residual; RMSNorm->head",
+            "launches_per_step": 1}
 
 
 def build_stack_graph(torch, L, _native, layers, head, h0, stream, dev):

@@ -239,6 +239,35 @@ NEXUS_GPU_API int32_t nexus_gpu_stack_destroy(void* stack);
 NEXUS_GPU_API int32_t nexus_gpu_stack_create_sharded(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n_tasks,
                                                      uint64_t input_cols, uint32_t world, uint32_t rank,
                                                      void** out_stack);
+/* A stack task with the operations around the GEMV fused into it, so that a
+ * stack can run the reference's decode layer (src/forward_pass.cpp:504-562:
+ * RMSNorm -> q,k,v; o + residual; RMSNorm -> gate, up; SwiGLU -> down +
+ * residual) in one launch.  Fields as NexusGpuStackTask, plus:
+ *   x_source2       -1, or an earlier task: the GEMV input is
+ *                   silu(x_source's output) * x_source2's output (SwiGLU,
+ *                   include/transformer_ops.hpp:86-95);
+ *   norm_weight     NULL, or cols fp32 weights on the device (16-byte aligned):
+ *                   the input is RMSNorm(x) * norm_weight with norm_eps
+ *                   (TransformerOps::rmsnorm, include/transformer_ops.hpp:23-44),
+ *                   applied after the SwiGLU when both are given;
+ *   residual_source -2 none, -1 the stack input, or an earlier task with as
+ *                   many rows: y = GEMV + that vector (the residual adds of
+ *                   src/forward_pass.cpp:539-541,558-561).
+ * world == 1 builds an unsharded stack (y required); world > 1 a sharded one
+ * (y NULL, then export / connect as for nexus_gpu_stack_create_sharded). */
+typedef struct {
+    const void* W;
+    uint64_t rows, cols;
+    float* y;
+    int32_t x_source;
+    int32_t after;
+    int32_t x_source2;
+    int32_t residual_source;
+    const float* norm_weight;
+    float norm_eps;
+} NexusGpuStackTaskEx;
+NEXUS_GPU_API int32_t nexus_gpu_stack_create_ex(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t n_tasks,
+                                                uint64_t input_cols, uint32_t world, uint32_t rank, void** out_stack);
 /* Blob size when blob == NULL; else writes *blob_bytes (>= that size) bytes. */
 NEXUS_GPU_API int32_t nexus_gpu_stack_export(void* stack, void* blob, uint64_t* blob_bytes);
 NEXUS_GPU_API int32_t nexus_gpu_stack_connect(void* stack, const void* blobs, uint64_t blobs_bytes);

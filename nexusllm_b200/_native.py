@@ -52,6 +52,7 @@ SIGNATURES = {
     "nexus_gpu_stack_create": (_I32, [_U32, _VP, _U32, ctypes.c_uint64, ctypes.POINTER(_VP)]),
     "nexus_gpu_stack_run": (_I32, [_VP, _VP, _VP]),
     "nexus_gpu_stack_destroy": (_I32, [_VP]),
+    "nexus_gpu_stack_create_ex": (_I32, [_U32, _VP, _U32, ctypes.c_uint64, _U32, _U32, ctypes.POINTER(_VP)]),
     "nexus_gpu_stack_create_sharded": (_I32, [_U32, _VP, _U32, ctypes.c_uint64, _U32, _U32, ctypes.POINTER(_VP)]),
     "nexus_gpu_stack_export": (_I32, [_VP, _VP, ctypes.POINTER(ctypes.c_uint64)]),
     "nexus_gpu_stack_connect": (_I32, [_VP, _VP, ctypes.c_uint64]),
@@ -68,6 +69,13 @@ class StackTask(ctypes.Structure):
     """NexusGpuStackTask (include/nexus_gpu.h)."""
     _fields_ = [("W", _VP), ("rows", ctypes.c_uint64), ("cols", ctypes.c_uint64), ("y", _VP),
                 ("x_source", ctypes.c_int32), ("after", ctypes.c_int32)]
+
+
+class StackTaskEx(ctypes.Structure):
+    """NexusGpuStackTaskEx (include/nexus_gpu.h): a stack task with fusions."""
+    _fields_ = [("W", _VP), ("rows", ctypes.c_uint64), ("cols", ctypes.c_uint64), ("y", _VP),
+                ("x_source", ctypes.c_int32), ("after", ctypes.c_int32), ("x_source2", ctypes.c_int32),
+                ("residual_source", ctypes.c_int32), ("norm_weight", _VP), ("norm_eps", ctypes.c_float)]
 
 
 _lib = None

@@ -871,6 +871,7 @@ struct StackHandle {
     int n_tasks = 0;
     int world = 1, rank = 0;
     bool connected = true;  // sharded stacks need nexus_gpu_stack_connect first
+    bool fused = false;     // some task has a norm, a SwiGLU or a residual: the kernel variant with them
     uint64_t fingerprint = 0;
     StackParams params{};
     StackTask* d_tasks = nullptr;
@@ -888,19 +889,21 @@ struct StackBlob {
 };
 constexpr uint32_t kStackBlobMagic = 0x4e535442u;  // "NSTB"
 
-template <class F, int G>
+template <class F, int G, bool FX>
 int32_t stack_kernel_attrs(const Device& d, size_t smem) {
-    CUDA_TRY(cudaFuncSetAttribute(gemv_stack_kernel<F, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, d.smem_optin));
+    CUDA_TRY(cudaFuncSetAttribute(gemv_stack_kernel<F, G, FX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  d.smem_optin));
     int per_sm = 0;
-    CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_stack_kernel<F, G>, kGemvThreads, smem));
+    CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_stack_kernel<F, G, FX>, kGemvThreads, smem));
     if (per_sm < 1) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "stack kernel cannot be resident (smem %zu)", smem);
     return NEXUS_GPU_SUCCESS;
 }
 
 template <class F>
-int32_t stack_attrs_for(int group, const Device& d, size_t smem) {
-    if (F::kGroup > 1 && group == F::kGroup) return stack_kernel_attrs<F, F::kGroup>(d, smem);
-    return stack_kernel_attrs<F, 1>(d, smem);
+int32_t stack_attrs_for(int group, bool fused, const Device& d, size_t smem) {
+    const bool grouped = F::kGroup > 1 && group == F::kGroup;
+    if (fused) return grouped ? stack_kernel_attrs<F, F::kGroup, true>(d, smem) : stack_kernel_attrs<F, 1, true>(d, smem);
+    return grouped ? stack_kernel_attrs<F, F::kGroup, false>(d, smem) : stack_kernel_attrs<F, 1, false>(d, smem);
 }
 
 template <class F>
@@ -915,10 +918,14 @@ int32_t stack_launch_for(const StackHandle& h, cudaStream_t st) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (F::kGroup > 1 && h.group == F::kGroup)
-        CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stack_kernel<F, F::kGroup>, h.params));
-    else
-        CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stack_kernel<F, 1>, h.params));
+    const bool grouped = F::kGroup > 1 && h.group == F::kGroup;
+    if (h.fused) {
+        if (grouped) CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stack_kernel<F, F::kGroup, true>, h.params));
+        else CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stack_kernel<F, 1, true>, h.params));
+    } else {
+        if (grouped) CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stack_kernel<F, F::kGroup, false>, h.params));
+        else CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stack_kernel<F, 1, false>, h.params));
+    }
     return NEXUS_GPU_SUCCESS;
 }
 
@@ -941,7 +948,8 @@ inline void shard_rows(uint64_t N, int world, int rank, uint64_t& r0, uint64_t& 
     r1 = N * (uint64_t)(rank + 1) / (uint64_t)world;
 }
 
-uint64_t stack_fingerprint(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n, uint64_t input_cols, int world) {
+uint64_t stack_fingerprint(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t n, uint64_t input_cols,
+                           int world) {
     uint64_t h = 1469598103934665603ull;
     auto mix = [&](uint64_t v) {
         for (int i = 0; i < 8; ++i) {
@@ -958,11 +966,17 @@ uint64_t stack_fingerprint(uint32_t dtype, const NexusGpuStackTask* tasks, uint3
         mix(tasks[i].cols);
         mix((uint64_t)(int64_t)tasks[i].x_source);
         mix((uint64_t)(int64_t)tasks[i].after);
+        mix((uint64_t)(int64_t)tasks[i].x_source2);
+        mix((uint64_t)(int64_t)tasks[i].residual_source);
+        mix(tasks[i].norm_weight != nullptr);
+        uint32_t eb;
+        memcpy(&eb, &tasks[i].norm_eps, 4);
+        mix(tasks[i].norm_weight ? eb : 0u);
     }
     return h;
 }
 
-int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n, uint64_t input_cols, int world,
+int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t n, uint64_t input_cols, int world,
                      int rank, void** out) {
     if (!out || (!tasks && n)) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null argument");
     *out = nullptr;
@@ -987,7 +1001,7 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n,
     int group = -1;
     size_t slot = 0;
     for (uint32_t i = 0; i < n; ++i) {
-        const NexusGpuStackTask& u = tasks[i];
+        const NexusGpuStackTaskEx& u = tasks[i];
         if ((rc = check_shape(dtype, u.rows, u.cols, f))) return fail(rc, "task %u: %s", i, t_last_error.c_str());
         if (!u.W || u.rows == 0) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u: null W or no rows", i);
         if (sharded ? u.y != nullptr : u.y == nullptr)
@@ -1004,6 +1018,21 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n,
         if (!sharded && u.x_source >= 0 && ((uintptr_t)tasks[u.x_source].y & 15) != 0)
             return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %d feeds x but its y is not 16-byte aligned",
                         u.x_source);
+        if (u.x_source2 != -1 &&
+            (u.x_source2 < 0 || u.x_source2 >= (int32_t)i || tasks[u.x_source2].rows != u.cols || u.x_source < 0))
+            return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH,
+                        "task %u: x_source2 %d must be an earlier task of %llu rows beside a task x_source", i,
+                        u.x_source2, (unsigned long long)u.cols);
+        if (!sharded && u.x_source2 >= 0 && ((uintptr_t)tasks[u.x_source2].y & 15) != 0)
+            return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %d feeds x2 but its y is not 16-byte aligned",
+                        u.x_source2);
+        if (u.residual_source < -2 || u.residual_source >= (int32_t)i ||
+            (u.residual_source == -1 && input_cols != u.rows) ||
+            (u.residual_source >= 0 && tasks[u.residual_source].rows != u.rows))
+            return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "task %u: residual_source %d does not give %llu values", i,
+                        u.residual_source, (unsigned long long)u.rows);
+        if (u.norm_weight && ((uintptr_t)u.norm_weight & 15) != 0)
+            return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u: norm_weight not 16-byte aligned", i);
         uint64_t r0 = 0, r1 = u.rows;
         if (sharded) shard_rows(u.rows, world, rank, r0, r1);
         if (r1 <= r0 || u.rows > (uint64_t)INT32_MAX)
@@ -1061,11 +1090,15 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n,
     h->connected = !sharded;
     h->fingerprint = stack_fingerprint(dtype, tasks, n, input_cols, world);
     h->smem = kStackSmemHeader + x_smem + (size_t)ns * slot;
+    for (uint32_t i = 0; i < n; ++i)
+        h->fused |= tasks[i].x_source2 >= 0 || tasks[i].residual_source != -2 || tasks[i].norm_weight != nullptr;
 
     std::vector<char> waited_for(n, 0);
     for (uint32_t i = 0; i < n; ++i) {
         if (tasks[i].after >= 0) waited_for[tasks[i].after] = 1;
         if (tasks[i].x_source >= 0) waited_for[tasks[i].x_source] = 1;
+        if (tasks[i].x_source2 >= 0) waited_for[tasks[i].x_source2] = 1;
+        if (tasks[i].residual_source >= 0) waited_for[tasks[i].residual_source] = 1;
     }
     StackLayout& lay = h->lay;
     lay.done = 0;
@@ -1105,10 +1138,20 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n,
         T.after = tasks[i].after;
         T.signal = waited_for[i];
         T.sig_ord = T.signal ? n_signal++ : -1;
-        // same input, same plan (same cols), and no new ordering dependency:
-        // keep the previous task's x slices and skip the wait and the staging
+        T.x2 = tasks[i].x_source2 < 0 ? nullptr : h->outputs[tasks[i].x_source2];
+        T.src2 = tasks[i].x_source2 < 0 ? -1 : tasks[i].x_source2;
+        T.norm_w = tasks[i].norm_weight;
+        T.norm_eps = tasks[i].norm_eps;
+        T.res = tasks[i].residual_source >= 0 ? h->outputs[tasks[i].residual_source] : nullptr;
+        T.res_input = tasks[i].residual_source == -1;
+        T.res_src = tasks[i].residual_source >= 0 ? tasks[i].residual_source : -1;
+        // same input (and fusions), same plan (same cols), and no new ordering
+        // dependency: keep the previous task's x slices, skip the wait and the staging
         T.reuse_x = i > 0 && tasks[i].x_source == tasks[i - 1].x_source && tasks[i].cols == tasks[i - 1].cols &&
-                    (tasks[i].after == -1 || tasks[i].after == tasks[i - 1].after);
+                    tasks[i].x_source2 == tasks[i - 1].x_source2 && tasks[i].norm_weight == tasks[i - 1].norm_weight &&
+                    (!tasks[i].norm_weight || memcmp(&tasks[i].norm_eps, &tasks[i - 1].norm_eps, 4) == 0) &&
+                    (tasks[i].after == -1 || tasks[i].after == tasks[i - 1].after) &&
+                    (tasks[i].residual_source < 0 || tasks[i].residual_source == tasks[i - 1].residual_source);
         // Consumer warps drift apart only within an x group (they meet at every
         // group head), so a group holds fewer signalled tasks than there are
         // shared completion slots: warps never post to a slot's next round
@@ -1145,10 +1188,10 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n,
     P.peer_block[rank] = h->d_block;
 
     switch (dtype) {
-        case NEXUS_GPU_GGUF_Q4_0: rc = stack_attrs_for<FmtQ4_0>(group, *d, h->smem); break;
-        case NEXUS_GPU_GGUF_Q8_0: rc = stack_attrs_for<FmtQ8_0>(group, *d, h->smem); break;
-        case NEXUS_GPU_GGUF_Q5_K: rc = stack_attrs_for<FmtQ5_K>(group, *d, h->smem); break;
-        default: rc = stack_attrs_for<FmtQ6_K>(group, *d, h->smem); break;
+        case NEXUS_GPU_GGUF_Q4_0: rc = stack_attrs_for<FmtQ4_0>(group, h->fused, *d, h->smem); break;
+        case NEXUS_GPU_GGUF_Q8_0: rc = stack_attrs_for<FmtQ8_0>(group, h->fused, *d, h->smem); break;
+        case NEXUS_GPU_GGUF_Q5_K: rc = stack_attrs_for<FmtQ5_K>(group, h->fused, *d, h->smem); break;
+        default: rc = stack_attrs_for<FmtQ6_K>(group, h->fused, *d, h->smem); break;
     }
     if (rc) {
         stack_free(h);
@@ -1490,10 +1533,37 @@ NEXUS_GPU_API int32_t nexus_gpu_gemv_noalloc(const void* dW, uint32_t dtype, con
     return run_gemv(*d, dW, dtype, dX, x_dtype, dY, M, rows, cols, scratch, static_cast<cudaStream_t>(stream), false);
 }
 
+// The plain stack tasks as fused-task descriptions with no fusions.
+std::vector<NexusGpuStackTaskEx> plain_tasks(const NexusGpuStackTask* tasks, uint32_t n) {
+    std::vector<NexusGpuStackTaskEx> v(tasks ? n : 0);
+    for (size_t i = 0; i < v.size(); ++i) {
+        v[i].W = tasks[i].W;
+        v[i].rows = tasks[i].rows;
+        v[i].cols = tasks[i].cols;
+        v[i].y = tasks[i].y;
+        v[i].x_source = tasks[i].x_source;
+        v[i].after = tasks[i].after;
+        v[i].x_source2 = -1;
+        v[i].residual_source = -2;
+        v[i].norm_weight = nullptr;
+        v[i].norm_eps = 0.0f;
+    }
+    return v;
+}
+
 NEXUS_GPU_API int32_t nexus_gpu_stack_create(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n_tasks,
                                              uint64_t input_cols, void** out_stack) {
     t_last_error.clear();
-    return stack_create(dtype, tasks, n_tasks, input_cols, 1, 0, out_stack);
+    const auto ex = plain_tasks(tasks, n_tasks);
+    return stack_create(dtype, tasks ? ex.data() : nullptr, n_tasks, input_cols, 1, 0, out_stack);
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_stack_create_ex(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t n_tasks,
+                                                uint64_t input_cols, uint32_t world, uint32_t rank, void** out_stack) {
+    t_last_error.clear();
+    if (world < 1 || world > (uint32_t)kMaxWorld || rank >= world)
+        return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "rank %u of world %u (1..%d GPUs)", rank, world, kMaxWorld);
+    return stack_create(dtype, tasks, n_tasks, input_cols, (int)world, (int)rank, out_stack);
 }
 
 NEXUS_GPU_API int32_t nexus_gpu_stack_create_sharded(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n_tasks,
@@ -1503,7 +1573,8 @@ NEXUS_GPU_API int32_t nexus_gpu_stack_create_sharded(uint32_t dtype, const Nexus
     if (world < 2) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "a sharded stack needs 2..%d ranks", kMaxWorld);
     if (world > (uint32_t)kMaxWorld || rank >= world)
         return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "rank %u of world %u (2..%d GPUs)", rank, world, kMaxWorld);
-    return stack_create(dtype, tasks, n_tasks, input_cols, (int)world, (int)rank, out_stack);
+    const auto ex = plain_tasks(tasks, n_tasks);
+    return stack_create(dtype, tasks ? ex.data() : nullptr, n_tasks, input_cols, (int)world, (int)rank, out_stack);
 }
 
 NEXUS_GPU_API int32_t nexus_gpu_stack_export(void* stack, void* blob, uint64_t* blob_bytes) {

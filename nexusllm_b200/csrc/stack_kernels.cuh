@@ -57,6 +57,15 @@ struct StackTask {
     int reuse_x;                         // same input and plan as the previous task: keep its x
     int signal;                          // a later task waits for this one: count it on the counters
     int sig_ord;                         // ordinal among the signalled tasks (shared completion slot)
+    // fusions around the GEMV (TransformerOps, include/transformer_ops.hpp:23-44,86-95;
+    // the decode layer in src/forward_pass.cpp:504-562)
+    const float* x2;                     // SwiGLU: x = silu(x) * x2 (x the gate's output, x2 the up's), or null
+    int src2;                            // x2's task, or -1
+    const float* norm_w;                 // RMSNorm of x with these fp32 weights, or null
+    float norm_eps;
+    const float* res;                    // residual added to every output row (full length), or null
+    int res_input;                       // the residual is the stack input
+    int res_src;                         // the residual's task, or -1 (waited for with the input)
 };
 
 struct StackParams {
@@ -122,7 +131,8 @@ __device__ __noinline__ bool wait_count_bounded(const unsigned long long* ctr, u
 
 constexpr int kSigSlots = 16;  // shared per-task completion counters (cumulative, by signal ordinal)
 // mbarriers, a broadcast flag, the end-of-run post count, the completion slots
-constexpr int kStackBarBytes = 16 * kMaxStages + 32 + 4 * kSigSlots;
+// + RMSNorm partial sums and per-warp scales
+constexpr int kStackBarBytes = 16 * kMaxStages + 32 + 4 * kSigSlots + 4 * 16 + 4 * 16;
 constexpr int kStackSmemHeader = ((kStackBarBytes + 127) / 128) * 128 + kSmemHeader - kBarBytes;
 
 __device__ __forceinline__ void red_release_shared_add(uint32_t addr, uint32_t v) {
@@ -233,10 +243,33 @@ __device__ __forceinline__ int ld_task_i32(const int* p) {
     return v;
 }
 
+// The residual vector of task T (the stack input, a task's output, or null).
+__device__ __forceinline__ const float* task_residual(const StackParams& P, const StackTask* T) {
+    return ld_task_i32(&T->res_input) ? P.x_in : reinterpret_cast<const float*>(ld_task_u64(&T->res));
+}
+
+// Row r's residual, loaded when the row starts so that the L2 latency
+// overlaps its dot product (written earlier in this run, possibly by peers).
+__device__ __forceinline__ float residual_of(const StackParams& P, const StackTask* T, int r) {
+    const float* res = task_residual(P, T);
+    return res ? __ldcg(res + (uint64_t)ld_task_i32(&T->row_off) + (uint64_t)r) : 0.0f;
+}
+
 // Write row r (of this rank's slice) of task T: this rank's output and --
-// sharded -- every peer's copy (plain stores over NVLink).
-__device__ __forceinline__ void put_row(const StackParams& P, const StackTask* T, int r, float v) {
+// sharded -- every peer's copy (plain stores over NVLink).  v is the row's
+// dot product; in the fused variant (FX) the RMSNorm scale of the task's
+// input (1 without one) and the residual rv (residual_of) are applied here:
+// y = v * scale + rv.  The scale is read from shared memory at the store, so
+// that it holds no register through the row loop.
+template <bool FX>
+__device__ __forceinline__ void put_row(const StackParams& P, const StackTask* T, int r, float v,
+                                        const volatile float* scale, float rv) {
     const uint64_t g = (uint64_t)ld_task_i32(&T->row_off) + (uint64_t)r;  // global row
+    if constexpr (FX) {
+        const float sc = *scale;
+        if (sc != 1.0f) v = __fmul_rn(v, sc);
+        if (task_residual(P, T)) v = __fadd_rn(v, rv);
+    }
     reinterpret_cast<float*>(ld_task_u64(&T->y))[g] = v;
     if (P.world > 1) {
         const uint64_t y_off = ld_task_u64(&T->y_off);
@@ -246,7 +279,9 @@ __device__ __forceinline__ void put_row(const StackParams& P, const StackTask* T
     }
 }
 
-template <class F, int G>
+// FX: the variant with the fused RMSNorm / SwiGLU / residual; stacks without
+// them run the variant that has none of their code.
+template <class F, int G, bool FX>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const StackParams P) {
     using XT = typename std::conditional<F::kIntX, XInt, XF16>::type;
     static_assert(F::kIntX, "the stack kernel serves the integer formats");
@@ -257,6 +292,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
     volatile int* s_flag = reinterpret_cast<volatile int*>(smem + 16 * kMaxStages);  // warp-0 verdicts
     const uint32_t tend = sbase + 16 * kMaxStages + 16;  // consumer warps done with every task
     const uint32_t tdone = tend + 16;                     // [kSigSlots] u32 task completion posts
+    float* s_norm = reinterpret_cast<float*>(smem + 16 * kMaxStages + 32 + 4 * kSigSlots);  // [16] RMSNorm partials
+    volatile float* s_scale = s_norm + 16;  // [16] each warp's copy of its group's RMSNorm scale
     constexpr int kHdr = ((kStackBarBytes + 127) / 128) * 128;
     float* slots = reinterpret_cast<float*>(smem + kHdr);
     int* counters = reinterpret_cast<int*>(smem + kHdr + kMaxSlots * 4);  // [kMaxStages][kMaxStageRows]
@@ -426,20 +463,27 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
         bool has[kMaxJ];
         lane_items<G>(lane, sg, SW, J, NW, wi, has);
         if (tid == 0) {  // the input's CTAs (all ranks) are done, and the ordering dependency
-            const int src = __ldg(&H.src), after = __ldg(&H.after);
+            const int src = __ldg(&H.src), src2 = __ldg(&H.src2), after = __ldg(&H.after), rs = __ldg(&H.res_src);
             const unsigned long long target = (run + 1) * (unsigned long long)P.world * (unsigned long long)n_cta;
             int ok = *reinterpret_cast<volatile unsigned*>(P.abort_flag) == 0;  // poisoned by an earlier run
             if (ok && src >= 0) ok = wait_count_bounded(&P.done[src * kCounterStride], target, P.abort_flag, sys);
+            if (ok && src2 >= 0) ok = wait_count_bounded(&P.done[src2 * kCounterStride], target, P.abort_flag, sys);
             if (ok && after >= 0) ok = wait_count_bounded(&P.done[after * kCounterStride], target, P.abort_flag, sys);
+            if (FX && ok && rs >= 0) ok = wait_count_bounded(&P.done[rs * kCounterStride], target, P.abort_flag, sys);
             __threadfence();
             s_flag[0] = ok;
         }
         consumer_bar();  // also: every warp is done with the previous group's x staging
         bool failed = s_flag[0] == 0;
-        if (!failed) {   // read x (L2) and quantize it, two lanes per 32-element block
+        const float4* nw =
+            FX ? reinterpret_cast<const float4*>(__ldg(reinterpret_cast<const unsigned long long*>(&H.norm_w))) : nullptr;
+        if (!failed) {   // read x (L2), apply the fusions, quantize, two lanes per 32-element block
             const float4* xv = reinterpret_cast<const float4*>(__ldg(reinterpret_cast<const unsigned long long*>(&H.x)));
             if (xv == nullptr) xv = reinterpret_cast<const float4*>(P.x_in);
+            const float4* xv2 =
+                FX ? reinterpret_cast<const float4*>(__ldg(reinterpret_cast<const unsigned long long*>(&H.x2))) : nullptr;
             const int nxb = K / 32, nxbp = x_stage_planes_len(K), hf = lane & 1;
+            float ss = 0.0f;  // RMSNorm: sum of squares of this thread's elements, in a fixed order
             for (int base = 0; base < nxb; base += kConsumers / 2) {
                 const int b = base + (tid >> 1);
                 float e[16];
@@ -451,13 +495,55 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                     e[4 * q + 2] = v.z;
                     e[4 * q + 3] = v.w;
                 }
+                // SwiGLU (transformer_ops.hpp:86-95): silu(gate) * up.  Every CTA computes the
+                // whole vector, so with the __expf / __fdividef intrinsics (relative error ~1e-6,
+                // far below the 16-bit fixed-point quantization that follows)
+                if (xv2 != nullptr && b < nxb) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float4 u = __ldcg(xv2 + 8 * b + 4 * hf + q);
+                        const float uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const float g = e[4 * q + k];
+                            e[4 * q + k] = __fmul_rn(__fdividef(g, __fadd_rn(1.0f, __expf(-g))), uu[k]);
+                        }
+                    }
+                }
+                if (nw != nullptr && b < nxb) {  // RMSNorm: sum x^2 here, quantize x * w; 1/rms scales the rows
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float4 w = __ldg(nw + 8 * b + 4 * hf + q);
+                        const float ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            ss = fmaf(e[4 * q + k], e[4 * q + k], ss);
+                            e[4 * q + k] = __fmul_rn(e[4 * q + k], ww[k]);
+                        }
+                    }
+                }
                 quantize_x_pair(e, hf, b < nxb, xs, nxbp, b);
+            }
+            if (nw != nullptr) {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+                if (lane == 0) s_norm[warp] = ss;
             }
         }
         if (consumer_bar_any(failed)) {  // every consumer leaves together after a failed wait
             stop = true;
             break;
         }
+        // RMSNorm scale of this group's input: 1 / sqrt(sum x^2 / K + eps)
+        // (transformer_ops.hpp:23-30), the warps' sums added in warp order
+        float gscale = 1.0f;
+        if (nw != nullptr) {
+            float tot = 0.0f;
+#pragma unroll 1
+            for (int w = 0; w < kConsumerWarps; ++w) tot = __fadd_rn(tot, s_norm[w]);
+            gscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), __ldg(&H.norm_eps))));
+        }
+        if (FX && lane == 0) s_scale[warp] = gscale;  // read back by this lane at its row stores
         XT X[kMaxJ];
         {
             const int nxbp = x_stage_planes_len(K);
@@ -490,11 +576,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                     if (grp >= n_grp) rl = nr;  // the 15 - S*n_grp warps past the last row group idle
                     for (; rl < nr; rl += n_grp) {
                         const uint32_t row = base + (uint32_t)(rl * rbytes);
+                        float rv = 0.0f;
+                        if (FX && lane == 0) rv = residual_of(P, &T, r0 + rl);
                         float acc = row_partial<F, G>(row, wi, has, X);
 #pragma unroll
                         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
                         if (S == 1) {
-                            if (lane == 0) put_row(P, &T, r0 + rl, acc);
+                            if (lane == 0) put_row<FX>(P, &T, r0 + rl, acc, s_scale + warp, rv);
                         } else if (lane == 0) {
                             float* sl = slots + s * P.slot_stride + rl * S;
                             sl[sg] = acc;
@@ -504,7 +592,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                                 __threadfence_block();
                                 float v = 0.f;
                                 for (int k = 0; k < S; ++k) v += *(volatile float*)(sl + k);
-                                put_row(P, &T, r0 + rl, v);
+                                put_row<FX>(P, &T, r0 + rl, v, s_scale + warp, rv);
                                 counters[s * kMaxStageRows + rl] = 0;
                             }
                         }

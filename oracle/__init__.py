@@ -104,6 +104,23 @@ class _Lib:
         self._fn(self._d + "fp8_e4m3", [_VP, _VP, _SZ, ctypes.c_float])(_ptr(data), _ptr(out), count, scale)
         return out
 
+    # --------------------------- decode-layer ops (TransformerOps::rmsnorm, swiglu)
+    def rmsnorm(self, x: np.ndarray, w, eps: float) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros_like(x)
+        wp = None if w is None else _ptr(np.ascontiguousarray(w, np.float32))
+        name = "oracle_rmsnorm" if self._g.startswith("oracle") else "ref_rmsnorm"
+        self._fn(name, [_VP, _VP, _VP, _SZ, ctypes.c_float])(_ptr(x), wp, _ptr(out), x.size, eps)
+        return out
+
+    def swiglu(self, g: np.ndarray, u: np.ndarray) -> np.ndarray:
+        g = np.ascontiguousarray(g, np.float32)
+        u = np.ascontiguousarray(u, np.float32)
+        out = np.zeros_like(g)
+        name = "oracle_swiglu" if self._g.startswith("oracle") else "ref_swiglu"
+        self._fn(name, [_VP, _VP, _VP, _SZ])(_ptr(g), _ptr(u), _ptr(out), g.size)
+        return out
+
     def dequantize(self, dtype: int, W: np.ndarray, count: int) -> np.ndarray:
         name = _NAMES[int(dtype)]
         out = np.zeros(count, np.float32)

@@ -409,6 +409,34 @@ void oracle_gemv_fp8(const uint8_t* W, const float* x, float* y, size_t rows, si
     }
 }
 
+/* ------------------------------------------- decode-layer ops beside the GEMV */
+
+/* TransformerOps::rmsnorm (include/transformer_ops.hpp:23-44), fp32 weights or
+ * none: sum_sq += x*x left to right (a separate multiply and add in the
+ * reference build, checked against it), inv_rms = 1 / sqrt(sum_sq / dim +
+ * eps), out = x * inv_rms * w. */
+void oracle_rmsnorm(const float* x, const float* w, float* out, size_t dim, float eps) {
+    float sum_sq = 0.0f;
+    for (size_t i = 0; i < dim; ++i) {
+        const float p = x[i] * x[i];
+        sum_sq = sum_sq + p;
+    }
+    const float inv_rms = 1.0f / sqrtf((sum_sq / (float)dim) + eps);
+    for (size_t i = 0; i < dim; ++i) {
+        const float t = x[i] * inv_rms;
+        out[i] = w ? t * w[i] : t;
+    }
+}
+
+/* TransformerOps::silu / swiglu (include/transformer_ops.hpp:86-95):
+ * out = (g / (1 + exp(-g))) * u. */
+void oracle_swiglu(const float* g, const float* u, float* out, size_t dim) {
+    for (size_t i = 0; i < dim; ++i) {
+        const float s = g[i] / (1.0f + expf(-g[i]));
+        out[i] = s * u[i];
+    }
+}
+
 /* Dispatch by NexusLLM DataType value (include/nexus_common.hpp:244-260), as
  * TransformerOps::matmul_vec_dispatch does (include/transformer_ops.hpp:157-173).
  * Returns 0 on success, -3 (ERROR_FORMAT_UNSUPPORTED) for other types. */

@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "quantization.hpp"
+#include "transformer_ops.hpp"
 
 #if defined(_OPENMP)
 #include <omp.h>
@@ -98,6 +99,15 @@ REF_API void ref_dequantize_int4_awq(const uint32_t* packed, const float* scales
 }
 REF_API void ref_dequantize_fp8_e4m3(const uint8_t* in, float* out, size_t count, float scale) {
     QuantizationKernel::dequantize_fp8_e4m3(in, out, count, scale);
+}
+
+// TransformerOps (include/transformer_ops.hpp:23-44,86-95): the decode
+// layer's RMSNorm and SwiGLU, header-only in the reference.
+REF_API void ref_rmsnorm(const float* x, const float* w, float* out, size_t dim, float eps) {
+    nexus::TransformerOps::rmsnorm(x, w, out, dim, eps);
+}
+REF_API void ref_swiglu(const float* g, const float* u, float* out, size_t dim) {
+    nexus::TransformerOps::swiglu(g, u, out, dim);
 }
 
 // Bytes of one weight row for a NexusLLM DataType value (nexus_common.hpp:244-260).

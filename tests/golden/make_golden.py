@@ -143,6 +143,24 @@ def int4_fp8(ref, g) -> None:
         g[key + "/y"] = ref.gemv_fp8(W, x, rows, cols, 0.0625)
 
 
+def layer_ops(ref, g) -> None:
+    """TransformerOps::rmsnorm / swiglu (include/transformer_ops.hpp:23-44,86-95),
+    the decode layer's ops around the GEMV, from the reference build."""
+    r = np.random.default_rng(9990)
+    for j, (n, scale, eps) in enumerate([(4096, 1.0, 1e-5), (512, 300.0, 1e-6), (33, 1e-3, 1e-5), (14336, 7.0, 1e-5)]):
+        x = (r.standard_normal(n) * scale).astype(np.float32)
+        w = (1.0 + 0.1 * r.standard_normal(n)).astype(np.float32)
+        key = f"ops/rmsnorm/{j}"
+        g[key + "/x"], g[key + "/w"], g[key + "/eps"] = x, w, np.array([eps], np.float32)
+        g[key + "/out"] = ref.rmsnorm(x, w, eps)
+        g[key + "/out_now"] = ref.rmsnorm(x, None, eps)
+    gate = np.concatenate([(r.standard_normal(4000) * 6).astype(np.float32),
+                           np.array([-100, -88, -87, 0, -0.0, 80, 100, 1e-30, -1e-30], np.float32)])
+    up = r.standard_normal(gate.size).astype(np.float32)
+    g["ops/swiglu/g"], g["ops/swiglu/u"] = gate, up
+    g["ops/swiglu/out"] = ref.swiglu(gate, up)
+
+
 def main() -> None:
     ref = oracle.reference()
     g = {}
@@ -193,6 +211,7 @@ def main() -> None:
         g[key + "/y"] = ref.gemv(int(dt), W, x, rows, cols)
 
     int4_fp8(ref, g)
+    layer_ops(ref, g)
     np.savez_compressed(OUT, **g)
     print(f"wrote {OUT}: {len(g)} arrays, {os.path.getsize(OUT)} bytes")
 

@@ -112,3 +112,15 @@ def test_workspace_size_grows_with_cols():
     assert L.nexus_gpu_gemv_int4_workspace_size(8192) > L.nexus_gpu_gemv_int4_workspace_size(4096)
     assert isinstance(L.nexus_gpu_gemv_int4_workspace_size(0), int)
     _ = ctypes  # the entry points bind through _native.SIGNATURES
+
+
+def test_layer_ops_bit_exact(golden, port):
+    """RMSNorm and SwiGLU restated in the oracle against the reference build
+    (TransformerOps, include/transformer_ops.hpp:23-44,86-95)."""
+    for j in range(4):
+        key = f"ops/rmsnorm/{j}"
+        x, w, eps = golden[key + "/x"], golden[key + "/w"], float(golden[key + "/eps"][0])
+        np.testing.assert_array_equal(_bits(port.rmsnorm(x, w, eps)), _bits(golden[key + "/out"]), err_msg=key)
+        np.testing.assert_array_equal(_bits(port.rmsnorm(x, None, eps)), _bits(golden[key + "/out_now"]), err_msg=key)
+    np.testing.assert_array_equal(_bits(port.swiglu(golden["ops/swiglu/g"], golden["ops/swiglu/u"])),
+                                  _bits(golden["ops/swiglu/out"]))
