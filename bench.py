@@ -287,6 +287,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-formats", action="store_true",
                     help="skip the INT4-AWQ / FP8-E4M3 per-shape GEMV timings")
+    ap.add_argument("--no-gguf", action="store_true",
+                    help="skip the GGUF file -> device upload measurement")
     ap.add_argument("--no-fused", action="store_true",
                     help="skip the decode stack with RMSNorm / SwiGLU / residual fused in")
     ap.add_argument("--no-batched", action="store_true",
@@ -303,7 +305,7 @@ def main():
     if args.model == "70b":
         # the 70B configuration is the batch-1 sharded stack; batched points,
         # per-format timings and the host-weight path stay with the 8B headline
-        args.no_batched = args.no_formats = args.no_fused = True
+        args.no_batched = args.no_formats = args.no_fused = args.no_gguf = True
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
@@ -449,6 +451,8 @@ def main():
             extra["int4_awq_fp8"] = other_formats(torch, L, stream, dev, timed, peak)
         if not args.no_fused:
             extra["fused_decode_stack"] = fused_decode_stack(torch, L, layers, head, h0, stream, dev, timed, args, peak)
+        if not args.no_gguf:
+            extra["gguf_upload"] = gguf_upload(torch, L, dev)
         del stack_graph
         L.nexus_gpu_stack_destroy(stack)
     else:
@@ -650,8 +654,9 @@ def fused_decode_stack(torch, L, layers, head, h0, stream, dev, timed, args, pea
     """The same weights as the headline, with the reference decode layer's
     dataflow (src/forward_pass.cpp:504-562) fused into ONE stack launch:
     RMSNorm -> q, k, v; o (x = q, standing in for attention) + residual;
-    RMSNorm -> gate, up; SwiGLU -> down + residual; final RMSNorm -> LM head
-    (nexus_gpu_stack_create_ex).  Norm weights ~ 1 + N(0, 0.1^2)."""
+    RMSNorm -> gate+up pair with the SwiGLU epilogue; down + residual; final
+    RMSNorm -> LM head (nexus_gpu_stack_create_ex, 6 tasks per layer).  Norm
+    weights ~ 1 + N(0, 0.1^2)."""
     import ctypes
 
     from nexusllm_b200 import _native
@@ -665,14 +670,17 @@ def fused_decode_stack(torch, L, layers, head, h0, stream, dev, timed, args, pea
         b = len(tasks)
         na, nf = norm(), norm()
         keep += [na, nf]
-        spec = [("q", prev, -1, -2, na), ("k", prev, -1, -2, na), ("v", prev, -1, -2, na), ("o", b, -1, prev, None),
-                ("gate", b + 3, -1, -2, nf), ("up", b + 3, -1, -2, nf), ("down", b + 4, b + 5, b + 3, None)]
-        for (name, src, src2, res, nw), (_, n, k) in zip(spec, LAYER_SHAPES):
+        spec = [("q", prev, -2, na, None), ("k", prev, -2, na, None), ("v", prev, -2, na, None),
+                ("o", b, prev, None, None), ("gate", b + 3, -2, nf, "up"), ("down", b + 4, b + 3, None, None)]
+        shapes = {name: (n, k) for name, n, k in LAYER_SHAPES}
+        for name, src, res, nw, pair in spec:
+            n, k = shapes[name]
             y = torch.empty(n, dtype=torch.float32, device=dev)
             keep.append(y)
-            tasks.append(_native.StackTaskEx(mats[name].data_ptr(), n, k, y.data_ptr(), src, -1, src2, res,
-                                             None if nw is None else nw.data_ptr(), eps))
-        prev = b + 6
+            tasks.append(_native.StackTaskEx(mats[name].data_ptr(), n, k, y.data_ptr(), src, -1, -1, res,
+                                             None if nw is None else nw.data_ptr(), eps,
+                                             None if pair is None else mats[pair].data_ptr()))
+        prev = b + 5
     no = norm()
     y = torch.empty(VOCAB, dtype=torch.float32, device=dev)
     keep += [no, y]
@@ -699,8 +707,108 @@ def fused_decode_stack(torch, L, layers, head, h0, stream, dev, timed, args, pea
     L.nexus_gpu_stack_destroy(h)
     return {"ms_per_step": round(ms, 4), "tokens_per_s": round(1e3 / ms, 2), "value": round(gbs, 1), "unit": "GB/s",
             "pct_of_measured_hbm": round(100 * gbs / peak, 2), "steps": reps,
-            "dataflow": "RMSNorm->q,k,v; o(x=q)+residual; RMSNorm->gate,up; SwiGLU->down+residual; RMSNorm->head",
+            "dataflow": "RMSNorm->q,k,v; o(x=q)+residual; RMSNorm->gate+up pair, SwiGLU epilogue; down+residual; "
+                        "RMSNorm->head",
             "launches_per_step": 1}
+
+
+def gguf_upload(torch, L, dev):
+    """The GGUF load path: a Llama-3-8B-shaped Q4_0 GGUF file (token_embd,
+    32 layers x 7 matrices, output; tensor data repeats one 64 MiB random
+    block) is written to a temporary directory, parsed (nexus_gpu_gguf_open)
+    and uploaded into one preallocated device image (nexus_gpu_gguf_upload:
+    host threads fill pinned staging buffers from the mapping while the
+    previous pieces copy).  The file was just written, so the page cache is
+    warm.  Beside it: the pinned host-to-device copy rate (the link's
+    ceiling) and per-tensor pageable copies from a numpy memmap of the file
+    (the plain way: torch .to(device) per tensor)."""
+    import ctypes
+    import shutil
+    import tempfile
+    import time
+
+    import numpy as np
+
+    from nexusllm_b200 import _native, gguf
+
+    block = np.random.default_rng(3).integers(0, 256, 64 << 20, dtype=np.uint8).tobytes()
+
+    def filler(n):
+        def fn(f):
+            left = n
+            while left:
+                k = min(left, len(block))
+                f.write(block[:k])
+                left -= k
+        return (n, fn)
+
+    q4 = lambda rows, cols: filler(rows * cols // 32 * 18)  # noqa: E731
+    tensors = [("token_embd.weight", gguf.GGML_Q4_0, [HIDDEN, VOCAB], q4(VOCAB, HIDDEN))]
+    names = {"q": "attn_q", "k": "attn_k", "v": "attn_v", "o": "attn_output", "gate": "ffn_gate", "up": "ffn_up",
+             "down": "ffn_down"}
+    for l in range(LAYERS):
+        for name, n, k in LAYER_SHAPES:
+            tensors.append((f"blk.{l}.{names[name]}.weight", gguf.GGML_Q4_0, [k, n], q4(n, k)))
+    tensors.append(("output.weight", gguf.GGML_Q4_0, [HIDDEN, VOCAB], q4(VOCAB, HIDDEN)))
+    meta = [("general.architecture", gguf.STRING, "llama"), ("llama.embedding_length", gguf.U32, HIDDEN),
+            ("llama.block_count", gguf.U32, LAYERS), ("llama.feed_forward_length", gguf.U32, FFN)]
+    d = tempfile.mkdtemp(prefix="nexus_gguf_")
+    path = os.path.join(d, "llama3-8b-q4_0.gguf")
+    try:
+        t0 = time.perf_counter()
+        gguf.write_gguf(path, meta, tensors)
+        write_s = time.perf_counter() - t0
+        file_bytes = os.path.getsize(path)
+        with gguf.GGUFFile(path) as f:
+            idx = list(range(len(f.tensors)))
+            arr = (ctypes.c_uint64 * len(idx))(*idx)
+            offs = (ctypes.c_uint64 * len(idx))()
+            size = L.nexus_gpu_gguf_upload_size(f._h, arr, len(idx))
+            image = torch.empty(size, dtype=torch.uint8, device=dev)
+            st = torch.cuda.current_stream(dev).cuda_stream
+            times = []
+            for _ in range(4):  # the first call also makes the staging ring
+                torch.cuda.synchronize(dev)
+                t0 = time.perf_counter()
+                _native.check(L.nexus_gpu_gguf_upload(f._h, arr, len(idx), image.data_ptr(), size, offs, st))
+                times.append(time.perf_counter() - t0)
+            data_bytes = sum(t["bytes"] for t in f.tensors)
+            # spot check: first and last tensor on the device equal the file
+            mm = np.memmap(path, dtype=np.uint8, mode="r")
+            for i in (0, len(idx) - 1):
+                t = f.tensors[i]
+                dev_bytes = image[offs[i]:offs[i] + 4096].cpu().numpy()
+                if not np.array_equal(dev_bytes, mm[t["file_offset"]:t["file_offset"] + 4096]):
+                    raise RuntimeError("GGUF upload produced wrong bytes")
+            # plain per-tensor pageable copies
+            torch.cuda.synchronize(dev)
+            t0 = time.perf_counter()
+            for t in f.tensors:
+                torch.from_numpy(mm[t["file_offset"]:t["file_offset"] + t["bytes"]]).to(dev)
+            torch.cuda.synchronize(dev)
+            plain_s = time.perf_counter() - t0
+            del mm
+        host = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
+        dbuf = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        dbuf.copy_(host, non_blocking=True)
+        ev[0].record()
+        for _ in range(3):
+            dbuf.copy_(host, non_blocking=True)
+        ev[1].record()
+        torch.cuda.synchronize(dev)
+        pinned_gbs = 3 * (1 << 30) / (ev[0].elapsed_time(ev[1]) * 1e-3) / 1e9
+        del image, host, dbuf
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+    best = min(times[1:])
+    gbs = data_bytes / best / 1e9
+    return {"file_bytes": file_bytes, "tensor_bytes": data_bytes,
+            "tensors": len(tensors), "upload_s": round(best, 4), "upload_gbs": round(gbs, 2),
+            "first_upload_s": round(times[0], 4), "pinned_h2d_gbs": round(pinned_gbs, 2),
+            "frac_of_pinned_h2d": round(gbs / pinned_gbs, 3),
+            "plain_per_tensor_pageable_gbs": round(data_bytes / plain_s / 1e9, 2),
+            "write_file_s": round(write_s, 2), "page_cache": "warm (file just written)"}
 
 
 def build_stack_graph(torch, L, _native, layers, head, h0, stream, dev):

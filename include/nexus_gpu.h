@@ -252,7 +252,12 @@ NEXUS_GPU_API int32_t nexus_gpu_stack_create_sharded(uint32_t dtype, const Nexus
  *                   applied after the SwiGLU when both are given;
  *   residual_source -2 none, -1 the stack input, or an earlier task with as
  *                   many rows: y = GEMV + that vector (the residual adds of
- *                   src/forward_pass.cpp:539-541,558-561).
+ *                   src/forward_pass.cpp:539-541,558-561);
+ *   W_up            NULL, or a second matrix of the same shape and format
+ *                   (16-byte aligned; sharded: this rank's row slice, like W):
+ *                   the task is the gate+up pair with its SwiGLU epilogue,
+ *                   y = silu(W.x) * (W_up.x) (src/forward_pass.cpp:544-547), and
+ *                   a down task reads it as its plain x_source.
  * world == 1 builds an unsharded stack (y required); world > 1 a sharded one
  * (y NULL, then export / connect as for nexus_gpu_stack_create_sharded). */
 typedef struct {
@@ -265,6 +270,7 @@ typedef struct {
     int32_t residual_source;
     const float* norm_weight;
     float norm_eps;
+    const void* W_up;
 } NexusGpuStackTaskEx;
 NEXUS_GPU_API int32_t nexus_gpu_stack_create_ex(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t n_tasks,
                                                 uint64_t input_cols, uint32_t world, uint32_t rank, void** out_stack);
@@ -278,6 +284,72 @@ NEXUS_GPU_API int32_t nexus_gpu_stack_output(void* stack, uint32_t task, float**
 /* Bit-exact dequantization of `count` elements (a whole number of blocks)
  * from device blocks to device floats, asynchronous on `stream`. */
 NEXUS_GPU_API int32_t nexus_gpu_dequantize(const void* dW, uint32_t dtype, float* dOut, size_t count, void* stream);
+
+/* ------------------------------------------------ GGUF file -> device upload
+ *
+ * The on-disk side of the path: UniversalModelLoader::load_gguf
+ * (src/model_loader.cpp:416-836) memory-maps a GGUF v2/v3 file and registers
+ * every tensor; these calls do the same parse (host only, no device needed)
+ * and then copy chosen tensors into ONE caller-owned device allocation.
+ * Differences from the reference, on purpose:
+ *   - ggml types map one to one (model_loader.cpp:735-746 maps Q4_1 onto
+ *     Q4_0, Q5_1 onto Q5_0, Q8_1 onto Q8_0 and every type >= 24 onto BF16);
+ *     types without a NexusLLM DataType get dtype -1 and are not uploaded;
+ *   - byte sizes are the true block sizes (TensorShape::total_bytes,
+ *     include/nexus_common.hpp:262-281, over-counts Q4_0 and Q6_K);
+ *   - rows/cols follow GGUF's dimension order, cols = dims[0] (the row
+ *     length) and rows = dims[1] * ... (src/forward_pass.cpp:581 takes the
+ *     LM head's dims[0] as the vocabulary size, which is the hidden size);
+ *   - a tensor that ends past the end of the file is skipped, as the
+ *     reference skips one that starts past it (model_loader.cpp:728-731).
+ * Metadata (NexusGpuGgufModel) follows model_loader.cpp:538-653 and its
+ * fallbacks at 803-824: the same keys, defaults and inferences. */
+typedef struct {
+    char architecture[64];
+    uint32_t version, alignment;
+    uint64_t tensor_count;   /* tensors registered (skipped ones excluded) */
+    uint64_t skipped;        /* tensors outside the file */
+    uint64_t data_offset;    /* file offset of the tensor data section */
+    uint32_t vocab_size, hidden_size, intermediate_size, num_hidden_layers;
+    uint32_t num_attention_heads, num_key_value_heads, max_position_embeddings;
+    float rms_norm_eps, rope_theta;
+    uint32_t is_moe, num_experts, num_experts_per_tok;
+} NexusGpuGgufModel;
+
+typedef struct {
+    char name[128];          /* truncated to 127 bytes; nexus_gpu_gguf_find matches the full name */
+    uint32_t ggml_type;      /* as stored in the file */
+    int32_t dtype;           /* NexusLLM DataType (NEXUS_GPU_* values), or -1 */
+    uint32_t served;         /* 1: nexus_gpu_gemv takes this dtype (Q4_0, Q8_0, Q5_K, Q6_K, FP16) */
+    uint32_t n_dims;
+    uint64_t dims[4];        /* GGUF order: dims[0] is the row length */
+    uint64_t rows, cols;     /* rows = dims[1] * dims[2] * dims[3], cols = dims[0] */
+    uint64_t file_offset;    /* absolute offset of the data in the file */
+    uint64_t bytes;          /* true size in the file (0 when the type's block size is unknown) */
+} NexusGpuGgufTensor;
+
+/* Opens and parses `path` (memory-mapped, read-only).  Host only. */
+NEXUS_GPU_API int32_t nexus_gpu_gguf_open(const char* path, void** out_file);
+NEXUS_GPU_API int32_t nexus_gpu_gguf_close(void* file);
+NEXUS_GPU_API int32_t nexus_gpu_gguf_model(void* file, NexusGpuGgufModel* out);
+NEXUS_GPU_API int32_t nexus_gpu_gguf_tensor(void* file, uint64_t index, NexusGpuGgufTensor* out);
+/* Index of the tensor `name`: that name, else the first tensor with the same
+ * canonical key in the reference's alias classes (register_aliases,
+ * model_loader.cpp:60-302: e.g. "layers.0.wq" finds "blk.0.attn_q.weight" or
+ * "model.layers.0.self_attn.q_proj.weight"; MTP-head aliases are not kept),
+ * else, for the LM head, the token embedding when the file has no LM head
+ * (tied weights, model_loader.cpp:793-801).  NEXUS_GPU_ERROR_INVALID_ARGUMENT
+ * if absent. */
+NEXUS_GPU_API int32_t nexus_gpu_gguf_find(void* file, const char* name, uint64_t* index);
+/* Device bytes that nexus_gpu_gguf_upload needs for these tensors: each one
+ * starts on a 256-byte boundary of the image. */
+NEXUS_GPU_API uint64_t nexus_gpu_gguf_upload_size(void* file, const uint64_t* indices, uint64_t n);
+/* Copies the tensors into d_dst (dst_bytes >= nexus_gpu_gguf_upload_size),
+ * each at the offset it returns in offsets[i], through pinned staging
+ * buffers filled by host threads, on `stream`.  Returns when the bytes are on
+ * the device.  Tensors with dtype -1 or unknown size are refused. */
+NEXUS_GPU_API int32_t nexus_gpu_gguf_upload(void* file, const uint64_t* indices, uint64_t n, void* d_dst,
+                                            uint64_t dst_bytes, uint64_t* offsets, void* stream);
 
 /* ------------------------------------------------------------- diagnostics */
 

@@ -63,6 +63,13 @@ SIGNATURES = {
     "nexus_gpu_device_info": (_I32, [ctypes.c_char_p, _SZ, ctypes.POINTER(ctypes.c_int),
                                      ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
     "nexus_gpu_version": (ctypes.c_char_p, []),
+    "nexus_gpu_gguf_open": (_I32, [ctypes.c_char_p, ctypes.POINTER(_VP)]),
+    "nexus_gpu_gguf_close": (_I32, [_VP]),
+    "nexus_gpu_gguf_model": (_I32, [_VP, _VP]),
+    "nexus_gpu_gguf_tensor": (_I32, [_VP, ctypes.c_uint64, _VP]),
+    "nexus_gpu_gguf_find": (_I32, [_VP, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint64)]),
+    "nexus_gpu_gguf_upload_size": (ctypes.c_uint64, [_VP, _VP, ctypes.c_uint64]),
+    "nexus_gpu_gguf_upload": (_I32, [_VP, _VP, ctypes.c_uint64, _VP, ctypes.c_uint64, _VP, _VP]),
 }
 
 class StackTask(ctypes.Structure):
@@ -75,7 +82,28 @@ class StackTaskEx(ctypes.Structure):
     """NexusGpuStackTaskEx (include/nexus_gpu.h): a stack task with fusions."""
     _fields_ = [("W", _VP), ("rows", ctypes.c_uint64), ("cols", ctypes.c_uint64), ("y", _VP),
                 ("x_source", ctypes.c_int32), ("after", ctypes.c_int32), ("x_source2", ctypes.c_int32),
-                ("residual_source", ctypes.c_int32), ("norm_weight", _VP), ("norm_eps", ctypes.c_float)]
+                ("residual_source", ctypes.c_int32), ("norm_weight", _VP), ("norm_eps", ctypes.c_float),
+                ("W_up", _VP)]
+
+
+class GgufModel(ctypes.Structure):
+    """NexusGpuGgufModel (include/nexus_gpu.h)."""
+    _fields_ = [("architecture", ctypes.c_char * 64), ("version", ctypes.c_uint32), ("alignment", ctypes.c_uint32),
+                ("tensor_count", ctypes.c_uint64), ("skipped", ctypes.c_uint64), ("data_offset", ctypes.c_uint64),
+                ("vocab_size", ctypes.c_uint32), ("hidden_size", ctypes.c_uint32),
+                ("intermediate_size", ctypes.c_uint32), ("num_hidden_layers", ctypes.c_uint32),
+                ("num_attention_heads", ctypes.c_uint32), ("num_key_value_heads", ctypes.c_uint32),
+                ("max_position_embeddings", ctypes.c_uint32), ("rms_norm_eps", ctypes.c_float),
+                ("rope_theta", ctypes.c_float), ("is_moe", ctypes.c_uint32), ("num_experts", ctypes.c_uint32),
+                ("num_experts_per_tok", ctypes.c_uint32)]
+
+
+class GgufTensor(ctypes.Structure):
+    """NexusGpuGgufTensor (include/nexus_gpu.h)."""
+    _fields_ = [("name", ctypes.c_char * 128), ("ggml_type", ctypes.c_uint32), ("dtype", ctypes.c_int32),
+                ("served", ctypes.c_uint32), ("n_dims", ctypes.c_uint32), ("dims", ctypes.c_uint64 * 4),
+                ("rows", ctypes.c_uint64), ("cols", ctypes.c_uint64), ("file_offset", ctypes.c_uint64),
+                ("bytes", ctypes.c_uint64)]
 
 
 _lib = None

@@ -19,6 +19,7 @@
 #include "stack_kernels.cuh"
 #include "awq_fp8_kernels.cuh"
 #include "mma_kernels.cuh"
+#include "gguf_file.cuh"
 
 namespace nexus_gpu {
 
@@ -972,6 +973,7 @@ uint64_t stack_fingerprint(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uin
         uint32_t eb;
         memcpy(&eb, &tasks[i].norm_eps, 4);
         mix(tasks[i].norm_weight ? eb : 0u);
+        mix(tasks[i].W_up != nullptr);
     }
     return h;
 }
@@ -1033,6 +1035,8 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
                         u.residual_source, (unsigned long long)u.rows);
         if (u.norm_weight && ((uintptr_t)u.norm_weight & 15) != 0)
             return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u: norm_weight not 16-byte aligned", i);
+        if (u.W_up && ((uintptr_t)u.W_up & 15) != 0)
+            return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u: W_up not 16-byte aligned", i);
         uint64_t r0 = 0, r1 = u.rows;
         if (sharded) shard_rows(u.rows, world, rank, r0, r1);
         if (r1 <= r0 || u.rows > (uint64_t)INT32_MAX)
@@ -1043,7 +1047,8 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
         GemvParams gp{};
         size_t sm = 0;
         const uint64_t rb = row_bytes_of(f, u.cols);
-        if (!plan_for(dtype, *d, (int)local_rows[i], (int)u.cols, rb, gp, sm))
+        // a gate+up pair plans with its two rows as one (twice the bytes per ring row)
+        if (!plan_for(dtype, *d, (int)local_rows[i], (int)u.cols, u.W_up ? 2 * rb : rb, gp, sm))
             return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "task %u (%llux%llu) is outside the fast kernel's limits", i,
                         (unsigned long long)local_rows[i], (unsigned long long)u.cols);
         if (group < 0) group = gp.group;
@@ -1062,7 +1067,12 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
         T.stage_rows = gp.stage_rows;
         T.stage_bytes = gp.stage_bytes;
         T.row_off = (int)row_off[i];
-        slot = std::max(slot, (size_t)gp.stage_bytes);
+        if (u.W_up) {  // the up rows of a stage sit half a slot after the gate rows
+            T.W2 = static_cast<const uint8_t*>(u.W_up);
+            T.half = (int)((gp.stage_rows * rb + 32 + 15) / 16 * 16);
+            T.stage_bytes = 2 * T.half;
+        }
+        slot = std::max(slot, (size_t)T.stage_bytes);
     }
     size_t x_smem = 0;
     for (const StackTask& T : ht) x_smem = std::max(x_smem, (size_t)x_stage_planes_len(T.K) * (kXQLimbBytes + kXQMetaBytes));
@@ -1073,7 +1083,7 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
     int ns = (int)std::min<uint64_t>(kMaxStages, avail / slot);
     auto fits = [&](int k) {
         for (const StackTask& T : ht)
-            if (T.stage_rows * T.segments > kMaxSlots / k) return false;
+            if (T.stage_rows * T.segments * (T.W2 ? 2 : 1) > kMaxSlots / k) return false;
         return true;
     };
     while (ns > 2 && !fits(ns)) --ns;
@@ -1091,7 +1101,8 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
     h->fingerprint = stack_fingerprint(dtype, tasks, n, input_cols, world);
     h->smem = kStackSmemHeader + x_smem + (size_t)ns * slot;
     for (uint32_t i = 0; i < n; ++i)
-        h->fused |= tasks[i].x_source2 >= 0 || tasks[i].residual_source != -2 || tasks[i].norm_weight != nullptr;
+        h->fused |= tasks[i].x_source2 >= 0 || tasks[i].residual_source != -2 || tasks[i].norm_weight != nullptr ||
+                    tasks[i].W_up != nullptr;
 
     std::vector<char> waited_for(n, 0);
     for (uint32_t i = 0; i < n; ++i) {
@@ -1547,6 +1558,7 @@ std::vector<NexusGpuStackTaskEx> plain_tasks(const NexusGpuStackTask* tasks, uin
         v[i].residual_source = -2;
         v[i].norm_weight = nullptr;
         v[i].norm_eps = 0.0f;
+        v[i].W_up = nullptr;
     }
     return v;
 }
@@ -1681,5 +1693,194 @@ NEXUS_GPU_API int32_t nexus_gpu_device_info(char* name, size_t name_len, int* sm
 }
 
 NEXUS_GPU_API const char* nexus_gpu_version(void) { return "nexus_gpu 0.1.0 (sm_100a)"; }
+
+// ------------------------------------------------ GGUF file -> device upload
+
+NEXUS_GPU_API int32_t nexus_gpu_gguf_open(const char* path, void** out_file) {
+    if (!path || !out_file) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null path or out_file");
+    *out_file = nullptr;
+    auto* f = new (std::nothrow) gguf::File();
+    if (!f) return fail(NEXUS_GPU_ERROR_OUT_OF_HOST_MEMORY, "out of host memory");
+    std::string err;
+    bool ok = false;
+    try {
+        ok = gguf::parse(path, *f, err);
+    } catch (const std::bad_alloc&) {
+        err = "out of host memory while parsing";
+    }
+    if (!ok) {
+        gguf::close_file(*f);
+        delete f;
+        return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "%s: %s", path, err.c_str());
+    }
+    *out_file = f;
+    return NEXUS_GPU_SUCCESS;
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_gguf_close(void* file) {
+    if (!file) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null file");
+    auto* f = static_cast<gguf::File*>(file);
+    if (!f->ring.empty()) cudaSetDevice(f->device);
+    gguf::close_file(*f);
+    delete f;
+    return NEXUS_GPU_SUCCESS;
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_gguf_model(void* file, NexusGpuGgufModel* out) {
+    if (!file || !out) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null file or out");
+    const gguf::File& f = *static_cast<gguf::File*>(file);
+    const gguf::Model& m = f.model;
+    memset(out, 0, sizeof(*out));
+    snprintf(out->architecture, sizeof(out->architecture), "%s", m.architecture.c_str());
+    out->version = f.version;
+    out->alignment = f.alignment;
+    out->tensor_count = f.tensors.size();
+    out->skipped = f.skipped;
+    out->data_offset = f.data_offset;
+    out->vocab_size = m.vocab;
+    out->hidden_size = m.hidden;
+    out->intermediate_size = m.ffn;
+    out->num_hidden_layers = m.layers;
+    out->num_attention_heads = m.heads;
+    out->num_key_value_heads = m.kv_heads;
+    out->max_position_embeddings = m.ctx;
+    out->rms_norm_eps = m.eps;
+    out->rope_theta = m.rope;
+    out->is_moe = m.moe;
+    out->num_experts = m.experts;
+    out->num_experts_per_tok = m.experts_per_tok;
+    return NEXUS_GPU_SUCCESS;
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_gguf_tensor(void* file, uint64_t index, NexusGpuGgufTensor* out) {
+    if (!file || !out) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null file or out");
+    const gguf::File& f = *static_cast<gguf::File*>(file);
+    if (index >= f.tensors.size())
+        return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "tensor index %llu of %zu", (unsigned long long)index,
+                    f.tensors.size());
+    const gguf::Tensor& t = f.tensors[index];
+    memset(out, 0, sizeof(*out));
+    snprintf(out->name, sizeof(out->name), "%s", t.name.c_str());
+    out->ggml_type = t.ggml_type;
+    out->dtype = t.dtype;
+    out->served = gguf::served(t.dtype);
+    out->n_dims = t.n_dims;
+    for (int d = 0; d < 4; ++d) out->dims[d] = d < (int)t.n_dims ? t.dims[d] : 1;
+    out->cols = t.dims[0];
+    out->rows = t.dims[1] * t.dims[2] * t.dims[3];
+    out->file_offset = t.file_offset;
+    out->bytes = t.bytes;
+    return NEXUS_GPU_SUCCESS;
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_gguf_find(void* file, const char* name, uint64_t* index) {
+    if (!file || !name || !index) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null argument");
+    if (!gguf::find(*static_cast<gguf::File*>(file), name, *index))
+        return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "no tensor named %s", name);
+    return NEXUS_GPU_SUCCESS;
+}
+
+NEXUS_GPU_API uint64_t nexus_gpu_gguf_upload_size(void* file, const uint64_t* indices, uint64_t n) {
+    if (!file || (n && !indices)) return 0;
+    const gguf::File& f = *static_cast<gguf::File*>(file);
+    for (uint64_t i = 0; i < n; ++i)
+        if (indices[i] >= f.tensors.size()) return 0;
+    return gguf::image_layout(f, indices, n, nullptr);
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_gguf_upload(void* file, const uint64_t* indices, uint64_t n, void* d_dst,
+                                            uint64_t dst_bytes, uint64_t* offsets, void* stream) {
+    if (!file || (n && (!indices || !offsets))) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null argument");
+    gguf::File& f = *static_cast<gguf::File*>(file);
+    for (uint64_t i = 0; i < n; ++i) {
+        if (indices[i] >= f.tensors.size())
+            return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "tensor index %llu of %zu", (unsigned long long)indices[i],
+                        f.tensors.size());
+        const gguf::Tensor& t = f.tensors[indices[i]];
+        if (t.dtype < 0 || t.bytes == 0)
+            return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "tensor %s: ggml type %u has no NexusLLM data type",
+                        t.name.c_str(), t.ggml_type);
+    }
+    const uint64_t total = gguf::image_layout(f, indices, n, offsets);
+    if (total == 0) return NEXUS_GPU_SUCCESS;
+    if (!d_dst) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null device buffer");
+    if (dst_bytes < total)
+        return fail(NEXUS_GPU_ERROR_WORKSPACE, "device buffer of %llu bytes, the image needs %llu",
+                    (unsigned long long)dst_bytes, (unsigned long long)total);
+    Device* d = nullptr;
+    int32_t rc = get_device(&d);
+    if (rc) return rc;
+    if (!f.ring.empty() && f.device != d->id) {  // staging of another device: remake it here
+        CUDA_TRY(cudaSetDevice(f.device));
+        for (gguf::Staging& s : f.ring) {
+            cudaEventSynchronize(s.done);
+            cudaEventDestroy(s.done);
+            cudaFreeHost(s.host);
+        }
+        f.ring.clear();
+        CUDA_TRY(cudaSetDevice(d->id));
+    }
+    if (f.ring.empty()) {
+        f.device = d->id;
+        f.ring.resize(gguf::kStages);
+        for (gguf::Staging& s : f.ring) {
+            CUDA_TRY(cudaHostAlloc(&s.host, gguf::kStageBytes, cudaHostAllocDefault));
+            CUDA_TRY(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming));
+        }
+    }
+    std::vector<gguf::Segment> seg(n);
+    for (uint64_t i = 0; i < n; ++i) {
+        const gguf::Tensor& t = f.tensors[indices[i]];
+        seg[i] = {offsets[i], t.bytes, f.base + t.file_offset};
+    }
+    std::sort(seg.begin(), seg.end(), [](const gguf::Segment& a, const gguf::Segment& b) {
+        return a.image_off < b.image_off;
+    });
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int threads = (int)std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+    auto drain = [&]() {  // leave no copy in flight from the staging buffers
+        for (gguf::Staging& s : f.ring)
+            if (s.busy) {
+                cudaEventSynchronize(s.done);
+                s.busy = false;
+            }
+    };
+    int k = 0;
+    for (uint64_t c0 = 0; c0 < total; c0 += gguf::kStageBytes, ++k) {
+        gguf::Staging& s = f.ring[k % gguf::kStages];
+        if (s.busy) {
+            const cudaError_t e = cudaEventSynchronize(s.done);
+            s.busy = false;
+            if (e != cudaSuccess) {
+                drain();
+                return fail(NEXUS_GPU_ERROR_CUDA, "staging copy failed: %s", cudaGetErrorString(e));
+            }
+        }
+        const uint64_t c1 = std::min<uint64_t>(total, c0 + gguf::kStageBytes);
+        uint8_t* host = static_cast<uint8_t*>(s.host);
+        // host threads copy slices of the piece out of the mapping
+        const uint64_t slice = ((c1 - c0 + threads - 1) / threads + 4095) / 4096 * 4096;
+        std::vector<std::thread> pool;
+        try {
+            for (uint64_t a = c0 + slice; a < c1; a += slice)
+                pool.emplace_back(gguf::fill_range, std::cref(seg), a, std::min(c1, a + slice), host + (a - c0));
+        } catch (const std::exception&) {  // no more threads: this one copies the rest
+            const uint64_t a = c0 + slice * (pool.size() + 1);
+            if (a < c1) gguf::fill_range(seg, a, c1, host + (a - c0));
+        }
+        gguf::fill_range(seg, c0, std::min(c1, c0 + slice), host);
+        for (std::thread& th : pool) th.join();
+        cudaError_t e = cudaMemcpyAsync(static_cast<uint8_t*>(d_dst) + c0, host, c1 - c0, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaEventRecord(s.done, st);
+        if (e != cudaSuccess) {
+            drain();
+            cudaStreamSynchronize(st);
+            return fail(NEXUS_GPU_ERROR_CUDA, "upload copy failed: %s", cudaGetErrorString(e));
+        }
+        s.busy = true;
+    }
+    drain();
+    return NEXUS_GPU_SUCCESS;
+}
 
 }  // extern "C"

@@ -66,6 +66,8 @@ struct StackTask {
     const float* res;                    // residual added to every output row (full length), or null
     int res_input;                       // the residual is the stack input
     int res_src;                         // the residual's task, or -1 (waited for with the input)
+    const uint8_t* W2;                   // gate+up pair: the up matrix (rows as W's), or null
+    int half;                            // pair: byte offset of W2's rows in a ring slot
 };
 
 struct StackParams {
@@ -258,16 +260,21 @@ __device__ __forceinline__ float residual_of(const StackParams& P, const StackTa
 // Write row r (of this rank's slice) of task T: this rank's output and --
 // sharded -- every peer's copy (plain stores over NVLink).  v is the row's
 // dot product; in the fused variant (FX) the RMSNorm scale of the task's
-// input (1 without one) and the residual rv (residual_of) are applied here:
-// y = v * scale + rv.  The scale is read from shared memory at the store, so
+// input (1 without one), the SwiGLU of a gate+up pair (u: the up row's dot
+// product) and the residual rv (residual_of) are applied here:
+// y = v * scale + rv, or silu(v * scale) * (u * scale) + rv for a pair.  The scale is read from shared memory at the store, so
 // that it holds no register through the row loop.
 template <bool FX>
 __device__ __forceinline__ void put_row(const StackParams& P, const StackTask* T, int r, float v,
-                                        const volatile float* scale, float rv) {
+                                        const volatile float* scale, float rv, float u) {
     const uint64_t g = (uint64_t)ld_task_i32(&T->row_off) + (uint64_t)r;  // global row
     if constexpr (FX) {
         const float sc = *scale;
         if (sc != 1.0f) v = __fmul_rn(v, sc);
+        if (ld_task_u64(&T->W2)) {  // gate+up pair: silu(gate) * up (transformer_ops.hpp:86-95)
+            if (sc != 1.0f) u = __fmul_rn(u, sc);
+            v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u);
+        }
         if (task_residual(P, T)) v = __fadd_rn(v, rv);
     }
     reinterpret_cast<float*>(ld_task_u64(&T->y))[g] = v;
@@ -277,6 +284,66 @@ __device__ __forceinline__ void put_row(const StackParams& P, const StackTask* T
         for (int p = 0; p < P.world; ++p)
             if (p != P.rank) reinterpret_cast<float*>(P.peer_block[p])[y_off + g] = v;
     }
+}
+
+// Stage a group's input x into shared memory: read it (L2), apply the fused
+// SwiGLU (xv2) and RMSNorm weights (nw), quantize two lanes per 32-element
+// block.  Returns this thread's sum of squares of x (for the RMSNorm scale).
+template <bool FX>
+__device__ __forceinline__ float stage_x(const float4* xv, const float4* xv2, const float4* nw, int K, uint32_t xs,
+                                         int tid, int lane) {
+    const int nxb = K / 32, nxbp = x_stage_planes_len(K), hf = lane & 1;
+    float ss = 0.0f;  // in a fixed order
+    for (int base = 0; base < nxb; base += kConsumers / 2) {
+        const int b = base + (tid >> 1);
+        float e[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 v = b < nxb ? __ldcg(xv + 8 * b + 4 * hf + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+            e[4 * q + 0] = v.x;
+            e[4 * q + 1] = v.y;
+            e[4 * q + 2] = v.z;
+            e[4 * q + 3] = v.w;
+        }
+        if constexpr (FX) {
+            // SwiGLU (transformer_ops.hpp:86-95): silu(gate) * up.  Every CTA computes the
+            // whole vector, so with the __expf / __fdividef intrinsics (relative error ~1e-6,
+            // far below the 16-bit fixed-point quantization that follows)
+            if (xv2 != nullptr && b < nxb) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float4 u = __ldcg(xv2 + 8 * b + 4 * hf + q);
+                    const float uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float g = e[4 * q + k];
+                        e[4 * q + k] = __fmul_rn(__fdividef(g, __fadd_rn(1.0f, __expf(-g))), uu[k]);
+                    }
+                }
+            }
+            if (nw != nullptr && b < nxb) {  // RMSNorm: sum x^2 here, quantize x * w; 1/rms scales the rows
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float4 w = __ldg(nw + 8 * b + 4 * hf + q);
+                    const float ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        ss = fmaf(e[4 * q + k], e[4 * q + k], ss);
+                        e[4 * q + k] = __fmul_rn(e[4 * q + k], ww[k]);
+                    }
+                }
+            }
+        }
+        quantize_x_pair(e, hf, b < nxb, xs, nxbp, b);
+    }
+    return ss;
+}
+
+// The fused variant's staging, kept out of line: its registers (the SwiGLU
+// and norm operands) then never compete with the row loop's x slices.
+__device__ __noinline__ float stage_x_fused(const float4* xv, const float4* xv2, const float4* nw, int K,
+                                            uint32_t xs, int tid, int lane) {
+    return stage_x<true>(xv, xv2, nw, K, xs, tid, lane);
 }
 
 // FX: the variant with the fused RMSNorm / SwiGLU / residual; stacks without
@@ -359,6 +426,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
             const StackTask& T = P.tasks[t];
             const uint64_t rb = __ldg(&T.row_bytes), total = __ldg(&T.total_bytes);
             const uint8_t* W = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.W)));
+            const uint8_t* W2 =
+                FX ? reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.W2))) : nullptr;
             const int N = __ldg(&T.N), R = __ldg(&T.stage_rows);
             int row_begin, row_end;
             cta_rows(N, c, n_cta, row_begin, row_end);
@@ -394,8 +463,22 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                     fence_proxy_async_smem();
                 }
                 const uint32_t n = bend > a ? (uint32_t)(bend - a) : 0u;
-                mbar_arrive_expect_tx(full_bar + 8 * s, n);
-                if (n) bulk_g2s(dst, W + a, n, full_bar + 8 * s);
+                if (FX && W2 != nullptr) {  // gate+up pair: the same rows of the up matrix, half a slot on
+                    const uint32_t dst2 = dst + (uint32_t)__ldg(&T.half);
+                    if (bend < end) {
+                        for (uint64_t pos = (bend > a ? bend : a); pos < end; pos += 2)
+                            sts16(dst2 + (uint32_t)(pos - a), *reinterpret_cast<const uint16_t*>(W2 + pos));
+                        fence_proxy_async_smem();
+                    }
+                    mbar_arrive_expect_tx(full_bar + 8 * s, 2 * n);
+                    if (n) {
+                        bulk_g2s(dst, W + a, n, full_bar + 8 * s);
+                        bulk_g2s(dst2, W2 + a, n, full_bar + 8 * s);
+                    }
+                } else {
+                    mbar_arrive_expect_tx(full_bar + 8 * s, n);
+                    if (n) bulk_g2s(dst, W + a, n, full_bar + 8 * s);
+                }
                 start = end;
                 if (++s == NS) {
                     s = 0;
@@ -482,48 +565,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
             if (xv == nullptr) xv = reinterpret_cast<const float4*>(P.x_in);
             const float4* xv2 =
                 FX ? reinterpret_cast<const float4*>(__ldg(reinterpret_cast<const unsigned long long*>(&H.x2))) : nullptr;
-            const int nxb = K / 32, nxbp = x_stage_planes_len(K), hf = lane & 1;
-            float ss = 0.0f;  // RMSNorm: sum of squares of this thread's elements, in a fixed order
-            for (int base = 0; base < nxb; base += kConsumers / 2) {
-                const int b = base + (tid >> 1);
-                float e[16];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float4 v = b < nxb ? __ldcg(xv + 8 * b + 4 * hf + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    e[4 * q + 0] = v.x;
-                    e[4 * q + 1] = v.y;
-                    e[4 * q + 2] = v.z;
-                    e[4 * q + 3] = v.w;
-                }
-                // SwiGLU (transformer_ops.hpp:86-95): silu(gate) * up.  Every CTA computes the
-                // whole vector, so with the __expf / __fdividef intrinsics (relative error ~1e-6,
-                // far below the 16-bit fixed-point quantization that follows)
-                if (xv2 != nullptr && b < nxb) {
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const float4 u = __ldcg(xv2 + 8 * b + 4 * hf + q);
-                        const float uu[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) {
-                            const float g = e[4 * q + k];
-                            e[4 * q + k] = __fmul_rn(__fdividef(g, __fadd_rn(1.0f, __expf(-g))), uu[k]);
-                        }
-                    }
-                }
-                if (nw != nullptr && b < nxb) {  // RMSNorm: sum x^2 here, quantize x * w; 1/rms scales the rows
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const float4 w = __ldg(nw + 8 * b + 4 * hf + q);
-                        const float ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) {
-                            ss = fmaf(e[4 * q + k], e[4 * q + k], ss);
-                            e[4 * q + k] = __fmul_rn(e[4 * q + k], ww[k]);
-                        }
-                    }
-                }
-                quantize_x_pair(e, hf, b < nxb, xs, nxbp, b);
-            }
+            float ss;  // RMSNorm: sum of squares of this thread's elements
+            if constexpr (FX) ss = stage_x_fused(xv, xv2, nw, K, xs, tid, lane);
+            else ss = stage_x<false>(xv, nullptr, nullptr, K, xs, tid, lane);
             if (nw != nullptr) {
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -557,6 +601,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
             const StackTask& T = P.tasks[t];
             const int N = __ldg(&T.N), R = __ldg(&T.stage_rows);
             const uint64_t rbytes = __ldg(&T.row_bytes);
+            const uint32_t half = FX ? (uint32_t)__ldg(&T.half) : 0u;  // a gate+up pair when non-zero
             int row_begin, row_end;
             cta_rows(N, c, n_cta, row_begin, row_end);
             const int n_st = (row_end - row_begin + R - 1) / R;
@@ -581,18 +626,27 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                         float acc = row_partial<F, G>(row, wi, has, X);
 #pragma unroll
                         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                        float up = 0.0f;  // a pair's up row: the same row of W2, half a slot on
+                        if (FX && half) {
+                            up = row_partial<F, G>(row + half, wi, has, X);
+#pragma unroll
+                            for (int o = 16; o > 0; o >>= 1) up += __shfl_xor_sync(0xffffffffu, up, o);
+                        }
                         if (S == 1) {
-                            if (lane == 0) put_row<FX>(P, &T, r0 + rl, acc, s_scale + warp, rv);
+                            if (lane == 0) put_row<FX>(P, &T, r0 + rl, acc, s_scale + warp, rv, up);
                         } else if (lane == 0) {
-                            float* sl = slots + s * P.slot_stride + rl * S;
+                            float* sl = slots + s * P.slot_stride + rl * S * (half ? 2 : 1);
                             sl[sg] = acc;
+                            if (FX && half) sl[S + sg] = up;
                             __threadfence_block();
                             const int prev = atomicAdd(&counters[s * kMaxStageRows + rl], 1);
                             if (prev == S - 1) {  // last segment of this row: sum in segment order
                                 __threadfence_block();
-                                float v = 0.f;
+                                float v = 0.f, u = 0.f;
                                 for (int k = 0; k < S; ++k) v += *(volatile float*)(sl + k);
-                                put_row<FX>(P, &T, r0 + rl, v, s_scale + warp, rv);
+                                if (FX && half)
+                                    for (int k = 0; k < S; ++k) u += *(volatile float*)(sl + S + k);
+                                put_row<FX>(P, &T, r0 + rl, v, s_scale + warp, rv, u);
                                 counters[s * kMaxStageRows + rl] = 0;
                             }
                         }

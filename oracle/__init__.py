@@ -8,6 +8,9 @@ Two libraries, both built by oracle/Makefile:
 * ``reference`` -- oracle/_ref/libnexus_ref.so, NexusLLM's own
                    src/quantization.cpp compiled unmodified (only present where
                    the reference sources were available at build time).
+* ``reference_gguf_load`` -- oracle/_ref/libnexus_ref_gguf.so, NexusLLM's
+                   GGUF loader (src/model_loader.cpp + memory_tier.cpp)
+                   compiled unmodified behind the ref_gguf.cpp shim.
 
 Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg may
 import this package, and only to check or to time the CPU path; the product
@@ -23,6 +26,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_SO = os.path.join(HERE, "build", "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libnexus_ref.so")
+REF_GGUF_SO = os.path.join(HERE, "_ref", "libnexus_ref_gguf.so")
 
 # NexusLLM DataType values (include/nexus_common.hpp:244-260)
 _NAMES = {1: "fp16", 7: "q4_0", 9: "q8_0", 11: "q5_k", 12: "q6_k"}
@@ -165,3 +169,50 @@ def l2_rel(a: np.ndarray, b: np.ndarray) -> float:
     b = np.asarray(b, np.float64).reshape(-1)
     nb = np.linalg.norm(b)
     return float(np.linalg.norm(a - b) / nb) if nb > 0 else float(np.linalg.norm(a - b))
+
+
+class _RefGgufModel(ctypes.Structure):
+    _fields_ = [("architecture", ctypes.c_char * 64), ("vocab_size", ctypes.c_uint32), ("hidden_size", ctypes.c_uint32),
+                ("intermediate_size", ctypes.c_uint32), ("num_hidden_layers", ctypes.c_uint32),
+                ("num_attention_heads", ctypes.c_uint32), ("num_key_value_heads", ctypes.c_uint32),
+                ("max_position_embeddings", ctypes.c_uint32), ("rms_norm_eps", ctypes.c_float),
+                ("rope_theta", ctypes.c_float), ("is_moe", ctypes.c_uint32), ("num_experts", ctypes.c_uint32),
+                ("num_experts_per_tok", ctypes.c_uint32), ("loaded_tensor_count", ctypes.c_uint64)]
+
+
+class _RefGgufTensor(ctypes.Structure):
+    _fields_ = [("found", ctypes.c_int32), ("dtype", ctypes.c_int32), ("n_dims", ctypes.c_uint32),
+                ("dims", ctypes.c_uint64 * 8), ("byte_size", ctypes.c_uint64), ("fnv", ctypes.c_uint64)]
+
+
+def reference_gguf_available() -> bool:
+    return os.path.exists(REF_GGUF_SO)
+
+
+def reference_gguf_load(path: str, names, hash_bytes):
+    """NexusLLM's loader on `path` (oracle/ref_gguf.cpp): (status, metadata
+    dict, [per-name dict: found, dtype, dims, byte_size, fnv of hash_bytes[i]
+    bytes at the tensor's data pointer])."""
+    lib = ctypes.CDLL(REF_GGUF_SO)
+    f = lib.ref_gguf_load
+    f.restype = ctypes.c_int32
+    f.argtypes = [ctypes.c_char_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]
+    n = len(names)
+    c_names = (ctypes.c_char_p * max(1, n))(*[x.encode() for x in names])
+    hb = (ctypes.c_uint64 * max(1, n))(*hash_bytes)
+    out = (_RefGgufTensor * max(1, n))()
+    m = _RefGgufModel()
+    st = f(path.encode(), ctypes.byref(m), c_names, hb, n, out)
+    model = {k: getattr(m, k) for k, _ in m._fields_}
+    model["architecture"] = m.architecture.decode()
+    res = [{"found": t.found, "dtype": t.dtype, "dims": list(t.dims)[:t.n_dims], "byte_size": t.byte_size,
+            "fnv": t.fnv} for t in out[:n]]
+    return st, model, res
+
+
+def fnv1a(data: bytes) -> int:
+    """FNV-1a 64 (the hash ref_gguf.cpp reports)."""
+    h = 1469598103934665603
+    for b in data:
+        h = ((h ^ b) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+    return h

@@ -5,6 +5,13 @@ built from the reference sources (``make -C oracle ref REF=<checkout>``):
 
     python tests/golden/make_golden.py
 
+``python tests/golden/make_golden.py gguf`` writes tests/golden/gguf_ref.json
+instead: what NexusLLM's own GGUF loader (oracle/_ref/libnexus_ref_gguf.so,
+``make -C oracle ref-gguf``) reads from the synthetic files of
+tests/gguf_cases.py -- metadata, which names resolve, each tensor's DataType,
+dims, byte size and an FNV-1a hash of the bytes at its data pointer (over the
+tensor's true size, as this library's parser reports it).
+
 Every expected output in the fixture comes from the reference build
 (src/quantization.cpp compiled unmodified with its build.sh flags, AVX2+FMA
 branch).  The one exception is Q8_0 dequantization, which the reference only
@@ -34,6 +41,7 @@ from nexusllm_b200 import synth  # noqa: E402
 from nexusllm_b200.formats import DataType  # noqa: E402
 
 OUT = os.path.join(ROOT, "tests", "golden", "golden.npz")
+OUT_GGUF = os.path.join(ROOT, "tests", "golden", "gguf_ref.json")
 
 # fp16 bit patterns whose decoding the reference treats specially or that sit
 # on the edges of the format
@@ -216,5 +224,34 @@ def main() -> None:
     print(f"wrote {OUT}: {len(g)} arrays, {os.path.getsize(OUT)} bytes")
 
 
+def gguf_fixture() -> None:
+    import json
+    import tempfile
+
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import gguf_cases
+    from nexusllm_b200 import gguf
+
+    out = {}
+    with tempfile.TemporaryDirectory() as d:
+        for case, (path, tensors) in gguf_cases.build(d).items():
+            names = [t[0] for t in tensors] + gguf_cases.ALIASES
+            hb = []
+            with gguf.GGUFFile(path) as f:  # our sizes; 0 where our parser has no such tensor
+                for n in names:
+                    try:
+                        hb.append(f.tensors[f.find(n)]["bytes"])
+                    except Exception:
+                        hb.append(0)
+            st, model, res = oracle.reference_gguf_load(path, names, hb)
+            out[case] = {"status": st, "model": model, "names": names, "hash_bytes": hb, "tensors": res}
+    with open(OUT_GGUF, "w") as fh:
+        json.dump(out, fh, indent=1, sort_keys=True)
+    print(f"wrote {OUT_GGUF}")
+
+
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["gguf"]:
+        gguf_fixture()
+    else:
+        main()

@@ -1,6 +1,7 @@
 """GEMV stacks with the decode layer's operations fused in (nexus_gpu_stack_create_ex):
-RMSNorm on a task's input, SwiGLU from two source tasks, residual adds
-(src/forward_pass.cpp:504-562; TransformerOps, include/transformer_ops.hpp).
+RMSNorm on a task's input, SwiGLU either from two source tasks or as the
+epilogue of a gate+up pair, residual adds (src/forward_pass.cpp:504-562;
+TransformerOps, include/transformer_ops.hpp).
 
 A small two-layer decoder (attention stood in by q -> o, as in bench.py) runs
 as one stack.  Every task's output is checked against the C oracle fed with
@@ -28,8 +29,10 @@ def L():
     return _native.lib()
 
 
-def decoder_tasks(H, KV, F, V, layers, seed):
-    """(task dicts, weights, norm weights) of a fused decode stack."""
+def decoder_tasks(H, KV, F, V, layers, seed, paired=False):
+    """(task dicts, norm weights) of a fused decode stack.  paired: gate and up
+    as one gate+up task with the SwiGLU epilogue; else two tasks whose outputs
+    the down task combines (x_source2)."""
     g = torch.Generator().manual_seed(seed)
     tasks, norms = [], {}
     prev = -1  # the stack input is layer 0's residual stream
@@ -40,15 +43,21 @@ def decoder_tasks(H, KV, F, V, layers, seed):
         tasks += [dict(name="q", rows=H, cols=H, src=prev, norm=f"attn{l}"),
                   dict(name="k", rows=KV, cols=H, src=prev, norm=f"attn{l}"),
                   dict(name="v", rows=KV, cols=H, src=prev, norm=f"attn{l}"),
-                  dict(name="o", rows=H, cols=H, src=b + 0, res=prev),
-                  dict(name="gate", rows=F, cols=H, src=b + 3, norm=f"ffn{l}"),
-                  dict(name="up", rows=F, cols=H, src=b + 3, norm=f"ffn{l}"),
-                  dict(name="down", rows=H, cols=F, src=b + 4, src2=b + 5, res=b + 3)]
-        prev = b + 6
+                  dict(name="o", rows=H, cols=H, src=b + 0, res=prev)]
+        if paired:
+            tasks += [dict(name="gate_up", rows=F, cols=H, src=b + 3, norm=f"ffn{l}", pair=True),
+                      dict(name="down", rows=H, cols=F, src=b + 4, res=b + 3)]
+        else:
+            tasks += [dict(name="gate", rows=F, cols=H, src=b + 3, norm=f"ffn{l}"),
+                      dict(name="up", rows=F, cols=H, src=b + 3, norm=f"ffn{l}"),
+                      dict(name="down", rows=H, cols=F, src=b + 4, src2=b + 5, res=b + 3)]
+        prev = len(tasks) - 1
     norms["out"] = (1.0 + 0.1 * torch.randn(H, generator=g)).cuda()
     tasks.append(dict(name="head", rows=V, cols=H, src=prev, norm="out"))
     for i, t in enumerate(tasks):
         t["W"] = synth.blocks_torch(Q4_0, t["rows"], t["cols"], seed + 31 * i)
+        if t.get("pair"):
+            t["W_up"] = synth.blocks_torch(Q4_0, t["rows"], t["cols"], seed + 31 * i + 7)
         t["y"] = torch.empty(t["rows"], device="cuda")
     return tasks, norms
 
@@ -58,7 +67,8 @@ def make_stack(L, tasks, norms, hidden, eps=1e-5):
     for i, t in enumerate(tasks):
         arr[i] = _native.StackTaskEx(t["W"].data_ptr(), t["rows"], t["cols"], t["y"].data_ptr(), t["src"], -1,
                                      t.get("src2", -1), t.get("res", -2),
-                                     norms[t["norm"]].data_ptr() if "norm" in t else None, eps)
+                                     norms[t["norm"]].data_ptr() if "norm" in t else None, eps,
+                                     t["W_up"].data_ptr() if "W_up" in t else None)
     h = ctypes.c_void_p()
     rc = L.nexus_gpu_stack_create_ex(Q4_0, arr, len(tasks), hidden, 1, 0, ctypes.byref(h))
     assert rc == 0, L.nexus_gpu_last_error()
@@ -75,15 +85,18 @@ def expected(port, tasks, norms, i, x_in, eps=1e-5):
     if "norm" in t:
         x = port.rmsnorm(x, norms[t["norm"]].cpu().numpy(), eps)
     y = port.gemv(Q4_0, t["W"].cpu().numpy(), x, t["rows"], t["cols"])
+    if "W_up" in t:  # the pair's SwiGLU epilogue
+        y = port.swiglu(y, port.gemv(Q4_0, t["W_up"].cpu().numpy(), x, t["rows"], t["cols"]))
     if "res" in t and t["res"] != -2:
         y = (y + out(t["res"])).astype(np.float32)
     return y
 
 
-@pytest.mark.parametrize("dims", [(1024, 256, 2048, 1000, 2), (4096, 1024, 14336, 4099, 1)])
-def test_fused_decoder_stack_matches_oracle(L, port, dims):
+@pytest.mark.parametrize("paired", [False, True])
+@pytest.mark.parametrize("dims", [(1024, 256, 2048, 1000, 2), (4096, 1024, 14336, 4099, 1), (8192, 1024, 28672, 512, 1)])
+def test_fused_decoder_stack_matches_oracle(L, port, dims, paired):
     H, KV, F, V, layers = dims
-    tasks, norms = decoder_tasks(H, KV, F, V, layers, 700 + H)
+    tasks, norms = decoder_tasks(H, KV, F, V, layers, 700 + H, paired)
     h = make_stack(L, tasks, norms, H)
     x = torch.from_numpy(synth.activations_numpy(1, H, 5)[0]).cuda()
     st = torch.cuda.current_stream().cuda_stream
@@ -114,18 +127,19 @@ def test_fused_task_argument_checks(L):
     h = ctypes.c_void_p()
 
     def create(**kw):
-        base = dict(src=-1, src2=-1, res=-2, norm=None)
+        base = dict(src=-1, src2=-1, res=-2, norm=None, w_up=None)
         base.update(kw)
         arr = (_native.StackTaskEx * 2)()
         arr[0] = _native.StackTaskEx(W.data_ptr(), H, H, y0.data_ptr(), -1, -1, -1, -2, None, 0.0)
         arr[1] = _native.StackTaskEx(W.data_ptr(), H, H, y1.data_ptr(), base["src"], -1, base["src2"], base["res"],
-                                     base["norm"], 1e-5)
+                                     base["norm"], 1e-5, base["w_up"])
         return L.nexus_gpu_stack_create_ex(Q4_0, arr, 2, H, 1, 0, ctypes.byref(h))
 
     assert create(src=0, src2=1) == -5          # x_source2 must be an earlier task
     assert create(src=-1, src2=0) == -5         # SwiGLU needs a task x_source
     assert create(src=0, res=5) == -5           # residual source not earlier
     assert create(src=0, norm=nw.data_ptr() + 4) == -9  # misaligned norm weights
+    assert create(src=0, w_up=W.data_ptr() + 8) == -9    # misaligned up matrix
     assert create(src=0, src2=0, res=0, norm=nw.data_ptr()) == 0
     L.nexus_gpu_stack_destroy(h)
 
