@@ -134,7 +134,7 @@ __device__ __noinline__ bool wait_count_bounded(const unsigned long long* ctr, u
 constexpr int kSigSlots = 16;  // shared per-task completion counters (cumulative, by signal ordinal)
 // mbarriers, a broadcast flag, the end-of-run post count, the completion slots
 // + RMSNorm partial sums and per-warp scales
-constexpr int kStackBarBytes = 16 * kMaxStages + 32 + 4 * kSigSlots + 4 * 16 + 4 * 16;
+constexpr int kStackBarBytes = 16 * kMaxStages + 32 + 4 * kSigSlots + 4 * 16 + 16 * 16;
 constexpr int kStackSmemHeader = ((kStackBarBytes + 127) / 128) * 128 + kSmemHeader - kBarBytes;
 
 __device__ __forceinline__ void red_release_shared_add(uint32_t addr, uint32_t v) {
@@ -245,37 +245,48 @@ __device__ __forceinline__ int ld_task_i32(const int* p) {
     return v;
 }
 
-// The residual vector of task T (the stack input, a task's output, or null).
-__device__ __forceinline__ const float* task_residual(const StackParams& P, const StackTask* T) {
-    return ld_task_i32(&T->res_input) ? P.x_in : reinterpret_cast<const float*>(ld_task_u64(&T->res));
+// The fused variant's per-warp epilogue descriptor in shared memory, one
+// 16-byte word per consumer warp: x,y = the residual pointer already offset to
+// this rank's first row (0 when the task has none), z = the RMSNorm scale of
+// the group's input (1 without one), w = 1 for a gate+up pair.  Lane 0 writes
+// it once per task (z once per group) and reads it at each row, so the row
+// loop holds none of it in registers and makes no dependent loads of the task.
+__device__ __forceinline__ float4 ld_ep(const volatile float4* p) {
+    float4 v;
+    asm volatile("ld.volatile.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(smem_u32(const_cast<const float4*>(p))));
+    return v;
+}
+
+__device__ __forceinline__ const float* ep_residual(const float4 e) {
+    return reinterpret_cast<const float*>(((uint64_t)__float_as_uint(e.y) << 32) | __float_as_uint(e.x));
 }
 
 // Row r's residual, loaded when the row starts so that the L2 latency
 // overlaps its dot product (written earlier in this run, possibly by peers).
-__device__ __forceinline__ float residual_of(const StackParams& P, const StackTask* T, int r) {
-    const float* res = task_residual(P, T);
-    return res ? __ldcg(res + (uint64_t)ld_task_i32(&T->row_off) + (uint64_t)r) : 0.0f;
+__device__ __forceinline__ float residual_of(const volatile float4* ep, int r) {
+    const float* res = ep_residual(ld_ep(ep));
+    return res ? __ldcg(res + r) : 0.0f;
 }
 
 // Write row r (of this rank's slice) of task T: this rank's output and --
 // sharded -- every peer's copy (plain stores over NVLink).  v is the row's
-// dot product; in the fused variant (FX) the RMSNorm scale of the task's
-// input (1 without one), the SwiGLU of a gate+up pair (u: the up row's dot
-// product) and the residual rv (residual_of) are applied here:
-// y = v * scale + rv, or silu(v * scale) * (u * scale) + rv for a pair.  The scale is read from shared memory at the store, so
-// that it holds no register through the row loop.
+// dot product; in the fused variant (FX) the epilogue of the descriptor ep
+// is applied: y = v * scale + rv, or silu(v * scale) * (u * scale) + rv for
+// a gate+up pair (u: the up row's dot product, rv: residual_of).
 template <bool FX>
 __device__ __forceinline__ void put_row(const StackParams& P, const StackTask* T, int r, float v,
-                                        const volatile float* scale, float rv, float u) {
+                                        const volatile float4* ep, float rv, float u) {
     const uint64_t g = (uint64_t)ld_task_i32(&T->row_off) + (uint64_t)r;  // global row
     if constexpr (FX) {
-        const float sc = *scale;
-        if (sc != 1.0f) v = __fmul_rn(v, sc);
-        if (ld_task_u64(&T->W2)) {  // gate+up pair: silu(gate) * up (transformer_ops.hpp:86-95)
-            if (sc != 1.0f) u = __fmul_rn(u, sc);
+        const float4 e = ld_ep(ep);
+        if (e.z != 1.0f) v = __fmul_rn(v, e.z);
+        if (__float_as_int(e.w)) {  // gate+up pair: silu(gate) * up (transformer_ops.hpp:86-95)
+            if (e.z != 1.0f) u = __fmul_rn(u, e.z);
             v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u);
         }
-        if (task_residual(P, T)) v = __fadd_rn(v, rv);
+        if (ep_residual(e)) v = __fadd_rn(v, rv);
     }
     reinterpret_cast<float*>(ld_task_u64(&T->y))[g] = v;
     if (P.world > 1) {
@@ -339,13 +350,6 @@ __device__ __forceinline__ float stage_x(const float4* xv, const float4* xv2, co
     return ss;
 }
 
-// The fused variant's staging, kept out of line: its registers (the SwiGLU
-// and norm operands) then never compete with the row loop's x slices.
-__device__ __noinline__ float stage_x_fused(const float4* xv, const float4* xv2, const float4* nw, int K,
-                                            uint32_t xs, int tid, int lane) {
-    return stage_x<true>(xv, xv2, nw, K, xs, tid, lane);
-}
-
 // FX: the variant with the fused RMSNorm / SwiGLU / residual; stacks without
 // them run the variant that has none of their code.
 template <class F, int G, bool FX>
@@ -360,7 +364,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
     const uint32_t tend = sbase + 16 * kMaxStages + 16;  // consumer warps done with every task
     const uint32_t tdone = tend + 16;                     // [kSigSlots] u32 task completion posts
     float* s_norm = reinterpret_cast<float*>(smem + 16 * kMaxStages + 32 + 4 * kSigSlots);  // [16] RMSNorm partials
-    volatile float* s_scale = s_norm + 16;  // [16] each warp's copy of its group's RMSNorm scale
+    volatile float4* s_ep = reinterpret_cast<volatile float4*>(s_norm + 16);  // [16] epilogue descriptors
     constexpr int kHdr = ((kStackBarBytes + 127) / 128) * 128;
     float* slots = reinterpret_cast<float*>(smem + kHdr);
     int* counters = reinterpret_cast<int*>(smem + kHdr + kMaxSlots * 4);  // [kMaxStages][kMaxStageRows]
@@ -541,10 +545,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
         const StackTask& H = P.tasks[t];
         const int K = __ldg(&H.K), S = __ldg(&H.segments);
         const int NW = __ldg(&H.nwi), SW = __ldg(&H.seg_wi), J = __ldg(&H.wi_per_lane);
-        const int sg = warp % S, grp = warp / S, n_grp = kConsumerWarps / S;
-        int wi[kMaxJ];
-        bool has[kMaxJ];
-        lane_items<G>(lane, sg, SW, J, NW, wi, has);
         if (tid == 0) {  // the input's CTAs (all ranks) are done, and the ordering dependency
             const int src = __ldg(&H.src), src2 = __ldg(&H.src2), after = __ldg(&H.after), rs = __ldg(&H.res_src);
             const unsigned long long target = (run + 1) * (unsigned long long)P.world * (unsigned long long)n_cta;
@@ -566,7 +566,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
             const float4* xv2 =
                 FX ? reinterpret_cast<const float4*>(__ldg(reinterpret_cast<const unsigned long long*>(&H.x2))) : nullptr;
             float ss;  // RMSNorm: sum of squares of this thread's elements
-            if constexpr (FX) ss = stage_x_fused(xv, xv2, nw, K, xs, tid, lane);
+            if (FX && (xv2 != nullptr || nw != nullptr)) ss = stage_x<FX>(xv, xv2, nw, K, xs, tid, lane);
             else ss = stage_x<false>(xv, nullptr, nullptr, K, xs, tid, lane);
             if (nw != nullptr) {
 #pragma unroll
@@ -587,7 +587,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
             for (int w = 0; w < kConsumerWarps; ++w) tot = __fadd_rn(tot, s_norm[w]);
             gscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), __ldg(&H.norm_eps))));
         }
-        if (FX && lane == 0) s_scale[warp] = gscale;  // read back by this lane at its row stores
+        if (FX && lane == 0) s_ep[warp].z = gscale;  // read back by this lane at its row stores
+        // this lane's work items (after the staging, so they hold no registers through it)
+        const int sg = warp % S, grp = warp / S, n_grp = kConsumerWarps / S;
+        int wi[kMaxJ];
+        bool has[kMaxJ];
+        lane_items<G>(lane, sg, SW, J, NW, wi, has);
         XT X[kMaxJ];
         {
             const int nxbp = x_stage_planes_len(K);
@@ -604,6 +609,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
             const uint32_t half = FX ? (uint32_t)__ldg(&T.half) : 0u;  // a gate+up pair when non-zero
             int row_begin, row_end;
             cta_rows(N, c, n_cta, row_begin, row_end);
+            if (FX && lane == 0) {  // this task's residual and pair flag into the warp's descriptor
+                const float* res = ld_task_i32(&T.res_input) ? P.x_in
+                                                             : reinterpret_cast<const float*>(ld_task_u64(&T.res));
+                const uint64_t rp = res ? (uint64_t)(res + ld_task_i32(&T.row_off)) : 0ull;
+                s_ep[warp].x = __uint_as_float((uint32_t)rp);
+                s_ep[warp].y = __uint_as_float((uint32_t)(rp >> 32));
+                s_ep[warp].w = __int_as_float(half != 0u);
+            }
             const int n_st = (row_end - row_begin + R - 1) / R;
             int rot = 0;
             for (int i = 0; i < n_st; ++i) {
@@ -622,7 +635,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                     for (; rl < nr; rl += n_grp) {
                         const uint32_t row = base + (uint32_t)(rl * rbytes);
                         float rv = 0.0f;
-                        if (FX && lane == 0) rv = residual_of(P, &T, r0 + rl);
+                        if (FX && lane == 0) rv = residual_of(s_ep + warp, r0 + rl);
                         float acc = row_partial<F, G>(row, wi, has, X);
 #pragma unroll
                         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -633,7 +646,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                             for (int o = 16; o > 0; o >>= 1) up += __shfl_xor_sync(0xffffffffu, up, o);
                         }
                         if (S == 1) {
-                            if (lane == 0) put_row<FX>(P, &T, r0 + rl, acc, s_scale + warp, rv, up);
+                            if (lane == 0) put_row<FX>(P, &T, r0 + rl, acc, s_ep + warp, rv, up);
                         } else if (lane == 0) {
                             float* sl = slots + s * P.slot_stride + rl * S * (half ? 2 : 1);
                             sl[sg] = acc;
@@ -646,7 +659,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                                 for (int k = 0; k < S; ++k) v += *(volatile float*)(sl + k);
                                 if (FX && half)
                                     for (int k = 0; k < S; ++k) u += *(volatile float*)(sl + S + k);
-                                put_row<FX>(P, &T, r0 + rl, v, s_scale + warp, rv, u);
+                                put_row<FX>(P, &T, r0 + rl, v, s_ep + warp, rv, u);
                                 counters[s * kMaxStageRows + rl] = 0;
                             }
                         }
