@@ -52,8 +52,8 @@ class ShardedStack:
     ``tasks``: sequence of (W_slice_ptr, rows, cols, x_source, after) with the
     FULL row count and this rank's row slice of W (``shard_rows``), as for
     nexus_gpu_stack_create_sharded; optionally followed by (x_source2,
-    residual_source, norm_weight_ptr, norm_eps), the fusions of
-    nexus_gpu_stack_create_ex.  Outputs are full-length on every rank
+    residual_source, norm_weight_ptr, norm_eps, W_up_slice_ptr), the fusions
+    of nexus_gpu_stack_create_ex.  Outputs are full-length on every rank
     (``output(i)``)."""
 
     def __init__(self, dtype: int, tasks: Sequence[tuple], input_cols: int, world: int, rank: int,
@@ -63,9 +63,10 @@ class ShardedStack:
         arr = (_native.StackTaskEx * len(tasks))()
         for i, t in enumerate(tasks):
             w, rows, cols, src, after = t[:5]
-            # optional fusions (nexus_gpu_stack_create_ex): x_source2, residual_source, norm weights, eps
-            src2, res, nw, eps = tuple(t[5:]) + (-1, -2, None, 0.0)[len(t) - 5:]
-            arr[i] = _native.StackTaskEx(w, rows, cols, None, src, after, src2, res, nw, eps)
+            # optional fusions (nexus_gpu_stack_create_ex): x_source2, residual_source, norm
+            # weights, eps, and this rank's row slice of the up matrix of a gate+up pair
+            src2, res, nw, eps, w_up = tuple(t[5:]) + (-1, -2, None, 0.0, None)[len(t) - 5:]
+            arr[i] = _native.StackTaskEx(w, rows, cols, None, src, after, src2, res, nw, eps, w_up)
         h = ctypes.c_void_p()
         _native.check(self.L.nexus_gpu_stack_create_ex(dtype, arr, len(tasks), input_cols, world, rank,
                                                         ctypes.byref(h)))
