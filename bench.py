@@ -286,7 +286,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-formats", action="store_true",
-                    help="skip the INT4-AWQ / FP8-E4M3 per-shape GEMV timings")
+                    help="skip the per-format GEMV timings (GGUF formats, INT4-AWQ, FP8-E4M3)")
     ap.add_argument("--no-gguf", action="store_true",
                     help="skip the GGUF file -> device upload measurement")
     ap.add_argument("--no-fused", action="store_true",
@@ -448,6 +448,7 @@ def main():
         if not args.no_batched:
             extra["batched_decode"] = batched_decode(torch, L, layers, head, stream, dev, timed, args, peak)
         if not args.no_formats:
+            extra["gguf_gemv"] = gguf_formats(torch, L, stream, dev, timed, peak)
             extra["int4_awq_fp8"] = other_formats(torch, L, stream, dev, timed, peak)
         if not args.no_fused:
             extra["fused_decode_stack"] = fused_decode_stack(torch, L, layers, head, h0, stream, dev, timed, args, peak)
@@ -582,6 +583,55 @@ def batched_decode(torch, L, layers, head, stream, dev, timed, args, peak):
                     "path": "tcgen05 kind::f16 (gemm_q4_0_mma_kernel)" if M >= 16 else
                             "batch-1 CUDA-core kernel per token", "steps": reps})
         del g
+    return out
+
+
+def gguf_formats(torch, L, stream, dev, timed, peak):
+    """Batch-1 GEMV per GGUF format (Q4_0, Q8_0, Q5_K, Q6_K, FP16) through
+    nexus_gpu_gemv, the drop-in for the reference's fused_gemv_* (x quantized,
+    then the fused GEMV: two launches a call), on the Llama-3-8B FFN and LM
+    head shapes and the 70B FFN shapes.  Seeded blocks with the configs'
+    distributions; each shape cycles over enough weight copies for >= 512 MB
+    per graph pass (weights come from HBM); GB/s counts weights, x and y once
+    per call."""
+    from nexusllm_b200 import synth
+    from nexusllm_b200.formats import weight_bytes
+
+    shapes = [(14336, 4096), (4096, 14336), (128256, 4096), (28672, 8192), (8192, 28672)]
+    out = []
+    for dt, name in ((7, "q4_0"), (9, "q8_0"), (11, "q5_k"), (12, "q6_k"), (1, "fp16")):
+        for rows, cols in shapes:
+            wb = weight_bytes(dt, rows, cols)
+            alg = wb + cols * 4 + rows * 4
+            n = max(1, -(-(512 << 20) // wb))
+            W = [synth.blocks_torch(dt, rows, cols, 4000 + 7 * i + dt) for i in range(n)]
+            x = torch.randn(cols, device=dev, generator=torch.Generator(device=dev).manual_seed(cols))
+            y = torch.empty(rows, device=dev)
+            calls = 2 * n
+
+            def run():
+                st = torch.cuda.current_stream(dev).cuda_stream
+                for i in range(calls):
+                    rc = L.nexus_gpu_gemv(W[i % n].data_ptr(), dt, x.data_ptr(), 0, y.data_ptr(), 1, rows, cols, st)
+                    if rc:
+                        raise RuntimeError(L.nexus_gpu_last_error())
+
+            with torch.cuda.stream(stream):
+                run()
+            torch.cuda.synchronize(dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                run()
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    g.replay()
+            reps = 5
+            ms = timed(g.replay, reps) / (reps * calls)
+            gbs = alg / (ms * 1e-3) / 1e9
+            out.append({"format": name, "rows": rows, "cols": cols, "us_per_call": round(ms * 1e3, 2),
+                        "value": round(gbs, 1), "unit": "GB/s", "pct_of_measured_hbm": round(100 * gbs / peak, 1),
+                        "gemv_calls_per_s": round(1e3 / ms, 1), "bytes_per_call": alg, "weight_copies": n})
+            del g, W
     return out
 
 

@@ -40,6 +40,8 @@
 // ggml's) Q5_K / Q6_K bit orders (src/quantization.cpp:418-509).
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include <type_traits>
 
 #include "device_common.cuh"
@@ -397,11 +399,33 @@ __device__ __forceinline__ float dot_q6_k_x4(uint32_t o, int h, const XInt (&X)[
     return r;
 }
 
-// FP16: 16 halves at p (2-byte aligned) against x held in registers.
+// FP16: 16 halves at p against x held in registers.  FP16 rows are whole
+// 32-byte work items (K % 16 == 0) and the staging keeps them 16-byte
+// aligned, so two 128-bit shared loads fetch them.
+// The reference's decoder rebiases the exponent without special-casing zero
+// and subnormal halves (0x0000 -> 2^-15).  For every half whose exponent
+// field is at most 29 that equals half the IEEE value of h + 0x0400 (exponent
+// one higher), so the hardware conversion serves: one add per word, one
+// conversion per half, and the sum is halved at the end (exact: the partial
+// sums are all exactly doubled).  One SWAR test per word finds exponents 30
+// and 31 (|w| >= 32768, Inf, NaN), for which the bit-level decoder runs.
 __device__ __forceinline__ float dot_f16(uint32_t p, const XF16& X) {
-    uint32_t w[8];
-    lds_words_2a<8>(p, w);
+    const uint4 lo = lds128(p), hi = lds128(p + 16);
+    const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+    uint32_t big = 0;  // bit 15 of a half set when its exponent field is 30 or 31
+#pragma unroll
+    for (int q = 0; q < 8; ++q) big |= (w[q] & 0x7c007c00u) + 0x08000800u;
     float a0 = 0.f, a1 = 0.f;
+    if ((big & 0x80008000u) == 0u) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const uint32_t v = w[q] + 0x04000400u;  // no carry between the halves: both exponents <= 29
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&v));
+            a0 = fmaf(f.x, X.v[2 * q], a0);
+            a1 = fmaf(f.y, X.v[2 * q + 1], a1);
+        }
+        return (a0 + a1) * 0.5f;
+    }
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
         a0 = fmaf(nexus_fp16(w[q] & 0xffffu), X.v[2 * q], a0);

@@ -247,3 +247,31 @@ def test_errors_and_status(L, be):
     bits = ctypes.c_uint32(99)
     assert L.nexus_gpu_device_status(ctypes.byref(bits)) == 0
     assert bits.value == 0, "a bounded device wait expired during the tests"
+
+
+def test_fp16_special_halves_take_the_exact_decoder(be):
+    """FP16 weights holding every kind of half the two kernel paths split on:
+    zeros and subnormals (which the reference decodes as 2^-15 (1 + m/1024),
+    served by the shifted hardware conversion), exponent 30 (|w| >= 32768)
+    and Inf/NaN (decoded to 0), which send their 16-weight item to the
+    bit-level decoder.  Rows mix both paths; compared with the C oracle."""
+    port = oracle.port()
+    rows, cols = 512, 4096
+    r = np.random.default_rng(17)
+    W = (r.standard_normal((rows, cols)) * 0.02).astype(np.float16).view(np.uint16)
+    specials = np.array([0x0000, 0x8000, 0x0001, 0x83FF, 0x03FF, 0x7800, 0xF9FF, 0x7BFF, 0x7C00, 0xFC00, 0x7E00,
+                         0xFFFF], np.uint16)
+    for i in range(rows):  # most rows get a few special halves, some none
+        k = r.integers(0, 4)
+        W[i, r.integers(0, cols, size=k)] = r.choice(specials, size=k)
+    W[0, :16] = 0x7C00  # a whole work item of Inf
+    W[1, ::2] = 0x0000   # zeros everywhere in a row
+    W = np.ascontiguousarray(W.reshape(-1))
+    x = r.standard_normal(cols).astype(np.float32) * 0.01
+    got = gpu_gemv(be, DataType.FP16, W, x, rows, cols)
+    want = port.gemv(int(DataType.FP16), W, x, rows, cols)
+    assert np.isfinite(got).all() and np.isfinite(want).all()
+    assert oracle.l2_rel(got, want) <= TOL
+    # row by row as well: the large values of exponent-30 halves must not hide a wrong row
+    rel = np.abs(got - want) / np.maximum(np.abs(want), 1e-3)
+    assert np.median(rel) < 1e-4 and rel.max() < 1e-2
