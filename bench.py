@@ -781,7 +781,13 @@ def gguf_upload(torch, L, dev):
 
     from nexusllm_b200 import _native, gguf
 
-    block = np.random.default_rng(3).integers(0, 256, 64 << 20, dtype=np.uint8).tobytes()
+    # one ~64 MiB pattern of whole Q4_0 blocks (scales ~U[0.005, 0.02], random nibbles), repeated
+    rng = np.random.default_rng(3)
+    nbk = (64 << 20) // 18
+    blk = np.empty((nbk, 18), np.uint8)
+    blk[:, :2] = rng.uniform(0.005, 0.02, nbk).astype(np.float16).view(np.uint8).reshape(nbk, 2)
+    blk[:, 2:] = rng.integers(0, 256, (nbk, 16), dtype=np.uint8)
+    block = blk.tobytes()
 
     def filler(n):
         def fn(f):
@@ -796,10 +802,14 @@ def gguf_upload(torch, L, dev):
     tensors = [("token_embd.weight", gguf.GGML_Q4_0, [HIDDEN, VOCAB], q4(VOCAB, HIDDEN))]
     names = {"q": "attn_q", "k": "attn_k", "v": "attn_v", "o": "attn_output", "gate": "ffn_gate", "up": "ffn_up",
              "down": "ffn_down"}
+    ones = np.ones(HIDDEN, np.float32).tobytes()
     for l in range(LAYERS):
         for name, n, k in LAYER_SHAPES:
             tensors.append((f"blk.{l}.{names[name]}.weight", gguf.GGML_Q4_0, [k, n], q4(n, k)))
-    tensors.append(("output.weight", gguf.GGML_Q4_0, [HIDDEN, VOCAB], q4(VOCAB, HIDDEN)))
+        tensors += [(f"blk.{l}.attn_norm.weight", gguf.GGML_F32, [HIDDEN], ones),
+                    (f"blk.{l}.ffn_norm.weight", gguf.GGML_F32, [HIDDEN], ones)]
+    tensors += [("output_norm.weight", gguf.GGML_F32, [HIDDEN], ones),
+                ("output.weight", gguf.GGML_Q4_0, [HIDDEN, VOCAB], q4(VOCAB, HIDDEN))]
     meta = [("general.architecture", gguf.STRING, "llama"), ("llama.embedding_length", gguf.U32, HIDDEN),
             ("llama.block_count", gguf.U32, LAYERS), ("llama.feed_forward_length", gguf.U32, FFN)]
     d = tempfile.mkdtemp(prefix="nexus_gguf_")
@@ -838,6 +848,35 @@ def gguf_upload(torch, L, dev):
             torch.cuda.synchronize(dev)
             plain_s = time.perf_counter() - t0
             del mm
+        # the decode step from this file: weights and norms uploaded once, one fused stack per token
+        from nexusllm_b200.decode import GgufDecodeStack
+
+        t0 = time.perf_counter()
+        dec = GgufDecodeStack(path, device=dev)
+        load_s = time.perf_counter() - t0
+        xh = torch.randn(HIDDEN, device=dev, generator=torch.Generator(device=dev).manual_seed(1))
+        sdec = torch.cuda.Stream(dev)
+        with torch.cuda.stream(sdec):
+            dec.step(xh, sdec)
+        torch.cuda.synchronize(dev)
+        gdec = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gdec, stream=sdec):
+            dec.step(xh, sdec)
+        with torch.cuda.stream(sdec):
+            for _ in range(3):
+                gdec.replay()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+            ev[0].record()
+            for _ in range(50):
+                gdec.replay()
+            ev[1].record()
+        torch.cuda.synchronize(dev)
+        dec_ms = ev[0].elapsed_time(ev[1]) / 50
+        if not bool(torch.isfinite(dec.outputs[-1][1]).all()):
+            raise RuntimeError("decode step from the GGUF file produced non-finite logits")
+        del gdec
+        dec.close()
+        del dec
         host = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
         dbuf = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
@@ -858,7 +897,11 @@ def gguf_upload(torch, L, dev):
             "first_upload_s": round(times[0], 4), "pinned_h2d_gbs": round(pinned_gbs, 2),
             "frac_of_pinned_h2d": round(gbs / pinned_gbs, 3),
             "plain_per_tensor_pageable_gbs": round(data_bytes / plain_s / 1e9, 2),
-            "write_file_s": round(write_s, 2), "page_cache": "warm (file just written)"}
+            "write_file_s": round(write_s, 2), "page_cache": "warm (file just written)",
+            "decode_from_file": {"load_s": round(load_s, 3), "ms_per_step": round(dec_ms, 4),
+                                 "tokens_per_s": round(1e3 / dec_ms, 1),
+                                 "path": "GgufDecodeStack: parse, upload, one fused stack (norms, gate+up pair, "
+                                         "residuals) per token"}}
 
 
 def build_stack_graph(torch, L, _native, layers, head, h0, stream, dev):
