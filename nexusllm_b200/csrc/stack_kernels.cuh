@@ -31,6 +31,12 @@
 //    run ends when every rank's rows of every task have landed everywhere:
 //    each CTA posts its end to every rank after a system-scope release, and
 //    one thread per rank waits for all of them.
+//  * The fused variant (template flag FX, nexus_gpu_stack_create_ex) adds the
+//    decode layer's operations around the GEMVs: the group's x staging
+//    applies a SwiGLU of two sources and the RMSNorm weights and sums x^2;
+//    rows are scaled by 1/rms, a gate+up pair computes both rows from one
+//    ring slot and stores silu(gate) * up, and a residual vector is added at
+//    the store.  Stacks without these run the plain variant.
 //  * All CTAs must be resident at once (they wait on one another): the host
 //    launches the kernel cooperatively with one CTA per SM.  Every wait is
 //    bounded; an expired wait raises a global abort flag that ends every CTA's
