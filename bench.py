@@ -446,7 +446,7 @@ def main():
         launches_note = f"1 gemv_stack_kernel per step x {args.steps} steps (plus one counter memset per step)"
         extra = {"per_gemv_graph": per_gemv, "e2e_per_gemv_dispatch": e2e_dispatch}
         if not args.no_batched:
-            extra["batched_decode"] = batched_decode(torch, L, layers, head, stream, dev, timed, args, peak)
+            extra["batched_decode"] = batched_decode(torch, L, layers, head, stream, dev, timed, args, peak, stack)
         if not args.no_formats:
             extra["gguf_gemv"] = gguf_formats(torch, L, stream, dev, timed, peak)
             extra["int4_awq_fp8"] = other_formats(torch, L, stream, dev, timed, peak)
@@ -535,7 +535,7 @@ def check_status(L):
         raise RuntimeError(f"device status word {bits.value:#x} (a bounded wait expired)")
 
 
-def batched_decode(torch, L, layers, head, stream, dev, timed, args, peak):
+def batched_decode(torch, L, layers, head, stream, dev, timed, args, peak, stack=None):
     """configs[3] at M = 4, 16, 64 tokens per step (N=1): the step's 225
     GEMVs with M activation rows each, one nexus_gpu_gemv_ws call per GEMV,
     captured in a CUDA graph.  M >= 16 runs on the tcgen05 tensor cores; M = 4
@@ -582,6 +582,37 @@ def batched_decode(torch, L, layers, head, stream, dev, timed, args, peak):
                     "value": round(gbs, 1), "unit": "GB/s", "pct_of_measured_hbm": round(100 * gbs / peak, 2),
                     "path": "tcgen05 kind::f16 (gemm_q4_0_mma_kernel)" if M >= 16 else
                             "batch-1 CUDA-core kernel per token", "steps": reps})
+        del g
+    if stack is not None:
+        # M = 4 tokens through the GEMV stack, one launch per token (the batch-1
+        # CUDA-core path, without per-GEMV launches); each token has its own
+        # input, and each run overwrites the previous token's outputs (an engine
+        # reads a token's logits before its next run)
+        M = 4
+        xs = [torch.randn(HIDDEN, generator=torch.Generator(device=dev).manual_seed(40 + m), device=dev)
+              for m in range(M)]
+
+        def step4():
+            st = torch.cuda.current_stream(dev).cuda_stream
+            for m in range(M):
+                _native_check(L.nexus_gpu_stack_run(stack, xs[m].data_ptr(), st))
+
+        with torch.cuda.stream(stream):
+            step4()
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step4()
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                g.replay()
+        reps = max(5, min(50, args.steps // 20))
+        ms = timed(g.replay, reps) / reps
+        gbs = step_bytes(layers=len(layers)) / (ms * 1e-3) / 1e9  # weights once per step, as above
+        out.append({"M": M, "ms_per_step": round(ms, 4), "tokens_per_s": round(M * 1e3 / ms, 1),
+                    "value": round(gbs, 1), "unit": "GB/s", "pct_of_measured_hbm": round(100 * gbs / peak, 2),
+                    "path": "GEMV stack once per token (batch-1 CUDA-core path, one launch per token)",
+                    "steps": reps})
         del g
     return out
 
