@@ -1720,8 +1720,13 @@ NEXUS_GPU_API int32_t nexus_gpu_gguf_open(const char* path, void** out_file) {
 NEXUS_GPU_API int32_t nexus_gpu_gguf_close(void* file) {
     if (!file) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null file");
     auto* f = static_cast<gguf::File*>(file);
-    if (!f->ring.empty()) cudaSetDevice(f->device);
+    int cur = -1;
+    if (!f->ring.empty()) {  // the staging buffers belong to the upload's device
+        cudaGetDevice(&cur);
+        cudaSetDevice(f->device);
+    }
     gguf::close_file(*f);
+    if (cur >= 0) cudaSetDevice(cur);  // leave the caller's current device as it was
     delete f;
     return NEXUS_GPU_SUCCESS;
 }
@@ -1820,13 +1825,23 @@ NEXUS_GPU_API int32_t nexus_gpu_gguf_upload(void* file, const uint64_t* indices,
         f.ring.clear();
         CUDA_TRY(cudaSetDevice(d->id));
     }
-    if (f.ring.empty()) {
-        f.device = d->id;
-        f.ring.resize(gguf::kStages);
-        for (gguf::Staging& s : f.ring) {
-            CUDA_TRY(cudaHostAlloc(&s.host, gguf::kStageBytes, cudaHostAllocDefault));
-            CUDA_TRY(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming));
+    if (f.ring.empty()) {  // pinned staging ring, kept for later uploads; all or nothing
+        std::vector<gguf::Staging> ring(gguf::kStages);
+        cudaError_t e = cudaSuccess;
+        for (gguf::Staging& s : ring) {
+            if (e == cudaSuccess) e = cudaHostAlloc(&s.host, gguf::kStageBytes, cudaHostAllocDefault);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming);
         }
+        if (e != cudaSuccess) {
+            for (gguf::Staging& s : ring) {
+                if (s.done) cudaEventDestroy(s.done);
+                if (s.host) cudaFreeHost(s.host);
+            }
+            cudaGetLastError();
+            return fail(NEXUS_GPU_ERROR_OUT_OF_HOST_MEMORY, "pinned staging buffers: %s", cudaGetErrorString(e));
+        }
+        f.device = d->id;
+        f.ring = std::move(ring);
     }
     std::vector<gguf::Segment> seg(n);
     for (uint64_t i = 0; i < n; ++i) {
