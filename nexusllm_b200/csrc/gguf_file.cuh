@@ -94,7 +94,8 @@ struct File {
     int fd = -1;
     const uint8_t* base = nullptr;
     size_t size = 0;
-    uint32_t version = 0, alignment = 32;
+    uint32_t version = 0;
+    uint64_t alignment = 32;  // general.alignment as stored (validated after the metadata)
     uint64_t data_offset = 0, skipped = 0;
     Model model;
     std::vector<Tensor> tensors;
@@ -168,8 +169,8 @@ inline bool has(const std::string& key, const char* part) { return key.find(part
 // A numeric metadata value, read as the reference reads it
 // (model_loader.cpp:598-631): the unsigned bits of integers, floats also
 // truncated to an integer.
-inline void apply_number(Model& m, uint32_t& alignment, const std::string& key, uint64_t u, float f) {
-    if (key == "general.alignment") alignment = (uint32_t)(u > 0 ? u : 32);
+inline void apply_number(Model& m, uint64_t& alignment, const std::string& key, uint64_t u, float f) {
+    if (key == "general.alignment") alignment = u > 0 ? u : 32;
     else if (has(key, ".context_length")) m.ctx = (uint32_t)u;
     else if (has(key, ".embedding_length")) m.hidden = (uint32_t)u;
     else if (has(key, ".feed_forward_length")) m.ffn = (uint32_t)u;
@@ -347,8 +348,13 @@ inline bool parse(const char* path, File& f, std::string& err) {
         if (!r.get(t.ggml_type) || !r.get(t.rel_offset)) return err = "truncated tensor table", false;
         all.push_back(std::move(t));
     }
+    // The reference rounds up with a mask after casting the value to 32 bits
+    // (model_loader.cpp:640,720), which is only the intended rounding for a
+    // power of two below 2^32; any other value is refused here.
+    if ((f.alignment & (f.alignment - 1)) != 0 || f.alignment > (uint64_t(1) << 31))
+        return err = "general.alignment " + std::to_string(f.alignment) + " is not a power of two up to 2^31", false;
     const uint64_t cur = (uint64_t)(r.p - f.base);
-    f.data_offset = (cur + f.alignment - 1) / f.alignment * f.alignment;
+    f.data_offset = (cur + f.alignment - 1) & ~(f.alignment - 1);
 
     long max_layer = -1;
     for (Tensor& t : all) {

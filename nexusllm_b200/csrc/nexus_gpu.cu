@@ -295,7 +295,12 @@ int32_t run_gemm_tc(Device& d, const void* dW, const void* dX, int xbf, float* d
                     uint8_t* ws, cudaStream_t st);
 
 // Workspace bytes of one GEMV call (gemv_ws_bytes with the tensor path allowed).
+// Activation rows one GEMV call accepts: the x quantizer's grid has one row
+// of CTAs per token (gridDim.y <= 65535).
+constexpr size_t kMaxActivationRows = 65535;
+
 size_t gemv_ws_bytes(int sms, uint32_t dtype, size_t M, size_t rows, size_t cols, bool allow_tc) {
+    if (M > kMaxActivationRows) return 0;  // refused by every entry point before any size matters
     if (allow_tc && tc_eligible(dtype, M, cols)) return tc_group_bytes(sms, rows, cols);
     return xq_bytes(dtype, M, cols);
 }
@@ -309,6 +314,8 @@ int32_t run_gemv(Device& d, const void* dW, uint32_t dtype, const void* dX, uint
     if (rc) return rc;
     if (x_dtype != NEXUS_GPU_FP32 && x_dtype != NEXUS_GPU_BF16)
         return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "unsupported activation dtype %u", x_dtype);
+    if (M > kMaxActivationRows)
+        return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "M=%zu activation rows, at most %zu", M, kMaxActivationRows);
     if (M == 0 || rows == 0) return NEXUS_GPU_SUCCESS;
     if (cols == 0) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "cols == 0");
     if (!dW || !dX || !dY) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null device pointer");
@@ -1066,6 +1073,7 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
         T.wi_per_lane = gp.wi_per_lane;
         T.stage_rows = gp.stage_rows;
         T.stage_bytes = gp.stage_bytes;
+        T.rot_step = gp.stage_rows % (kConsumerWarps / gp.segments);
         T.row_off = (int)row_off[i];
         if (u.W_up) {  // the up rows of a stage sit half a slot after the gate rows
             T.W2 = static_cast<const uint8_t*>(u.W_up);
@@ -1127,7 +1135,14 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
         }
     }
 
-    cudaError_t e = cudaMalloc(&h->d_tasks, n * sizeof(StackTask));
+    // each task's rows for each CTA, balanced: [N*c/grid, N*(c+1)/grid) of this rank's slice
+    const size_t task_bytes = align256(n * sizeof(StackTask));
+    std::vector<int2> cta_rows((size_t)n * h->grid);
+    for (uint32_t i = 0; i < n; ++i)
+        for (int c = 0; c < h->grid; ++c)
+            cta_rows[(size_t)i * h->grid + c] = make_int2((int)(local_rows[i] * (uint64_t)c / (uint64_t)h->grid),
+                                                          (int)(local_rows[i] * (uint64_t)(c + 1) / (uint64_t)h->grid));
+    cudaError_t e = cudaMalloc(&h->d_tasks, task_bytes + cta_rows.size() * sizeof(int2));
     if (e == cudaSuccess) e = cudaMalloc(&h->d_block, lay.total);
     if (e == cudaSuccess) e = cudaMemset(h->d_block, 0, lay.total);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -1175,12 +1190,16 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
         if (T.signal) ++sig_in_group;
     }
     e = cudaMemcpy(h->d_tasks, ht.data(), n * sizeof(StackTask), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(reinterpret_cast<uint8_t*>(h->d_tasks) + task_bytes, cta_rows.data(),
+                       cta_rows.size() * sizeof(int2), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
         stack_free(h);
         return fail(NEXUS_GPU_ERROR_CUDA, "stack upload failed: %s", cudaGetErrorString(e));
     }
     StackParams& P = h->params;
     P.tasks = h->d_tasks;
+    P.cta_rows = reinterpret_cast<const int2*>(reinterpret_cast<uint8_t*>(h->d_tasks) + task_bytes);
     P.n_tasks = (int)n;
     P.n_stages = ns;
     P.stage_slot = (int)slot;
@@ -1359,6 +1378,9 @@ int32_t noalloc_device(Device** out_dev, uint8_t** out_scratch) {
         CUDA_TRY(cudaDeviceGetAttribute(&e.dev.sms, cudaDevAttrMultiProcessorCount, id));
         CUDA_TRY(cudaDeviceGetAttribute(&e.dev.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, id));
         e.scratch = static_cast<uint8_t*>(ptr);
+        // kernel attributes too, under the lock: later calls only read e.dev
+        int32_t rc = ensure_attrs(e.dev);
+        if (rc) return rc;
         e.ready = true;
     }
     *out_dev = &e.dev;
@@ -1499,6 +1521,8 @@ NEXUS_GPU_API int32_t nexus_gpu_gemv_ws(const void* dW, uint32_t dtype, const vo
                                         size_t M, size_t rows, size_t cols, void* workspace, size_t workspace_bytes,
                                         void* stream) {
     t_last_error.clear();
+    if (M > kMaxActivationRows)
+        return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "M=%zu activation rows, at most %zu", M, kMaxActivationRows);
     Device* d = nullptr;
     int32_t rc = get_device(&d);
     if (rc) return rc;
@@ -1531,6 +1555,9 @@ NEXUS_GPU_API int32_t nexus_gpu_gemv_noalloc(const void* dW, uint32_t dtype, con
     FormatInfo f;
     int32_t rc = check_shape(dtype, rows, cols, f);
     if (rc) return rc;
+    // bound M first, so that the scratch size below cannot overflow
+    if (M > kMaxActivationRows)
+        return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "M=%zu activation rows, at most %zu", M, kMaxActivationRows);
     const size_t need = xq_bytes(dtype, M, cols);
     if (need > kNoAllocScratchBytes)
         return fail(NEXUS_GPU_ERROR_WORKSPACE,
@@ -1738,7 +1765,7 @@ NEXUS_GPU_API int32_t nexus_gpu_gguf_model(void* file, NexusGpuGgufModel* out) {
     memset(out, 0, sizeof(*out));
     snprintf(out->architecture, sizeof(out->architecture), "%s", m.architecture.c_str());
     out->version = f.version;
-    out->alignment = f.alignment;
+    out->alignment = (uint32_t)f.alignment;  // at most 2^31: checked by the parser
     out->tensor_count = f.tensors.size();
     out->skipped = f.skipped;
     out->data_offset = f.data_offset;

@@ -54,6 +54,7 @@ struct StackTask {
     uint64_t row_bytes, total_bytes;
     int N, K;
     int nwi, segments, seg_wi, wi_per_lane, stage_rows, stage_bytes;
+    int rot_step;                        // stage_rows % (row groups): how the row-to-group deal advances per stage
     float* y;                            // this rank's full-length output (slice written at row_off)
     uint64_t y_off;                      // sharded: y's float offset in every rank's block
     const float* x;                      // fp32 x: the source task's y, or null for the stack input
@@ -78,6 +79,7 @@ struct StackTask {
 
 struct StackParams {
     const StackTask* tasks;
+    const int2* cta_rows;                // [n_tasks][n_cta]: rows [x, y) of each task for each CTA (balanced)
     int n_tasks;
     int n_stages;
     int stage_slot;                      // bytes per ring slot (>= every task's stage_bytes)
@@ -100,11 +102,6 @@ struct StackParams {
 // (e = 0, 1, ...) waits for (e + 1) * world * n_cta.
 constexpr int kCounterStride = 16;
 
-// Rows [rb, re) of an N-row task for CTA c of n_cta, balanced.
-__device__ __forceinline__ void cta_rows(int N, int c, int n_cta, int& rb, int& re) {
-    rb = (int)((int64_t)N * c / n_cta);
-    re = (int)((int64_t)N * (c + 1) / n_cta);
-}
 
 __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p, bool sys) {
     unsigned long long v;
@@ -281,10 +278,11 @@ __device__ __forceinline__ float residual_of(const volatile float4* ep, int r) {
 // dot product; in the fused variant (FX) the epilogue of the descriptor ep
 // is applied: y = v * scale + rv, or silu(v * scale) * (u * scale) + rv for
 // a gate+up pair (u: the up row's dot product, rv: residual_of).
+// yl: this rank's output at its first row; yo: the float offset of that row
+// in every rank's stack block (sharded stacks).
 template <bool FX>
-__device__ __forceinline__ void put_row(const StackParams& P, const StackTask* T, int r, float v,
+__device__ __forceinline__ void put_row(const StackParams& P, float* yl, uint64_t yo, int r, float v,
                                         const volatile float4* ep, float rv, float u) {
-    const uint64_t g = (uint64_t)ld_task_i32(&T->row_off) + (uint64_t)r;  // global row
     if constexpr (FX) {
         const float4 e = ld_ep(ep);
         if (e.z != 1.0f) v = __fmul_rn(v, e.z);
@@ -294,12 +292,11 @@ __device__ __forceinline__ void put_row(const StackParams& P, const StackTask* T
         }
         if (ep_residual(e)) v = __fadd_rn(v, rv);
     }
-    reinterpret_cast<float*>(ld_task_u64(&T->y))[g] = v;
+    yl[r] = v;
     if (P.world > 1) {
-        const uint64_t y_off = ld_task_u64(&T->y_off);
 #pragma unroll 1
         for (int p = 0; p < P.world; ++p)
-            if (p != P.rank) reinterpret_cast<float*>(P.peer_block[p])[y_off + g] = v;
+            if (p != P.rank) reinterpret_cast<float*>(P.peer_block[p])[yo + (uint64_t)r] = v;
     }
 }
 
@@ -438,9 +435,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
             const uint8_t* W = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.W)));
             const uint8_t* W2 =
                 FX ? reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.W2))) : nullptr;
-            const int N = __ldg(&T.N), R = __ldg(&T.stage_rows);
-            int row_begin, row_end;
-            cta_rows(N, c, n_cta, row_begin, row_end);
+            const int R = __ldg(&T.stage_rows);
+            const int2 rr = __ldg(P.cta_rows + (size_t)t * n_cta + c);
+            const int row_begin = rr.x, row_end = rr.y;
             const uint64_t floor16 = total & ~(uint64_t)15;
             const uint64_t span = (uint64_t)R * rb, cta_end = (uint64_t)row_end * rb;
             for (uint64_t start = (uint64_t)row_begin * rb; start < cta_end; ++it) {
@@ -610,11 +607,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
         // ---- the group's tasks
         for (;;) {
             const StackTask& T = P.tasks[t];
-            const int N = __ldg(&T.N), R = __ldg(&T.stage_rows);
-            const uint64_t rbytes = __ldg(&T.row_bytes);
+            // task constants, held in registers for the task's rows
+            const int R = __ldg(&T.stage_rows), rot_step = __ldg(&T.rot_step);
+            const uint32_t rbytes = (uint32_t)__ldg(&T.row_bytes);
             const uint32_t half = FX ? (uint32_t)__ldg(&T.half) : 0u;  // a gate+up pair when non-zero
-            int row_begin, row_end;
-            cta_rows(N, c, n_cta, row_begin, row_end);
+            const int2 rr = __ldg(P.cta_rows + (size_t)t * n_cta + c);
+            const int row_off = __ldg(&T.row_off);
+            float* const yl = reinterpret_cast<float*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.y))) + row_off;
+            const uint64_t yo = __ldg(reinterpret_cast<const unsigned long long*>(&T.y_off)) + (uint64_t)row_off;
             if (FX && lane == 0) {  // this task's residual and pair flag into the warp's descriptor
                 const float* res = ld_task_i32(&T.res_input) ? P.x_in
                                                              : reinterpret_cast<const float*>(ld_task_u64(&T.res));
@@ -623,18 +623,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                 s_ep[warp].y = __uint_as_float((uint32_t)(rp >> 32));
                 s_ep[warp].w = __int_as_float(half != 0u);
             }
-            const int n_st = (row_end - row_begin + R - 1) / R;
-            int rot = 0;
-            for (int i = 0; i < n_st; ++i) {
-                const int r0 = row_begin + i * R;
-                const int nr = min(R, row_end - r0);
+            int rot = 0;  // (stage index * R) % n_grp: the group that takes a stage's first row
+            for (int r0 = rr.x; r0 < rr.y; r0 += R) {
+                const int nr = min(R, rr.y - r0);
                 if (alive && !mbar_wait_bounded(full_bar + 8 * s, phase)) {
                     atomicExch(P.abort_flag, 1u);
                     alive = false;  // no more waits; the loop ends at the next group head
                 }
                 if (alive) {
-                    const uint32_t base =
-                        stage0 + (uint32_t)(s * P.stage_slot) + (uint32_t)(((uint64_t)r0 * rbytes) & 15);
+                    // the stage's copy starts at the 16-byte boundary at or below row r0
+                    const uint32_t base = stage0 + (uint32_t)(s * P.stage_slot) + (((uint32_t)r0 * rbytes) & 15u);
                     int rl = grp - rot;
                     if (rl < 0) rl += n_grp;
                     if (grp >= n_grp) rl = nr;  // the 15 - S*n_grp warps past the last row group idle
@@ -652,7 +650,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                             for (int o = 16; o > 0; o >>= 1) up += __shfl_xor_sync(0xffffffffu, up, o);
                         }
                         if (S == 1) {
-                            if (lane == 0) put_row<FX>(P, &T, r0 + rl, acc, s_ep + warp, rv, up);
+                            if (lane == 0) put_row<FX>(P, yl, yo, r0 + rl, acc, s_ep + warp, rv, up);
                         } else if (lane == 0) {
                             float* sl = slots + s * P.slot_stride + rl * S * (half ? 2 : 1);
                             sl[sg] = acc;
@@ -665,7 +663,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                                 for (int k = 0; k < S; ++k) v += *(volatile float*)(sl + k);
                                 if (FX && half)
                                     for (int k = 0; k < S; ++k) u += *(volatile float*)(sl + S + k);
-                                put_row<FX>(P, &T, r0 + rl, v, s_ep + warp, rv, u);
+                                put_row<FX>(P, yl, yo, r0 + rl, v, s_ep + warp, rv, u);
                                 counters[s * kMaxStageRows + rl] = 0;
                             }
                         }
@@ -677,7 +675,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                     s = 0;
                     phase ^= 1;
                 }
-                rot += R % n_grp;
+                rot += rot_step;
                 if (rot >= n_grp) rot -= n_grp;
             }
             // this warp's rows of task t are stored: post it for the producer thread

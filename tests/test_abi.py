@@ -52,6 +52,12 @@ def test_argument_errors_need_no_device(L):
     assert L.nexus_gpu_gemv_dispatch(w, 7, x, y, 4, 33) == -5
     assert L.nexus_gpu_gemv_dispatch(w, 11, x, y, 1, 128) == -5
     assert b"multiple" in L.nexus_gpu_last_error()
+    # activation rows beyond the x quantizer's grid are refused before any size is computed
+    huge = 1 << 40
+    assert L.nexus_gpu_gemv_noalloc(w, 7, x, 0, y, huge, 4, 64, None) == -9
+    assert b"activation rows" in L.nexus_gpu_last_error()
+    assert L.nexus_gpu_gemv_ws(w, 7, x, 0, y, huge, 4, 64, None, 0, None) == -9
+    assert L.nexus_gpu_gemv_workspace_size(7, huge, 4, 64) == 0
 
 
 def test_device_api_rejects_null_or_reports_no_device(L):

@@ -165,9 +165,11 @@ def test_activation_edge_cases(be, port):
     assert np.isnan(got).all()
 
 
-@pytest.mark.parametrize("dt", [DataType.GGUF_Q4_0, DataType.GGUF_Q8_0, DataType.GGUF_Q6_K])
+@pytest.mark.parametrize("dt", [DataType.GGUF_Q4_0, DataType.GGUF_Q8_0, DataType.GGUF_Q5_K, DataType.GGUF_Q6_K])
 def test_weight_edge_blocks(be, port, golden, dt):
-    # the golden edge blocks (special fp16 scales, extreme codes) as one matrix
+    # the golden edge blocks (special fp16 scales -- zero, subnormal, Inf, NaN,
+    # the largest half, a subnormal Q5_K dmin -- and extreme codes) as one
+    # matrix of 256-weight rows (the generic kernel) ...
     W = golden[f"deq/{int(dt)}/W"]
     per, nb_ = BLOCK[dt]
     rows = W.size // nb_ * per // 256
@@ -175,6 +177,16 @@ def test_weight_edge_blocks(be, port, golden, dt):
     x = synth.activations_numpy(1, cols, 13)[0]
     got = gpu_gemv(be, dt, W, x, rows, cols)
     want = port.gemv(int(dt), W, x, rows, cols)
+    assert oracle.l2_rel(got, want) <= TOL
+    # ... and cycled through rows of 4096 weights, where the fast kernel runs
+    blocks = W.reshape(-1, nb_)
+    nb, per_row, rows = blocks.shape[0], 4096 // per, 24
+    idx = (np.arange(rows)[:, None] * 7 + np.arange(per_row)[None, :]) % nb
+    Wt = np.ascontiguousarray(blocks[idx.reshape(-1)]).reshape(-1)
+    x = synth.activations_numpy(1, 4096, 14)[0]
+    got = gpu_gemv(be, dt, Wt, x, rows, 4096)
+    want = port.gemv(int(dt), Wt, x, rows, 4096)
+    assert np.isfinite(want).all()
     assert oracle.l2_rel(got, want) <= TOL
 
 

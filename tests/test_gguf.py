@@ -166,6 +166,33 @@ def test_open_rejects_malformed_files(tmp_path):
     assert L.nexus_gpu_gguf_open(None, ctypes.byref(h)) == -9
 
 
+@pytest.mark.parametrize("vtype,value,ok", [
+    (gguf.U32, 0, True),             # 0 means the default, 32 (model_loader.cpp:640)
+    (gguf.U32, 64, True),
+    (gguf.U64, 1 << 31, True),
+    (gguf.U64, 1 << 32, False),      # the reference's 32-bit cast would make this 0
+    (gguf.U64, 1 << 40, False),
+    (gguf.U32, 48, False),           # not a power of two: the reference's mask rounding differs
+    (gguf.U32, 3, False),
+])
+def test_open_checks_the_alignment(tmp_path, vtype, value, ok):
+    """general.alignment must be a power of two up to 2^31; anything else is
+    refused with a message instead of a division by zero or a wrong offset."""
+    L = _native.lib()
+    p = tmp_path / "a.gguf"
+    norm = struct.pack("<4f", 1.0, 1.0, 1.0, 1.0)
+    gguf.write_gguf(str(p), [("general.architecture", gguf.STRING, "llama"), ("general.alignment", vtype, value)],
+                    [("blk.0.attn_norm.weight", gguf.GGML_F32, [4], norm)], alignment=32)
+    h = ctypes.c_void_p()
+    rc = L.nexus_gpu_gguf_open(str(p).encode(), ctypes.byref(h))
+    if ok:
+        assert rc == 0, L.nexus_gpu_last_error()
+        assert L.nexus_gpu_gguf_close(h) == 0
+    else:
+        assert rc == -3 and h.value is None
+        assert b"general.alignment" in L.nexus_gpu_last_error()
+
+
 def test_upload_checks_before_touching_a_device(files):
     """Refusals that need no device: an unmapped type, a small buffer."""
     with gguf.GGUFFile(files["mixed_types"][0]) as f:

@@ -6,10 +6,12 @@ synchronisation an allocation can cause, callers with no workspace of their
 own.  For them the library keeps the quantized activations in a fixed 1 MiB
 array of its own instead of a workspace.  These tests call the entry point
 through the C ABI and check it against the ordinary entry point
-(nexus_gpu_gemv) within the GEMV tolerance used everywhere (1e-3
-L2-relative), on two calls in a row with different activations, so that a
-stale scratch from the first call would show up in the second.  The file is
-named to be collected last, and it needs no state from other tests.
+(nexus_gpu_gemv) and against the CPU oracle within the GEMV tolerance used
+everywhere (1e-3 L2-relative), on two calls in a row with different
+activations, so that a stale scratch from the first call would show up in
+the second.  A further test checks that the device's free memory does not
+move across calls.  The file is named to be collected last, and it needs no
+state from other tests.
 """
 import ctypes
 
@@ -44,15 +46,41 @@ def _call(fn, W, dt, X, rows, cols):
 @pytest.mark.parametrize("dt", [7, 9, 11, 12, 1], ids=["q4_0", "q8_0", "q5_k", "q6_k", "fp16"])
 def test_noalloc_matches_the_allocating_entry_point_twice(L, dt):
     rows, cols = 1000, 4096
-    W = synth.blocks_torch(dt, rows, cols, 500 + dt)
+    Wh = synth.blocks_numpy(dt, rows, cols, 500 + dt)
+    W = torch.from_numpy(Wh.view(np.uint8)).cuda()
+    port = oracle.port()
     for call, M in enumerate((1, 3)):
-        X = torch.from_numpy(synth.activations_numpy(M, cols, 600 + 10 * dt + call)).cuda()
+        Xh = synth.activations_numpy(M, cols, 600 + 10 * dt + call)
+        X = torch.from_numpy(Xh).cuda()
         rc_a, y_a = _call(L.nexus_gpu_gemv, W, dt, X, rows, cols)
         rc_b, y_b = _call(L.nexus_gpu_gemv_noalloc, W, dt, X, rows, cols)
         torch.cuda.synchronize()
         assert rc_a == 0 and rc_b == 0, L.nexus_gpu_last_error()
         assert torch.isfinite(y_b).all()
-        assert oracle.l2_rel(y_b.cpu().numpy(), y_a.cpu().numpy()) <= TOL, (dt, call)
+        got = y_b.cpu().numpy()
+        assert oracle.l2_rel(got, y_a.cpu().numpy()) <= TOL, (dt, call)
+        want = port.gemv_batched(dt, Wh, Xh, rows, cols)
+        assert oracle.l2_rel(got.reshape(-1), want.reshape(-1)) <= TOL, (dt, call)
+
+
+def test_noalloc_calls_leave_device_memory_unchanged(L):
+    """After the first call (which loads the module and resolves the scratch
+    address), calls of several shapes change the device's free memory by
+    nothing: no cudaMalloc, no allocating library routine."""
+    rows, cols = 512, 4096
+    W = synth.blocks_torch(7, rows, cols, 77)
+    Xs = [torch.randn(M, cols, device="cuda") for M in (1, 2, 3)]
+    ys = [torch.empty(M, rows, device="cuda") for M in (1, 2, 3)]
+    st = torch.cuda.current_stream().cuda_stream
+    assert L.nexus_gpu_gemv_noalloc(W.data_ptr(), 7, Xs[0].data_ptr(), 0, ys[0].data_ptr(), 1, rows, cols, st) == 0
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(3):
+        for X, y in zip(Xs, ys):
+            rc = L.nexus_gpu_gemv_noalloc(W.data_ptr(), 7, X.data_ptr(), 0, y.data_ptr(), X.shape[0], rows, cols, st)
+            assert rc == 0, L.nexus_gpu_last_error()
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch(L):
