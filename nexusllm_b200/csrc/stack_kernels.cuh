@@ -370,7 +370,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
     volatile float4* s_ep = reinterpret_cast<volatile float4*>(s_norm + 16);  // [16] epilogue descriptors
     constexpr int kHdr = ((kStackBarBytes + 127) / 128) * 128;
     float* slots = reinterpret_cast<float*>(smem + kHdr);
-    int* counters = reinterpret_cast<int*>(smem + kHdr + kMaxSlots * 4);  // [kMaxStages][kMaxStageRows]
     const uint32_t stage0 = sbase + kStackSmemHeader + (uint32_t)P.x_smem;  // after the x staging buffer
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -387,7 +386,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
         for (int k = 0; k < 4 + kSigSlots; ++k) reinterpret_cast<volatile uint32_t*>(smem + 16 * kMaxStages + 16)[k] = 0;
         fence_mbar_init();
     }
-    for (int i = threadIdx.x; i < kMaxStages * kMaxStageRows; i += blockDim.x) counters[i] = 0;
     __syncthreads();
 
     if (warp == kConsumerWarps) {
@@ -651,21 +649,32 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                         }
                         if (S == 1) {
                             if (lane == 0) put_row<FX>(P, yl, yo, r0 + rl, acc, s_ep + warp, rv, up);
-                        } else if (lane == 0) {
+                        } else if (lane == 0) {  // this segment's partial (summed below)
                             float* sl = slots + s * P.slot_stride + rl * S * (half ? 2 : 1);
                             sl[sg] = acc;
                             if (FX && half) sl[S + sg] = up;
-                            __threadfence_block();
-                            const int prev = atomicAdd(&counters[s * kMaxStageRows + rl], 1);
-                            if (prev == S - 1) {  // last segment of this row: sum in segment order
-                                __threadfence_block();
-                                float v = 0.f, u = 0.f;
-                                for (int k = 0; k < S; ++k) v += *(volatile float*)(sl + k);
-                                if (FX && half)
-                                    for (int k = 0; k < S; ++k) u += *(volatile float*)(sl + S + k);
-                                put_row<FX>(P, yl, yo, r0 + rl, v, s_ep + warp, rv, u);
-                                counters[s * kMaxStageRows + rl] = 0;
-                            }
+                        }
+                    }
+                }
+                if (S > 1 && grp < n_grp) {
+                    // The S warps of the row group meet once per stage (named barrier 2 + grp,
+                    // which orders their partials in shared memory); then the lanes of the
+                    // segment-0 warp finish the group's rows of the stage, one row per lane,
+                    // summing the partials in segment order.  Every warp of the group reaches
+                    // this barrier once per stage on every path, so a failed wait cannot
+                    // leave another warp waiting here.
+                    asm volatile("bar.sync %0, %1;" ::"r"(2 + grp), "r"(32 * S) : "memory");
+                    if (alive && sg == 0) {
+                        int first = grp - rot;
+                        if (first < 0) first += n_grp;
+                        for (int rl = first + n_grp * lane; rl < nr; rl += 32 * n_grp) {
+                            const float* sl = slots + s * P.slot_stride + rl * S * (half ? 2 : 1);
+                            float v = 0.f, u = 0.f;
+                            for (int k = 0; k < S; ++k) v += sl[k];
+                            if (FX && half)
+                                for (int k = 0; k < S; ++k) u += sl[S + k];
+                            const float rv = FX ? residual_of(s_ep + warp, r0 + rl) : 0.0f;
+                            put_row<FX>(P, yl, yo, r0 + rl, v, s_ep + warp, rv, u);
                         }
                     }
                 }
