@@ -421,9 +421,7 @@ def main():
         with torch.cuda.stream(stream):
             graph.replay()
         torch.cuda.synchronize(dev)
-        for name, y in (("head", ys[-1]), ("down", ys[-2]), ("gate", ys[-4])):
-            if not torch.equal(y, out[name]):
-                raise RuntimeError(f"stack output of {name} differs from the per-GEMV path")
+        check_against_per_gemv(torch, (("head", ys[-1]), ("down", ys[-2]), ("gate", ys[-4])), out, "stack")
         verify_head(torch, be, head, h0, ys[-1], world, rank)
         ms_step = ms / args.steps
         value = sb * args.steps / (ms / 1e3) / 1e9
@@ -470,9 +468,8 @@ def main():
         with torch.cuda.stream(stream):
             graph.replay()
         torch.cuda.synchronize(dev)
-        for name, idx in (("head", -1), ("down", -2), ("gate", -4)):
-            if not torch.equal(souts[idx], out[name]):
-                raise RuntimeError(f"sharded stack output of {name} differs from the per-GEMV NCCL path")
+        check_against_per_gemv(torch, (("head", souts[-1]), ("down", souts[-2]), ("gate", souts[-4])), out,
+                               "sharded stack")
         ms_step = ms / args.steps
         value = sb * args.steps / (ms / 1e3) / 1e9
         reps = max(10, args.steps // 5)
@@ -524,6 +521,22 @@ def main():
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+
+
+def check_against_per_gemv(torch, pairs, out, what):
+    """The stack against the same GEMVs launched one by one: bit for bit where
+    the task reads the stack input (the LM head), and within 1e-5 L2-relative
+    where it reads another task's output (the stack hands a dependent task its
+    source's output with the lowest mantissa bit cleared; the per-GEMV path
+    passes the exact floats)."""
+    for name, y in pairs:
+        ref = out[name]
+        if name == "head":
+            ok = torch.equal(y, ref)
+        else:
+            ok = float(torch.linalg.vector_norm(y - ref) / torch.linalg.vector_norm(ref)) <= 1e-5
+        if not ok:
+            raise RuntimeError(f"{what} output of {name} differs from the per-GEMV path")
 
 
 def check_status(L):

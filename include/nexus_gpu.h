@@ -221,13 +221,14 @@ NEXUS_GPU_API int32_t nexus_gpu_stack_run(void* stack, const float* dX, void* st
 NEXUS_GPU_API int32_t nexus_gpu_stack_destroy(void* stack);
 
 /* Row-sharded GEMV stacks over `world` GPUs (2..8) of one node, one process
- * (or thread) per GPU, each holding the full x.  SURVEY-style row sharding of
- * the reference's GEMVs (src/forward_pass.cpp:504-585) with the all-gather
- * fused into the kernel: rank r computes rows [rows*r/world, rows*(r+1)/world)
- * of every task and writes them straight into every peer's copy of the
- * output over NVLink (peer stores), then counts itself on every peer's
- * counter; each task waits for all ranks' CTAs.  No counterpart in the
- * reference.
+ * (or thread) per GPU, each holding the full x.  Row sharding of the
+ * reference's GEMVs (src/forward_pass.cpp:504-585) with the all-gather fused
+ * into the kernel: rank r computes rows [rows*r/world, rows*(r+1)/world) of
+ * every task and writes them straight into every peer's copy of the output
+ * over NVLink (peer stores); a task that another task depends on also writes
+ * each row as a tagged 8-byte word, which the dependent task's readers check,
+ * so no fence or counter sits between ranks inside a run.  No counterpart in
+ * the reference.
  *   tasks[i].rows = the FULL row count; tasks[i].W = this rank's row slice
  *   (contiguous GGUF rows); tasks[i].y must be NULL: outputs belong to the
  *   stack (full-length on every rank, nexus_gpu_stack_output).
@@ -277,6 +278,19 @@ NEXUS_GPU_API int32_t nexus_gpu_stack_create_ex(uint32_t dtype, const NexusGpuSt
 /* Blob size when blob == NULL; else writes *blob_bytes (>= that size) bytes. */
 NEXUS_GPU_API int32_t nexus_gpu_stack_export(void* stack, void* blob, uint64_t* blob_bytes);
 NEXUS_GPU_API int32_t nexus_gpu_stack_connect(void* stack, const void* blobs, uint64_t blobs_bytes);
+/* Connect the `n_stacks` ranks of one sharded stack that live in THIS process
+ * (stacks[r] = rank r's handle; one thread or loop driving several GPUs, or
+ * several ranks on one GPU): peers are reached by device pointer, with peer
+ * access enabled between distinct devices.  Replaces export / connect. */
+NEXUS_GPU_API int32_t nexus_gpu_stack_connect_local(void* const* stacks, uint32_t n_stacks);
+/* Limit, in nanoseconds, of the stack's waits for rows of other CTAs and ranks
+ * (0: the default, 2 s).  A wait that runs out sets the timeout bit of
+ * nexus_gpu_device_status and poisons the stack. */
+NEXUS_GPU_API int32_t nexus_gpu_stack_set_wait_limit(void* stack, uint64_t limit_ns);
+/* Synchronize `stream`, then report NEXUS_GPU_ERROR_TIMEOUT if a bounded wait
+ * of the stack expired (the reference's status convention,
+ * include/nexus_common.hpp:329-340); the stack must then be destroyed. */
+NEXUS_GPU_API int32_t nexus_gpu_stack_wait(void* stack, void* stream);
 /* Device pointer to task `task`'s output on this rank (the caller's y for an
  * unsharded stack). */
 NEXUS_GPU_API int32_t nexus_gpu_stack_output(void* stack, uint32_t task, float** y);

@@ -57,6 +57,9 @@ SIGNATURES = {
     "nexus_gpu_stack_export": (_I32, [_VP, _VP, ctypes.POINTER(ctypes.c_uint64)]),
     "nexus_gpu_stack_connect": (_I32, [_VP, _VP, ctypes.c_uint64]),
     "nexus_gpu_stack_output": (_I32, [_VP, _U32, ctypes.POINTER(_VP)]),
+    "nexus_gpu_stack_connect_local": (_I32, [_VP, _U32]),
+    "nexus_gpu_stack_set_wait_limit": (_I32, [_VP, ctypes.c_uint64]),
+    "nexus_gpu_stack_wait": (_I32, [_VP, _VP]),
     "nexus_gpu_dequantize": (_I32, [_VP, _U32, _VP, _SZ, _VP]),
     "nexus_gpu_last_error": (ctypes.c_char_p, []),
     "nexus_gpu_device_status": (_I32, [ctypes.POINTER(ctypes.c_uint32)]),

@@ -862,12 +862,15 @@ void report_void(const char* fn, int32_t rc) {
 
 
 // ------------------------------------------------------------ GEMV stacks
-// Device block of a stack: the control area (per-task counters, abort flag,
-// run epoch, CTA-exit count, end-of-run count), then -- sharded stacks only --
-// every task's full-length output.  Peers map this block through CUDA IPC.
+// Device block of a stack: the control area (abort flag, run epoch, CTA-exit
+// count, end-of-run counts), then -- sharded stacks only -- every task's
+// full-length output, then the tagged copy (a 32-bit word per row, the run's
+// parity in the lowest bit) of every task that a later task depends on.
+// Peers map this block through CUDA IPC.
 struct StackLayout {
-    size_t done = 0, abort = 0, epoch = 0, fin = 0, end = 0, ctrl = 0, total = 0;
+    size_t abort = 0, epoch = 0, fin = 0, end = 0, local_end = 0, ctrl = 0, total = 0;
     std::vector<uint64_t> out_off;  // sharded: output of task i at float offset out_off[i]
+    std::vector<uint64_t> tg_off;   // task i's tagged copy at 32-bit word offset tg_off[i] (0: none)
 };
 
 struct StackHandle {
@@ -1120,12 +1123,12 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
         if (tasks[i].residual_source >= 0) waited_for[tasks[i].residual_source] = 1;
     }
     StackLayout& lay = h->lay;
-    lay.done = 0;
-    lay.abort = (size_t)n * kCounterStride * sizeof(unsigned long long);
+    lay.abort = 0;
     lay.epoch = lay.abort + 128;
     lay.fin = lay.epoch + 128;
     lay.end = lay.fin + 128;
-    lay.ctrl = align256(lay.end + 128);
+    lay.local_end = lay.end + 128;
+    lay.ctrl = align256(lay.local_end + 128);
     lay.total = lay.ctrl;
     if (sharded) {
         lay.out_off.resize(n);
@@ -1133,6 +1136,12 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
             lay.out_off[i] = lay.total / sizeof(float);
             lay.total += align256(tasks[i].rows * sizeof(float));
         }
+    }
+    lay.tg_off.assign(n, 0);
+    for (uint32_t i = 0; i < n; ++i) {
+        if (!waited_for[i]) continue;
+        lay.tg_off[i] = lay.total / sizeof(uint32_t);
+        lay.total += align256(tasks[i].rows * sizeof(uint32_t));
     }
 
     // each task's rows for each CTA, balanced: [N*c/grid, N*(c+1)/grid) of this rank's slice
@@ -1154,23 +1163,21 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
     h->outputs.resize(n);
     for (uint32_t i = 0; i < n; ++i)
         h->outputs[i] = sharded ? reinterpret_cast<float*>(h->d_block) + lay.out_off[i] : tasks[i].y;
-    int n_signal = 0, sig_in_group = 0;
     for (uint32_t i = 0; i < n; ++i) {
         StackTask& T = ht[i];
         T.y = h->outputs[i];
         T.y_off = sharded ? lay.out_off[i] : 0;
-        T.x = tasks[i].x_source < 0 ? nullptr : h->outputs[tasks[i].x_source];
+        T.tg = waited_for[i] ? reinterpret_cast<uint32_t*>(h->d_block) + lay.tg_off[i] : nullptr;
+        T.tg_off = lay.tg_off[i];
         T.src = tasks[i].x_source < 0 ? -1 : tasks[i].x_source;
         T.after = tasks[i].after;
-        T.signal = waited_for[i];
-        T.sig_ord = T.signal ? n_signal++ : -1;
-        T.x2 = tasks[i].x_source2 < 0 ? nullptr : h->outputs[tasks[i].x_source2];
+        T.after_rows = tasks[i].after >= 0 ? (int)tasks[tasks[i].after].rows : 0;
         T.src2 = tasks[i].x_source2 < 0 ? -1 : tasks[i].x_source2;
         T.norm_w = tasks[i].norm_weight;
         T.norm_eps = tasks[i].norm_eps;
-        T.res = tasks[i].residual_source >= 0 ? h->outputs[tasks[i].residual_source] : nullptr;
         T.res_input = tasks[i].residual_source == -1;
         T.res_src = tasks[i].residual_source >= 0 ? tasks[i].residual_source : -1;
+        T.res_rows = (int)tasks[i].rows;
         // same input (and fusions), same plan (same cols), and no new ordering
         // dependency: keep the previous task's x slices, skip the wait and the staging
         T.reuse_x = i > 0 && tasks[i].x_source == tasks[i - 1].x_source && tasks[i].cols == tasks[i - 1].cols &&
@@ -1178,16 +1185,6 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
                     (!tasks[i].norm_weight || memcmp(&tasks[i].norm_eps, &tasks[i - 1].norm_eps, 4) == 0) &&
                     (tasks[i].after == -1 || tasks[i].after == tasks[i - 1].after) &&
                     (tasks[i].residual_source < 0 || tasks[i].residual_source == tasks[i - 1].residual_source);
-        // Consumer warps drift apart only within an x group (they meet at every
-        // group head), so a group holds fewer signalled tasks than there are
-        // shared completion slots: warps never post to a slot's next round
-        // before every warp has posted the current one.
-        if (!T.reuse_x) sig_in_group = 0;
-        if (T.signal && sig_in_group == kSigSlots / 2) {
-            T.reuse_x = 0;
-            sig_in_group = 0;
-        }
-        if (T.signal) ++sig_in_group;
     }
     e = cudaMemcpy(h->d_tasks, ht.data(), n * sizeof(StackTask), cudaMemcpyHostToDevice);
     if (e == cudaSuccess)
@@ -1206,14 +1203,15 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
     P.x_smem = (int)x_smem;
     P.slot_stride = kMaxSlots / ns;
     P.x_in = nullptr;
-    P.done = reinterpret_cast<unsigned long long*>(h->d_block + lay.done);
+    P.wait_ns = kWaitLimitNs;
+    P.wait_polls = (uint32_t)(kWaitLimitNs / kTagPollNs);
     P.abort_flag = reinterpret_cast<unsigned*>(h->d_block + lay.abort);
     P.epoch = reinterpret_cast<unsigned long long*>(h->d_block + lay.epoch);
     P.fin = reinterpret_cast<unsigned long long*>(h->d_block + lay.fin);
     P.end_done = reinterpret_cast<unsigned long long*>(h->d_block + lay.end);
+    P.local_end = reinterpret_cast<unsigned long long*>(h->d_block + lay.local_end);
     P.world = world;
     P.rank = rank;
-    P.peer_done[rank] = P.done;
     P.peer_end[rank] = P.end_done;
     P.peer_block[rank] = h->d_block;
 
@@ -1269,7 +1267,7 @@ int32_t stack_connect(void* handle, const void* blobs, uint64_t bytes) {
     StackHandle* h = static_cast<StackHandle*>(handle);
     if (!h || !blobs) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null handle or blobs");
     if (h->world < 2) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "not a sharded stack");
-    if (!h->peer_mappings.empty()) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "stack already connected");
+    if (h->connected) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "stack already connected");
     if (bytes != (uint64_t)h->world * sizeof(StackBlob))
         return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "%llu blob bytes, need %d x %zu", (unsigned long long)bytes,
                     h->world, sizeof(StackBlob));
@@ -1302,12 +1300,77 @@ int32_t stack_connect(void* handle, const void* blobs, uint64_t bytes) {
     for (int p = 0; p < h->world; ++p) {
         if (p == h->rank) continue;
         uint8_t* base = static_cast<uint8_t*>(maps[p]);
-        P.peer_done[p] = reinterpret_cast<unsigned long long*>(base + h->lay.done);
         P.peer_end[p] = reinterpret_cast<unsigned long long*>(base + h->lay.end);
         P.peer_block[p] = base;
     }
     h->peer_mappings = maps;
     h->connected = true;
+    return NEXUS_GPU_SUCCESS;
+}
+
+// Ranks of one sharded stack that live in this process (one thread or one
+// loop driving several GPUs, or -- for tests -- several ranks on one GPU):
+// connect them by their device pointers, with peer access enabled between
+// distinct devices.  Same checks as stack_connect.
+int32_t stack_connect_local(void* const* stacks, uint32_t n) {
+    if (!stacks || n < 2 || n > (uint32_t)kMaxWorld)
+        return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "%u stacks (2..%d ranks)", n, kMaxWorld);
+    std::vector<StackHandle*> hs(n);
+    for (uint32_t i = 0; i < n; ++i) {
+        hs[i] = static_cast<StackHandle*>(stacks[i]);
+        if (!hs[i]) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null stack %u", i);
+        if (hs[i]->world != (int)n || hs[i]->rank != (int)i)
+            return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "stack %u is rank %d of %d, not rank %u of %u", i,
+                        hs[i]->rank, hs[i]->world, i, n);
+        if (hs[i]->connected) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "stack %u already connected", i);
+        if (hs[i]->fingerprint != hs[0]->fingerprint || hs[i]->lay.total != hs[0]->lay.total)
+            return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "rank %u built a different task list", i);
+        if (hs[i]->grid != hs[0]->grid)
+            return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "rank %u runs %d CTAs, rank 0 %d", i, hs[i]->grid, hs[0]->grid);
+    }
+    int cur = -1;
+    CUDA_TRY(cudaGetDevice(&cur));
+    for (uint32_t i = 0; i < n; ++i)
+        for (uint32_t j = 0; j < n; ++j) {
+            if (hs[i]->dev == hs[j]->dev) continue;
+            int can = 0;
+            CUDA_TRY(cudaDeviceCanAccessPeer(&can, hs[i]->dev, hs[j]->dev));
+            if (!can) {
+                cudaSetDevice(cur);
+                return fail(NEXUS_GPU_ERROR_CUDA, "device %d cannot reach device %d", hs[i]->dev, hs[j]->dev);
+            }
+            CUDA_TRY(cudaSetDevice(hs[i]->dev));
+            const cudaError_t e = cudaDeviceEnablePeerAccess(hs[j]->dev, 0);
+            if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+            else if (e != cudaSuccess) {
+                cudaSetDevice(cur);
+                return fail(NEXUS_GPU_ERROR_CUDA, "peer access %d -> %d: %s", hs[i]->dev, hs[j]->dev,
+                            cudaGetErrorString(e));
+            }
+        }
+    CUDA_TRY(cudaSetDevice(cur));
+    for (uint32_t i = 0; i < n; ++i) {
+        StackParams& P = hs[i]->params;
+        for (uint32_t p = 0; p < n; ++p) {
+            P.peer_end[p] = hs[p]->params.end_done;
+            P.peer_block[p] = hs[p]->d_block;
+        }
+        hs[i]->connected = true;
+    }
+    return NEXUS_GPU_SUCCESS;
+}
+
+// Wait for the stack's last run on `stream`; a wait that gave up (a peer that
+// never ran, a stalled pipeline) poisons the stack and is reported here.
+int32_t stack_wait(void* handle, cudaStream_t st) {
+    StackHandle* h = static_cast<StackHandle*>(handle);
+    if (!h) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null handle");
+    int32_t rc = stack_current_device(h);
+    if (rc) return rc;
+    CUDA_TRY(cudaStreamSynchronize(st));
+    unsigned aborted = 0;
+    CUDA_TRY(cudaMemcpy(&aborted, h->params.abort_flag, sizeof(aborted), cudaMemcpyDeviceToHost));
+    if (aborted) return fail(NEXUS_GPU_ERROR_TIMEOUT, "a bounded wait of the stack expired; destroy the stack");
     return NEXUS_GPU_SUCCESS;
 }
 
@@ -1634,6 +1697,25 @@ NEXUS_GPU_API int32_t nexus_gpu_stack_output(void* stack, uint32_t task, float**
 NEXUS_GPU_API int32_t nexus_gpu_stack_run(void* stack, const float* dX, void* stream) {
     t_last_error.clear();
     return stack_run(stack, dX, static_cast<cudaStream_t>(stream));
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_stack_connect_local(void* const* stacks, uint32_t n_stacks) {
+    t_last_error.clear();
+    return stack_connect_local(stacks, n_stacks);
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_stack_set_wait_limit(void* stack, uint64_t limit_ns) {
+    t_last_error.clear();
+    StackHandle* h = static_cast<StackHandle*>(stack);
+    if (!h) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null stack");
+    h->params.wait_ns = limit_ns ? limit_ns : kWaitLimitNs;
+    h->params.wait_polls = (uint32_t)std::min<uint64_t>(h->params.wait_ns / kTagPollNs + 1, UINT32_MAX);
+    return NEXUS_GPU_SUCCESS;
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_stack_wait(void* stack, void* stream) {
+    t_last_error.clear();
+    return stack_wait(stack, static_cast<cudaStream_t>(stream));
 }
 
 NEXUS_GPU_API int32_t nexus_gpu_stack_destroy(void* stack) {

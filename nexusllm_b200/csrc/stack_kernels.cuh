@@ -13,14 +13,15 @@
 //  * Each task's consumer work is the single-GEMV kernel's (same plan, same
 //    per-row arithmetic, so results are bit-identical to nexus_gpu_gemv).
 //    Rows are balanced over the CTAs.
-//  * A task's x is either the stack input or the y of an earlier task.  Each
-//    task that a later task reads or waits for has a counter, cumulative over
-//    runs.  When all consumer warps of a CTA have posted a task done (shared
-//    memory, release), the CTA's producer thread -- between weight copies --
-//    makes one release fence for every task finished since its last look and
-//    adds 1 to each one's counter on every rank; the consumers never wait for
-//    a fence or an atomic.  A dependent task's CTA waits (one thread) until
-//    the counter reaches every CTA of every rank, then reads x.
+//  * A task's x is either the stack input or the y of an earlier task.  A task
+//    that a later task reads or waits for also stores each output row as an
+//    8-byte word (float bits | run tag << 32) with a single-copy-atomic relaxed
+//    store -- into every rank's copy when sharded.  The tag is the run number
+//    + 1, so a reader that sees the current tag in a word has the current
+//    value in it: the dependent CTA's staging loads are the wait, and no
+//    fence, counter or flag sits between a row's store and its use (at N > 1
+//    this removes the system-scope fences from every data dependency).  An
+//    `after` dependency waits for every row of its task the same way.
 //  * The consumer warps of a CTA step through the tasks together, one x group
 //    (a task and the following tasks with the same input and plan) at a time:
 //    the CTA reads the group's x once, quantizes it into shared memory itself
@@ -29,8 +30,8 @@
 //  * Sharded over GPUs, a rank computes its row slice of every task and
 //    stores each output row into every peer as well (plain stores).  The
 //    run ends when every rank's rows of every task have landed everywhere:
-//    each CTA posts its end to every rank after a system-scope release, and
-//    one thread per rank waits for all of them.
+//    each rank's last CTA to finish posts the rank's end to every rank after
+//    a system-scope release, and one thread per rank waits for all ranks.
 //  * The fused variant (template flag FX, nexus_gpu_stack_create_ex) adds the
 //    decode layer's operations around the GEMVs: the group's x staging
 //    applies a SwiGLU of two sources and the RMSNorm weights and sums x^2;
@@ -57,22 +58,22 @@ struct StackTask {
     int rot_step;                        // stage_rows % (row groups): how the row-to-group deal advances per stage
     float* y;                            // this rank's full-length output (slice written at row_off)
     uint64_t y_off;                      // sharded: y's float offset in every rank's block
-    const float* x;                      // fp32 x: the source task's y, or null for the stack input
-    int src;                             // the source task, or -1 (the stack input)
-    int after;                           // -1, or a task that must complete before this one starts
+    uint32_t* tg;                        // a later task depends on this one: its tagged copy (full
+                                         // length, this rank's), or null
+    uint64_t tg_off;                     // the tagged copy's word offset in every rank's block
+    int src;                             // x is task src's output (tagged copy), or -1: the stack input
+    int after;                           // -1, or a task whose every row must be stored before this one starts
+    int after_rows;                      // rows of task `after`
     int row_off;                         // first global row of this rank's slice (0 unless sharded)
     int reuse_x;                         // same input and plan as the previous task: keep its x
-    int signal;                          // a later task waits for this one: count it on the counters
-    int sig_ord;                         // ordinal among the signalled tasks (shared completion slot)
     // fusions around the GEMV (TransformerOps, include/transformer_ops.hpp:23-44,86-95;
     // the decode layer in src/forward_pass.cpp:504-562)
-    const float* x2;                     // SwiGLU: x = silu(x) * x2 (x the gate's output, x2 the up's), or null
-    int src2;                            // x2's task, or -1
+    int src2;                            // SwiGLU: x = silu(x) * (task src2's output), or -1
     const float* norm_w;                 // RMSNorm of x with these fp32 weights, or null
     float norm_eps;
-    const float* res;                    // residual added to every output row (full length), or null
     int res_input;                       // the residual is the stack input
-    int res_src;                         // the residual's task, or -1 (waited for with the input)
+    int res_src;                         // the residual is task res_src's output (tagged copy), or -1
+    int res_rows;                        // rows of the residual (this task's full row count)
     const uint8_t* W2;                   // gate+up pair: the up matrix (rows as W's), or null
     int half;                            // pair: byte offset of W2's rows in a ring slot
 };
@@ -86,46 +87,56 @@ struct StackParams {
     int x_smem;                          // bytes of the shared x staging buffer
     int slot_stride;                     // partial-sum floats per ring slot (>= R * S of every task)
     const float* x_in;                   // stack input, fp32, 16-byte aligned
-    unsigned long long* done;            // [n_tasks * kCounterStride]: CTAs (of every rank) that
-                                         // finished each task, summed over all runs of the stack
+    uint64_t wait_ns;                    // limit of every wait on other CTAs or ranks
+    uint32_t wait_polls;                 // the same limit for tag polls (wait_ns / kTagPollNs)
     unsigned* abort_flag;                // sticky: an expired wait poisons the stack
     unsigned long long* epoch;           // runs completed on this rank
     unsigned long long* fin;             // CTAs of this rank that left, summed over all runs
-    unsigned long long* end_done;        // sharded: CTAs of all ranks whose rows all landed here, all runs
+    unsigned long long* end_done;        // sharded: ranks whose rows all landed here, all runs
     int world, rank;                     // row sharding over `world` GPUs (1, rank 0: unsharded)
-    unsigned long long* peer_done[kMaxWorld]; // every rank's `done` (own included)
+    unsigned long long* local_end;       // sharded: CTAs of this rank that stored every row, all runs
     unsigned long long* peer_end[kMaxWorld];  // every rank's end_done (own included)
     uint8_t* peer_block[kMaxWorld];           // every rank's stack block (own included)
 };
 
-// One 128-byte line per counter.  Counters are never reset: run e of a stack
-// (e = 0, 1, ...) waits for (e + 1) * world * n_cta.
-constexpr int kCounterStride = 16;
+// Counters and tags are never reset: run e of a stack (e = 0, 1, ...) tags
+// its rows e + 1, and a sharded run ends when end_done reaches (e + 1) * world.
 
 
-__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p, bool sys) {
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p, bool sys) {
     unsigned long long v;
-    if (sys) asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    else asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    if (sys) asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    else asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
+}
+// Acquire side of a relaxed poll that succeeded (relaxed read + fence = acquire).
+__device__ __forceinline__ void fence_acquire(bool sys) {
+    if (sys) asm volatile("fence.acq_rel.sys;" ::: "memory");
+    else asm volatile("fence.acq_rel.gpu;" ::: "memory");
 }
 // Add 1 to a counter, on this GPU or (sys) on a peer, after the caller's fence.
 __device__ __forceinline__ void red_add_u64(unsigned long long* p, bool sys) {
     if (sys) asm volatile("red.relaxed.sys.global.add.u64 [%0], 1;" ::"l"(p) : "memory");
     else asm volatile("red.relaxed.gpu.global.add.u64 [%0], 1;" ::"l"(p) : "memory");
 }
-// Wait (one thread) until *ctr >= target.  Bounded: gives up when another CTA
-// raised the abort flag or after kWaitLimitNs, raising it itself.
+// Wait (one thread) until *ctr >= target, then acquire.  Bounded: gives up
+// when another CTA raised the abort flag or after limit_ns, raising it itself.
 __device__ __noinline__ bool wait_count_bounded(const unsigned long long* ctr, unsigned long long target,
-                                                unsigned* abort_flag, bool sys) {
-    if (ld_acquire_u64(ctr, sys) >= target) return true;
+                                                unsigned* abort_flag, bool sys, uint64_t limit_ns) {
+    if (ld_relaxed_u64(ctr, sys) >= target) {
+        fence_acquire(sys);
+        return true;
+    }
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t k = 1;; ++k) {
-        __nanosleep(64);
-        if (ld_acquire_u64(ctr, sys) >= target) return true;
+        __nanosleep(32);
+        if (ld_relaxed_u64(ctr, sys) >= target) {
+            fence_acquire(sys);
+            return true;
+        }
         if ((k & 15u) == 0) {
             if (*reinterpret_cast<volatile unsigned*>(abort_flag)) return false;
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            if (globaltimer_ns() - t0 > limit_ns) {
                 atomicOr(&g_device_status, kStatusWaitTimeout);
                 atomicExch(abort_flag, 1u);
                 return false;
@@ -134,24 +145,133 @@ __device__ __noinline__ bool wait_count_bounded(const unsigned long long* ctr, u
     }
 }
 
-constexpr int kSigSlots = 16;  // shared per-task completion counters (cumulative, by signal ordinal)
-// mbarriers, a broadcast flag, the end-of-run post count, the completion slots
-// + RMSNorm partial sums and per-warp scales
-constexpr int kStackBarBytes = 16 * kMaxStages + 32 + 4 * kSigSlots + 4 * 16 + 16 * 16;
-constexpr int kStackSmemHeader = ((kStackBarBytes + 127) / 128) * 128 + kSmemHeader - kBarBytes;
-
-__device__ __forceinline__ void red_release_shared_add(uint32_t addr, uint32_t v) {
-    asm volatile("red.release.cta.shared::cta.add.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+// ------------------------------------------------------------- tagged rows
+// A task that a later task depends on also stores each output row into its
+// tagged copy: the float with its lowest mantissa bit replaced by the run's
+// parity, (run + 1) & 1.  Every run rewrites every row, so a word holds either
+// this run's or the previous run's row, and its parity bit tells which; each
+// 32-bit word is single-copy atomic, so a reader that sees this run's parity
+// has this run's value.  Readers clear the bit before use, so what a task
+// consumes does not depend on the run (a relative change of at most 2^-23,
+// far below the 16-bit fixed-point x that follows).  The buffers start at 0
+// (parity 0), and run 0 writes parity 1.
+__device__ __forceinline__ void st_tagged(uint32_t* p, float v, uint32_t par, bool sys) {
+    const uint32_t w = (__float_as_uint(v) & ~1u) | par;
+    if (sys) asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(p), "r"(w) : "memory");
+    else asm volatile("st.relaxed.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(w) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_shared(uint32_t addr) {
-    uint32_t v;
-    asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+__device__ __forceinline__ uint4 ld_tagged4(const uint32_t* p, bool sys) {
+    uint4 v;
+    if (sys)
+        asm volatile("ld.relaxed.sys.global.v4.b32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p) : "memory");
+    else
+        asm volatile("ld.relaxed.gpu.global.v4.b32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p) : "memory");
     return v;
 }
-// Release fences (the counters that follow are relaxed atomics).
-__device__ __forceinline__ void fence_release(bool sys) {
-    if (sys) asm volatile("fence.acq_rel.sys;" ::: "memory");
-    else asm volatile("fence.acq_rel.gpu;" ::: "memory");
+__device__ __forceinline__ uint32_t ld_tagged1(const uint32_t* p, bool sys) {
+    uint32_t v;
+    if (sys) asm volatile("ld.relaxed.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    else asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ float untag(uint32_t w) { return __uint_as_float(w & ~1u); }
+// 16 consecutive tagged words at p (16-byte aligned) into e; true when every
+// word carries this run's parity.
+__device__ __forceinline__ bool ld_tagged16(const uint32_t* p, uint32_t par, bool sys, float (&e)[16]) {
+    uint32_t bad = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint4 v = ld_tagged4(p + 4 * q, sys);
+        e[4 * q + 0] = untag(v.x);
+        e[4 * q + 1] = untag(v.y);
+        e[4 * q + 2] = untag(v.z);
+        e[4 * q + 3] = untag(v.w);
+        bad |= (v.x ^ par) | (v.y ^ par) | (v.z ^ par) | (v.w ^ par);
+    }
+    return (bad & 1u) == 0;
+}
+// The wait's expiry.
+__device__ __forceinline__ void tag_wait_expired(unsigned* abort_flag) {
+    atomicOr(&g_device_status, kStatusWaitTimeout);
+    atomicExch(abort_flag, 1u);
+}
+// Read 16 words until every one carries this run's parity.  Bounded by an
+// iteration count (P.wait_polls: the stack's wait limit over the ~kTagPollNs
+// a poll takes, so the loop holds one counter, not a clock): false when
+// another CTA raised the abort flag or the polls ran out (raising it and the
+// status bit).
+constexpr uint32_t kTagPollNs = 200;
+__device__ __forceinline__ bool wait_tagged16(const uint32_t* p, uint32_t par, bool sys, float (&e)[16],
+                                              unsigned* abort_flag, uint32_t polls) {
+    for (uint32_t k = 0; !ld_tagged16(p, par, sys, e); ++k) {
+        __nanosleep(kTagPollNs / 2);
+        if ((k & 7u) == 7u && *reinterpret_cast<volatile unsigned*>(abort_flag)) return false;
+        if (k >= polls) {
+            tag_wait_expired(abort_flag);
+            return false;
+        }
+    }
+    return true;
+}
+// Every row [0, n) of a tagged copy carries this run's parity; this thread
+// checks rows 4*tid .. 4*tid+3, then every 4*kConsumers on (buffer 16-byte
+// aligned; a partial last group of rows is read word by word).
+__device__ __forceinline__ bool tagged_group_current(const uint32_t* p, int m, uint32_t par, bool sys) {
+    if (m == 4) {
+        const uint4 v = ld_tagged4(p, sys);
+        return (((v.x ^ par) | (v.y ^ par) | (v.z ^ par) | (v.w ^ par)) & 1u) == 0;
+    }
+    uint32_t bad = 0;
+    for (int k = 0; k < m; ++k) bad |= ld_tagged1(p + k, sys) ^ par;
+    return (bad & 1u) == 0;
+}
+__device__ __forceinline__ bool wait_rows_tagged(const uint32_t* tg, int n, uint32_t par, bool sys, int tid,
+                                                 unsigned* abort_flag, uint32_t polls) {
+    for (int i = 4 * tid; i < n; i += 4 * kConsumers) {
+        const int m = min(4, n - i);
+        for (uint32_t k = 0; !tagged_group_current(tg + i, m, par, sys); ++k) {
+            __nanosleep(kTagPollNs / 2);
+            if ((k & 7u) == 7u && *reinterpret_cast<volatile unsigned*>(abort_flag)) return false;
+            if (k >= polls) {
+                tag_wait_expired(abort_flag);
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
+// mbarriers, a broadcast flag, the end-of-run post count, the RMSNorm partial
+// sums, the per-warp epilogue descriptors and the per-warp output offsets
+constexpr int kStackBarBytes = 16 * kMaxStages + 32 + 4 * 16 + 16 * 16 + 16 * 16;
+constexpr int kStackSmemHeader = ((kStackBarBytes + 127) / 128) * 128 + kSmemHeader - kBarBytes;
+
+__device__ __forceinline__ uint32_t atom_add_acq_rel_shared(uint32_t addr, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(addr), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ unsigned long long atom_add_acq_rel_gpu(unsigned long long* p) {
+    unsigned long long old;
+    asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], 1;" : "=l"(old) : "l"(p) : "memory");
+    return old;
+}
+__device__ __forceinline__ void red_release_gpu(unsigned long long* p) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(p) : "memory");
+}
+
+// Sharded end of run: count this CTA as done (called by its last consumer
+// warp, after it acquired the other warps' posts, so their stores -- to this
+// GPU and to peers -- are ordered before).  CTAs count at GPU scope on this
+// rank's counter; the CTA that completes the rank's count makes ONE
+// system-scope release and adds 1 on every rank's end counter.
+__device__ __forceinline__ void release_end(const StackParams& P, unsigned long long run, int n_cta) {
+    if (atom_add_acq_rel_gpu(P.local_end) + 1 != (run + 1) * (unsigned long long)n_cta) return;
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+#pragma unroll 1
+    for (int p = 0; p < P.world; ++p) red_add_u64(P.peer_end[p], true);
 }
 
 // Named barrier of the consumer warps (the producer warp never joins it).
@@ -247,6 +367,9 @@ __device__ __forceinline__ int ld_task_i32(const int* p) {
     asm volatile("ld.global.nc.s32 %0, [%1];" : "=r"(v) : "l"(p));
     return v;
 }
+__device__ __forceinline__ uint32_t* ld_task_ptr(uint32_t* const* p) {
+    return reinterpret_cast<uint32_t*>(ld_task_u64(p));
+}
 
 // The fused variant's per-warp epilogue descriptor in shared memory, one
 // 16-byte word per consumer warp: x,y = the residual pointer already offset to
@@ -262,15 +385,22 @@ __device__ __forceinline__ float4 ld_ep(const volatile float4* p) {
     return v;
 }
 
-__device__ __forceinline__ const float* ep_residual(const float4 e) {
-    return reinterpret_cast<const float*>(((uint64_t)__float_as_uint(e.y) << 32) | __float_as_uint(e.x));
+// The descriptor's residual address: the stack input's floats, or -- bit 0
+// set -- a task's tagged copy (both already offset to this rank's first row).
+__device__ __forceinline__ uint64_t ep_residual(const float4 e) {
+    return ((uint64_t)__float_as_uint(e.y) << 32) | __float_as_uint(e.x);
 }
 
 // Row r's residual, loaded when the row starts so that the L2 latency
-// overlaps its dot product (written earlier in this run, possibly by peers).
-__device__ __forceinline__ float residual_of(const volatile float4* ep, int r) {
-    const float* res = ep_residual(ld_ep(ep));
-    return res ? __ldcg(res + r) : 0.0f;
+// overlaps its dot product.  A task's residual rows were all seen with this
+// run's tag at the group head, so the same words read now hold this run's
+// values (coherence of each word).
+__device__ __forceinline__ float residual_of(const volatile float4* ep, int r, bool sys) {
+    const uint64_t a = ep_residual(ld_ep(ep));
+    if (!a) return 0.0f;
+    if (a & 1u)
+        return untag(ld_tagged1(reinterpret_cast<const uint32_t*>(a - 1) + r, sys));
+    return __ldcg(reinterpret_cast<const float*>(a) + r);
 }
 
 // Write row r (of this rank's slice) of task T: this rank's output and --
@@ -278,11 +408,15 @@ __device__ __forceinline__ float residual_of(const volatile float4* ep, int r) {
 // dot product; in the fused variant (FX) the epilogue of the descriptor ep
 // is applied: y = v * scale + rv, or silu(v * scale) * (u * scale) + rv for
 // a gate+up pair (u: the up row's dot product, rv: residual_of).
-// yl: this rank's output at its first row; yo: the float offset of that row
-// in every rank's stack block (sharded stacks).
+// yl: this rank's output at its first row.  The warp's output descriptor od
+// (shared, written once per task) holds yo, the float offset of that row in
+// every rank's stack block (sharded stacks), and to, the word offset of that
+// row of the task's tagged copy in every rank's block (0 when no task depends
+// on this one); reading it at the store keeps both out of the row loop's
+// registers.
 template <bool FX>
-__device__ __forceinline__ void put_row(const StackParams& P, float* yl, uint64_t yo, int r, float v,
-                                        const volatile float4* ep, float rv, float u) {
+__device__ __forceinline__ void put_row(const StackParams& P, float* yl, uint64_t yo, uint64_t to, uint32_t par,
+                                        int r, float v, const volatile float4* ep, float rv, float u) {
     if constexpr (FX) {
         const float4 e = ld_ep(ep);
         if (e.z != 1.0f) v = __fmul_rn(v, e.z);
@@ -293,47 +427,58 @@ __device__ __forceinline__ void put_row(const StackParams& P, float* yl, uint64_
         if (ep_residual(e)) v = __fadd_rn(v, rv);
     }
     yl[r] = v;
-    if (P.world > 1) {
+    const bool sys = P.world > 1;
+    if (to) st_tagged(reinterpret_cast<uint32_t*>(P.peer_block[P.rank]) + to + (uint64_t)r, v, par, sys);
+    if (sys) {
 #pragma unroll 1
-        for (int p = 0; p < P.world; ++p)
-            if (p != P.rank) reinterpret_cast<float*>(P.peer_block[p])[yo + (uint64_t)r] = v;
+        for (int p = 0; p < P.world; ++p) {
+            if (p == P.rank) continue;
+            reinterpret_cast<float*>(P.peer_block[p])[yo + (uint64_t)r] = v;
+            if (to) st_tagged(reinterpret_cast<uint32_t*>(P.peer_block[p]) + to + (uint64_t)r, v, par, true);
+        }
     }
 }
 
-// Stage a group's input x into shared memory: read it (L2), apply the fused
-// SwiGLU (xv2) and RMSNorm weights (nw), quantize two lanes per 32-element
-// block.  Returns this thread's sum of squares of x (for the RMSNorm scale).
+// Stage a group's input x into shared memory: read it -- the stack input's
+// floats (xv), or a task's tagged copy (xt), each thread waiting for this
+// run's tags on its own words -- apply the fused SwiGLU (xt2) and RMSNorm
+// weights (nw), quantize two lanes per 32-element block.  Returns this
+// thread's sum of squares of x (for the RMSNorm scale); `ok` turns false when
+// a wait gave up (every lane still runs the quantizer's shuffles).
 template <bool FX>
-__device__ __forceinline__ float stage_x(const float4* xv, const float4* xv2, const float4* nw, int K, uint32_t xs,
-                                         int tid, int lane) {
+__device__ __forceinline__ float stage_x(const float4* xv, const uint32_t* xt,
+                                         const uint32_t* xt2, const float4* nw, int K, uint32_t xs, int tid,
+                                         int lane, uint32_t par, const StackParams& P, bool& ok) {
     const int nxb = K / 32, nxbp = x_stage_planes_len(K), hf = lane & 1;
+    const bool sys = P.world > 1;
     float ss = 0.0f;  // in a fixed order
     for (int base = 0; base < nxb; base += kConsumers / 2) {
         const int b = base + (tid >> 1);
         float e[16];
+        if (b >= nxb) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const float4 v = b < nxb ? __ldcg(xv + 8 * b + 4 * hf + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-            e[4 * q + 0] = v.x;
-            e[4 * q + 1] = v.y;
-            e[4 * q + 2] = v.z;
-            e[4 * q + 3] = v.w;
+            for (int k = 0; k < 16; ++k) e[k] = 0.0f;
+        } else if (xt != nullptr) {
+            ok = wait_tagged16(xt + 32 * b + 16 * hf, par, sys, e, P.abort_flag, P.wait_polls) && ok;
+        } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 v = __ldcg(xv + 8 * b + 4 * hf + q);
+                e[4 * q + 0] = v.x;
+                e[4 * q + 1] = v.y;
+                e[4 * q + 2] = v.z;
+                e[4 * q + 3] = v.w;
+            }
         }
         if constexpr (FX) {
             // SwiGLU (transformer_ops.hpp:86-95): silu(gate) * up.  Every CTA computes the
             // whole vector, so with the __expf / __fdividef intrinsics (relative error ~1e-6,
             // far below the 16-bit fixed-point quantization that follows)
-            if (xv2 != nullptr && b < nxb) {
+            if (xt2 != nullptr && b < nxb) {
+                float u[16];
+                ok = wait_tagged16(xt2 + 32 * b + 16 * hf, par, sys, u, P.abort_flag, P.wait_polls) && ok;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float4 u = __ldcg(xv2 + 8 * b + 4 * hf + q);
-                    const float uu[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const float g = e[4 * q + k];
-                        e[4 * q + k] = __fmul_rn(__fdividef(g, __fadd_rn(1.0f, __expf(-g))), uu[k]);
-                    }
-                }
+                for (int k = 0; k < 16; ++k) e[k] = __fmul_rn(__fdividef(e[k], __fadd_rn(1.0f, __expf(-e[k]))), u[k]);
             }
             if (nw != nullptr && b < nxb) {  // RMSNorm: sum x^2 here, quantize x * w; 1/rms scales the rows
 #pragma unroll
@@ -363,11 +508,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
     const uint32_t sbase = smem_u32(smem);
     const uint32_t full_bar = sbase;
     const uint32_t empty_bar = sbase + 8 * kMaxStages;
-    volatile int* s_flag = reinterpret_cast<volatile int*>(smem + 16 * kMaxStages);  // warp-0 verdicts
+    volatile int* s_flag = reinterpret_cast<volatile int*>(smem + 16 * kMaxStages);
     const uint32_t tend = sbase + 16 * kMaxStages + 16;  // consumer warps done with every task
-    const uint32_t tdone = tend + 16;                     // [kSigSlots] u32 task completion posts
-    float* s_norm = reinterpret_cast<float*>(smem + 16 * kMaxStages + 32 + 4 * kSigSlots);  // [16] RMSNorm partials
+    float* s_norm = reinterpret_cast<float*>(smem + 16 * kMaxStages + 32);  // [16] RMSNorm partials
     volatile float4* s_ep = reinterpret_cast<volatile float4*>(s_norm + 16);  // [16] epilogue descriptors
+    volatile ulonglong2* s_od = reinterpret_cast<volatile ulonglong2*>(s_norm + 16 + 4 * 16);  // [16] output offsets
     constexpr int kHdr = ((kStackBarBytes + 127) / 128) * 128;
     float* slots = reinterpret_cast<float*>(smem + kHdr);
     const uint32_t stage0 = sbase + kStackSmemHeader + (uint32_t)P.x_smem;  // after the x staging buffer
@@ -383,45 +528,18 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
             mbar_init(empty_bar + 8 * s, kConsumerWarps);
         }
         s_flag[0] = 1;
-        for (int k = 0; k < 4 + kSigSlots; ++k) reinterpret_cast<volatile uint32_t*>(smem + 16 * kMaxStages + 16)[k] = 0;
+        for (int k = 0; k < 4; ++k) reinterpret_cast<volatile uint32_t*>(smem + 16 * kMaxStages + 16)[k] = 0;
         fence_mbar_init();
     }
     __syncthreads();
 
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------- producer
-        // Lane 0 streams weights and, between copies, releases the tasks this
-        // CTA's consumer warps have all posted done: one release fence (system
-        // scope when sharded), then this CTA is counted on every rank's counter.
+        // Lane 0 streams weights, never waiting for activations.
         if (lane != 0) return;
         int it = 0, s = 0;
         uint32_t phase = 0;
         bool ok = true;
-        int st = 0, sk = 0;  // next task to count, its signal ordinal
-        while (st < P.n_tasks && !__ldg(&P.tasks[st].signal)) ++st;
-        auto poll = [&]() -> bool {  // true when tasks were released
-            // every consecutive finished task goes out under ONE release fence
-            int e = st, ek = sk;
-            while (e < P.n_tasks) {
-                const uint32_t need = (uint32_t)kConsumerWarps * (uint32_t)(ek / kSigSlots + 1);
-                if (ld_acquire_shared(tdone + 4 * (ek % kSigSlots)) < need) break;
-                ++ek;
-                ++e;
-                while (e < P.n_tasks && !__ldg(&P.tasks[e].signal)) ++e;
-            }
-            if (e == st) return false;
-            fence_release(sys);
-            for (int t = st; t < e; ++t) {
-                if (!__ldg(&P.tasks[t].signal)) continue;
-                if (sys)
-                    for (int p = 0; p < P.world; ++p) red_add_u64(P.peer_done[p] + t * kCounterStride, true);
-                else
-                    red_add_u64(P.done + t * kCounterStride, false);
-            }
-            st = e;
-            sk = ek;
-            return true;
-        };
         auto give_up = [&]() {
             atomicOr(&g_device_status, kStatusWaitTimeout);
             atomicExch(P.abort_flag, 1u);
@@ -439,13 +557,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
             const uint64_t floor16 = total & ~(uint64_t)15;
             const uint64_t span = (uint64_t)R * rb, cta_end = (uint64_t)row_end * rb;
             for (uint64_t start = (uint64_t)row_begin * rb; start < cta_end; ++it) {
-                poll();
-                if (it >= NS && !mbar_test_wait(empty_bar + 8 * s, phase)) {
-                    // ring full: keep counting finished tasks while the slot drains
-                    uint64_t t0 = globaltimer_ns();
-                    for (uint32_t k = 1; !mbar_test_wait(empty_bar + 8 * s, phase); ++k) {
-                        if (poll()) t0 = globaltimer_ns();
-                        if ((k & 255u) == 0) {
+                if (it >= NS && !mbar_try_wait(empty_bar + 8 * s, phase)) {
+                    // ring full: wait (sleeping in try_wait) for the slot to drain
+                    const uint64_t t0 = globaltimer_ns();
+                    for (uint32_t k = 1; !mbar_try_wait(empty_bar + 8 * s, phase); ++k) {
+                        if ((k & 15u) == 0) {
                             if (*reinterpret_cast<volatile unsigned*>(P.abort_flag)) {
                                 ok = false;
                                 break;
@@ -491,33 +607,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                 }
             }
         }
-        // every copy issued: count the remaining tasks as the consumers finish
-        // them; sharded, then tell every rank that this CTA's rows of every
-        // task have been stored (one system-scope release per run)
-        if (ok) {
-            uint64_t t0 = globaltimer_ns();
-            for (uint32_t k = 1; st < P.n_tasks || (sys && ld_acquire_shared(tend) < (uint32_t)kConsumerWarps); ++k) {
-                if (poll()) {
-                    t0 = globaltimer_ns();
-                    continue;
-                }
-                __nanosleep(32);
-                if ((k & 63u) == 0) {
-                    if (*reinterpret_cast<volatile unsigned*>(P.abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    if (globaltimer_ns() - t0 > kWaitLimitNs) {
-                        give_up();
-                        break;
-                    }
-                }
-            }
-            if (ok && sys) {
-                asm volatile("fence.acq_rel.sys;" ::: "memory");
-                for (int p = 0; p < P.world; ++p) red_add_u64(P.peer_end[p], true);
-            }
-        }
         if (!ok) {  // leave no copy in flight
             for (int k = 0; k < NS && k < it; ++k) {
                 const int j = it - 1 - k;
@@ -536,8 +625,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
     // group, so the staging loads can all be in flight at once.
     const int tid = threadIdx.x;  // 0 .. kConsumers-1
     const uint32_t xs = sbase + kStackSmemHeader;  // x staging (xsw layout)
-    // this run's number: counter targets sit on top of all earlier runs
-    const unsigned long long run = *reinterpret_cast<volatile unsigned long long*>(P.epoch);
+    // this run's number: its rows carry tag run + 1
+    const uint32_t par = (uint32_t)(*reinterpret_cast<volatile unsigned long long*>(P.epoch) + 1) & 1u;
     bool alive = true, stop = false;
     int s = 0;
     uint32_t phase = 0;
@@ -546,36 +635,38 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
         const StackTask& H = P.tasks[t];
         const int K = __ldg(&H.K), S = __ldg(&H.segments);
         const int NW = __ldg(&H.nwi), SW = __ldg(&H.seg_wi), J = __ldg(&H.wi_per_lane);
-        if (tid == 0) {  // the input's CTAs (all ranks) are done, and the ordering dependency
-            const int src = __ldg(&H.src), src2 = __ldg(&H.src2), after = __ldg(&H.after), rs = __ldg(&H.res_src);
-            const unsigned long long target = (run + 1) * (unsigned long long)P.world * (unsigned long long)n_cta;
-            int ok = *reinterpret_cast<volatile unsigned*>(P.abort_flag) == 0;  // poisoned by an earlier run
-            if (ok && src >= 0) ok = wait_count_bounded(&P.done[src * kCounterStride], target, P.abort_flag, sys);
-            if (ok && src2 >= 0) ok = wait_count_bounded(&P.done[src2 * kCounterStride], target, P.abort_flag, sys);
-            if (ok && after >= 0) ok = wait_count_bounded(&P.done[after * kCounterStride], target, P.abort_flag, sys);
-            if (FX && ok && rs >= 0) ok = wait_count_bounded(&P.done[rs * kCounterStride], target, P.abort_flag, sys);
-            __threadfence();
-            s_flag[0] = ok;
+        // ordering dependencies: every row of `after` (and of the residual's task)
+        // stored in this run; each thread checks its share of the rows
+        bool ok = *reinterpret_cast<volatile unsigned*>(P.abort_flag) == 0;  // poisoned by an earlier run
+        const int src = __ldg(&H.src), after = __ldg(&H.after);
+        if (ok && after >= 0)
+            ok = wait_rows_tagged(ld_task_ptr(&P.tasks[after].tg), __ldg(&H.after_rows), par, sys, tid, P.abort_flag,
+                                  P.wait_polls);
+        if constexpr (FX) {
+            const int rs = __ldg(&H.res_src);
+            if (ok && rs >= 0)
+                ok = wait_rows_tagged(ld_task_ptr(&P.tasks[rs].tg), __ldg(&H.res_rows), par, sys, tid, P.abort_flag,
+                                      P.wait_polls);
         }
-        consumer_bar();  // also: every warp is done with the previous group's x staging
-        bool failed = s_flag[0] == 0;
+        consumer_bar();  // every warp is done with the previous group's x staging
         const float4* nw =
             FX ? reinterpret_cast<const float4*>(__ldg(reinterpret_cast<const unsigned long long*>(&H.norm_w))) : nullptr;
-        if (!failed) {   // read x (L2), apply the fusions, quantize, two lanes per 32-element block
-            const float4* xv = reinterpret_cast<const float4*>(__ldg(reinterpret_cast<const unsigned long long*>(&H.x)));
-            if (xv == nullptr) xv = reinterpret_cast<const float4*>(P.x_in);
-            const float4* xv2 =
-                FX ? reinterpret_cast<const float4*>(__ldg(reinterpret_cast<const unsigned long long*>(&H.x2))) : nullptr;
+        {   // read x (L2; a task's output waits for this run's tags), apply the fusions,
+            // quantize, two lanes per 32-element block
+            const float4* xv = reinterpret_cast<const float4*>(P.x_in);
+            const uint32_t* xt = src >= 0 ? ld_task_ptr(&P.tasks[src].tg) : nullptr;
+            const int src2 = FX ? __ldg(&H.src2) : -1;
+            const uint32_t* xt2 = src2 >= 0 ? ld_task_ptr(&P.tasks[src2].tg) : nullptr;
             float ss;  // RMSNorm: sum of squares of this thread's elements
-            if (FX && (xv2 != nullptr || nw != nullptr)) ss = stage_x<FX>(xv, xv2, nw, K, xs, tid, lane);
-            else ss = stage_x<false>(xv, nullptr, nullptr, K, xs, tid, lane);
+            if (FX && (xt2 != nullptr || nw != nullptr)) ss = stage_x<FX>(xv, xt, xt2, nw, K, xs, tid, lane, par, P, ok);
+            else ss = stage_x<false>(xv, xt, nullptr, nullptr, K, xs, tid, lane, par, P, ok);
             if (nw != nullptr) {
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
                 if (lane == 0) s_norm[warp] = ss;
             }
         }
-        if (consumer_bar_any(failed)) {  // every consumer leaves together after a failed wait
+        if (consumer_bar_any(!ok)) {  // every consumer leaves together after a failed wait
             stop = true;
             break;
         }
@@ -613,10 +704,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
             const int row_off = __ldg(&T.row_off);
             float* const yl = reinterpret_cast<float*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.y))) + row_off;
             const uint64_t yo = __ldg(reinterpret_cast<const unsigned long long*>(&T.y_off)) + (uint64_t)row_off;
+            const uint64_t tg_off = __ldg(reinterpret_cast<const unsigned long long*>(&T.tg_off));
+            const uint64_t to = tg_off ? tg_off + (uint64_t)row_off : 0ull;
             if (FX && lane == 0) {  // this task's residual and pair flag into the warp's descriptor
-                const float* res = ld_task_i32(&T.res_input) ? P.x_in
-                                                             : reinterpret_cast<const float*>(ld_task_u64(&T.res));
-                const uint64_t rp = res ? (uint64_t)(res + ld_task_i32(&T.row_off)) : 0ull;
+                const int rs = ld_task_i32(&T.res_src);
+                uint64_t rp = 0;
+                if (ld_task_i32(&T.res_input)) rp = (uint64_t)(P.x_in + ld_task_i32(&T.row_off));
+                else if (rs >= 0) rp = (uint64_t)(ld_task_ptr(&P.tasks[rs].tg) + ld_task_i32(&T.row_off)) | 1u;
                 s_ep[warp].x = __uint_as_float((uint32_t)rp);
                 s_ep[warp].y = __uint_as_float((uint32_t)(rp >> 32));
                 s_ep[warp].w = __int_as_float(half != 0u);
@@ -637,7 +731,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                     for (; rl < nr; rl += n_grp) {
                         const uint32_t row = base + (uint32_t)(rl * rbytes);
                         float rv = 0.0f;
-                        if (FX && lane == 0) rv = residual_of(s_ep + warp, r0 + rl);
+                        if (FX && lane == 0) rv = residual_of(s_ep + warp, r0 + rl, sys);
                         float acc = row_partial<F, G>(row, wi, has, X);
 #pragma unroll
                         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -648,7 +742,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                             for (int o = 16; o > 0; o >>= 1) up += __shfl_xor_sync(0xffffffffu, up, o);
                         }
                         if (S == 1) {
-                            if (lane == 0) put_row<FX>(P, yl, yo, r0 + rl, acc, s_ep + warp, rv, up);
+                            if (lane == 0) put_row<FX>(P, yl, yo, to, par, r0 + rl, acc, s_ep + warp, rv, up);
                         } else if (lane == 0) {  // this segment's partial (summed below)
                             float* sl = slots + s * P.slot_stride + rl * S * (half ? 2 : 1);
                             sl[sg] = acc;
@@ -673,8 +767,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                             for (int k = 0; k < S; ++k) v += sl[k];
                             if (FX && half)
                                 for (int k = 0; k < S; ++k) u += sl[S + k];
-                            const float rv = FX ? residual_of(s_ep + warp, r0 + rl) : 0.0f;
-                            put_row<FX>(P, yl, yo, r0 + rl, v, s_ep + warp, rv, u);
+                            const float rv = FX ? residual_of(s_ep + warp, r0 + rl, sys) : 0.0f;
+                            put_row<FX>(P, yl, yo, to, par, r0 + rl, v, s_ep + warp, rv, u);
                         }
                     }
                 }
@@ -687,24 +781,22 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                 rot += rot_step;
                 if (rot >= n_grp) rot -= n_grp;
             }
-            // this warp's rows of task t are stored: post it for the producer thread
-            if (__ldg(&T.signal)) {
-                __syncwarp();
-                if (lane == 0) red_release_shared_add(tdone + 4 * (__ldg(&T.sig_ord) % kSigSlots), 1u);
-            }
             if (++t >= P.n_tasks || !__ldg(&P.tasks[t].reuse_x)) break;
         }
     }
     // A sharded run ends only when every rank's rows of every task have landed
-    // here: each warp posts that it is done, the producer thread then counts
-    // this CTA on every rank's end counter, and one thread of CTA 0 waits for
-    // all CTAs of all ranks (the kernel, and so the stream, completes after it).
+    // here: each warp posts that it is done, the CTA's last warp counts the CTA
+    // (release_end: the rank's last CTA tells every rank), and one thread of
+    // CTA 0 waits for all ranks (the kernel, and so the stream, completes after it).
+    // this run's number (the epoch advances only after every CTA of the rank left)
+    const unsigned long long run = *reinterpret_cast<volatile unsigned long long*>(P.epoch);
     if (sys) {
         __syncwarp();
-        if (lane == 0) red_release_shared_add(tend, 1u);
+        if (lane == 0 && atom_add_acq_rel_shared(tend, 1u) + 1 == (uint32_t)kConsumerWarps &&
+            *reinterpret_cast<volatile unsigned*>(P.abort_flag) == 0)
+            release_end(P, run, n_cta);
         if (c == 0 && tid == 0 && !stop)
-            wait_count_bounded(P.end_done, (run + 1) * (unsigned long long)P.world * (unsigned long long)n_cta,
-                               P.abort_flag, true);
+            wait_count_bounded(P.end_done, (run + 1) * (unsigned long long)P.world, P.abort_flag, true, P.wait_ns);
     }
     // the last CTA of this rank to leave advances the epoch for the next run
     consumer_bar();

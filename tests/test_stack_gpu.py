@@ -2,8 +2,10 @@
 persistent cooperative launch.
 
 The stack must give, task by task, exactly the bits of the same GEMVs run one
-at a time through nexus_gpu_gemv (same plan, same arithmetic), and stay within
-the 1e-3 L2-relative GEMV tolerance of the C oracle.
+at a time through nexus_gpu_gemv (same plan, same arithmetic) -- given the
+input the stack hands a dependent task: its source's output with the lowest
+mantissa bit cleared (the stack carries each run's parity there) -- and stay
+within the 1e-3 L2-relative GEMV tolerance of the C oracle.
 """
 import ctypes
 
@@ -56,12 +58,18 @@ def build(L, dt, spec, seed):
     return h, Ws, ys
 
 
+def stack_input(y):
+    """A task's output as a dependent task of the stack consumes it: the
+    lowest mantissa bit cleared."""
+    return (y.view(torch.int32) & ~1).view(torch.float32)
+
+
 def chain_single(L, dt, spec, Ws, x):
     """The same GEMVs one call at a time through nexus_gpu_gemv."""
     outs = []
     st = torch.cuda.current_stream().cuda_stream
     for i, (name, rows, cols, src, after) in enumerate(spec):
-        xi = x if src < 0 else outs[src]
+        xi = x if src < 0 else stack_input(outs[src])
         y = torch.empty(rows, device="cuda")
         assert L.nexus_gpu_gemv(Ws[i].data_ptr(), dt, xi.data_ptr(), 0, y.data_ptr(), 1, rows, cols, st) == 0
         outs.append(y)
@@ -85,7 +93,7 @@ def test_stack_equals_single_gemvs_and_oracle(L, port, dt, hidden, kv, ffn):
         # oracle on a few tasks, each with the input the stack gave it
         for i in (0, 3, 6, 13, len(spec) - 1):
             name, rows, cols, src, _ = spec[i]
-            xi = (x if src < 0 else ys[src]).cpu().numpy()
+            xi = (x if src < 0 else stack_input(ys[src])).cpu().numpy()
             Wh = Ws[i].cpu().numpy()
             want = port.gemv(dt, Wh, xi, rows, cols)
             assert oracle.l2_rel(ys[i].cpu().numpy(), want) <= TOL, (i, name)
