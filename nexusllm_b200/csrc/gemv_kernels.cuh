@@ -567,11 +567,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_m1_kernel(const GemvPara
                 if (i >= p.n_stages) phase ^= 1;  // passes 1, 2, ... wait parities 0, 1, ...
             }
         }
-        if (!ok) {  // leave no copy in flight
-            for (int k = 0; k < p.n_stages && k < i; ++k) {
-                const int j = i - 1 - k;
-                mbar_wait_bounded(full_bar + 8 * (j % p.n_stages), (j / p.n_stages) & 1);
-            }
+        // leave no copy in flight, also when consumers stopped after a failed wait
+        (void)ok;
+        for (int k = 0; k < p.n_stages && k < i; ++k) {
+            const int j = i - 1 - k;
+            mbar_wait_bounded(full_bar + 8 * (j % p.n_stages), (j / p.n_stages) & 1);
         }
         return;
     }

@@ -607,11 +607,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                 }
             }
         }
-        if (!ok) {  // leave no copy in flight
-            for (int k = 0; k < NS && k < it; ++k) {
-                const int j = it - 1 - k;
-                mbar_wait_bounded(full_bar + 8 * (j % NS), (j / NS) & 1);
-            }
+        // leave no copy in flight: the last stages issued complete on their own
+        // (consumers that stopped after a failed wait no longer wait for them)
+        for (int k = 0; k < NS && k < it; ++k) {
+            const int j = it - 1 - k;
+            mbar_wait_bounded(full_bar + 8 * (j % NS), (j / NS) & 1);
         }
         return;
     }
