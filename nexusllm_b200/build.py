@@ -16,8 +16,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 SRC = os.path.join(HERE, "csrc", "nexus_gpu.cu")
 OUT = os.path.join(HERE, "lib", "libnexus_gpu.so")
-DEPS = [os.path.join(HERE, "csrc", f) for f in os.listdir(os.path.join(HERE, "csrc"))] + [
+DEPS = [os.path.join(HERE, "csrc", f) for f in os.listdir(os.path.join(HERE, "csrc")) if f.endswith((".cu", ".cuh"))] + [
     os.path.join(ROOT, "include", "nexus_gpu.h")]
+DROPIN_SRC = os.path.join(HERE, "csrc", "dropin.cpp")
+DROPIN_OUT = os.path.join(HERE, "lib", "libnexus_dropin.so")
 
 NVCC_FLAGS = [
     "-O3", "-std=c++17",
@@ -55,6 +57,23 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if verbose:
         sys.stderr.write(res.stderr)
     return OUT
+
+
+def build_dropin(reference_include: str, out: str = DROPIN_OUT) -> str:
+    """The C++ drop-in (csrc/dropin.cpp): NexusLLM's QuantizationKernel GGUF
+    methods and an INexusComputeBackend device, compiled against the
+    reference's own headers (`reference_include` = <NexusLLM>/include) and
+    linked to libnexus_gpu.so.  Needs those headers, so it is built where the
+    reference tree is present; the built .so travels with the library."""
+    lib = build()
+    os.makedirs(os.path.dirname(out), exist_ok=True)
+    cmd = [shutil.which("g++") or "g++", "-O2", "-std=c++20", "-fPIC", "-shared",
+           f"-I{reference_include}", "-o", out, DROPIN_SRC, f"-L{os.path.dirname(lib)}", "-lnexus_gpu",
+           "-Wl,-rpath,$ORIGIN"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"drop-in build failed:\n{res.stderr}")
+    return out
 
 
 if __name__ == "__main__":
