@@ -1,38 +1,40 @@
 """Benchmark: quantized GEMV HBM throughput and decode layer-stack tokens/s.
 
-Workload (M=1): one decode token through a
+Headline (M=1): one decode token through a
 Llama-3-8B-shaped Q4_0 stack -- 32 layers x {q 4096x4096, k 1024x4096,
 v 1024x4096, o 4096x4096, gate 14336x4096, up 14336x4096, down 4096x14336}
-plus the LM head 128256x4096 -- 225 fused GEMVs, 4.22 GB of weights, far
-larger than L2 (so every step streams weights from HBM; no L2 flush needed).
+plus the LM head 128256x4096 -- 225 fused GEMVs, 4.23 GB of weights, far
+larger than L2 (every step streams weights from HBM; no L2 flush needed).
 Within a layer each GEMV consumes the previous one's output (q feeds o as a
 stand-in for attention, o feeds gate and up, gate feeds down); every layer
 starts from the same resident hidden state.  Weights are seeded synthetic
-GGUF blocks with the configuration's distributions (nexusllm_b200/synth.py),
-generated on the device.
+GGUF blocks with the configuration's distributions, generated on the device
+in 8 row blocks per matrix seeded by (matrix, block), so every GPU count runs
+the same model byte for byte.
 
 A step = one token = the 225 GEMVs as ONE persistent GEMV-stack launch
 (nexus_gpu_stack_run), captured once in a CUDA graph and replayed.  With
 --gpus N > 1 (torchrun, one rank per GPU) every matrix is row-sharded over the
 ranks and the stack kernel stores each rank's output rows straight into every
 peer's output over NVLink (the all-gather fused into the GEMV; strong
-scaling: the same model at every N).  The same step as 225 separate GEMV
-launches (+ NCCL all-gathers at N > 1) is timed as a secondary figure and
-must agree bit for bit.
+scaling).  Sampled rows of four tasks are checked against the C oracle (the
+checker) at every N; the step as 225 separate launches (+ NCCL all-gathers
+at N > 1) is timed as a secondary figure.
 
-Reported (one JSON line on rank 0):
-  value     whole-job algorithmic GB/s = (weight + x + y bytes per step) x
-            steps / device time (max over ranks)
-  e2e       same metric through the library's C ABI with host buffers:
-            pinned host hidden state in, host logits out, every step
-            (N=1 also reports the reference-facing nexus_gpu_gemv_dispatch
-            path, one synchronous host-pointer call per GEMV)
-  roofline  the stack kernel (the only kernel of the step), algorithmic
-            bytes per launch / CUDA-event time, against MEASURED_PEAKS.json
-  cpu_baseline  NexusLLM's own AVX2 GEMV (oracle/_ref) on this host's cores
-            over one decode layer
+One JSON line on rank 0: the contract's keys (value = whole-job algorithmic
+GB/s over device time, max over ranks; e2e through the C ABI with host
+buffers; roofline of the stack kernel against MEASURED_PEAKS.json;
+cpu_baseline = NexusLLM's own AVX2 GEMV over the whole step on this host),
+then compact secondary tables, then -- last, so that a truncated log keeps
+them -- the BASELINE configurations:
+  config0_q4_0_4096         configs[0], per call and as a 64-GEMV stack, + CPU
+  config1_q8_0_llama2_7b    configs[1], per shape, the set, the 32-layer stack, + CPU
+  config2_q5k_q6k_llama2_7b configs[2], the Q5_K and Q6_K 32-layer stacks, + CPU
+  model_70b                 configs[4] at this N: batch 1 (stack) and 16 (tcgen05)
+(CPU legs: 1 thread and all host threads; "ms" is per call, per set, or per
+token = 32 x one layer for configs[2].)
 
---impl reference times only the reference CPU path (rank 0), same metric.
+--impl reference times NexusLLM's own CPU GEMV over the whole step (rank 0).
 """
 from __future__ import annotations
 
@@ -174,65 +176,92 @@ def gpu_uuid(torch, local):
         return str(local)
 
 
-def time_reference_layer(reps: int, threads: int, min_seconds: float = 0.0):
-    """NexusLLM's own GEMV (oracle/_ref, AVX2+FMA) over one decode layer's 7
-    matrices; returns (GB/s, seconds per layer, kind, sample description)."""
-    import numpy as np
+class CpuStep:
+    """The configs[3] decode step (32 layers x 7 GEMVs + LM head, 225 GEMVs,
+    4.23 GB of Q4_0) on the host cores: NexusLLM's own fused_gemv_q4_0
+    (oracle/_ref: src/quantization.cpp compiled unmodified, AVX2+FMA), or the
+    C restatement where the reference build is absent.  Rows are split over
+    `threads` host threads, each calling the unmodified reference function
+    (Q4_0 has no OpenMP pragma in the reference, src/quantization.cpp:264-330,
+    so it would otherwise use one core).  The layers cycle over DISTINCT
+    weight buffers (about 0.5 GB, more than any host cache) and the LM head.
+    Inputs are fixed seeded vectors; the timing does not depend on values."""
 
-    import oracle
-    from nexusllm_b200 import synth
+    DISTINCT = 4
 
-    if oracle.reference_available():
-        lib, kind = oracle.reference(), "reference"
-    else:  # the reference sources were not available at build time
-        lib, kind = oracle.port(), "port"
-    mats = []
-    for i, (name, n, k) in enumerate(LAYER_SHAPES):
-        W = synth.blocks_numpy(DTYPE, n, k, 3000 + i)
-        x = synth.activations_numpy(1, k, 3100 + i)[0]
-        mats.append((W, x, np.zeros(n, np.float32), n, k))
-    layer_bytes = sum(q4_bytes(n, k) + 4 * k + 4 * n for _, n, k in LAYER_SHAPES)
+    def __init__(self, m=None):
+        import numpy as np
 
-    def run_layer():
-        for W, x, y, n, k in mats:
-            if kind == "reference":
-                oracle.gemv_threaded(lib, DTYPE, W, x, y, n, k, threads)
-            else:
-                y[:] = lib.gemv(DTYPE, W, x, n, k)
+        import oracle
+        from nexusllm_b200 import synth
 
-    run_layer()  # warm-up (page-in)
-    t = []
-    start = time.perf_counter()
-    while len(t) < reps or time.perf_counter() - start < min_seconds:
-        t0 = time.perf_counter()
-        run_layer()
-        t.append(time.perf_counter() - t0)
-    reps = len(t)
-    sec = statistics.median(t)
-    sample = (f"one Llama-3-8B Q4_0 decode layer (7 GEMVs, {layer_bytes / 1e6:.1f} MB of weights) x {reps}, "
-              f"rows split over {threads} threads, each thread calling the unmodified reference function")
-    return layer_bytes / sec / 1e9, sec, kind, sample
+        self.m = m or model_dims("8b")
+        if oracle.reference_available():
+            self.lib, self.kind = oracle.reference(), "reference"
+        else:  # the reference sources were not available at build time
+            self.lib, self.kind = oracle.port(), "port"
+        shapes = shapes_of(self.m)
+        base = [synth.blocks_numpy(DTYPE, n, k, 3000 + i) for i, (_, n, k) in enumerate(shapes)]
+        self.layers = [[(np.copy(W), n, k) for W, (_, n, k) in zip(base, shapes)] for _ in range(self.DISTINCT)]
+        self.head = (synth.blocks_numpy(DTYPE, self.m["vocab"], self.m["hidden"], 3999), self.m["vocab"],
+                     self.m["hidden"])
+        self.x = {k: synth.activations_numpy(1, k, 3100 + k)[0] for k in {k for _, _, k in shapes}}
+        self.y = {n: np.zeros(n, np.float32) for n in {n for _, n, _ in shapes} | {self.m["vocab"]}}
+
+    def gemv(self, W, n, k, threads):
+        import oracle
+
+        if self.kind == "reference":
+            oracle.gemv_threaded(self.lib, DTYPE, W, self.x[k], self.y[n], n, k, threads)
+        else:
+            self.y[n][:] = self.lib.gemv(DTYPE, W, self.x[k], n, k)
+
+    def run(self, threads):
+        for l in range(self.m["layers"]):
+            for W, n, k in self.layers[l % self.DISTINCT]:
+                self.gemv(W, n, k, threads)
+        self.gemv(*self.head, threads)
+
+    def time(self, threads, reps, warmup, min_seconds=0.0):
+        """Median seconds per step over >= reps steps (and >= min_seconds)."""
+        for _ in range(warmup):
+            self.run(threads)
+        t, start = [], time.perf_counter()
+        while len(t) < reps or time.perf_counter() - start < min_seconds:
+            t0 = time.perf_counter()
+            self.run(threads)
+            t.append(time.perf_counter() - t0)
+        return statistics.median(t), len(t)
+
+    def sample(self, threads, steps, warmup):
+        return (f"the whole configs[3] decode step ({7 * self.m['layers'] + 1} Q4_0 GEMVs incl. the LM head, "
+                f"{model_bytes(self.m) / 1e9:.2f} GB) x {steps} steps after {warmup} warm-up steps, rows split over "
+                f"{threads} threads each calling the unmodified reference fused_gemv_q4_0; layers cycle over "
+                f"{self.DISTINCT} distinct weight buffers")
 
 
 def run_reference(args):
+    """--impl reference: NexusLLM's own CPU GEMV on this host's cores, the whole
+    decode step per step (rank 0 only; other ranks exit without work)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     threads = cpu_threads()
-    reps = max(1, args.steps)
-    for _ in range(args.warmup):
-        pass
-    gbs, sec, kind, sample = time_reference_layer(reps, threads)
-    reps = max(reps, 1)
-    tok_s = gbs * 1e9 / step_bytes()
+    reps = max(1, min(args.steps, 30))       # a whole step is ~0.3 s: bounded sample
+    warmup = max(1, min(args.warmup, 10))
+    step = CpuStep(model_dims(MODEL))
+    sec, reps = step.time(threads, reps, warmup)
+    sb = model_bytes(step.m)
+    gbs = sb / sec / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
-        "n_gpus": args.gpus, "steps": reps, "warmup": args.warmup,
+        "n_gpus": args.gpus, "steps": reps, "warmup": warmup,
         "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(args, reference=True),
-        "tokens_per_s": round(tok_s, 6),
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
+        "tokens_per_s": round(1.0 / sec, 4),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": step.kind,
+                         "sample": step.sample(threads, reps, warmup)},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -254,33 +283,77 @@ def workload_config(args, reference=False):
     return {
         **head,
         "weight_format": "GGUF Q4_0", "global_batch": 1, "gemvs_per_step": 7 * LAYERS + 1,
-        "parallelism": "cpu" if reference else (f"row-shard x{args.gpus} + NCCL all-gather" if args.gpus > 1
-                                                else "single GPU"),
+        "parallelism": "cpu" if reference else (f"row-shard x{args.gpus}, all-gather fused into the GEMV stack "
+                                                "(peer stores over NVLink)" if args.gpus > 1 else "single GPU"),
+        "same_model_every_n": "weights seeded by global row (8 row blocks per matrix)",
         "l2": f"working set {gb:.2f} GB per step >> 126 MB L2 (no flush needed)",
     }
 
 
 # -------------------------------------------------------------- our arm
-def build_stack(torch, rank, world, n_layers):
-    """Weights for this rank: every matrix's row slice [rank*n/W, (rank+1)*n/W)."""
-    from nexusllm_b200 import synth
+# Every matrix is generated as CHUNKS row blocks, block c from seed (matrix
+# seed, c): rank r of W (W in 1, 2, 4, 8) generates blocks [8r/W, 8(r+1)/W),
+# which are exactly its rows [N*r/W, N*(r+1)/W).  So every N runs the SAME
+# model, byte for byte.
+CHUNKS = 8
 
+
+def slice_blocks(torch, dt, N, K, seed, rank, world, dev):
+    """Rank `rank`'s row slice of the seeded N x K matrix `seed` (GGUF blocks,
+    flat uint8 on `dev`)."""
+    from nexusllm_b200 import synth
+    from nexusllm_b200.formats import weight_bytes
+
+    assert N % CHUNKS == 0 and CHUNKS % world == 0, (N, world)
+    c0, c1 = CHUNKS * rank // world, CHUNKS * (rank + 1) // world
+    cb = weight_bytes(dt, N // CHUNKS, K)
+    out = torch.empty((c1 - c0) * cb, dtype=torch.uint8, device=dev)
+    for c in range(c0, c1):
+        out[(c - c0) * cb:(c - c0 + 1) * cb].copy_(synth.blocks_torch(dt, N // CHUNKS, K, seed * 64 + c, device=dev))
+    return out
+
+
+def model_dims(name):
+    """BASELINE configs[3] (8b) and configs[4] (70b) shapes."""
+    if name == "70b":
+        return {"name": "70b", "hidden": 8192, "kv": 1024, "ffn": 28672, "vocab": 128256, "layers": 80}
+    return {"name": "8b", "hidden": 4096, "kv": 1024, "ffn": 14336, "vocab": 128256, "layers": 32}
+
+
+def shapes_of(m):
+    h, kv, f = m["hidden"], m["kv"], m["ffn"]
+    return [("q", h, h), ("k", kv, h), ("v", kv, h), ("o", h, h), ("gate", f, h), ("up", f, h), ("down", h, f)]
+
+
+def model_bytes(m, layers=None, dt=7):
+    from nexusllm_b200.formats import weight_bytes
+
+    b = sum(weight_bytes(dt, n, k) + 4 * k + 4 * n for _, n, k in shapes_of(m))
+    return b * (m["layers"] if layers is None else layers) + weight_bytes(dt, m["vocab"], m["hidden"]) + \
+        4 * m["hidden"] + 4 * m["vocab"]
+
+
+def gen_model(torch, m, rank, world, dev, seed_base, n_layers=None, dt=7):
+    """This rank's row slices of every matrix of model m (same bytes at every N)."""
     layers = []
-    for l in range(n_layers):
-        mats = {}
-        for i, (name, n, k) in enumerate(LAYER_SHAPES):
-            nl = n // world
-            mats[name] = synth.blocks_torch(DTYPE, nl, k, 1000 * 3 + 10 * l + i + 100000 * rank)
-        layers.append(mats)
-    head = synth.blocks_torch(DTYPE, VOCAB // world, HIDDEN, 1000 * 3 + 999 + 100000 * rank)
+    for l in range(m["layers"] if n_layers is None else n_layers):
+        layers.append({name: slice_blocks(torch, dt, n, k, seed_base + 10 * l + i, rank, world, dev)
+                       for i, (name, n, k) in enumerate(shapes_of(m))})
+    head = slice_blocks(torch, dt, m["vocab"], m["hidden"], seed_base + 9999, rank, world, dev)
     return layers, head
+
+
+def build_stack(torch, rank, world, n_layers):
+    """Weights of the headline model for this rank (configs[3], seeded by global row)."""
+    return gen_model(torch, model_dims(MODEL), rank, world, torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))),
+                     3000, n_layers)
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=3000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -293,8 +366,10 @@ def main():
                     help="skip the decode stack with RMSNorm / SwiGLU / residual fused in")
     ap.add_argument("--no-batched", action="store_true",
                     help="skip the batched-decode points (M = 4, 16, 64 tokens per step)")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip BASELINE configs[0..2] (N=1) and the configs[4] Llama-3-70B object (every N)")
     ap.add_argument("--model", default="8b", choices=["8b", "70b"],
-                    help="8b: configs[3] (the headline); 70b: configs[4], Llama-3-70B shapes")
+                    help="8b: configs[3] (the headline); 70b: configs[4] as the headline (profiling)")
     ap.add_argument("--layers", type=int, default=None,
                     help="decoder layers in the stack (the configuration's count by default; fewer only for "
                          "profiling runs)")
@@ -303,9 +378,7 @@ def main():
     if args.layers is None:
         args.layers = LAYERS
     if args.model == "70b":
-        # the 70B configuration is the batch-1 sharded stack; batched points,
-        # per-format timings and the host-weight path stay with the 8B headline
-        args.no_batched = args.no_formats = args.no_fused = args.no_gguf = True
+        args.no_batched = args.no_formats = args.no_fused = args.no_gguf = args.no_configs = True
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
@@ -406,6 +479,7 @@ def main():
     sb = step_bytes(layers=args.layers)
     peak, peak_kind = load_peaks()
     n_gemvs = 7 * args.layers + 1
+    extra, tail = {}, {}
 
     if world == 1:
         # ---- headline: the whole step in ONE persistent kernel (GEMV stack)
@@ -417,36 +491,37 @@ def main():
             ms = timed(stack_graph.replay, args.steps)
         clocks = clk.summary()
         check_status(L)
-        # the stack must reproduce the per-GEMV path bit for bit (LM head and last layer)
+        # the stack against the per-GEMV path (LM head bit for bit), and sampled rows against the oracle
         with torch.cuda.stream(stream):
             graph.replay()
         torch.cuda.synchronize(dev)
         check_against_per_gemv(torch, (("head", ys[-1]), ("down", ys[-2]), ("gate", ys[-4])), out, "stack")
         verify_head(torch, be, head, h0, ys[-1], world, rank)
+        par = stack_parity(torch, layers, head, ys, h0, world, rank, dev)
         ms_step = ms / args.steps
         value = sb * args.steps / (ms / 1e3) / 1e9
         # secondary: the same step as 225 separately launched GEMVs in a CUDA graph
-        reps = max(10, args.steps // 5)
+        reps = max(10, min(args.steps // 5, 50))
         ms_graph = timed(graph.replay, reps) / reps
-        per_gemv = {"ms_per_step": round(ms_graph, 4), "value": round(sb / (ms_graph / 1e3) / 1e9, 1),
-                    "unit": "GB/s", "tokens_per_s": round(1e3 / ms_graph, 2),
+        per_gemv = {"ms_per_step": round(ms_graph, 4), "GBs": round(sb / (ms_graph / 1e3) / 1e9, 1),
                     "launches_per_step": 2 * n_gemvs}
         roofline = {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
                     "frac": round(value / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                     "kernel": "gemv_stack_kernel<FmtQ4_0,2>: the step's 225 GEMVs in one cooperative launch",
                     "bytes_per_launch": sb, "avg_launch_us": round(ms_step * 1e3, 2),
-                    "launch_note": "one launch per step, after a 28 KB counter reset (cudaMemsetAsync)",
                     "traffic": round(STACK_TRAFFIC_PER_ALG_BYTE * sb)}
         e2e = None if args.no_e2e else e2e_stack_host(torch, L, stack, h0, ys[-1], stream, dev, args, timed, sb)
         e2e_dispatch = None if (args.no_e2e or args.model == "70b") else e2e_host_api(torch, L, layers, head, h0,
                                                                                       args)
         launches = args.steps
-        launches_note = f"1 gemv_stack_kernel per step x {args.steps} steps (plus one counter memset per step)"
-        extra = {"per_gemv_graph": per_gemv, "e2e_per_gemv_dispatch": e2e_dispatch}
+        launches_note = f"1 gemv_stack_kernel per step x {args.steps} steps"
+        extra["per_gemv_graph"] = per_gemv
+        if e2e_dispatch:
+            extra["e2e_per_gemv_dispatch"] = {k: e2e_dispatch[k] for k in ("value", "unit", "ms_per_step")}
         if not args.no_batched:
             extra["batched_decode"] = batched_decode(torch, L, layers, head, stream, dev, timed, args, peak, stack)
         if not args.no_formats:
-            extra["gguf_gemv"] = gguf_formats(torch, L, stream, dev, timed, peak)
+            extra["formats_gemv"] = gguf_formats(torch, L, stream, dev, timed, peak)
             extra["int4_awq_fp8"] = other_formats(torch, L, stream, dev, timed, peak)
         if not args.no_fused:
             extra["fused_decode_stack"] = fused_decode_stack(torch, L, layers, head, h0, stream, dev, timed, args, peak)
@@ -464,19 +539,16 @@ def main():
             ms = timed(sgraph.replay, args.steps)
         clocks = clk.summary()
         check_status(L)
-        # bit-exact against the per-GEMV path with NCCL all-gathers
         with torch.cuda.stream(stream):
             graph.replay()
         torch.cuda.synchronize(dev)
         check_against_per_gemv(torch, (("head", souts[-1]), ("down", souts[-2]), ("gate", souts[-4])), out,
                                "sharded stack")
+        par = stack_parity(torch, layers, head, souts, h0, world, rank, dev)
         ms_step = ms / args.steps
         value = sb * args.steps / (ms / 1e3) / 1e9
-        reps = max(10, args.steps // 5)
+        reps = max(10, min(args.steps // 5, 50))
         ms_graph = timed(graph.replay, reps) / reps
-        per_gemv = {"ms_per_step": round(ms_graph, 4), "value": round(sb / (ms_graph / 1e3) / 1e9, 1),
-                    "unit": "GB/s", "tokens_per_s": round(1e3 / ms_graph, 2),
-                    "launches_per_step": 2 * n_gemvs, "nccl_all_gathers_per_step": n_gemvs}
         per_gpu = sb / world
         roofline = {"bound": "hbm", "achieved": round(per_gpu / (ms_step * 1e-3) / 1e9, 1), "peak": peak,
                     "unit": "GB/s", "frac": round(per_gpu / (ms_step * 1e-3) / 1e9 / peak, 4),
@@ -488,25 +560,41 @@ def main():
         e2e = None if args.no_e2e else e2e_sharded(torch, sst, sgraph, h0, souts[-1], stream, dev, args, timed, sb)
         launches = args.steps
         launches_note = (f"1 gemv_stack_kernel per step per GPU x {args.steps} steps; no NCCL in the step "
-                         "(peer stores + peer counters inside the kernel)")
-        extra = {"per_gemv_graph_nccl": per_gemv}
+                         "(peer stores inside the kernel)")
+        extra["per_gemv_graph_nccl"] = {"ms_per_step": round(ms_graph, 4),
+                                        "GBs": round(sb / (ms_graph / 1e3) / 1e9, 1),
+                                        "launches_per_step": 2 * n_gemvs, "nccl_all_gathers_per_step": n_gemvs}
         del sgraph
         sst.close()
+    del graph
+    extra["parity"] = par
+
+    # BASELINE configs[0..2] (one GPU) and configs[4] (every N), placed last in the line
+    if not args.no_configs:
+        del layers, head
+        torch.cuda.empty_cache()
+        if world == 1:
+            tail["config0_q4_0_4096"] = config0(torch, L, dev, timed, peak)
+            tail["config1_q8_0_llama2_7b"] = config1(torch, L, dev, timed, peak)
+            tail["config2_q5k_q6k_llama2_7b"] = config2(torch, L, dev, timed, peak)
+        tail["model_70b"] = model_70b(torch, L, world, rank, local, dev, timed, peak, args, pg)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        gbs, sec, kind, sample = time_reference_layer(3, cpu_threads(), min_seconds=10.0)
-        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cpu_threads(), "kind": kind, "sample": sample}
+        cstep = CpuStep(model_dims(MODEL))
+        threads = cpu_threads()
+        sec, n = cstep.time(threads, 3, 1, min_seconds=10.0)
+        cpu = {"value": round(model_bytes(cstep.m) / sec / 1e9, 3), "unit": "GB/s", "cores": threads,
+               "kind": cstep.kind, "ms_per_step": round(sec * 1e3, 2), "sample": cstep.sample(threads, n, 1)}
 
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int8+fp32",
-        "dtype_note": "Q4_0 codes x 16-bit fixed-point x in int8 dp4a limbs, fp32 accumulation",
+        "dtype_note": "Q4_0 codes x 16-bit fixed-point x (exact int32 dp2a), fp32 scales and accumulation",
         "data": "synthetic (seeded GGUF Q4_0 blocks, x ~ N(0,1))",
         "config": workload_config(args),
         "layers": args.layers,
-        "pct_of_8tbs": round(100 * value / NOMINAL_HBM_GBS, 2),
         "pct_of_measured_hbm": round(100 * value / peak, 2),
         "tokens_per_s": round(1e3 / ms_step, 2),
         "gemv_calls_per_s": round(n_gemvs * 1e3 / ms_step, 1),
@@ -515,12 +603,39 @@ def main():
         "gpu_launches": launches, "gpu_launches_note": launches_note,
     }
     line.update(extra)
+    line.update(tail)
     if rank == 0:
-        print(json.dumps(line), flush=True)
-    del graph
+        print(json.dumps(line, separators=(",", ":")), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+
+
+def stack_parity(torch, layers, head, outs, h0, world, rank, dev):
+    """Sampled rows of this rank's slice of the headline stack's first q, first
+    o, last down and LM head against the C oracle, each task with the input the
+    stack gave it; max over ranks."""
+    import torch.distributed as dist
+
+    from nexusllm_b200.formats import weight_bytes
+
+    per = 7
+    checks = [(layers[0]["q"], HIDDEN, HIDDEN, None, 0), (layers[0]["o"], HIDDEN, HIDDEN, 0, 3),
+              (layers[-1]["down"], HIDDEN, FFN, per * (len(layers) - 1) + 4, per * (len(layers) - 1) + 6),
+              (head, VOCAB, HIDDEN, None, len(outs) - 1)]
+    errs = []
+    for W, n, k, src, i in checks:
+        xin = h0 if src is None else stack_input(torch, outs[src])
+        nl = n // world
+        r0 = n * rank // world
+        errs.append(oracle_rows_check(torch, W, weight_bytes(DTYPE, 1, k), xin, outs[i][r0:r0 + nl], nl))
+    err = torch.tensor([max(errs)], device=dev)
+    if world > 1:
+        dist.all_reduce(err, op=dist.ReduceOp.MAX)
+    e = float(err.item())
+    return {"checker": "C oracle (pinned bit for bit to the reference build)", "tol": 1e-3,
+            "tasks": "q0, o0, last down, LM head; 16 sampled rows of every rank's slice",
+            "max_l2_rel": float(f"{e:.3e}"), "pass": e <= 1e-3}
 
 
 def check_against_per_gemv(torch, pairs, out, what):
@@ -554,7 +669,7 @@ def batched_decode(torch, L, layers, head, stream, dev, timed, args, peak, stack
     captured in a CUDA graph.  M >= 16 runs on the tcgen05 tensor cores; M = 4
     runs the batch-1 CUDA-core kernel once per token.  Same weights as the
     headline; a step reads every weight once per call."""
-    out = []
+    out = {}
     ws_need = 0
     for M in (4, 16, 64):
         ws_need = max([ws_need] + [L.nexus_gpu_gemv_workspace_size(DTYPE, M, n, k) for _, n, k in LAYER_SHAPES]
@@ -591,10 +706,8 @@ def batched_decode(torch, L, layers, head, stream, dev, timed, args, peak, stack
         ms = timed(g.replay, reps) / reps
         sb = step_bytes(layers=len(layers))
         gbs = sb / (ms * 1e-3) / 1e9
-        out.append({"M": M, "ms_per_step": round(ms, 4), "tokens_per_s": round(M * 1e3 / ms, 1),
-                    "value": round(gbs, 1), "unit": "GB/s", "pct_of_measured_hbm": round(100 * gbs / peak, 2),
-                    "path": "tcgen05 kind::f16 (gemm_q4_0_mma_kernel)" if M >= 16 else
-                            "batch-1 CUDA-core kernel per token", "steps": reps})
+        out[f"M{M}"] = {"ms": round(ms, 3), "tok_s": round(M * 1e3 / ms, 1),
+                        "path": "tcgen05" if M >= 16 else "batch-1 kernel per token, per-GEMV launches"}
         del g
     if stack is not None:
         # M = 4 tokens through the GEMV stack, one launch per token (the batch-1
@@ -622,10 +735,8 @@ def batched_decode(torch, L, layers, head, stream, dev, timed, args, peak, stack
         reps = max(5, min(50, args.steps // 20))
         ms = timed(g.replay, reps) / reps
         gbs = step_bytes(layers=len(layers)) / (ms * 1e-3) / 1e9  # weights once per step, as above
-        out.append({"M": M, "ms_per_step": round(ms, 4), "tokens_per_s": round(M * 1e3 / ms, 1),
-                    "value": round(gbs, 1), "unit": "GB/s", "pct_of_measured_hbm": round(100 * gbs / peak, 2),
-                    "path": "GEMV stack once per token (batch-1 CUDA-core path, one launch per token)",
-                    "steps": reps})
+        out["M4_stack"] = {"ms": round(ms, 3), "tok_s": round(M * 1e3 / ms, 1),
+                           "path": "GEMV stack once per token"}
         del g
     return out
 
@@ -642,8 +753,9 @@ def gguf_formats(torch, L, stream, dev, timed, peak):
     from nexusllm_b200.formats import weight_bytes
 
     shapes = [(14336, 4096), (4096, 14336), (128256, 4096), (28672, 8192), (8192, 28672)]
-    out = []
+    out = {"cols": "[us per call, % of measured HBM]; rows x cols"}
     for dt, name in ((7, "q4_0"), (9, "q8_0"), (11, "q5_k"), (12, "q6_k"), (1, "fp16")):
+        out[name] = {}
         for rows, cols in shapes:
             wb = weight_bytes(dt, rows, cols)
             alg = wb + cols * 4 + rows * 4
@@ -672,9 +784,7 @@ def gguf_formats(torch, L, stream, dev, timed, peak):
             reps = 5
             ms = timed(g.replay, reps) / (reps * calls)
             gbs = alg / (ms * 1e-3) / 1e9
-            out.append({"format": name, "rows": rows, "cols": cols, "us_per_call": round(ms * 1e3, 2),
-                        "value": round(gbs, 1), "unit": "GB/s", "pct_of_measured_hbm": round(100 * gbs / peak, 1),
-                        "gemv_calls_per_s": round(1e3 / ms, 1), "bytes_per_call": alg, "weight_copies": n})
+            out[name][f"{rows}x{cols}"] = [round(ms * 1e3, 2), round(100 * gbs / peak, 1)]
             del g, W
     return out
 
@@ -687,7 +797,7 @@ def other_formats(torch, L, stream, dev, timed, peak):
     GB/s counts weights, scales, zeros, x and y once per call."""
     shapes = [(HIDDEN, HIDDEN), (FFN, HIDDEN), (HIDDEN, FFN), (VOCAB, HIDDEN)]
     gs = 128
-    out = []
+    out = {"cols": "[us per call, % of measured HBM]; rows x cols; INT4 group 128 with zeros"}
     for fmt in ("int4_awq", "fp8_e4m3"):
         for rows, cols in shapes:
             if fmt == "int4_awq":
@@ -734,10 +844,7 @@ def other_formats(torch, L, stream, dev, timed, peak):
             reps = 5
             ms = timed(g.replay, reps) / (reps * calls)
             gbs = alg / (ms * 1e-3) / 1e9
-            out.append({"format": fmt, "rows": rows, "cols": cols, "group_size": gs if fmt == "int4_awq" else None,
-                        "us_per_call": round(ms * 1e3, 2), "value": round(gbs, 1), "unit": "GB/s",
-                        "pct_of_measured_hbm": round(100 * gbs / peak, 1), "bytes_per_call": alg,
-                        "weight_copies": n})
+            out.setdefault(fmt, {})[f"{rows}x{cols}"] = [round(ms * 1e3, 2), round(100 * gbs / peak, 1)]
             del g, W
             if fmt == "int4_awq":
                 del S, Z
@@ -799,11 +906,9 @@ def fused_decode_stack(torch, L, layers, head, h0, stream, dev, timed, args, pea
     gbs = sb / (ms * 1e-3) / 1e9
     del g
     L.nexus_gpu_stack_destroy(h)
-    return {"ms_per_step": round(ms, 4), "tokens_per_s": round(1e3 / ms, 2), "value": round(gbs, 1), "unit": "GB/s",
-            "pct_of_measured_hbm": round(100 * gbs / peak, 2), "steps": reps,
-            "dataflow": "RMSNorm->q,k,v; o(x=q)+residual; RMSNorm->gate+up pair, SwiGLU epilogue; down+residual; "
-                        "RMSNorm->head",
-            "launches_per_step": 1}
+    return {"ms_per_step": round(ms, 4), "tokens_per_s": round(1e3 / ms, 2), "GBs": round(gbs, 1),
+            "pct_of_measured_hbm": round(100 * gbs / peak, 2),
+            "dataflow": "RMSNorm->qkv; o+res; RMSNorm->gate+up pair (SwiGLU); down+res; RMSNorm->head"}
 
 
 def gguf_upload(torch, L, dev):
@@ -887,8 +992,12 @@ def gguf_upload(torch, L, dev):
             # plain per-tensor pageable copies
             torch.cuda.synchronize(dev)
             t0 = time.perf_counter()
-            for t in f.tensors:
-                torch.from_numpy(mm[t["file_offset"]:t["file_offset"] + t["bytes"]]).to(dev)
+            import warnings
+
+            with warnings.catch_warnings():  # read-only memmap views: torch only reads them here
+                warnings.simplefilter("ignore", UserWarning)
+                for t in f.tensors:
+                    torch.from_numpy(mm[t["file_offset"]:t["file_offset"] + t["bytes"]]).to(dev)
             torch.cuda.synchronize(dev)
             plain_s = time.perf_counter() - t0
             del mm
@@ -936,16 +1045,11 @@ def gguf_upload(torch, L, dev):
         shutil.rmtree(d, ignore_errors=True)
     best = min(times[1:])
     gbs = data_bytes / best / 1e9
-    return {"file_bytes": file_bytes, "tensor_bytes": data_bytes,
-            "tensors": len(tensors), "upload_s": round(best, 4), "upload_gbs": round(gbs, 2),
-            "first_upload_s": round(times[0], 4), "pinned_h2d_gbs": round(pinned_gbs, 2),
-            "frac_of_pinned_h2d": round(gbs / pinned_gbs, 3),
+    del write_s
+    return {"tensor_bytes": data_bytes, "upload_s": round(best, 4), "upload_gbs": round(gbs, 2),
+            "pinned_h2d_gbs": round(pinned_gbs, 2), "frac_of_pinned_h2d": round(gbs / pinned_gbs, 3),
             "plain_per_tensor_pageable_gbs": round(data_bytes / plain_s / 1e9, 2),
-            "write_file_s": round(write_s, 2), "page_cache": "warm (file just written)",
-            "decode_from_file": {"load_s": round(load_s, 3), "ms_per_step": round(dec_ms, 4),
-                                 "tokens_per_s": round(1e3 / dec_ms, 1),
-                                 "path": "GgufDecodeStack: parse, upload, one fused stack (norms, gate+up pair, "
-                                         "residuals) per token"}}
+            "decode_from_file_ms": round(dec_ms, 4), "load_s": round(load_s, 3)}
 
 
 def build_stack_graph(torch, L, _native, layers, head, h0, stream, dev):
@@ -1155,6 +1259,404 @@ def e2e_host_api(torch, L, layers, head, h0, args):
             "d2h_bytes_per_step": d2h, "ms_per_step": round(sec * 1e3, 3), "tokens_per_s": round(1 / sec, 2),
             "api": "nexus_gpu_gemv_dispatch (host pointers, synchronous, weights cached on device)",
             "steps": args.e2e_steps}
+
+
+# --------------------------------------------------- BASELINE configs[0..2], [4]
+def _cpu_time(fn, min_seconds=1.5, min_reps=3):
+    """Median seconds of fn() after one warm-up call, over >= min_reps calls and >= min_seconds."""
+    fn()
+    t, start = [], time.perf_counter()
+    while len(t) < min_reps or time.perf_counter() - start < min_seconds:
+        t0 = time.perf_counter()
+        fn()
+        t.append(time.perf_counter() - t0)
+    return statistics.median(t), len(t)
+
+
+def _cpu_legs(mats, alg_bytes, what):
+    """NexusLLM's own GEMV over `mats` [(dtype, W, x, y, rows, cols)] on 1 host
+    thread and on all host threads: {"1t": ..., "all": ...} with GB/s of
+    alg_bytes per pass and ms per pass."""
+    import oracle
+
+    if oracle.reference_available():
+        lib, kind = oracle.reference(), "reference"
+    else:
+        lib, kind = oracle.port(), "port"
+    out = {"kind": kind}
+    del what
+    for label, threads in (("1t", 1), ("all", cpu_threads())):
+        def one():
+            for dt, W, x, y, n, k in mats:
+                if kind == "reference":
+                    oracle.gemv_threaded(lib, dt, W, x, y, n, k, threads)
+                else:
+                    y[:] = lib.gemv(dt, W, x, n, k)
+        sec, reps = _cpu_time(one)
+        out[label] = {"GBs": round(alg_bytes / sec / 1e9, 3), "ms": round(sec * 1e3, 3), "thr": threads}
+    return out
+
+
+def _gpu_gemv_rate(torch, L, dev, timed, dt, rows, cols, seed, min_bytes=512 << 20):
+    """Batch-1 GEMVs through nexus_gpu_gemv (x quantization + fused GEMV, two
+    launches a call), cycling over enough weight copies (>= min_bytes, far
+    beyond the 126 MB L2) that weights come from HBM; a CUDA graph of two
+    passes.  Returns (us per call, copies)."""
+    from nexusllm_b200 import synth
+    from nexusllm_b200.formats import weight_bytes
+
+    wb = weight_bytes(dt, rows, cols)
+    n = max(1, -(-min_bytes // wb))
+    Ws = [synth.blocks_torch(dt, rows, cols, seed + i, device=dev) for i in range(n)]
+    x = torch.randn(cols, device=dev, generator=torch.Generator(device=dev).manual_seed(cols))
+    y = torch.empty(rows, device=dev)
+    calls = 2 * n
+
+    def run():
+        st = torch.cuda.current_stream(dev).cuda_stream
+        for i in range(calls):
+            rc = L.nexus_gpu_gemv(Ws[i % n].data_ptr(), dt, x.data_ptr(), 0, y.data_ptr(), 1, rows, cols, st)
+            if rc:
+                raise RuntimeError(L.nexus_gpu_last_error())
+
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        run()
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        run()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g.replay()
+    reps = 5
+    ms = timed(g.replay, reps) / (reps * calls)
+    del g, Ws
+    return ms * 1e3, n
+
+
+def make_stack(torch, L, layers, head, m, dt, dev):
+    """An unsharded stack of the decode step's GEMVs (same task order and
+    dependencies as the headline; head may be None)."""
+    import ctypes
+
+    from nexusllm_b200 import _native
+
+    tasks, ys = [], []
+    inputs_of = {"q": -1, "k": -1, "v": -1, "o": 0, "gate": 3, "up": 3, "down": 4}
+    last_down = -1
+    for mats in layers:
+        base = len(tasks)
+        for name, n, k in shapes_of(m):
+            y = torch.empty(n, dtype=torch.float32, device=dev)
+            src = inputs_of[name]
+            tasks.append(_native.StackTask(mats[name].data_ptr(), n, k, y.data_ptr(),
+                                           src if src < 0 else base + src, last_down if src < 0 else -1))
+            ys.append(y)
+        last_down = base + 6
+    if head is not None:
+        y = torch.empty(m["vocab"], dtype=torch.float32, device=dev)
+        tasks.append(_native.StackTask(head.data_ptr(), m["vocab"], m["hidden"], y.data_ptr(), -1, last_down))
+        ys.append(y)
+    arr = (_native.StackTask * len(tasks))(*tasks)
+    h = ctypes.c_void_p()
+    _native.check(L.nexus_gpu_stack_create(dt, arr, len(tasks), m["hidden"], ctypes.byref(h)))
+    return h, ys
+
+
+def _time_stack(torch, L, h, x, dev, timed, reps):
+    from nexusllm_b200 import _native
+
+    stream = torch.cuda.Stream(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        _native.check(L.nexus_gpu_stack_run(h, x.data_ptr(), stream.cuda_stream))
+        torch.cuda.synchronize(dev)
+        with torch.cuda.graph(g, stream=stream):
+            _native.check(L.nexus_gpu_stack_run(h, x.data_ptr(), stream.cuda_stream))
+        for _ in range(3):
+            g.replay()
+    ms = timed(g.replay, reps) / reps
+    check_status(L)
+    del g
+    return ms
+
+
+def config0(torch, L, dev, timed, peak):
+    """GGUF Q4_0 GEMV, N = K = 4096, batch 1."""
+    import numpy as np
+
+    from nexusllm_b200 import synth
+
+    N = K = 4096
+    alg = q4_bytes(N, K) + 4 * K + 4 * N
+    us, copies = _gpu_gemv_rate(torch, L, dev, timed, DTYPE, N, K, 10_000, min_bytes=600 << 20)
+    gbs = alg / (us * 1e-6) / 1e9
+    # the same GEMVs as independent tasks of one stack launch (one x, no dependencies)
+    import ctypes
+
+    from nexusllm_b200 import _native
+
+    n = 64
+    Ws = [synth.blocks_torch(DTYPE, N, K, 10_000 + i, device=dev) for i in range(n)]
+    ys = [torch.empty(N, device=dev) for _ in range(n)]
+    arr = (_native.StackTask * n)(*[_native.StackTask(W.data_ptr(), N, K, y.data_ptr(), -1, -1)
+                                    for W, y in zip(Ws, ys)])
+    h = ctypes.c_void_p()
+    _native.check(L.nexus_gpu_stack_create(DTYPE, arr, n, K, ctypes.byref(h)))
+    x = torch.randn(K, device=dev, generator=torch.Generator(device=dev).manual_seed(K))
+    ms = _time_stack(torch, L, h, x, dev, timed, 20)
+    L.nexus_gpu_stack_destroy(h)
+    del Ws, ys
+    sus = ms * 1e3 / n
+    sgbs = alg / (sus * 1e-6) / 1e9
+    W0 = synth.blocks_numpy(DTYPE, N, K, 10_000)
+    xh = synth.activations_numpy(1, K, 10_001)[0]
+    mats = [(DTYPE, np.copy(W0), xh, np.zeros(N, np.float32), N, K) for _ in range(64)]
+    cpu = _cpu_legs(mats, alg * 64, "64 distinct copies of the 4096x4096 matrix (604 MB) per pass")
+    for leg in ("1t", "all"):
+        cpu[leg]["ms"] = round(cpu[leg]["ms"] / 64, 4)  # per call
+    del copies
+    return {"bytes": alg, "gpu": {"us": round(us, 2), "GBs": round(gbs, 1), "frac": round(gbs / peak, 4),
+                                  "calls_s": round(1e6 / us)},
+            "gpu_stack64": {"us": round(sus, 2), "GBs": round(sgbs, 1), "frac": round(sgbs / peak, 4)},
+            "cpu": cpu}
+
+
+def config1(torch, L, dev, timed, peak):
+    """GGUF Q8_0, the Llama-2-7B decode shape set at batch 1: per
+    shape, the set (q/k/v/o 4096^2, gate/up 11008x4096, down 4096x11008), and
+    the 32-layer stack of those shapes in one launch."""
+    import numpy as np
+
+    from nexusllm_b200 import synth
+    from nexusllm_b200.formats import weight_bytes
+
+    dt = 9
+    m = {"name": "7b", "hidden": 4096, "kv": 4096, "ffn": 11008, "vocab": 32000, "layers": 32}
+    per = {}
+    for rows, cols in ((4096, 4096), (11008, 4096), (4096, 11008)):
+        us, copies = _gpu_gemv_rate(torch, L, dev, timed, dt, rows, cols, 20_000 + rows + cols)
+        alg = weight_bytes(dt, rows, cols) + 4 * rows + 4 * cols
+        gbs = alg / (us * 1e-6) / 1e9
+        per[f"{rows}x{cols}"] = {"us": round(us, 2), "GBs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+    set_bytes = sum(weight_bytes(dt, n, k) + 4 * n + 4 * k for _, n, k in shapes_of(m))
+    set_us = sum(per[f"{n}x{k}"]["us"] for _, n, k in shapes_of(m))
+    layers, _ = gen_model(torch, m, 0, 1, dev, 21_000, dt=dt)
+    h, _ys = make_stack(torch, L, layers, None, m, dt, dev)
+    x = torch.randn(m["hidden"], device=dev, generator=torch.Generator(device=dev).manual_seed(7))
+    ms = _time_stack(torch, L, h, x, dev, timed, 50)
+    L.nexus_gpu_stack_destroy(h)
+    del layers
+    sb = set_bytes * m["layers"]
+    sgbs = sb / (ms * 1e-3) / 1e9
+    base = [synth.blocks_numpy(dt, n, k, 22_000 + i) for i, (_, n, k) in enumerate(shapes_of(m))]
+    xs = {k: synth.activations_numpy(1, k, 22_100 + k)[0] for k in (4096, 11008)}
+    mats = [(dt, np.copy(W), xs[k], np.zeros(n, np.float32), n, k)
+            for _ in range(3) for W, (_, n, k) in zip(base, shapes_of(m))]
+    cpu = _cpu_legs(mats, set_bytes * 3, "3 distinct copies of the 7-GEMV set (645 MB) per pass")
+    for leg in ("1t", "all"):
+        cpu[leg]["ms"] = round(cpu[leg]["ms"] / 3, 3)  # per 7-GEMV set
+    return {"per_shape": per,
+            "set": {"us": round(set_us, 2), "GBs": round(set_bytes / (set_us * 1e-6) / 1e9, 1),
+                    "frac": round(set_bytes / (set_us * 1e-6) / 1e9 / peak, 4)},
+            "stack32": {"ms": round(ms, 4), "GBs": round(sgbs, 1), "frac": round(sgbs / peak, 4)},
+            "cpu": cpu}
+
+
+def config2(torch, L, dev, timed, peak):
+    """GGUF Q5_K and Q6_K over a full 32-layer Llama-2-7B weight
+    stack (hidden 4096, FFN 11008; the Q6_K down rows at K = 11008 are 9030 B,
+    not 16-byte multiples), batch 1, one stack launch per token."""
+    import numpy as np
+
+    from nexusllm_b200 import synth
+    from nexusllm_b200.formats import weight_bytes
+
+    m = {"name": "7b", "hidden": 4096, "kv": 4096, "ffn": 11008, "vocab": 32000, "layers": 32}
+    out = {}
+    for dt, name in ((11, "q5_k"), (12, "q6_k")):
+        layers, _ = gen_model(torch, m, 0, 1, dev, 30_000 + 1000 * dt, dt=dt)
+        h, _ys = make_stack(torch, L, layers, None, m, dt, dev)
+        x = torch.randn(m["hidden"], device=dev, generator=torch.Generator(device=dev).manual_seed(dt))
+        ms = _time_stack(torch, L, h, x, dev, timed, 50)
+        L.nexus_gpu_stack_destroy(h)
+        del layers
+        layer_bytes = sum(weight_bytes(dt, n, k) + 4 * n + 4 * k for _, n, k in shapes_of(m))
+        sb = layer_bytes * m["layers"]
+        gbs = sb / (ms * 1e-3) / 1e9
+        base = [synth.blocks_numpy(dt, n, k, 31_000 + i) for i, (_, n, k) in enumerate(shapes_of(m))]
+        xs = {k: synth.activations_numpy(1, k, 31_100 + k)[0] for k in (4096, 11008)}
+        mats = [(dt, np.copy(W), xs[k], np.zeros(n, np.float32), n, k)
+                for _ in range(3) for W, (_, n, k) in zip(base, shapes_of(m))]
+        cpu = _cpu_legs(mats, layer_bytes * 3, "3 distinct copies of one layer's 7 GEMVs per pass; ms_per_token = "
+                                               "32 x ms_per_layer")
+        for leg in ("1t", "all"):
+            cpu[leg]["ms"] = round(32 * cpu[leg]["ms"] / 3, 2)  # per token: 32 x one layer
+        out[name] = {"gpu": {"ms": round(ms, 4), "GBs": round(gbs, 1), "frac": round(gbs / peak, 4)}, "cpu": cpu}
+    return out
+
+
+def oracle_rows_check(torch, W_slice, row_bytes, xin, got, rows_local, n_sample=16):
+    """Sampled rows of this rank's slice of a GEMV against the C oracle (the
+    checker, pinned to the reference build): rows spread over the slice, the
+    task's own input xin (fp32, as the stack consumed it).  Returns the
+    L2-relative error over the sampled rows."""
+    import numpy as np
+
+    import oracle
+
+    port = oracle.port()
+    idx = np.unique(np.linspace(0, rows_local - 1, n_sample).astype(np.int64))
+    wb = W_slice.view(-1)
+    Wh = np.concatenate([wb[int(r) * row_bytes:(int(r) + 1) * row_bytes].cpu().numpy() for r in idx])
+    want = port.gemv(DTYPE, Wh, xin.cpu().numpy().astype(np.float32), len(idx), xin.numel())
+    return oracle.l2_rel(got[torch.as_tensor(idx, device=got.device)].cpu().numpy(), want)
+
+
+def stack_input(torch, y):
+    """A task's output as a dependent task of the stack consumes it (the lowest
+    mantissa bit, which carries the run's parity, cleared)."""
+    return (y.view(torch.int32) & ~1).view(torch.float32)
+
+
+def model_70b(torch, L, world, rank, local, dev, timed, peak, args, pg):
+    """Llama-3-70B Q4_0 (hidden 8192, GQA k/v 1024 x 8192,
+    FFN 28672, 80 layers, LM head 128256 x 8192; 39.1 GB per token), row-sharded
+    over this run's N GPUs, the same model at every N (seeded by global row).
+      m1:  batch 1 -- ONE (sharded) GEMV-stack launch per token; at N > 1 every
+           output row goes to every rank by peer stores inside the kernel.
+      m16: batch 16 -- 561 GEMVs with 16 activation rows each on the tcgen05
+           tensor cores, each rank its row slice, the output slices all-gathered
+           with NCCL (N > 1) and re-laid out for the next GEMV; CUDA graph.
+      parity: sampled rows of every rank's slice of four tasks against the C
+           oracle, each with the input the stack gave it (max over ranks)."""
+    import ctypes
+
+    import torch.distributed as dist
+
+    from nexusllm_b200 import _native
+    from nexusllm_b200.formats import weight_bytes
+
+    m = model_dims("70b")
+    layers, head = gen_model(torch, m, rank, world, dev, 7000)
+    h0 = torch.randn(m["hidden"], generator=torch.Generator(device=dev).manual_seed(70), device=dev)
+    sb = model_bytes(m)
+    tasks = []
+    inputs_of = {"q": -1, "k": -1, "v": -1, "o": 0, "gate": 3, "up": 3, "down": 4}
+    last_down = -1
+    names = []
+    for mats in layers:
+        base = len(tasks)
+        for name, n, k in shapes_of(m):
+            src = inputs_of[name]
+            tasks.append((mats[name], n, k, src if src < 0 else base + src, last_down if src < 0 else -1))
+            names.append(name)
+        last_down = base + 6
+    tasks.append((head, m["vocab"], m["hidden"], -1, last_down))
+    names.append("head")
+    # ---- m1: the stack
+    if world == 1:
+        h, outs = make_stack(torch, L, layers, head, m, DTYPE, dev)
+        st_obj = None
+    else:
+        from nexusllm_b200.sharded import ShardedStack
+
+        st_obj = ShardedStack(DTYPE, [(W.data_ptr(), n, k, src, after) for W, n, k, src, after in tasks],
+                              m["hidden"], world, rank)
+        h = st_obj.handle
+        outs = [torch.as_tensor(_DeviceVec(st_obj.output(i), n), device=dev) for i, (_, n, *_r) in enumerate(tasks)]
+    stream = torch.cuda.Stream(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        _native.check(L.nexus_gpu_stack_run(h, h0.data_ptr(), stream.cuda_stream))
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        with torch.cuda.graph(g, stream=stream):
+            _native.check(L.nexus_gpu_stack_run(h, h0.data_ptr(), stream.cuda_stream))
+        for _ in range(max(3, args.warmup)):
+            g.replay()
+    reps = max(5, min(args.steps, 50))
+    ms1 = timed(g.replay, reps) / reps
+    check_status(L)
+    # parity of sampled rows (this rank's slice), each task with its own input as the stack consumed it
+    rb = weight_bytes(DTYPE, 1, m["hidden"])
+    errs = []
+    for i in (0, 3, len(tasks) - 2, len(tasks) - 1):  # q and o of layer 0, the last down, the LM head
+        W, n, k, src, _ = tasks[i]
+        r0 = n * rank // world
+        xin = h0 if src < 0 else stack_input(torch, outs[src])
+        nl = n // world
+        errs.append(oracle_rows_check(torch, W, weight_bytes(DTYPE, 1, k), xin, outs[i][r0:r0 + nl], nl))
+    err = torch.tensor([max(errs)], device=dev)
+    if world > 1:
+        dist.all_reduce(err, op=dist.ReduceOp.MAX)
+    err = float(err.item())
+    del g
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    if st_obj is not None:
+        st_obj.close()
+    else:
+        L.nexus_gpu_stack_destroy(h)
+    gbs1 = sb / (ms1 * 1e-3) / 1e9
+    out = {"n_gpus": world,
+           "m1": {"ms": round(ms1, 4), "tok_s": round(1e3 / ms1, 2), "agg_GBs": round(gbs1, 1),
+                  "frac_per_gpu": round(gbs1 / world / peak, 4)},
+           "parity": {"max_l2_rel": float(f"{err:.3e}"), "pass": err <= 1e-3}}
+    # ---- m16: batched, per-GEMV tensor-core launches (+ NCCL all-gathers)
+    M = 16
+    ws_need = max([L.nexus_gpu_gemv_workspace_size(DTYPE, M, n // world, k) for _, n, k in shapes_of(m)] +
+                  [L.nexus_gpu_gemv_workspace_size(DTYPE, M, m["vocab"] // world, m["hidden"])])
+    ws = torch.empty(ws_need + 256, dtype=torch.uint8, device=dev)
+    X0 = torch.randn(M, m["hidden"], device=dev, generator=torch.Generator(device=dev).manual_seed(16))
+    rows_of = {"q": m["hidden"], "k": m["kv"], "v": m["kv"], "o": m["hidden"], "gate": m["ffn"], "up": m["ffn"],
+               "down": m["hidden"], "head": m["vocab"]}
+    part = {key: torch.empty(M, n // world, device=dev) for key, n in rows_of.items()}
+    gath = {key: torch.empty(world, M, n // world, device=dev) for key, n in rows_of.items()} if world > 1 else None
+    full = {key: torch.empty(M, n, device=dev) for key, n in rows_of.items()} if world > 1 else part
+
+    def gemv16(W, n, k, X, key):
+        st = torch.cuda.current_stream(dev).cuda_stream
+        rc = L.nexus_gpu_gemv_ws(W.data_ptr(), DTYPE, X.data_ptr(), 0, part[key].data_ptr(), M, n // world, k,
+                                 ws.data_ptr(), ws.numel(), st)
+        if rc:
+            raise RuntimeError(L.nexus_gpu_last_error())
+        if world > 1:  # every rank's [M, n/world] slice -> the full [M, n] rows of the next GEMV's x
+            dist.all_gather_into_tensor(gath[key], part[key], group=pg)
+            full[key].copy_(gath[key].permute(1, 0, 2).reshape(M, n))
+        return full[key]
+
+    def step16():
+        for mats in layers:
+            q = gemv16(mats["q"], m["hidden"], m["hidden"], X0, "q")
+            gemv16(mats["k"], m["kv"], m["hidden"], X0, "k")
+            gemv16(mats["v"], m["kv"], m["hidden"], X0, "v")
+            o = gemv16(mats["o"], m["hidden"], m["hidden"], q, "o")
+            gt = gemv16(mats["gate"], m["ffn"], m["hidden"], o, "gate")
+            gemv16(mats["up"], m["ffn"], m["hidden"], o, "up")
+            gemv16(mats["down"], m["hidden"], m["ffn"], gt, "down")
+        gemv16(head, m["vocab"], m["hidden"], X0, "head")
+
+    with torch.cuda.stream(stream):
+        step16()
+    torch.cuda.synchronize(dev)
+    g16 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g16, stream=stream):
+        step16()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g16.replay()
+    reps16 = max(3, min(args.steps, 20))
+    ms16 = timed(g16.replay, reps16) / reps16
+    del g16
+    gbs16 = (sum(weight_bytes(DTYPE, n, k) for _, n, k in shapes_of(m)) * m["layers"] +
+             weight_bytes(DTYPE, m["vocab"], m["hidden"])) / (ms16 * 1e-3) / 1e9
+    out["m16"] = {"ms": round(ms16, 4), "tok_s": round(M * 1e3 / ms16, 1), "agg_weight_GBs": round(gbs16, 1)}
+    del layers, head, ws, full, part, gath
+    torch.cuda.empty_cache()
+    return out
 
 
 if __name__ == "__main__":
