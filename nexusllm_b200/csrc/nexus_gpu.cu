@@ -1177,7 +1177,6 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
         T.norm_eps = tasks[i].norm_eps;
         T.res_input = tasks[i].residual_source == -1;
         T.res_src = tasks[i].residual_source >= 0 ? tasks[i].residual_source : -1;
-        T.res_rows = (int)tasks[i].rows;
         // same input (and fusions), same plan (same cols), and no new ordering
         // dependency: keep the previous task's x slices, skip the wait and the staging
         T.reuse_x = i > 0 && tasks[i].x_source == tasks[i - 1].x_source && tasks[i].cols == tasks[i - 1].cols &&

@@ -73,7 +73,6 @@ struct StackTask {
     float norm_eps;
     int res_input;                       // the residual is the stack input
     int res_src;                         // the residual is task res_src's output (tagged copy), or -1
-    int res_rows;                        // rows of the residual (this task's full row count)
     const uint8_t* W2;                   // gate+up pair: the up matrix (rows as W's), or null
     int half;                            // pair: byte offset of W2's rows in a ring slot
 };
@@ -392,14 +391,34 @@ __device__ __forceinline__ uint64_t ep_residual(const float4 e) {
 }
 
 // Row r's residual, loaded when the row starts so that the L2 latency
-// overlaps its dot product.  A task's residual rows were all seen with this
-// run's tag at the group head, so the same words read now hold this run's
-// values (coherence of each word).
-__device__ __forceinline__ float residual_of(const volatile float4* ep, int r, bool sys) {
+// overlaps its dot product.  A task's residual word is read until it carries
+// this run's parity (a residual's task finished before this task's own input
+// in a decode layer, so the first read almost always does); bounded like every
+// wait, the expiry raising the abort flag and the status bit.
+__device__ __forceinline__ uint32_t residual_wait(const uint32_t* p, uint32_t par, bool sys, unsigned* abort_flag,
+                                                  uint32_t polls) {
+    uint32_t w = ld_tagged1(p, sys);
+    for (uint32_t k = 0; ((w ^ par) & 1u) != 0; ++k) {
+        __nanosleep(kTagPollNs / 2);
+        w = ld_tagged1(p, sys);
+        if ((k & 7u) == 7u && *reinterpret_cast<volatile unsigned*>(abort_flag)) break;
+        if (k >= polls) {
+            tag_wait_expired(abort_flag);
+            break;
+        }
+    }
+    return w;
+}
+__device__ __forceinline__ float residual_of(const volatile float4* ep, int r, bool sys, uint32_t par,
+                                             const StackParams& P) {
     const uint64_t a = ep_residual(ld_ep(ep));
     if (!a) return 0.0f;
-    if (a & 1u)
-        return untag(ld_tagged1(reinterpret_cast<const uint32_t*>(a - 1) + r, sys));
+    if (a & 1u) {
+        const uint32_t* p = reinterpret_cast<const uint32_t*>(a - 1) + r;
+        uint32_t w = ld_tagged1(p, sys);
+        if (((w ^ par) & 1u) != 0) w = residual_wait(p, par, sys, P.abort_flag, P.wait_polls);
+        return untag(w);
+    }
     return __ldcg(reinterpret_cast<const float*>(a) + r);
 }
 
@@ -635,19 +654,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
         const StackTask& H = P.tasks[t];
         const int K = __ldg(&H.K), S = __ldg(&H.segments);
         const int NW = __ldg(&H.nwi), SW = __ldg(&H.seg_wi), J = __ldg(&H.wi_per_lane);
-        // ordering dependencies: every row of `after` (and of the residual's task)
-        // stored in this run; each thread checks its share of the rows
+        // ordering dependency: every row of `after` stored in this run; each
+        // thread checks its share of the rows (a residual's rows are checked as
+        // they are read, residual_of)
         bool ok = *reinterpret_cast<volatile unsigned*>(P.abort_flag) == 0;  // poisoned by an earlier run
         const int src = __ldg(&H.src), after = __ldg(&H.after);
         if (ok && after >= 0)
             ok = wait_rows_tagged(ld_task_ptr(&P.tasks[after].tg), __ldg(&H.after_rows), par, sys, tid, P.abort_flag,
                                   P.wait_polls);
-        if constexpr (FX) {
-            const int rs = __ldg(&H.res_src);
-            if (ok && rs >= 0)
-                ok = wait_rows_tagged(ld_task_ptr(&P.tasks[rs].tg), __ldg(&H.res_rows), par, sys, tid, P.abort_flag,
-                                      P.wait_polls);
-        }
         consumer_bar();  // every warp is done with the previous group's x staging
         const float4* nw =
             FX ? reinterpret_cast<const float4*>(__ldg(reinterpret_cast<const unsigned long long*>(&H.norm_w))) : nullptr;
@@ -731,7 +745,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                     for (; rl < nr; rl += n_grp) {
                         const uint32_t row = base + (uint32_t)(rl * rbytes);
                         float rv = 0.0f;
-                        if (FX && lane == 0) rv = residual_of(s_ep + warp, r0 + rl, sys);
+                        if (FX && lane == 0) rv = residual_of(s_ep + warp, r0 + rl, sys, par, P);
                         float acc = row_partial<F, G>(row, wi, has, X);
 #pragma unroll
                         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -767,7 +781,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                             for (int k = 0; k < S; ++k) v += sl[k];
                             if (FX && half)
                                 for (int k = 0; k < S; ++k) u += sl[S + k];
-                            const float rv = FX ? residual_of(s_ep + warp, r0 + rl, sys) : 0.0f;
+                            const float rv = FX ? residual_of(s_ep + warp, r0 + rl, sys, par, P) : 0.0f;
                             put_row<FX>(P, yl, yo, to, par, r0 + rl, v, s_ep + warp, rv, u);
                         }
                     }
