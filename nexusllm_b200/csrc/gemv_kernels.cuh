@@ -62,6 +62,9 @@ constexpr int kMaxSlots = 1024;      // n_stages * stage_rows * segments partial
 constexpr int kBarBytes = 256;       // 2 x kMaxStages mbarriers
 constexpr int kSmemHeader = kBarBytes + kMaxSlots * 4 + kMaxStages * kMaxStageRows * 4;  // + slots + counters
 constexpr int kStageTargetBytes = 32768;
+// A stack's stages hold two rows per warp where they fit (its consumer warps
+// work on two rows at once, sharing the x slices and one reduction).
+constexpr int kStackStageTargetBytes = 73728;
 constexpr int kStageMaxBytes = 73728;
 
 struct GemvParams {

@@ -223,7 +223,8 @@ int32_t launch(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st,
 // Fast-path geometry for a weight format and shape (see gemv_kernels.cuh).
 // Returns false when the shape is outside the fast kernel's limits.
 template <class F>
-bool plan_fast(const Device& d, int N, int K, uint64_t row_bytes, GemvParams& p, size_t& smem) {
+bool plan_fast(const Device& d, int N, int K, uint64_t row_bytes, GemvParams& p, size_t& smem,
+               uint64_t stage_target = kStageTargetBytes) {
     const int NW = K / F::kWIElems;
     if (NW < 32) return false;
     // K segments S (1..15): S warps share a row, n_grp = 15/S row groups work
@@ -254,7 +255,7 @@ bool plan_fast(const Device& d, int N, int K, uint64_t row_bytes, GemvParams& p,
     p.group = Gp;
     const int n_grp = kConsumerWarps / S;
     const uint64_t grp_bytes = (uint64_t)n_grp * row_bytes;
-    const int m = (int)std::max<uint64_t>(1, std::min<uint64_t>(4, kStageTargetBytes / grp_bytes));
+    const int m = (int)std::max<uint64_t>(1, std::min<uint64_t>(4, stage_target / grp_bytes));
     const int R = std::min(n_grp * m, kMaxStageRows);
     const uint64_t sb = (R * row_bytes + 32 + 15) / 16 * 16;
     const uint64_t avail = (uint64_t)d.smem_optin - kSmemHeader - 128;
@@ -281,13 +282,14 @@ int32_t launch_fast(Device& d, const GemvParams& p, size_t smem, cudaStream_t st
     return launch(gemv_m1_kernel<F, 1>, dim3(grid), dim3(kGemvThreads), smem, st, p);
 }
 
-bool plan_for(uint32_t dtype, const Device& d, int N, int K, uint64_t rb, GemvParams& p, size_t& smem) {
+bool plan_for(uint32_t dtype, const Device& d, int N, int K, uint64_t rb, GemvParams& p, size_t& smem,
+              uint64_t stage_target = kStageTargetBytes) {
     switch (dtype) {
-        case NEXUS_GPU_GGUF_Q4_0: return plan_fast<FmtQ4_0>(d, N, K, rb, p, smem);
-        case NEXUS_GPU_GGUF_Q8_0: return plan_fast<FmtQ8_0>(d, N, K, rb, p, smem);
-        case NEXUS_GPU_GGUF_Q5_K: return plan_fast<FmtQ5_K>(d, N, K, rb, p, smem);
-        case NEXUS_GPU_GGUF_Q6_K: return plan_fast<FmtQ6_K>(d, N, K, rb, p, smem);
-        default: return (K % 16 == 0) && plan_fast<FmtF16>(d, N, K, rb, p, smem);
+        case NEXUS_GPU_GGUF_Q4_0: return plan_fast<FmtQ4_0>(d, N, K, rb, p, smem, stage_target);
+        case NEXUS_GPU_GGUF_Q8_0: return plan_fast<FmtQ8_0>(d, N, K, rb, p, smem, stage_target);
+        case NEXUS_GPU_GGUF_Q5_K: return plan_fast<FmtQ5_K>(d, N, K, rb, p, smem, stage_target);
+        case NEXUS_GPU_GGUF_Q6_K: return plan_fast<FmtQ6_K>(d, N, K, rb, p, smem, stage_target);
+        default: return (K % 16 == 0) && plan_fast<FmtF16>(d, N, K, rb, p, smem, stage_target);
     }
 }
 
@@ -1058,7 +1060,7 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
         size_t sm = 0;
         const uint64_t rb = row_bytes_of(f, u.cols);
         // a gate+up pair plans with its two rows as one (twice the bytes per ring row)
-        if (!plan_for(dtype, *d, (int)local_rows[i], (int)u.cols, u.W_up ? 2 * rb : rb, gp, sm))
+        if (!plan_for(dtype, *d, (int)local_rows[i], (int)u.cols, u.W_up ? 2 * rb : rb, gp, sm, kStackStageTargetBytes))
             return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "task %u (%llux%llu) is outside the fast kernel's limits", i,
                         (unsigned long long)local_rows[i], (unsigned long long)u.cols);
         if (group < 0) group = gp.group;

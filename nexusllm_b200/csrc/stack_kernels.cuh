@@ -14,14 +14,15 @@
 //    per-row arithmetic, so results are bit-identical to nexus_gpu_gemv).
 //    Rows are balanced over the CTAs.
 //  * A task's x is either the stack input or the y of an earlier task.  A task
-//    that a later task reads or waits for also stores each output row as an
-//    8-byte word (float bits | run tag << 32) with a single-copy-atomic relaxed
-//    store -- into every rank's copy when sharded.  The tag is the run number
-//    + 1, so a reader that sees the current tag in a word has the current
-//    value in it: the dependent CTA's staging loads are the wait, and no
-//    fence, counter or flag sits between a row's store and its use (at N > 1
-//    this removes the system-scope fences from every data dependency).  An
-//    `after` dependency waits for every row of its task the same way.
+//    that a later task reads or waits for also stores each output row as a
+//    tagged 32-bit word (the float with its lowest mantissa bit replaced by the
+//    run's parity) with a single-copy-atomic relaxed store -- into every
+//    rank's copy when sharded.  A reader that sees this run's parity in a word
+//    has this run's value in it: the dependent CTA's staging loads are the
+//    wait, and no fence, counter or flag sits between a row's store and its
+//    use (at N > 1 this removes the system-scope fences from every data
+//    dependency).  An `after` dependency waits for every row of its task the
+//    same way.
 //  * The consumer warps of a CTA step through the tasks together, one x group
 //    (a task and the following tasks with the same input and plan) at a time:
 //    the CTA reads the group's x once, quantizes it into shared memory itself
@@ -742,6 +743,25 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                     int rl = grp - rot;
                     if (rl < 0) rl += n_grp;
                     if (grp >= n_grp) rl = nr;  // the 15 - S*n_grp warps past the last row group idle
+                    if constexpr (!FX) {
+                        // two rows of the stage at once: two independent dot products on the
+                        // same x slices, and one reduction for both -- lanes 0-15 finish the
+                        // first row, lanes 16-31 the second (each half's sum the same tree as
+                        // the one-row reduction's, up to the order of commutative adds)
+                        for (; rl + n_grp < nr; rl += 2 * n_grp) {
+                            const uint32_t row = base + (uint32_t)(rl * rbytes);
+                            const float a = row_partial<F, G>(row, wi, has, X);
+                            const float b = row_partial<F, G>(row + (uint32_t)(n_grp * rbytes), wi, has, X);
+                            float v = (lane < 16 ? a : b) + __shfl_xor_sync(0xffffffffu, lane < 16 ? b : a, 16);
+#pragma unroll
+                            for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                            const int rme = rl + (lane < 16 ? 0 : n_grp);
+                            if ((lane & 15) == 0) {
+                                if (S == 1) put_row<FX>(P, yl, yo, to, par, r0 + rme, v, s_ep + warp, 0.0f, 0.0f);
+                                else slots[s * P.slot_stride + rme * S + sg] = v;
+                            }
+                        }
+                    }
                     for (; rl < nr; rl += n_grp) {
                         const uint32_t row = base + (uint32_t)(rl * rbytes);
                         float rv = 0.0f;
