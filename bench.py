@@ -739,7 +739,71 @@ def batched_decode(torch, L, layers, head, stream, dev, timed, args, peak, stack
         out["M4_stack"] = {"ms": round(ms, 3), "tok_s": round(M * 1e3 / ms, 1),
                            "path": "GEMV stack once per token"}
         del g
+    for M in (2, 3, 4):
+        out[f"M{M}_tokens_stack"] = tokens_stack(torch, L, layers, head, M, stream, dev, timed, args, peak)
     return out
+
+
+def tokens_stack(torch, L, layers, head, M, stream, dev, timed, args, peak):
+    """configs[3] at M = 2..4 tokens: the headline's task list (same weights,
+    same dependencies) as ONE multi-token stack launch per step
+    (nexus_gpu_stack_create_tokens): every weight read once for all M tokens.
+    Parity: 16 sampled rows of the first q, the first o, the last down and the
+    LM head of the first and the last token against the C oracle, each fed the
+    input the stack gave it."""
+    import ctypes
+
+    from nexusllm_b200 import _native
+    from nexusllm_b200.formats import weight_bytes
+
+    tasks, ys = [], []
+    inputs_of = {"q": -1, "k": -1, "v": -1, "o": 0, "gate": 3, "up": 3, "down": 4}
+    last_down = -1
+    for mats in layers:
+        base = len(tasks)
+        for name, n, k in LAYER_SHAPES:
+            y = torch.empty(M, n, dtype=torch.float32, device=dev)
+            src = inputs_of[name]
+            tasks.append(_native.StackTask(mats[name].data_ptr(), n, k, y.data_ptr(), src if src < 0 else base + src,
+                                           last_down if src < 0 else -1))
+            ys.append(y)
+        last_down = base + 6
+    y = torch.empty(M, VOCAB, dtype=torch.float32, device=dev)
+    tasks.append(_native.StackTask(head.data_ptr(), VOCAB, HIDDEN, y.data_ptr(), -1, last_down))
+    ys.append(y)
+    arr = (_native.StackTask * len(tasks))(*tasks)
+    h = ctypes.c_void_p()
+    _native_check(L.nexus_gpu_stack_create_tokens(DTYPE, arr, len(tasks), HIDDEN, M, ctypes.byref(h)))
+    x = torch.randn(M, HIDDEN, generator=torch.Generator(device=dev).manual_seed(60 + M), device=dev)
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            _native_check(L.nexus_gpu_stack_run(h, x.data_ptr(), stream.cuda_stream))
+            torch.cuda.synchronize(dev)
+            with torch.cuda.graph(g, stream=stream):
+                _native_check(L.nexus_gpu_stack_run(h, x.data_ptr(), stream.cuda_stream))
+            for _ in range(3):
+                g.replay()
+        reps = max(5, min(50, args.steps // 20))
+        ms = timed(g.replay, reps) / reps
+        check_status(L)
+        errs = []
+        per, nl = 7, len(layers)
+        for t in (0, M - 1):
+            for W, n, k, src, i in [(layers[0]["q"], HIDDEN, HIDDEN, None, 0), (layers[0]["o"], HIDDEN, HIDDEN, 0, 3),
+                                    (layers[-1]["down"], HIDDEN, FFN, per * (nl - 1) + 4, per * (nl - 1) + 6),
+                                    (head, VOCAB, HIDDEN, None, len(ys) - 1)]:
+                xin = x[t] if src is None else stack_input(torch, ys[src][t])
+                errs.append(oracle_rows_check(torch, W, weight_bytes(DTYPE, 1, k), xin, ys[i][t], n))
+        del g
+    finally:
+        L.nexus_gpu_stack_destroy(h)
+    sb = step_bytes(layers=len(layers))
+    gbs = sb / (ms * 1e-3) / 1e9
+    e = max(errs)
+    return {"ms": round(ms, 3), "tok_s": round(M * 1e3 / ms, 1), "GBs_weights_once": round(gbs, 1),
+            "frac": round(gbs / peak, 4), "path": "multi-token GEMV stack, one launch per step",
+            "parity_max_l2_rel": float(f"{e:.3e}"), "parity_pass": e <= 1e-3}
 
 
 def gguf_formats(torch, L, stream, dev, timed, peak):

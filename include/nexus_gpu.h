@@ -220,13 +220,29 @@ NEXUS_GPU_API int32_t nexus_gpu_stack_create(uint32_t dtype, const NexusGpuStack
 NEXUS_GPU_API int32_t nexus_gpu_stack_run(void* stack, const float* dX, void* stream);
 NEXUS_GPU_API int32_t nexus_gpu_stack_destroy(void* stack);
 
+/* A stack for `tokens` activation vectors per run (2..4): batched decode of
+ * that many requests below the tensor-core range (M >= 16 takes tcgen05
+ * tiles through nexus_gpu_gemv).  Every weight is read from HBM once per run,
+ * not once per token; the reference decodes the requests one after another
+ * (src/forward_pass.cpp:633-667).  The tasks are those of
+ * nexus_gpu_stack_create; each tasks[i].y holds tokens * rows floats (token t
+ * at y + t * rows, 16-byte aligned), and nexus_gpu_stack_run's dX holds
+ * tokens * input_cols floats (token t at dX + t * input_cols).  Unsharded,
+ * integer GGUF formats.  Each token's outputs are within the GEMV tolerance
+ * of the single-token stack on that token (same arithmetic, another fixed
+ * summation order).  tokens = 1 is nexus_gpu_stack_create.  No counterpart in
+ * the reference. */
+NEXUS_GPU_API int32_t nexus_gpu_stack_create_tokens(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n_tasks,
+                                                    uint64_t input_cols, uint32_t tokens, void** out_stack);
+
 /* Row-sharded GEMV stacks over `world` GPUs (2..8) of one node, one process
  * (or thread) per GPU, each holding the full x.  Row sharding of the
  * reference's GEMVs (src/forward_pass.cpp:504-585) with the all-gather fused
  * into the kernel: rank r computes rows [rows*r/world, rows*(r+1)/world) of
  * every task and writes them straight into every peer's copy of the output
  * over NVLink (peer stores); a task that another task depends on also writes
- * each row as a tagged 8-byte word, which the dependent task's readers check,
+ * each row as a tagged 32-bit word (the run's parity in its lowest mantissa
+ * bit), which the dependent task's readers check,
  * so no fence or counter sits between ranks inside a run.  No counterpart in
  * the reference.
  *   tasks[i].rows = the FULL row count; tasks[i].W = this rank's row slice

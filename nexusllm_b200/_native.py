@@ -52,6 +52,7 @@ SIGNATURES = {
     "nexus_gpu_stack_create": (_I32, [_U32, _VP, _U32, ctypes.c_uint64, ctypes.POINTER(_VP)]),
     "nexus_gpu_stack_run": (_I32, [_VP, _VP, _VP]),
     "nexus_gpu_stack_destroy": (_I32, [_VP]),
+    "nexus_gpu_stack_create_tokens": (_I32, [_U32, _VP, _U32, ctypes.c_uint64, _U32, ctypes.POINTER(_VP)]),
     "nexus_gpu_stack_create_ex": (_I32, [_U32, _VP, _U32, ctypes.c_uint64, _U32, _U32, ctypes.POINTER(_VP)]),
     "nexus_gpu_stack_create_sharded": (_I32, [_U32, _VP, _U32, ctypes.c_uint64, _U32, _U32, ctypes.POINTER(_VP)]),
     "nexus_gpu_stack_export": (_I32, [_VP, _VP, ctypes.POINTER(ctypes.c_uint64)]),

@@ -17,6 +17,7 @@
 #include "../../include/nexus_gpu.h"
 #include "gemv_kernels.cuh"
 #include "stack_kernels.cuh"
+#include "stack_mt_kernels.cuh"
 #include "awq_fp8_kernels.cuh"
 #include "mma_kernels.cuh"
 #include "gguf_file.cuh"
@@ -222,9 +223,12 @@ int32_t launch(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st,
 
 // Fast-path geometry for a weight format and shape (see gemv_kernels.cuh).
 // Returns false when the shape is outside the fast kernel's limits.
+// max_j: the most work items a lane may hold (kMaxJ; 4 / tokens for the
+// multi-token stack, whose lanes hold every token's slices); grouped: whether
+// a lane may take a format's kGroup consecutive items together.
 template <class F>
 bool plan_fast(const Device& d, int N, int K, uint64_t row_bytes, GemvParams& p, size_t& smem,
-               uint64_t stage_target = kStageTargetBytes) {
+               uint64_t stage_target = kStageTargetBytes, int max_j = kMaxJ, bool grouped = true) {
     const int NW = K / F::kWIElems;
     if (NW < 32) return false;
     // K segments S (1..15): S warps share a row, n_grp = 15/S row groups work
@@ -234,14 +238,14 @@ bool plan_fast(const Device& d, int N, int K, uint64_t row_bytes, GemvParams& p,
     // segments, less partial-sum traffic), with J <= kMaxJ and a stage that
     // holds one row per group within kStageMaxBytes.  Segment boundaries fall
     // on whole lane groups.
-    const int Gp = (NW % F::kGroup == 0) ? F::kGroup : 1;
+    const int Gp = (grouped && NW % F::kGroup == 0) ? F::kGroup : 1;
     int S = 0, SW = 0, J = 0;
     double best = 1e30;
     for (int cand = 1; cand <= kMaxSegments; ++cand) {
         const int sw = ((NW + cand - 1) / cand + Gp - 1) / Gp * Gp;
         const int j = (sw + 32 * Gp - 1) / (32 * Gp) * Gp;
         const int groups = kConsumerWarps / cand;
-        if (j > kMaxJ || groups == 0) continue;
+        if (j > max_j || groups == 0) continue;
         if ((uint64_t)groups * row_bytes > (uint64_t)kStageMaxBytes && cand < kMaxSegments) continue;
         const double cost = (double)j / groups;
         if (cost < best - 1e-9) {
@@ -283,12 +287,12 @@ int32_t launch_fast(Device& d, const GemvParams& p, size_t smem, cudaStream_t st
 }
 
 bool plan_for(uint32_t dtype, const Device& d, int N, int K, uint64_t rb, GemvParams& p, size_t& smem,
-              uint64_t stage_target = kStageTargetBytes) {
+              uint64_t stage_target = kStageTargetBytes, int max_j = kMaxJ, bool grouped = true) {
     switch (dtype) {
-        case NEXUS_GPU_GGUF_Q4_0: return plan_fast<FmtQ4_0>(d, N, K, rb, p, smem, stage_target);
-        case NEXUS_GPU_GGUF_Q8_0: return plan_fast<FmtQ8_0>(d, N, K, rb, p, smem, stage_target);
-        case NEXUS_GPU_GGUF_Q5_K: return plan_fast<FmtQ5_K>(d, N, K, rb, p, smem, stage_target);
-        case NEXUS_GPU_GGUF_Q6_K: return plan_fast<FmtQ6_K>(d, N, K, rb, p, smem, stage_target);
+        case NEXUS_GPU_GGUF_Q4_0: return plan_fast<FmtQ4_0>(d, N, K, rb, p, smem, stage_target, max_j, grouped);
+        case NEXUS_GPU_GGUF_Q8_0: return plan_fast<FmtQ8_0>(d, N, K, rb, p, smem, stage_target, max_j, grouped);
+        case NEXUS_GPU_GGUF_Q5_K: return plan_fast<FmtQ5_K>(d, N, K, rb, p, smem, stage_target, max_j, grouped);
+        case NEXUS_GPU_GGUF_Q6_K: return plan_fast<FmtQ6_K>(d, N, K, rb, p, smem, stage_target, max_j, grouped);
         default: return (K % 16 == 0) && plan_fast<FmtF16>(d, N, K, rb, p, smem, stage_target);
     }
 }
@@ -885,6 +889,7 @@ struct StackHandle {
     int world = 1, rank = 0;
     bool connected = true;  // sharded stacks need nexus_gpu_stack_connect first
     bool fused = false;     // some task has a norm, a SwiGLU or a residual: the kernel variant with them
+    int tokens = 1;         // activation vectors per run (2..4: the multi-token kernel)
     uint64_t fingerprint = 0;
     StackParams params{};
     StackTask* d_tasks = nullptr;
@@ -912,8 +917,21 @@ int32_t stack_kernel_attrs(const Device& d, size_t smem) {
     return NEXUS_GPU_SUCCESS;
 }
 
+template <class F, int MT>
+int32_t stack_mt_kernel_attrs(const Device& d, size_t smem) {
+    CUDA_TRY(cudaFuncSetAttribute(gemv_stack_mt_kernel<F, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  d.smem_optin));
+    int per_sm = 0;
+    CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_stack_mt_kernel<F, MT>, kGemvThreads, smem));
+    if (per_sm < 1) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "stack kernel cannot be resident (smem %zu)", smem);
+    return NEXUS_GPU_SUCCESS;
+}
+
 template <class F>
-int32_t stack_attrs_for(int group, bool fused, const Device& d, size_t smem) {
+int32_t stack_attrs_for(int group, bool fused, int tokens, const Device& d, size_t smem) {
+    if (tokens == 2) return stack_mt_kernel_attrs<F, 2>(d, smem);
+    if (tokens == 3) return stack_mt_kernel_attrs<F, 3>(d, smem);
+    if (tokens == 4) return stack_mt_kernel_attrs<F, 4>(d, smem);
     const bool grouped = F::kGroup > 1 && group == F::kGroup;
     if (fused) return grouped ? stack_kernel_attrs<F, F::kGroup, true>(d, smem) : stack_kernel_attrs<F, 1, true>(d, smem);
     return grouped ? stack_kernel_attrs<F, F::kGroup, false>(d, smem) : stack_kernel_attrs<F, 1, false>(d, smem);
@@ -931,6 +949,12 @@ int32_t stack_launch_for(const StackHandle& h, cudaStream_t st) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    if (h.tokens > 1) {
+        if (h.tokens == 2) CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stack_mt_kernel<F, 2>, h.params));
+        else if (h.tokens == 3) CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stack_mt_kernel<F, 3>, h.params));
+        else CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stack_mt_kernel<F, 4>, h.params));
+        return NEXUS_GPU_SUCCESS;
+    }
     const bool grouped = F::kGroup > 1 && h.group == F::kGroup;
     if (h.fused) {
         if (grouped) CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stack_kernel<F, F::kGroup, true>, h.params));
@@ -991,12 +1015,16 @@ uint64_t stack_fingerprint(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uin
 }
 
 int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t n, uint64_t input_cols, int world,
-                     int rank, void** out) {
+                     int rank, void** out, int tokens = 1) {
     if (!out || (!tasks && n)) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null argument");
     *out = nullptr;
     if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world)
         return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "rank %d of world %d (1..%d GPUs)", rank, world, kMaxWorld);
     const bool sharded = world > 1;
+    if (tokens < 1 || tokens > kMaxStackTokens)
+        return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "%d tokens per run (1..%d)", tokens, kMaxStackTokens);
+    if (tokens > 1 && sharded)
+        return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "a multi-token stack is not sharded");
     if (dtype == NEXUS_GPU_FP16)
         return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "GEMV stacks serve the integer GGUF formats");
     FormatInfo f;
@@ -1023,6 +1051,8 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
                         sharded ? "task %u: y must be NULL in a sharded stack (outputs belong to the stack)"
                                 : "task %u: null y", i);
         if (((uintptr_t)u.W & 15) != 0) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u: W not 16-byte aligned", i);
+        if (tokens > 1 && (u.x_source2 != -1 || u.residual_source != -2 || u.norm_weight || u.W_up))
+            return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u: a multi-token stack has no fused operations", i);
         const uint64_t xlen = u.x_source < 0 ? input_cols : (u.x_source < (int32_t)i ? tasks[u.x_source].rows : 0);
         if (u.x_source >= (int32_t)i || xlen != u.cols)
             return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "task %u: x_source %d does not give a vector of %llu", i,
@@ -1060,7 +1090,13 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
         size_t sm = 0;
         const uint64_t rb = row_bytes_of(f, u.cols);
         // a gate+up pair plans with its two rows as one (twice the bytes per ring row)
-        if (!plan_for(dtype, *d, (int)local_rows[i], (int)u.cols, u.W_up ? 2 * rb : rb, gp, sm, kStackStageTargetBytes))
+        // multi-token stacks: one (two for 2 tokens) single-block work items per lane, smaller stages
+        const bool ok_plan = tokens > 1
+                                 ? plan_for(dtype, *d, (int)local_rows[i], (int)u.cols, rb, gp, sm, kStageTargetBytes,
+                                            kMaxJ / (tokens == 2 ? 2 : 4), false)
+                                 : plan_for(dtype, *d, (int)local_rows[i], (int)u.cols, u.W_up ? 2 * rb : rb, gp, sm,
+                                            kStackStageTargetBytes);
+        if (!ok_plan)
             return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "task %u (%llux%llu) is outside the fast kernel's limits", i,
                         (unsigned long long)local_rows[i], (unsigned long long)u.cols);
         if (group < 0) group = gp.group;
@@ -1088,7 +1124,8 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
         slot = std::max(slot, (size_t)T.stage_bytes);
     }
     size_t x_smem = 0;
-    for (const StackTask& T : ht) x_smem = std::max(x_smem, (size_t)x_stage_planes_len(T.K) * (kXQLimbBytes + kXQMetaBytes));
+    for (const StackTask& T : ht)
+        x_smem = std::max(x_smem, (size_t)tokens * x_stage_planes_len(T.K) * (kXQLimbBytes + kXQMetaBytes));
     x_smem = (x_smem + 127) / 128 * 128;
     if ((uint64_t)d->smem_optin < kStackSmemHeader + x_smem + 128 + 2 * slot)
         return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "stack stages do not fit shared memory");
@@ -1096,7 +1133,7 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
     int ns = (int)std::min<uint64_t>(kMaxStages, avail / slot);
     auto fits = [&](int k) {
         for (const StackTask& T : ht)
-            if (T.stage_rows * T.segments * (T.W2 ? 2 : 1) > kMaxSlots / k) return false;
+            if (T.stage_rows * T.segments * (T.W2 ? 2 : 1) * tokens > kMaxSlots / k) return false;
         return true;
     };
     while (ns > 2 && !fits(ns)) --ns;
@@ -1111,6 +1148,7 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
     h->world = world;
     h->rank = rank;
     h->connected = !sharded;
+    h->tokens = tokens;
     h->fingerprint = stack_fingerprint(dtype, tasks, n, input_cols, world);
     h->smem = kStackSmemHeader + x_smem + (size_t)ns * slot;
     for (uint32_t i = 0; i < n; ++i)
@@ -1143,7 +1181,7 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
     for (uint32_t i = 0; i < n; ++i) {
         if (!waited_for[i]) continue;
         lay.tg_off[i] = lay.total / sizeof(uint32_t);
-        lay.total += align256(tasks[i].rows * sizeof(uint32_t));
+        lay.total += align256(tasks[i].rows * tokens * sizeof(uint32_t));
     }
 
     // each task's rows for each CTA, balanced: [N*c/grid, N*(c+1)/grid) of this rank's slice
@@ -1217,10 +1255,10 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
     P.peer_block[rank] = h->d_block;
 
     switch (dtype) {
-        case NEXUS_GPU_GGUF_Q4_0: rc = stack_attrs_for<FmtQ4_0>(group, h->fused, *d, h->smem); break;
-        case NEXUS_GPU_GGUF_Q8_0: rc = stack_attrs_for<FmtQ8_0>(group, h->fused, *d, h->smem); break;
-        case NEXUS_GPU_GGUF_Q5_K: rc = stack_attrs_for<FmtQ5_K>(group, h->fused, *d, h->smem); break;
-        default: rc = stack_attrs_for<FmtQ6_K>(group, h->fused, *d, h->smem); break;
+        case NEXUS_GPU_GGUF_Q4_0: rc = stack_attrs_for<FmtQ4_0>(group, h->fused, tokens, *d, h->smem); break;
+        case NEXUS_GPU_GGUF_Q8_0: rc = stack_attrs_for<FmtQ8_0>(group, h->fused, tokens, *d, h->smem); break;
+        case NEXUS_GPU_GGUF_Q5_K: rc = stack_attrs_for<FmtQ5_K>(group, h->fused, tokens, *d, h->smem); break;
+        default: rc = stack_attrs_for<FmtQ6_K>(group, h->fused, tokens, *d, h->smem); break;
     }
     if (rc) {
         stack_free(h);
@@ -1659,6 +1697,14 @@ NEXUS_GPU_API int32_t nexus_gpu_stack_create(uint32_t dtype, const NexusGpuStack
     t_last_error.clear();
     const auto ex = plain_tasks(tasks, n_tasks);
     return stack_create(dtype, tasks ? ex.data() : nullptr, n_tasks, input_cols, 1, 0, out_stack);
+}
+
+NEXUS_GPU_API int32_t nexus_gpu_stack_create_tokens(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n_tasks,
+                                                    uint64_t input_cols, uint32_t tokens, void** out_stack) {
+    t_last_error.clear();
+    const auto ex = plain_tasks(tasks, n_tasks);
+    return stack_create(dtype, tasks ? ex.data() : nullptr, n_tasks, input_cols, 1, 0, out_stack,
+                        tokens > (uint32_t)kMaxStackTokens ? kMaxStackTokens + 1 : (int)tokens);
 }
 
 NEXUS_GPU_API int32_t nexus_gpu_stack_create_ex(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t n_tasks,

@@ -518,6 +518,92 @@ __device__ __forceinline__ float stage_x(const float4* xv, const uint32_t* xt,
     return ss;
 }
 
+// The producer (lane 0 of the last warp): streams this CTA's rows of task
+// after task through the ring of NS stage slots, never waiting for
+// activations; a gate+up pair (FX) copies the same rows of both matrices into
+// one slot.  It leaves only after its last copies landed, on every path.
+template <bool FX>
+__device__ __forceinline__ void stack_producer(const StackParams& P, uint32_t full_bar, uint32_t empty_bar,
+                                               uint32_t stage0, int c, int n_cta) {
+    const int NS = P.n_stages;
+    int it = 0, s = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    auto give_up = [&]() {
+        atomicOr(&g_device_status, kStatusWaitTimeout);
+        atomicExch(P.abort_flag, 1u);
+        ok = false;
+    };
+    for (int t = 0; t < P.n_tasks && ok; ++t) {
+        const StackTask& T = P.tasks[t];
+        const uint64_t rb = __ldg(&T.row_bytes), total = __ldg(&T.total_bytes);
+        const uint8_t* W = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.W)));
+        const uint8_t* W2 =
+            FX ? reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.W2))) : nullptr;
+        const int R = __ldg(&T.stage_rows);
+        const int2 rr = __ldg(P.cta_rows + (size_t)t * n_cta + c);
+        const int row_begin = rr.x, row_end = rr.y;
+        const uint64_t floor16 = total & ~(uint64_t)15;
+        const uint64_t span = (uint64_t)R * rb, cta_end = (uint64_t)row_end * rb;
+        for (uint64_t start = (uint64_t)row_begin * rb; start < cta_end; ++it) {
+            if (it >= NS && !mbar_try_wait(empty_bar + 8 * s, phase)) {
+                // ring full: wait (sleeping in try_wait) for the slot to drain
+                const uint64_t t0 = globaltimer_ns();
+                for (uint32_t k = 1; !mbar_try_wait(empty_bar + 8 * s, phase); ++k) {
+                    if ((k & 15u) == 0) {
+                        if (*reinterpret_cast<volatile unsigned*>(P.abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                            give_up();
+                            break;
+                        }
+                    }
+                }
+                if (!ok) break;
+            }
+            const uint64_t end = min(start + span, cta_end);
+            const uint64_t a = start & ~(uint64_t)15;
+            const uint64_t bend = min((end + 15) & ~(uint64_t)15, floor16);
+            const uint32_t dst = stage0 + (uint32_t)(s * P.stage_slot);
+            if (bend < end) {
+                for (uint64_t pos = (bend > a ? bend : a); pos < end; pos += 2)
+                    sts16(dst + (uint32_t)(pos - a), *reinterpret_cast<const uint16_t*>(W + pos));
+                fence_proxy_async_smem();
+            }
+            const uint32_t n = bend > a ? (uint32_t)(bend - a) : 0u;
+            if (FX && W2 != nullptr) {  // gate+up pair: the same rows of the up matrix, half a slot on
+                const uint32_t dst2 = dst + (uint32_t)__ldg(&T.half);
+                if (bend < end) {
+                    for (uint64_t pos = (bend > a ? bend : a); pos < end; pos += 2)
+                        sts16(dst2 + (uint32_t)(pos - a), *reinterpret_cast<const uint16_t*>(W2 + pos));
+                    fence_proxy_async_smem();
+                }
+                mbar_arrive_expect_tx(full_bar + 8 * s, 2 * n);
+                if (n) {
+                    bulk_g2s(dst, W + a, n, full_bar + 8 * s);
+                    bulk_g2s(dst2, W2 + a, n, full_bar + 8 * s);
+                }
+            } else {
+                mbar_arrive_expect_tx(full_bar + 8 * s, n);
+                if (n) bulk_g2s(dst, W + a, n, full_bar + 8 * s);
+            }
+            start = end;
+            if (++s == NS) {
+                s = 0;
+                if (it >= NS) phase ^= 1;
+            }
+        }
+    }
+    // leave no copy in flight: the last stages issued complete on their own
+    // (consumers that stopped after a failed wait no longer wait for them)
+    for (int k = 0; k < NS && k < it; ++k) {
+        const int j = it - 1 - k;
+        mbar_wait_bounded(full_bar + 8 * (j % NS), (j / NS) & 1);
+    }
+}
+
 // FX: the variant with the fused RMSNorm / SwiGLU / residual; stacks without
 // them run the variant that has none of their code.
 template <class F, int G, bool FX>
@@ -555,84 +641,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
 
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------- producer
-        // Lane 0 streams weights, never waiting for activations.
-        if (lane != 0) return;
-        int it = 0, s = 0;
-        uint32_t phase = 0;
-        bool ok = true;
-        auto give_up = [&]() {
-            atomicOr(&g_device_status, kStatusWaitTimeout);
-            atomicExch(P.abort_flag, 1u);
-            ok = false;
-        };
-        for (int t = 0; t < P.n_tasks && ok; ++t) {
-            const StackTask& T = P.tasks[t];
-            const uint64_t rb = __ldg(&T.row_bytes), total = __ldg(&T.total_bytes);
-            const uint8_t* W = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.W)));
-            const uint8_t* W2 =
-                FX ? reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.W2))) : nullptr;
-            const int R = __ldg(&T.stage_rows);
-            const int2 rr = __ldg(P.cta_rows + (size_t)t * n_cta + c);
-            const int row_begin = rr.x, row_end = rr.y;
-            const uint64_t floor16 = total & ~(uint64_t)15;
-            const uint64_t span = (uint64_t)R * rb, cta_end = (uint64_t)row_end * rb;
-            for (uint64_t start = (uint64_t)row_begin * rb; start < cta_end; ++it) {
-                if (it >= NS && !mbar_try_wait(empty_bar + 8 * s, phase)) {
-                    // ring full: wait (sleeping in try_wait) for the slot to drain
-                    const uint64_t t0 = globaltimer_ns();
-                    for (uint32_t k = 1; !mbar_try_wait(empty_bar + 8 * s, phase); ++k) {
-                        if ((k & 15u) == 0) {
-                            if (*reinterpret_cast<volatile unsigned*>(P.abort_flag)) {
-                                ok = false;
-                                break;
-                            }
-                            if (globaltimer_ns() - t0 > kWaitLimitNs) {
-                                give_up();
-                                break;
-                            }
-                        }
-                    }
-                    if (!ok) break;
-                }
-                const uint64_t end = min(start + span, cta_end);
-                const uint64_t a = start & ~(uint64_t)15;
-                const uint64_t bend = min((end + 15) & ~(uint64_t)15, floor16);
-                const uint32_t dst = stage0 + (uint32_t)(s * P.stage_slot);
-                if (bend < end) {
-                    for (uint64_t pos = (bend > a ? bend : a); pos < end; pos += 2)
-                        sts16(dst + (uint32_t)(pos - a), *reinterpret_cast<const uint16_t*>(W + pos));
-                    fence_proxy_async_smem();
-                }
-                const uint32_t n = bend > a ? (uint32_t)(bend - a) : 0u;
-                if (FX && W2 != nullptr) {  // gate+up pair: the same rows of the up matrix, half a slot on
-                    const uint32_t dst2 = dst + (uint32_t)__ldg(&T.half);
-                    if (bend < end) {
-                        for (uint64_t pos = (bend > a ? bend : a); pos < end; pos += 2)
-                            sts16(dst2 + (uint32_t)(pos - a), *reinterpret_cast<const uint16_t*>(W2 + pos));
-                        fence_proxy_async_smem();
-                    }
-                    mbar_arrive_expect_tx(full_bar + 8 * s, 2 * n);
-                    if (n) {
-                        bulk_g2s(dst, W + a, n, full_bar + 8 * s);
-                        bulk_g2s(dst2, W2 + a, n, full_bar + 8 * s);
-                    }
-                } else {
-                    mbar_arrive_expect_tx(full_bar + 8 * s, n);
-                    if (n) bulk_g2s(dst, W + a, n, full_bar + 8 * s);
-                }
-                start = end;
-                if (++s == NS) {
-                    s = 0;
-                    if (it >= NS) phase ^= 1;
-                }
-            }
-        }
-        // leave no copy in flight: the last stages issued complete on their own
-        // (consumers that stopped after a failed wait no longer wait for them)
-        for (int k = 0; k < NS && k < it; ++k) {
-            const int j = it - 1 - k;
-            mbar_wait_bounded(full_bar + 8 * (j % NS), (j / NS) & 1);
-        }
+        if (lane == 0) stack_producer<FX>(P, full_bar, empty_bar, stage0, c, n_cta);
         return;
     }
 
