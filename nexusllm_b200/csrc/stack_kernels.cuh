@@ -38,7 +38,9 @@
 //    applies a SwiGLU of two sources and the RMSNorm weights and sums x^2;
 //    rows are scaled by 1/rms, a gate+up pair computes both rows from one
 //    ring slot and stores silu(gate) * up, and a residual vector is added at
-//    the store.  Stacks without these run the plain variant.
+//    the store (a group head task's residual rows of the CTA are read into
+//    shared memory with the staging).  Stacks without these run the plain
+//    variant.
 //  * All CTAs must be resident at once (they wait on one another): the host
 //    launches the kernel cooperatively with one CTA per SM.  Every wait is
 //    bounded; an expired wait raises a global abort flag that ends every CTA's
@@ -244,8 +246,10 @@ __device__ __forceinline__ bool wait_rows_tagged(const uint32_t* tg, int n, uint
 }
 
 // mbarriers, a broadcast flag, the end-of-run post count, the RMSNorm partial
-// sums, the per-warp epilogue descriptors and the per-warp output offsets
-constexpr int kStackBarBytes = 16 * kMaxStages + 32 + 4 * 16 + 16 * 16 + 16 * 16;
+// sums, the per-warp epilogue descriptors, the per-warp output offsets and the
+// group head task's residual rows of this CTA (fused variant)
+constexpr int kResStageMax = 128;
+constexpr int kStackBarBytes = 16 * kMaxStages + 32 + 4 * 16 + 16 * 16 + 16 * 16 + 4 * kResStageMax;
 constexpr int kStackSmemHeader = ((kStackBarBytes + 127) / 128) * 128 + kSmemHeader - kBarBytes;
 
 __device__ __forceinline__ uint32_t atom_add_acq_rel_shared(uint32_t addr, uint32_t v) {
@@ -386,7 +390,8 @@ __device__ __forceinline__ float4 ld_ep(const volatile float4* p) {
 }
 
 // The descriptor's residual address: the stack input's floats, or -- bit 0
-// set -- a task's tagged copy (both already offset to this rank's first row).
+// set -- a task's tagged copy (both already offset to this rank's first row),
+// or kResInSmem: the CTA's rows staged in shared memory at the group head.
 __device__ __forceinline__ uint64_t ep_residual(const float4 e) {
     return ((uint64_t)__float_as_uint(e.y) << 32) | __float_as_uint(e.x);
 }
@@ -410,10 +415,12 @@ __device__ __forceinline__ uint32_t residual_wait(const uint32_t* p, uint32_t pa
     }
     return w;
 }
+constexpr uint64_t kResInSmem = 2;
 __device__ __forceinline__ float residual_of(const volatile float4* ep, int r, bool sys, uint32_t par,
-                                             const StackParams& P) {
+                                             const StackParams& P, const volatile float* s_res, int row0) {
     const uint64_t a = ep_residual(ld_ep(ep));
     if (!a) return 0.0f;
+    if (a == kResInSmem) return s_res[r - row0];
     if (a & 1u) {
         const uint32_t* p = reinterpret_cast<const uint32_t*>(a - 1) + r;
         uint32_t w = ld_tagged1(p, sys);
@@ -619,6 +626,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
     float* s_norm = reinterpret_cast<float*>(smem + 16 * kMaxStages + 32);  // [16] RMSNorm partials
     volatile float4* s_ep = reinterpret_cast<volatile float4*>(s_norm + 16);  // [16] epilogue descriptors
     volatile ulonglong2* s_od = reinterpret_cast<volatile ulonglong2*>(s_norm + 16 + 4 * 16);  // [16] output offsets
+    volatile float* s_res = reinterpret_cast<volatile float*>(s_od + 16);  // [kResStageMax] head task's residual rows
     constexpr int kHdr = ((kStackBarBytes + 127) / 128) * 128;
     float* slots = reinterpret_cast<float*>(smem + kHdr);
     const uint32_t stage0 = sbase + kStackSmemHeader + (uint32_t)P.x_smem;  // after the x staging buffer
@@ -662,6 +670,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
     for (int t = 0; t < P.n_tasks && !stop;) {
         // ---- group head: wait for the input, stage it, load the x slices
         const StackTask& H = P.tasks[t];
+        const int t_head = t;
         const int K = __ldg(&H.K), S = __ldg(&H.segments);
         const int NW = __ldg(&H.nwi), SW = __ldg(&H.seg_wi), J = __ldg(&H.wi_per_lane);
         // ordering dependency: every row of `after` stored in this run; each
@@ -688,6 +697,28 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
                 if (lane == 0) s_norm[warp] = ss;
+            }
+        }
+        // fused variant: the head task's residual rows of this CTA into shared memory, read
+        // once here with the staging (the residual's task finished before this group's input
+        // in a decode layer), so the row stores read no global memory
+        int res_rows = 0;
+        if constexpr (FX) {
+            const int rs = __ldg(&H.res_src), rin = __ldg(&H.res_input);
+            const int2 hr = __ldg(P.cta_rows + (size_t)t * n_cta + c);
+            if ((rin || rs >= 0) && hr.y - hr.x <= kResStageMax) {
+                res_rows = hr.y - hr.x;
+                const int first = __ldg(&H.row_off) + hr.x;
+                const uint32_t* rt = rs >= 0 ? ld_task_ptr(&P.tasks[rs].tg) + first : nullptr;
+                for (int i = tid; i < res_rows; i += kConsumers) {
+                    if (rin) {
+                        s_res[i] = __ldcg(P.x_in + first + i);
+                    } else {
+                        uint32_t w = ld_tagged1(rt + i, sys);
+                        if (((w ^ par) & 1u) != 0) w = residual_wait(rt + i, par, sys, P.abort_flag, P.wait_polls);
+                        s_res[i] = untag(w);
+                    }
+                }
             }
         }
         if (consumer_bar_any(!ok)) {  // every consumer leaves together after a failed wait
@@ -735,6 +766,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                 uint64_t rp = 0;
                 if (ld_task_i32(&T.res_input)) rp = (uint64_t)(P.x_in + ld_task_i32(&T.row_off));
                 else if (rs >= 0) rp = (uint64_t)(ld_task_ptr(&P.tasks[rs].tg) + ld_task_i32(&T.row_off)) | 1u;
+                if (rp && t == t_head && res_rows > 0) rp = kResInSmem;
                 s_ep[warp].x = __uint_as_float((uint32_t)rp);
                 s_ep[warp].y = __uint_as_float((uint32_t)(rp >> 32));
                 s_ep[warp].w = __int_as_float(half != 0u);
@@ -752,7 +784,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                     int rl = grp - rot;
                     if (rl < 0) rl += n_grp;
                     if (grp >= n_grp) rl = nr;  // the 15 - S*n_grp warps past the last row group idle
-                    if constexpr (!FX) {
+                    if (!FX || half == 0) {
                         // two rows of the stage at once: two independent dot products on the
                         // same x slices, and one reduction for both -- lanes 0-15 finish the
                         // first row, lanes 16-31 the second (each half's sum the same tree as
@@ -766,7 +798,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                             for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
                             const int rme = rl + (lane < 16 ? 0 : n_grp);
                             if ((lane & 15) == 0) {
-                                if (S == 1) put_row<FX>(P, yl, yo, to, par, r0 + rme, v, s_ep + warp, 0.0f, 0.0f);
+                                if (S == 1)
+                                    put_row<FX>(P, yl, yo, to, par, r0 + rme, v, s_ep + warp,
+                                                FX ? residual_of(s_ep + warp, r0 + rme, sys, par, P, s_res, rr.x) : 0.0f,
+                                                0.0f);
                                 else slots[s * P.slot_stride + rme * S + sg] = v;
                             }
                         }
@@ -774,7 +809,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                     for (; rl < nr; rl += n_grp) {
                         const uint32_t row = base + (uint32_t)(rl * rbytes);
                         float rv = 0.0f;
-                        if (FX && lane == 0) rv = residual_of(s_ep + warp, r0 + rl, sys, par, P);
+                        if (FX && lane == 0) rv = residual_of(s_ep + warp, r0 + rl, sys, par, P, s_res, rr.x);
                         float acc = row_partial<F, G>(row, wi, has, X);
 #pragma unroll
                         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -810,7 +845,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                             for (int k = 0; k < S; ++k) v += sl[k];
                             if (FX && half)
                                 for (int k = 0; k < S; ++k) u += sl[S + k];
-                            const float rv = FX ? residual_of(s_ep + warp, r0 + rl, sys, par, P) : 0.0f;
+                            const float rv = FX ? residual_of(s_ep + warp, r0 + rl, sys, par, P, s_res, rr.x) : 0.0f;
                             put_row<FX>(P, yl, yo, to, par, r0 + rl, v, s_ep + warp, rv, u);
                         }
                     }
