@@ -137,8 +137,14 @@ NEXUS_GPU_API int32_t nexus_gpu_synchronize(void* stream);
 /* Drop the cached device copy of a host weight buffer (call when the host
  * buffer is reused for another tensor, e.g. a recycled tier-0 slot,
  * src/memory_tier.cpp:341-356).  NULL drops every cached weight of the
- * current device.  The cache also re-uploads by itself when a sampled
- * fingerprint of the host bytes changes, but only this call is a guarantee. */
+ * current device.  The cache also re-uploads by itself when the host bytes'
+ * fingerprint changes.  The fingerprint is checked at every call:
+ *  - by default it covers the first and last 64 bytes and 16 bytes of every
+ *    64 KiB.  A new tensor that matches the old one at all of those bytes
+ *    goes undetected, so only this call is a guarantee;
+ *  - with the environment variable NEXUS_GPU_WEIGHT_CHECK=full it hashes
+ *    every byte (about 1 ms per 10 MB on one host thread), so any change is
+ *    detected, up to a 64-bit hash collision. */
 NEXUS_GPU_API int32_t nexus_gpu_weight_cache_invalidate(const void* host_W);
 /* Bytes of device memory currently held by the weight cache. */
 NEXUS_GPU_API size_t nexus_gpu_weight_cache_bytes(void);

@@ -662,16 +662,35 @@ uint64_t fnv1a(uint64_t h, const uint8_t* p, size_t n) {
     return h;
 }
 
-// Sampled fingerprint of a host buffer: head, tail and 16 evenly spaced
-// 8-byte probes.  Detects a buffer reused for another tensor; it is not a
-// full content hash.
+// 64-bit mix of 8-byte words (a multiply-xorshift hash; not cryptographic).
+inline uint64_t mix_words(uint64_t h, const uint8_t* p, size_t n) {
+    for (size_t i = 0; i + 8 <= n; i += 8) {
+        uint64_t w;
+        memcpy(&w, p + i, 8);
+        h = (h ^ w) * 0x9e3779b97f4a7c15ull;
+        h ^= h >> 29;
+    }
+    return fnv1a(h, p + (n & ~(size_t)7), n & 7);
+}
+
+// Fingerprint of a host weight buffer, checked at every host-pointer GEMV to
+// detect a buffer that now holds another tensor.  Default: the first and last
+// 64 bytes and 16 bytes of every 64 KiB in between (about 150 probes for a
+// 4096 x 4096 Q4_0 matrix, cheap next to the GEMV).  NEXUS_GPU_WEIGHT_CHECK=full
+// hashes every byte instead (about 1 ms per 10 MB of weights on one host
+// thread): then any change is detected, up to 64-bit hash collisions.
+constexpr size_t kFingerprintStride = 64 * 1024;
+bool full_weight_check() {
+    const char* v = getenv("NEXUS_GPU_WEIGHT_CHECK");
+    return v != nullptr && strcmp(v, "full") == 0;
+}
 uint64_t fingerprint(const void* p, size_t n) {
     const uint8_t* b = static_cast<const uint8_t*>(p);
     uint64_t h = 0xcbf29ce484222325ull ^ n;
-    h = fnv1a(h, b, std::min<size_t>(n, 64));
-    if (n > 64) h = fnv1a(h, b + n - 64, 64);
-    if (n > 256)
-        for (int k = 1; k < 16; ++k) h = fnv1a(h, b + (n - 8) * k / 16, 8);
+    if (full_weight_check()) return mix_words(h, b, n);
+    h = mix_words(h, b, std::min<size_t>(n, 64));
+    if (n > 64) h = mix_words(h, b + n - 64, 64);
+    for (size_t o = kFingerprintStride; o + 16 <= n; o += kFingerprintStride) h = mix_words(h, b + o, 16);
     return h;
 }
 

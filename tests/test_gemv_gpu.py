@@ -212,6 +212,31 @@ def test_host_api_weight_cache(L, port):
         -weight_bytes(dt, rows, cols) % 256)
 
 
+def test_host_api_full_weight_check(L, port, monkeypatch):
+    """NEXUS_GPU_WEIGHT_CHECK=full: a change the sampled fingerprint does not
+    look at (one block's scale, away from the 64 KiB probes) still re-uploads
+    the weights, so the result follows the new bytes."""
+    dt, rows, cols = DataType.GGUF_Q8_0, 4096, 4096  # 8.9 MB: many 64 KiB probes
+    W = synth.blocks_numpy(dt, rows, cols, 31)
+    x = synth.activations_numpy(1, cols, 32)[0]
+    y = np.zeros(rows, np.float32)
+    monkeypatch.setenv("NEXUS_GPU_WEIGHT_CHECK", "full")
+    L.nexus_gpu_weight_cache_invalidate(None)
+    try:
+        assert L.nexus_gpu_gemv_dispatch(W.ctypes.data, int(dt), x.ctypes.data, y.ctypes.data, rows, cols) == 0
+        raw = W.view(np.uint8).reshape(-1)
+        off = 34 * 6100  # block 6100's fp16 scale, between two 64 KiB probes (34-byte blocks)
+        assert 16 <= off % 65536 and off + 2 < raw.size - 64
+        raw[off:off + 2] = np.frombuffer(np.float16(0.5).tobytes(), np.uint8)
+        assert L.nexus_gpu_gemv_dispatch(W.ctypes.data, int(dt), x.ctypes.data, y.ctypes.data, rows, cols) == 0
+        assert oracle.l2_rel(y, port.gemv(int(dt), W, x, rows, cols)) <= TOL
+        r = off // (cols // 32 * 34)  # the changed row now matches the new scale
+        want = port.gemv(int(dt), W, x, rows, cols)[r]
+        assert abs(y[r] - want) <= 1e-3 * max(1.0, abs(want))
+    finally:
+        L.nexus_gpu_weight_cache_invalidate(None)
+
+
 def test_full_size_lm_head_sampled_rows(be, port):
     """BASELINE config 4's largest matrix (LM head 128256 x 4096, Q4_0): the
     whole GEMV on the GPU, checked row-by-row against the oracle on 512
