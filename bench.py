@@ -739,15 +739,16 @@ def batched_decode(torch, L, layers, head, stream, dev, timed, args, peak, stack
         out["M4_stack"] = {"ms": round(ms, 3), "tok_s": round(M * 1e3 / ms, 1),
                            "path": "GEMV stack once per token"}
         del g
-    for M in (2, 3, 4):
+    for M in (2, 3, 4, 16, 64):
         out[f"M{M}_tokens_stack"] = tokens_stack(torch, L, layers, head, M, stream, dev, timed, args, peak)
     return out
 
 
 def tokens_stack(torch, L, layers, head, M, stream, dev, timed, args, peak):
-    """configs[3] at M = 2..4 tokens: the headline's task list (same weights,
-    same dependencies) as ONE multi-token stack launch per step
-    (nexus_gpu_stack_create_tokens): every weight read once for all M tokens.
+    """configs[3] at M = 2..4 and 16..64 tokens: the headline's task list (same
+    weights, same dependencies) as ONE stack launch per step
+    (nexus_gpu_stack_create_tokens: CUDA cores below 16 tokens, tcgen05 tensor
+    cores from 16): every weight read once for all M tokens.
     Parity: 16 sampled rows of the first q, the first o, the last down and the
     LM head of the first and the last token against the C oracle, each fed the
     input the stack gave it."""
@@ -801,8 +802,10 @@ def tokens_stack(torch, L, layers, head, M, stream, dev, timed, args, peak):
     sb = step_bytes(layers=len(layers))
     gbs = sb / (ms * 1e-3) / 1e9
     e = max(errs)
+    path = ("tcgen05 GEMV stack (persistent, grid barriers at hops), one launch per step" if M >= 16
+            else "multi-token CUDA-core GEMV stack, one launch per step")
     return {"ms": round(ms, 3), "tok_s": round(M * 1e3 / ms, 1), "GBs_weights_once": round(gbs, 1),
-            "frac": round(gbs / peak, 4), "path": "multi-token GEMV stack, one launch per step",
+            "frac": round(gbs / peak, 4), "path": path,
             "parity_max_l2_rel": float(f"{e:.3e}"), "parity_pass": e <= 1e-3}
 
 

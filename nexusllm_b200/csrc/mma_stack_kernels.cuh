@@ -1,0 +1,590 @@
+// mma_stack_kernels.cuh -- batched decode (16..64 tokens) of a whole GEMV
+// stack on the tcgen05 tensor cores in ONE persistent launch, GGUF Q4_0.
+//
+// A decode step over M requests runs the step's GEMVs with M activation rows
+// each (src/forward_pass.cpp:504-585 per request; the reference serves
+// requests one after another, :633-667).  Launched one GEMM at a time, each
+// pays a launch, an x-preparation kernel, a TMEM allocation and a pipeline
+// fill and drain that cost more than its HBM time.  Here one cooperative
+// launch (one CTA per SM) runs the task list:
+//  * Each task is the single-GEMM kernel's work (gemm_q4_0_mma_kernel):
+//    128-row tiles x 256-weight chunks split stream-K over the task's CTAs,
+//    raw Q4_0 chunks and x tiles by TMA, the nibble decode into tensor memory
+//    by sixteen warps, tcgen05.mma from tensor memory and shared memory, and
+//    the fix-up of shared tiles by their last CTA.  The rings, barriers and
+//    accumulator carry on from task to task; only the operands change.
+//  * A "hop" is a task whose input differs from the previous task's (q, k, v
+//    share one input, gate and up another): there every CTA waits at a grid
+//    barrier for the previous tasks' outputs (and, with them, for every read
+//    of the shared x buffer), CTA b < NB converts token b of the new input
+//    into the fp16 B operand (x * 2^-e per token, K permuted to the decode's
+//    order, as mma_xprep_kernel does), and a second grid barrier publishes
+//    it.  Tasks that share an input run back to back with no barrier.
+//  * The producer streams the next task's raw weight chunks across the
+//    barriers (weights depend on nothing); only its x-tile copies wait for
+//    the second barrier.
+//  * The per-tile arrival counters of the fix-up only grow: a tile shared by
+//    n CTAs is complete at the arrival whose previous count is n - 1 modulo n,
+//    so no run resets them.  The grid barrier counter and the run counter
+//    grow the same way.
+// Every wait is bounded; an expired wait raises the stack's abort flag and
+// the device status word, every CTA stops at its next wait, the producer
+// drains its copies and the tensor memory is freed.  No cluster multicast.
+#pragma once
+
+#include "mma_kernels.cuh"
+
+namespace nexus_gpu {
+
+constexpr int kMmaMinTokens = 16;  // below this the CUDA-core stacks serve (north star: tensor cores for M >= 16)
+
+// One GEMM of the stack.  The tensor map comes first so that an array of
+// tasks keeps every map 64-byte aligned (sizeof is a multiple of 64).
+struct __align__(64) MmaTask {
+    CUtensorMap tmW;        // raw Q4_0 rows: {row bytes, N}, box {144, 128}
+    const float* x;         // input [M][K] fp32: an earlier task's y, or null: the stack input
+    float* y;               // output [M][N] fp32
+    unsigned* arrivals;     // [tiles] fix-up arrival counters (only grow)
+    int N, K, tiles, n_chunks;
+    long long total;        // tiles * n_chunks
+    int G;                  // CTAs that share the task's chunks (stream-K), <= gridDim.x
+    int hop;                // 1: a new input -- barriers and x conversion before the task
+    int hidx;               // index of the last hop at or before this task
+    int gpos;               // position of the task in its hop group (tasks from one hop to the next)
+};
+static_assert(sizeof(MmaTask) % 64 == 0, "tensor maps in an MmaTask array must stay 64-byte aligned");
+
+struct MmaStackParams {
+    const MmaTask* tasks;
+    int n_tasks, n_hops;
+    int M, NB;               // tokens; tokens rounded up to 16 (the UMMA N)
+    int kmax;                // row stride of the fp16 x buffer
+    int b_stages;            // x-tile ring depth in chunks
+    __half* xbuf;            // [NB][kmax] the current input in fp16 (B operand)
+    float* xscale;           // [NB] 2^e per token of the current input
+    float* partial;          // [gridDim.x][slots][NB][128] partial sums of shared tiles
+    int slots;               // partial-sum slots per CTA: 2 per task of the largest hop group
+    unsigned long long* bar_done;  // arrivals "done with the tasks before hop h" (hops 1..), all runs
+    unsigned long long* bar_pub;   // arrivals "hop h's input converted and published", all runs
+    unsigned long long* epoch;     // runs completed
+    unsigned long long* fin;       // CTAs that left, all runs
+    unsigned* abort_flag;          // sticky: an expired wait poisons the stack
+    const float* x_in;             // the stack input [M][K] fp32 of this run (tasks with x == null)
+};
+
+// Grid barrier arrival (one thread per CTA, after its CTA-local barrier):
+// release its CTA's writes at GPU scope.
+__device__ __forceinline__ void grid_arrive(unsigned long long* ctr) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(ctr) : "memory");
+}
+// Wait until `ctr` reached `target` (acquire).  Bounded: false when the abort
+// flag is up or after the wait limit (which raises it and the status bit).
+__device__ __forceinline__ bool grid_wait(const unsigned long long* ctr, unsigned long long target,
+                                          unsigned* abort_flag) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(ctr) : "memory");
+    if (v >= target) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t k = 1;; ++k) {
+        __nanosleep(64);
+        asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(ctr) : "memory");
+        if (v >= target) return true;
+        if ((k & 15u) == 0) {
+            if (*reinterpret_cast<volatile unsigned*>(abort_flag)) return false;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                atomicOr(&g_device_status, kStatusWaitTimeout);
+                atomicExch(abort_flag, 1u);
+                return false;
+            }
+        }
+    }
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// The 16 dequantizing warps' barrier (named barrier 1, 512 threads).
+__device__ __forceinline__ void dequant_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kDequantThreads) : "memory"); }
+
+// Two grid barriers per hop, each kind on its own counter: hop h >= 1 has a
+// "done" barrier before its conversion (bar_done reaches (run*(H-1) + h) * G),
+// every hop a "published" barrier after it (bar_pub reaches (run*H + h + 1) *
+// G), H hops a run.  With one counter per kind a CTA's next arrival on a
+// counter always follows its own wait for that counter's current target, so
+// early arrivals of a CTA that has no work between two hops cannot complete a
+// barrier for a CTA that has not arrived.
+__device__ __forceinline__ unsigned long long done_target(unsigned long long run, int n_hops, int h, int G) {
+    return (run * (unsigned long long)(n_hops - 1) + (unsigned long long)h) * (unsigned long long)G;
+}
+__device__ __forceinline__ unsigned long long pub_target(unsigned long long run, int n_hops, int h, int G) {
+    return (run * (unsigned long long)n_hops + (unsigned long long)h + 1ull) * (unsigned long long)G;
+}
+
+// This CTA's chunks of a task: the linear range [lo, hi) of tiles x chunks
+// (none when b is past the task's G CTAs).
+struct MmaTaskRange {
+    long long lo = 0, hi = 0;
+    int nc = 1, t0 = 0, t1 = -1;
+    bool any = false;
+};
+__device__ __forceinline__ MmaTaskRange mma_task_range(const MmaTask& T, int b) {
+    MmaTaskRange r;
+    const int G = __ldg(&T.G);
+    r.nc = __ldg(&T.n_chunks);
+    if (b >= G) return r;
+    const long long total = __ldg(&T.total);
+    r.lo = sk_lo(total, G, b);
+    r.hi = sk_lo(total, G, b + 1);
+    r.any = r.hi > r.lo;
+    if (r.any) {
+        r.t0 = (int)(r.lo / r.nc);
+        r.t1 = (int)((r.hi - 1) / r.nc);
+    }
+    return r;
+}
+
+// The producer's walk over this CTA's chunks of every task, in order.
+struct MmaChunkCursor {
+    int t = 0, nc = 1, hidx = 0;
+    long long L = 0, hi = 0;
+};
+__device__ __forceinline__ void mma_cursor_seek(MmaChunkCursor& k, const MmaStackParams& P, int t, int b) {
+    for (; t < P.n_tasks; ++t) {
+        const MmaTaskRange r = mma_task_range(P.tasks[t], b);
+        if (r.any) {
+            k.t = t;
+            k.L = r.lo;
+            k.hi = r.hi;
+            k.nc = r.nc;
+            k.hidx = __ldg(&P.tasks[t].hidx);
+            return;
+        }
+    }
+    k.t = P.n_tasks;
+}
+__device__ __forceinline__ void mma_cursor_next(MmaChunkCursor& k, const MmaStackParams& P, int b) {
+    if (++k.L == k.hi) mma_cursor_seek(k, P, k.t + 1, b);
+}
+
+// Token b of a hop's input (fp32 [M][K]; rows b >= M are zero) -> row b of
+// the fp16 B operand: x * 2^-e with amax * 2^-e in [2^13, 2^14), K permuted
+// inside every 32-weight block as q4_unit_decode orders the weights, and
+// xscale[b] = 2^e (mma_xprep_kernel's rule).  Run by the 512 dequantizing
+// threads of CTA b; s_red holds their 16 warps' maxima.
+__device__ __forceinline__ void mma_convert_token(const MmaStackParams& P, const float* x, int K, int b, int tid,
+                                                  volatile uint32_t* s_red) {
+    const bool real = b < P.M;
+    const float* row = x + (size_t)b * K;
+    uint32_t m = 0;
+    if (real)
+        for (int e = 4 * tid; e < K; e += 4 * kDequantThreads) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(row + e));
+            m = max(m, max(max(__float_as_uint(v.x) & 0x7fffffffu, __float_as_uint(v.y) & 0x7fffffffu),
+                           max(__float_as_uint(v.z) & 0x7fffffffu, __float_as_uint(v.w) & 0x7fffffffu)));
+        }
+    m = __reduce_max_sync(0xffffffffu, m);
+    if ((tid & 31) == 0) s_red[tid >> 5] = m;
+    dequant_bar();
+    uint32_t amax = 0;
+#pragma unroll
+    for (int w = 0; w < kDequantWarps; ++w) amax = max(amax, s_red[w]);
+    int ex = 0;
+    if (amax != 0 && amax < 0x7f800000u) ex = max((int)((amax >> 23) & 0xff) - 127 - 13, -110);
+    const float down = ldexpf(1.0f, -ex);
+    __half* out = P.xbuf + (size_t)b * P.kmax;
+    for (int e = 4 * tid; e < K; e += 4 * kDequantThreads) {
+        float v4[4] = {0.f, 0.f, 0.f, 0.f};
+        if (real) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(row + e));
+            v4[0] = v.x;
+            v4[1] = v.y;
+            v4[2] = v.z;
+            v4[3] = v.w;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int s = e + k, blk = s >> 5;
+            out[32 * blk + q4_perm_dst(s & 31, blk & 1)] = __float2half_rn(v4[k] * down);
+        }
+    }
+    if (tid == 0) P.xscale[b] = real ? ldexpf(1.0f, ex) : 0.0f;
+}
+
+constexpr int kMmaStackSmemBytes = kMmaSmemBytes + 96;  // + the hop decision and 16 warp maxima
+
+__global__ void __launch_bounds__(kMmaThreads, 1)
+    gemm_q4_0_mma_stack_kernel(const __grid_constant__ CUtensorMap tmX, const MmaStackParams P) {
+    extern __shared__ uint8_t mma_smem_raw[];
+    const uint32_t sraw = smem_u32(mma_smem_raw);
+    const uint32_t sbase = (sraw + 1023u) & ~1023u;  // 1024-byte aligned: swizzle atoms
+    uint8_t* smem = mma_smem_raw + (sbase - sraw);
+    const uint32_t bar0 = sbase + kMmaSmemBar;
+    const uint32_t raw_full = bar0, raw_empty = raw_full + 8 * kRawStages;
+    const uint32_t a_full = raw_empty + 8 * kRawStages, a_empty = a_full + 8 * kAStages;
+    const uint32_t b_full = a_empty + 8 * kAStages, b_empty = b_full + 8 * kMaxBStages;
+    const uint32_t acc_full = b_empty + 8 * kMaxBStages, acc_empty = acc_full + 8, drain = acc_empty + 8;
+    const uint32_t part_done = drain + 8, decided = part_done + 8;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kMmaSmemBar + 8 * kMmaBarCount);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+    volatile int* s_go = reinterpret_cast<volatile int*>(tmem_slot + 3);
+    volatile uint32_t* s_red = tmem_slot + 4;  // [16]
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = blockIdx.x, NB = P.NB;
+    const uint32_t nbs = (uint32_t)P.b_stages, b_unit = (uint32_t)NB * 128u, b_stage = 4u * b_unit;
+    // this run's number (runs are stream-ordered; the epoch advances after every CTA left)
+    const unsigned long long run = *reinterpret_cast<volatile unsigned long long*>(P.epoch);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kRawStages; ++s) {
+            mbar_init(raw_full + 8 * s, 1);
+            mbar_init(raw_empty + 8 * s, 1);
+        }
+        for (int s = 0; s < kAStages; ++s) {
+            mbar_init(a_full + 8 * s, kDequantWarps);
+            mbar_init(a_empty + 8 * s, 1);
+        }
+        for (int s = 0; s < kMaxBStages; ++s) {
+            mbar_init(b_full + 8 * s, 1);
+            mbar_init(b_empty + 8 * s, 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, kDequantWarps);
+        mbar_init(drain, 1);
+        mbar_init(part_done, kDequantWarps);
+        mbar_init(decided, 1);
+        *abort = *reinterpret_cast<volatile unsigned*>(P.abort_flag) ? 1 : 0;  // a poisoned stack does nothing
+        *last_flag = 0;
+        *s_go = 1;
+        fence_mbar_init();
+    }
+    const uint32_t tcols = kTmemCols;
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(tcols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_d = __shfl_sync(0xffffffffu, *reinterpret_cast<volatile uint32_t*>(tmem_slot), 0);
+
+    if (warp == 0) {
+        // ------------------- raw weight chunks (run ahead) and x tiles (after each hop's publication)
+        const bool leader = elect_one();
+        MmaChunkCursor rk, xk;
+        mma_cursor_seek(rk, P, 0, b);
+        mma_cursor_seek(xk, P, 0, b);
+        RingPos rp, bp;
+        uint32_t r_issued = 0, x_issued = 0;
+        int waited = -1;  // the last hop whose x this warp saw published
+        bool ok = *abort == 0;
+        while (ok && xk.t < P.n_tasks) {
+            // raw chunks up to kRawStages ahead of the x tiles: weights depend on nothing, so
+            // they stream across a hop's barriers.  Raw chunk j reuses the slot of chunk
+            // j - kRawStages, whose x tile is already issued, so its MMA can free it.
+            while (rk.t < P.n_tasks && r_issued < x_issued + kRawStages) {
+                if (r_issued >= kRawStages && !warp_wait(raw_empty + 8 * rp.stage, rp.phase ^ 1u, abort)) {
+                    ok = false;
+                    break;
+                }
+                if (leader) {
+                    const int tile = (int)(rk.L / rk.nc), c = (int)(rk.L - (long long)tile * rk.nc);
+                    mbar_arrive_expect_tx(raw_full + 8 * rp.stage, kRawChunkBytes);
+                    tma_load_2d(sbase + kMmaSmemRaw + rp.stage * kRawChunkBytes, &P.tasks[rk.t].tmW, c * kRawRowBytes,
+                                tile * kMmaRows, raw_full + 8 * rp.stage);
+                }
+                __syncwarp();
+                ++r_issued;
+                rp.next(kRawStages);
+                mma_cursor_next(rk, P, b);
+            }
+            if (!ok) break;
+            // the next x tile: its hop's conversion published (bar_pub), then made
+            // visible to the tensor-copy (async) proxy
+            if (xk.hidx > waited) {
+                bool go = true;
+                if (leader) {
+                    go = grid_wait(P.bar_pub, pub_target(run, P.n_hops, xk.hidx, gridDim.x), P.abort_flag);
+                    if (go) fence_proxy_async_global();
+                    else *abort = 1;
+                }
+                if (!__all_sync(0xffffffffu, leader ? go : true)) {
+                    ok = false;
+                    break;
+                }
+                waited = xk.hidx;
+            }
+            if (x_issued >= nbs && !warp_wait(b_empty + 8 * bp.stage, bp.phase ^ 1u, abort)) {
+                ok = false;
+                break;
+            }
+            if (leader) {
+                const int c = (int)(xk.L % xk.nc);
+                const uint32_t dst = sbase + kMmaSmemB + bp.stage * b_stage, bar = b_full + 8 * bp.stage;
+                mbar_arrive_expect_tx(bar, b_stage);
+#pragma unroll
+                for (int u = 0; u < kUnitsPerChunk; ++u) tma_load_2d(dst + u * b_unit, &tmX, c * kRawK + u * kUnitK, 0, bar);
+            }
+            __syncwarp();
+            ++x_issued;
+            bp.next(nbs);
+            mma_cursor_next(xk, P, b);
+        }
+        if (leader && *abort) {  // leave no copy in flight
+            for (uint32_t k = 0; k < r_issued && k < (uint32_t)kRawStages; ++k) {
+                const uint32_t j = r_issued - 1 - k;
+                mbar_wait_bounded(raw_full + 8 * (j % kRawStages), (j / kRawStages) & 1);
+            }
+            for (uint32_t k = 0; k < x_issued && k < nbs; ++k) {
+                const uint32_t j = x_issued - 1 - k;
+                mbar_wait_bounded(b_full + 8 * (j % nbs), (j / nbs) & 1);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // --------------------------------------------------------------- MMA
+        const uint32_t idesc = (1u << 4) | ((uint32_t)(NB >> 3) << 17) | ((uint32_t)(kMmaRows >> 4) << 24);
+        const uint32_t b_unit16 = b_unit >> 4;
+        const bool leader = elect_one();
+        RingPos ap, bp, rp;
+        bool ok = *abort == 0;
+        int k = 0;  // segments (accumulator uses) so far
+        for (int t = 0; t < P.n_tasks && ok; ++t) {
+            const MmaTaskRange tr = mma_task_range(P.tasks[t], b);
+            if (!tr.any) continue;
+            MmaRange R;
+            R.lo = tr.lo;
+            R.hi = tr.hi;
+            R.t0 = tr.t0;
+            R.t1 = tr.t1;
+            for (int tile = R.t0; tile <= R.t1 && ok; ++tile, ++k) {
+                const MmaSeg S = R.seg(tile, tr.nc);
+                if (k > 0 && !warp_wait(acc_empty, (k - 1) & 1, abort)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (int c = S.c0; c < S.c1; ++c, ap.next(kAStages), bp.next(nbs), rp.next(kRawStages)) {
+                    if (!warp_wait(a_full + 8 * ap.stage, ap.phase, abort) ||
+                        !warp_wait(b_full + 8 * bp.stage, bp.phase, abort)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = tmem_d + kAccCols + kAStageCols * ap.stage;
+                    const uint64_t b0 = umma_desc_sw128(sbase + kMmaSmemB + bp.stage * b_stage);
+                    if (leader) {
+#pragma unroll
+                        for (int u = 0; u < kUnitsPerChunk; ++u) {
+                            const uint64_t bu = b0 + (uint64_t)(u * b_unit16);
+                            umma_f16_tmem_a(tmem_d, a0 + 32 * u, bu, idesc, (c > S.c0 || u > 0) ? 1u : 0u);
+                            umma_f16_tmem_a(tmem_d, a0 + 32 * u + 8, bu + 2, idesc, 1u);
+                            umma_f16_tmem_a(tmem_d, a0 + 32 * u + 16, bu + 4, idesc, 1u);
+                            umma_f16_tmem_a(tmem_d, a0 + 32 * u + 24, bu + 6, idesc, 1u);
+                        }
+                        umma_commit(a_empty + 8 * ap.stage);
+                        umma_commit(b_empty + 8 * bp.stage);
+                        umma_commit(raw_empty + 8 * rp.stage);
+                    }
+                    __syncwarp();
+                }
+                if (ok && leader) umma_commit(acc_full);
+                __syncwarp();
+            }
+        }
+        if (leader) {
+            umma_commit(drain);
+            mbar_wait_bounded(drain, 0);
+        }
+        __syncwarp();
+    } else {
+        // ----------------------- hops (barriers, x conversion), dequantize, epilogue, fix-up
+        const int dw = warp - 2, grp = dw >> 2, quarter = warp & 3;
+        const int r = quarter * 32 + lane;  // accumulator lane = weight row of the tile
+        const uint32_t lane_base = tmem_d + ((uint32_t)(quarter * 32) << 16);
+        const bool leader = dw == 0 && lane == 0;
+        const int tid = (int)threadIdx.x - (kMmaThreads - kDequantThreads);
+        constexpr int kTokSlice = kMaxTokens / 4;
+        const int tok_lo = grp * (NB / 4), tok_hi = tok_lo + NB / 4;
+        RingPos rp, ap;
+        uint32_t chunks = 0, n_part = 0;
+        int k = 0;  // segments so far: the accumulator's parity
+        bool ok = *abort == 0;
+        for (int t = 0; t < P.n_tasks; ++t) {
+            const MmaTask& T = P.tasks[t];
+            if (__ldg(&T.hop)) {
+                // a new input: every CTA finished the tasks before it (which also ends every
+                // read of the x buffer), CTA b < NB converts token b, and the result is
+                // published at GPU scope for the other CTAs' tensor copies
+                const int hh = __ldg(&T.hidx);
+                if (!ok) *abort = 1;
+                dequant_bar();
+                if (leader) {
+                    bool go = *abort == 0;
+                    if (go && hh > 0) {
+                        grid_arrive(P.bar_done);
+                        go = grid_wait(P.bar_done, done_target(run, P.n_hops, hh, gridDim.x), P.abort_flag);
+                    }
+                    *s_go = (go && *abort == 0) ? 1 : 0;
+                }
+                dequant_bar();
+                if (!*s_go) {  // every dequantizing warp leaves together
+                    *abort = 1;
+                    ok = false;
+                    break;
+                }
+                if (b < NB) {
+                    const float* x = reinterpret_cast<const float*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.x)));
+                    mma_convert_token(P, x != nullptr ? x : P.x_in, __ldg(&T.K), b, tid, s_red);
+                }
+                fence_proxy_async_global();
+                dequant_bar();
+                if (leader) grid_arrive(P.bar_pub);
+            }
+            const MmaTaskRange tr = mma_task_range(T, b);
+            if (!tr.any || !ok) continue;  // after a failed wait: no work, but the hops' structure
+            MmaRange R;
+            R.lo = tr.lo;
+            R.hi = tr.hi;
+            R.t0 = tr.t0;
+            R.t1 = tr.t1;
+            const int nc = tr.nc, N = __ldg(&T.N), G = __ldg(&T.G);
+            const long long total = __ldg(&T.total);
+            float* const y = reinterpret_cast<float*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.y)));
+            unsigned* const arrivals =
+                reinterpret_cast<unsigned*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.arrivals)));
+            for (int tile = R.t0; tile <= R.t1 && ok; ++tile, ++k) {
+                const MmaSeg S = R.seg(tile, nc);
+                for (int c = S.c0; c < S.c1; ++c, ++chunks, rp.next(kRawStages), ap.next(kAStages)) {
+                    if (!warp_wait(raw_full + 8 * rp.stage, rp.phase, abort) ||
+                        (chunks >= kAStages && !warp_wait(a_empty + 8 * ap.stage, ap.phase ^ 1u, abort))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t raw_row =
+                        sbase + kMmaSmemRaw + rp.stage * kRawChunkBytes + (uint32_t)r * kRawRowBytes;
+                    const uint32_t ta = lane_base + kAccCols + kAStageCols * ap.stage;
+                    switch (grp) {
+                        case 0: q4_unit_tmem<0>(raw_row, ta); break;
+                        case 1: q4_unit_tmem<1>(raw_row, ta); break;
+                        case 2: q4_unit_tmem<2>(raw_row, ta); break;
+                        default: q4_unit_tmem<3>(raw_row, ta); break;
+                    }
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(a_full + 8 * ap.stage);
+                }
+                if (!ok || !warp_wait(acc_full, k & 1, abort)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                float v[kTokSlice];
+#pragma unroll
+                for (int j = 0; j < kTokSlice; j += 4)
+                    if (j < NB / 4) tmem_ld4(lane_base + (uint32_t)(tok_lo + j), v + j);
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(acc_empty);
+                const int row = tile * kMmaRows + r;
+                if (S.c0 == 0 && S.c1 == nc) {
+#pragma unroll
+                    for (int j = 0; j < kTokSlice; ++j) {
+                        const int tok = tok_lo + j;
+                        if (tok < tok_hi && tok < P.M && row < N) y[(size_t)tok * N + row] = v[j] * __ldcg(P.xscale + tok);
+                    }
+                    continue;
+                }
+                // a tile shared with other CTAs: store this CTA's partial sums, in the two slots
+                // of this task in its hop group -- tasks of a group run without a barrier, so
+                // another CTA may still be adding up an earlier task's tile of this CTA
+                const int gp = __ldg(&T.gpos);
+                const int slot = b * P.slots + 2 * gp + (tile == R.t0 ? 0 : 1);
+                float* mine = P.partial + (size_t)slot * NB * kMmaRows;
+#pragma unroll
+                for (int j = 0; j < kTokSlice; ++j) {
+                    const int tok = tok_lo + j;
+                    if (tok < tok_hi) mine[(size_t)tok * kMmaRows + r] = v[j];
+                }
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(part_done);
+                const int bf = sk_owner(total, G, (long long)tile * nc);
+                const int bl = sk_owner(total, G, (long long)(tile + 1) * nc - 1);
+                if (leader) {
+                    bool last = false;
+                    if (mma_wait(part_done, n_part & 1, abort)) {
+                        // the counter only grows: each run adds one arrival per sharing CTA
+                        const unsigned n = (unsigned)(bl - bf + 1);
+                        last = atomicAdd(arrivals + tile, 1u) % n == n - 1;
+                        __threadfence();
+                    }
+                    *last_flag = last ? 1 : 0;
+                    mbar_arrive(decided);
+                }
+                if (!warp_wait(decided, n_part & 1, abort)) {
+                    ok = false;
+                    break;
+                }
+                ++n_part;
+                if (*last_flag && !*abort) {
+                    // the last CTA to finish the tile adds every partial in CTA order
+                    __threadfence();
+                    const int n4 = NB * (kMmaRows / 4);
+                    constexpr int kFixBatch = 4;
+                    for (int f = tid; f < n4; f += kDequantThreads) {
+                        const int tok = f / (kMmaRows / 4);
+                        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                        for (int b0 = bf; b0 <= bl; b0 += kFixBatch) {
+                            float4 p[kFixBatch];
+#pragma unroll
+                            for (int i = 0; i < kFixBatch; ++i) {
+                                const int bb = b0 + i;
+                                if (bb <= bl) {
+                                    const int sl = bb * P.slots + 2 * gp + (tile == (int)(sk_lo(total, G, bb) / nc) ? 0 : 1);
+                                    p[i] = __ldcg(reinterpret_cast<const float4*>(P.partial + (size_t)sl * NB * kMmaRows) + f);
+                                }
+                            }
+#pragma unroll
+                            for (int i = 0; i < kFixBatch; ++i)
+                                if (b0 + i <= bl) {
+                                    acc.x += p[i].x;
+                                    acc.y += p[i].y;
+                                    acc.z += p[i].z;
+                                    acc.w += p[i].w;
+                                }
+                        }
+                        if (tok >= P.M) continue;
+                        const float sc = __ldcg(P.xscale + tok), a4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int rr = tile * kMmaRows + 4 * (f % (kMmaRows / 4)) + e;
+                            if (rr < N) y[(size_t)tok * N + rr] = a4[e] * sc;
+                        }
+                    }
+                }
+            }
+        }
+        if (!ok) *abort = 1;
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(tcols) : "memory");
+    }
+    // a failed wait poisons the stack; the last CTA of the run to leave advances the epoch
+    if (threadIdx.x == 0) {
+        if (*abort) atomicExch(P.abort_flag, 1u);
+        __threadfence();
+        const unsigned long long left = atomicAdd(P.fin, 1ull) + 1;
+        if (left == (run + 1) * (unsigned long long)gridDim.x) atomicExch(P.epoch, run + 1);
+    }
+}
+
+}  // namespace nexus_gpu

@@ -20,6 +20,7 @@
 #include "stack_mt_kernels.cuh"
 #include "awq_fp8_kernels.cuh"
 #include "mma_kernels.cuh"
+#include "mma_stack_kernels.cuh"
 #include "gguf_file.cuh"
 
 namespace nexus_gpu {
@@ -908,7 +909,10 @@ struct StackHandle {
     int world = 1, rank = 0;
     bool connected = true;  // sharded stacks need nexus_gpu_stack_connect first
     bool fused = false;     // some task has a norm, a SwiGLU or a residual: the kernel variant with them
-    int tokens = 1;         // activation vectors per run (2..4: the multi-token kernel)
+    int tokens = 1;         // activation vectors per run (2..4: the multi-token kernel; 16..64: tensor cores)
+    bool mma = false;       // the tcgen05 stack (tokens >= 16): mparams, tmX, d_block
+    MmaStackParams mparams{};
+    CUtensorMap tmX{};
     uint64_t fingerprint = 0;
     StackParams params{};
     StackTask* d_tasks = nullptr;
@@ -1033,15 +1037,21 @@ uint64_t stack_fingerprint(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uin
     return h;
 }
 
+int32_t mma_stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t n, uint64_t input_cols,
+                         int tokens, void** out);
+
 int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t n, uint64_t input_cols, int world,
                      int rank, void** out, int tokens = 1) {
+    if (tokens >= kMmaMinTokens && tokens <= kMaxTokens && world == 1)
+        return mma_stack_create(dtype, tasks, n, input_cols, tokens, out);
     if (!out || (!tasks && n)) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null argument");
     *out = nullptr;
     if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world)
         return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "rank %d of world %d (1..%d GPUs)", rank, world, kMaxWorld);
     const bool sharded = world > 1;
     if (tokens < 1 || tokens > kMaxStackTokens)
-        return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "%d tokens per run (1..%d)", tokens, kMaxStackTokens);
+        return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "%d tokens per run (1..%d on CUDA cores, %d..%d on tensor cores)",
+                    tokens, kMaxStackTokens, kMmaMinTokens, kMaxTokens);
     if (tokens > 1 && sharded)
         return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "a multi-token stack is not sharded");
     if (dtype == NEXUS_GPU_FP16)
@@ -1287,6 +1297,191 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
     return NEXUS_GPU_SUCCESS;
 }
 
+// ---------------------------------------------------- tensor-core stacks
+// A stack for 16..64 tokens on the tcgen05 tensor cores
+// (gemm_q4_0_mma_stack_kernel): GGUF Q4_0, every task's cols a multiple of
+// 256, unsharded, no fused operations.  Every task's y holds tokens x rows
+// floats; the stack input tokens x input_cols.
+int32_t mma_stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t n, uint64_t input_cols,
+                         int tokens, void** out) {
+    if (!out || (!tasks && n)) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    if (dtype != NEXUS_GPU_GGUF_Q4_0)
+        return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "tensor-core stacks (%d..%d tokens) serve GGUF Q4_0",
+                    kMmaMinTokens, kMaxTokens);
+    if (n == 0 || n > 100000) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task count %u", n);
+    if (input_cols == 0 || input_cols % kRawK || input_cols > (uint64_t)INT32_MAX)
+        return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "stack input length %llu is not a positive multiple of %d",
+                    (unsigned long long)input_cols, kRawK);
+    Device* d = nullptr;
+    int32_t rc = get_device(&d);
+    if (rc) return rc;
+    if ((rc = ensure_attrs(*d))) return rc;
+    if (d->smem_optin < kMmaStackSmemBytes)
+        return fail(NEXUS_GPU_ERROR_FORMAT_UNSUPPORTED, "tensor-core stack needs %d bytes of shared memory",
+                    kMmaStackSmemBytes);
+    TensorMapEncodeTiled encode = tensor_map_encoder();
+    if (!encode) return fail(NEXUS_GPU_ERROR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const int NB = (tokens + 15) / 16 * 16, G = d->sms;
+    std::vector<MmaTask> ht(n);
+    std::vector<size_t> arr_off(n);
+    size_t arr_words = 0;
+    int kmax = 0, hops = 0, last_hop = 0, gpos = 0, max_group = 1;
+    for (uint32_t i = 0; i < n; ++i) {
+        const NexusGpuStackTaskEx& u = tasks[i];
+        if (!u.W || !u.y || u.rows == 0 || u.rows > (uint64_t)INT32_MAX)
+            return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u: null W or y, or no rows", i);
+        if (u.cols == 0 || u.cols % kRawK || u.cols > (uint64_t)INT32_MAX)
+            return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "task %u: cols %llu is not a positive multiple of %d", i,
+                        (unsigned long long)u.cols, kRawK);
+        if (((uintptr_t)u.W & 15) || ((uintptr_t)u.y & 15))
+            return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u: W or y not 16-byte aligned", i);
+        if (u.x_source2 != -1 || u.residual_source != -2 || u.norm_weight || u.W_up)
+            return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u: a multi-token stack has no fused operations", i);
+        const uint64_t xlen = u.x_source < 0 ? input_cols : (u.x_source < (int32_t)i ? tasks[u.x_source].rows : 0);
+        if (u.x_source >= (int32_t)i || xlen != u.cols)
+            return fail(NEXUS_GPU_ERROR_SHAPE_MISMATCH, "task %u: x_source %d does not give a vector of %llu", i,
+                        u.x_source, (unsigned long long)u.cols);
+        if (u.after >= (int32_t)i || u.after < -1)
+            return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u: after=%d is not an earlier task", i, u.after);
+        // a hop (grid barriers, x conversion) where the input changes, or where an `after`
+        // task has not been behind a barrier yet
+        const bool hop = i == 0 || u.x_source != tasks[i - 1].x_source || (u.after >= 0 && u.after >= last_hop);
+        if (hop) {
+            ++hops;
+            last_hop = (int)i;
+            gpos = 0;
+        }
+        max_group = std::max(max_group, gpos + 1);
+        MmaTask& T = ht[i];
+        memset(&T, 0, sizeof(T));
+        const uint64_t rb = u.cols / 32 * 18;
+        const cuuint64_t dims[2] = {(cuuint64_t)rb, (cuuint64_t)u.rows};
+        const cuuint64_t strides[1] = {(cuuint64_t)rb};
+        const cuuint32_t box[2] = {(cuuint32_t)kRawRowBytes, (cuuint32_t)kMmaRows};
+        const cuuint32_t estr[2] = {1, 1};
+        if (encode(&T.tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(u.W), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return fail(NEXUS_GPU_ERROR_CUDA, "task %u: weight tensor map rejected", i);
+        T.x = u.x_source < 0 ? nullptr : tasks[u.x_source].y;
+        T.y = u.y;
+        T.N = (int)u.rows;
+        T.K = (int)u.cols;
+        T.tiles = (int)((u.rows + kMmaRows - 1) / kMmaRows);
+        T.n_chunks = (int)(u.cols / kRawK);
+        T.total = (long long)T.tiles * T.n_chunks;
+        T.G = (int)std::max<long long>(1, std::min<long long>(G, T.total / 2));
+        T.hop = hop ? 1 : 0;
+        T.hidx = hops - 1;
+        T.gpos = gpos++;
+        arr_off[i] = arr_words;
+        arr_words += (size_t)T.tiles;
+        kmax = std::max(kmax, T.K);
+    }
+    // device block: tasks (64-byte aligned maps), fp16 x, scales, partial sums, arrival
+    // counters, grid barrier / run / exit counters and the abort flag
+    size_t off = 0;
+    const size_t o_tasks = off;
+    off = align256(off + n * sizeof(MmaTask));
+    const size_t o_x = off;
+    off = align256(off + (size_t)NB * kmax * sizeof(__half));
+    const size_t o_scale = off;
+    off = align256(off + kMaxTokens * sizeof(float));
+    const size_t o_part = off;
+    off = align256(off + (size_t)G * 2 * max_group * NB * kMmaRows * sizeof(float));
+    const size_t o_arr = off;
+    off = align256(off + arr_words * sizeof(unsigned));
+    const size_t o_ctrl = off;
+    off = align256(off + 5 * sizeof(unsigned long long));
+    auto h = new StackHandle();
+    h->dev = d->id;
+    h->dtype = dtype;
+    h->grid = G;
+    h->n_tasks = (int)n;
+    h->tokens = tokens;
+    h->mma = true;
+    cudaError_t e = cudaMalloc(&h->d_block, off);
+    if (e == cudaSuccess) e = cudaMemset(h->d_block, 0, off);
+    if (e != cudaSuccess) {
+        stack_free(h);
+        cudaGetLastError();
+        return fail(NEXUS_GPU_ERROR_OUT_OF_TIER0_MEMORY, "stack allocation failed: %s", cudaGetErrorString(e));
+    }
+    uint8_t* blk = h->d_block;
+    for (uint32_t i = 0; i < n; ++i) ht[i].arrivals = reinterpret_cast<unsigned*>(blk + o_arr) + arr_off[i];
+    e = cudaMemcpy(blk + o_tasks, ht.data(), n * sizeof(MmaTask), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        stack_free(h);
+        return fail(NEXUS_GPU_ERROR_CUDA, "stack upload failed: %s", cudaGetErrorString(e));
+    }
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)kmax, (cuuint64_t)NB};
+        const cuuint64_t strides[1] = {(cuuint64_t)kmax * sizeof(__half)};
+        const cuuint32_t box[2] = {(cuuint32_t)kUnitK, (cuuint32_t)NB};
+        const cuuint32_t estr[2] = {1, 1};
+        if (encode(&h->tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, blk + o_x, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+            stack_free(h);
+            return fail(NEXUS_GPU_ERROR_CUDA, "activation tensor map rejected (%d x %d)", NB, kmax);
+        }
+    }
+    MmaStackParams& P = h->mparams;
+    P.tasks = reinterpret_cast<const MmaTask*>(blk + o_tasks);
+    P.n_tasks = (int)n;
+    P.n_hops = hops;
+    P.M = tokens;
+    P.NB = NB;
+    P.kmax = kmax;
+    P.b_stages = std::min(kMaxBStages, kBRingBytes / (NB * 512));
+    P.xbuf = reinterpret_cast<__half*>(blk + o_x);
+    P.xscale = reinterpret_cast<float*>(blk + o_scale);
+    P.partial = reinterpret_cast<float*>(blk + o_part);
+    P.slots = 2 * max_group;
+    unsigned long long* ctrl = reinterpret_cast<unsigned long long*>(blk + o_ctrl);
+    P.bar_done = ctrl;
+    P.bar_pub = ctrl + 1;
+    P.epoch = ctrl + 2;
+    P.fin = ctrl + 3;
+    P.abort_flag = reinterpret_cast<unsigned*>(ctrl + 4);
+    h->params.abort_flag = P.abort_flag;  // nexus_gpu_stack_wait reads it
+    h->outputs.resize(n);
+    for (uint32_t i = 0; i < n; ++i) h->outputs[i] = tasks[i].y;
+    auto attrs = [&]() -> int32_t {
+        CUDA_TRY(cudaFuncSetAttribute(gemm_q4_0_mma_stack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      kMmaStackSmemBytes));
+        int per_sm = 0;
+        CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemm_q4_0_mma_stack_kernel, kMmaThreads,
+                                                               kMmaStackSmemBytes));
+        if (per_sm < 1) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "tensor-core stack kernel cannot be resident");
+        return NEXUS_GPU_SUCCESS;
+    };
+    if ((rc = attrs())) {
+        stack_free(h);
+        return rc;
+    }
+    *out = h;
+    return NEXUS_GPU_SUCCESS;
+}
+
+int32_t mma_stack_launch(StackHandle& h, const float* x_in, cudaStream_t st) {
+    h.mparams.x_in = x_in;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(h.grid);
+    cfg.blockDim = dim3(kMmaThreads);
+    cfg.dynamicSmemBytes = kMmaStackSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // CTAs wait on one another at grid barriers: all resident
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_q4_0_mma_stack_kernel, h.tmX, h.mparams));
+    return NEXUS_GPU_SUCCESS;
+}
+
 int32_t stack_current_device(const StackHandle* h) {
     int cur = -1;
     CUDA_TRY(cudaGetDevice(&cur));
@@ -1447,6 +1642,7 @@ int32_t stack_run(void* handle, const float* x_in, cudaStream_t st) {
     if (!h->connected) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "sharded stack not connected to its peers");
     int32_t rc = stack_current_device(h);
     if (rc) return rc;
+    if (h->mma) return mma_stack_launch(*h, x_in, st);
     h->params.x_in = x_in;
     switch (h->dtype) {
         case NEXUS_GPU_GGUF_Q4_0: return stack_launch_for<FmtQ4_0>(*h, st);
@@ -1723,7 +1919,7 @@ NEXUS_GPU_API int32_t nexus_gpu_stack_create_tokens(uint32_t dtype, const NexusG
     t_last_error.clear();
     const auto ex = plain_tasks(tasks, n_tasks);
     return stack_create(dtype, tasks ? ex.data() : nullptr, n_tasks, input_cols, 1, 0, out_stack,
-                        tokens > (uint32_t)kMaxStackTokens ? kMaxStackTokens + 1 : (int)tokens);
+                        tokens > (uint32_t)kMaxTokens ? kMaxTokens + 1 : (int)tokens);
 }
 
 NEXUS_GPU_API int32_t nexus_gpu_stack_create_ex(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t n_tasks,
