@@ -226,18 +226,22 @@ NEXUS_GPU_API int32_t nexus_gpu_stack_create(uint32_t dtype, const NexusGpuStack
 NEXUS_GPU_API int32_t nexus_gpu_stack_run(void* stack, const float* dX, void* stream);
 NEXUS_GPU_API int32_t nexus_gpu_stack_destroy(void* stack);
 
-/* A stack for `tokens` activation vectors per run (2..4): batched decode of
- * that many requests below the tensor-core range (M >= 16 takes tcgen05
- * tiles through nexus_gpu_gemv).  Every weight is read from HBM once per run,
- * not once per token; the reference decodes the requests one after another
+/* A stack for `tokens` activation vectors per run: batched decode of that
+ * many requests.  Every weight is read from HBM once per run, not once per
+ * token; the reference decodes the requests one after another
  * (src/forward_pass.cpp:633-667).  The tasks are those of
  * nexus_gpu_stack_create; each tasks[i].y holds tokens * rows floats (token t
  * at y + t * rows, 16-byte aligned), and nexus_gpu_stack_run's dX holds
- * tokens * input_cols floats (token t at dX + t * input_cols).  Unsharded,
- * integer GGUF formats.  Each token's outputs are within the GEMV tolerance
- * of the single-token stack on that token (same arithmetic, another fixed
- * summation order).  tokens = 1 is nexus_gpu_stack_create.  No counterpart in
- * the reference. */
+ * tokens * input_cols floats (token t at dX + t * input_cols).  Unsharded.
+ *  - tokens 2..4: CUDA cores, integer GGUF formats.  Each token's outputs are
+ *    within the GEMV tolerance of the single-token stack on that token (same
+ *    arithmetic, another fixed summation order).
+ *  - tokens 16..64: tcgen05 tensor cores, GGUF Q4_0, every task's cols a
+ *    multiple of 256; one persistent launch whose CTAs meet at grid barriers
+ *    where a task's input changes.  Each task's outputs are within 1e-6 of
+ *    nexus_gpu_gemv with `tokens` rows on the same input.
+ *  - tokens = 1 is nexus_gpu_stack_create; other counts are refused.
+ * No counterpart in the reference. */
 NEXUS_GPU_API int32_t nexus_gpu_stack_create_tokens(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n_tasks,
                                                     uint64_t input_cols, uint32_t tokens, void** out_stack);
 
