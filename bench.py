@@ -1721,7 +1721,51 @@ def model_70b(torch, L, world, rank, local, dev, timed, peak, args, pg):
     del g16
     gbs16 = (sum(weight_bytes(DTYPE, n, k) for _, n, k in shapes_of(m)) * m["layers"] +
              weight_bytes(DTYPE, m["vocab"], m["hidden"])) / (ms16 * 1e-3) / 1e9
-    out["m16"] = {"ms": round(ms16, 4), "tok_s": round(M * 1e3 / ms16, 1), "agg_weight_GBs": round(gbs16, 1)}
+    out["m16"] = {"ms": round(ms16, 4), "tok_s": round(M * 1e3 / ms16, 1), "agg_weight_GBs": round(gbs16, 1),
+                  "path": "tcgen05 per GEMV" + (" + NCCL all-gathers" if world > 1 else "")}
+    if world == 1:
+        # ---- m16 as one tensor-core stack launch per step (the same GEMVs and inputs)
+        import ctypes
+
+        from nexusllm_b200 import _native
+
+        tasks, ys = [], []
+        src_of = {"q": -1, "k": -1, "v": -1, "o": 0, "gate": 3, "up": 3, "down": 4}
+        for mats in layers:
+            b0 = len(tasks)
+            for name, n, k in shapes_of(m):
+                y = torch.empty(M, n, device=dev)
+                ys.append(y)
+                src = src_of[name]
+                tasks.append(_native.StackTask(mats[name].data_ptr(), n, k, y.data_ptr(), src if src < 0 else b0 + src,
+                                               -1))
+        y = torch.empty(M, m["vocab"], device=dev)
+        ys.append(y)
+        tasks.append(_native.StackTask(head.data_ptr(), m["vocab"], m["hidden"], y.data_ptr(), -1, -1))
+        arr = (_native.StackTask * len(tasks))(*tasks)
+        hs = ctypes.c_void_p()
+        _native_check(L.nexus_gpu_stack_create_tokens(DTYPE, arr, len(tasks), m["hidden"], M, ctypes.byref(hs)))
+        try:
+            gs = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                _native_check(L.nexus_gpu_stack_run(hs, X0.data_ptr(), stream.cuda_stream))
+                torch.cuda.synchronize(dev)
+                with torch.cuda.graph(gs, stream=stream):
+                    _native_check(L.nexus_gpu_stack_run(hs, X0.data_ptr(), stream.cuda_stream))
+                for _ in range(3):
+                    gs.replay()
+            mss = timed(gs.replay, reps16) / reps16
+            check_status(L)
+            # the LM head of the stack equals the per-GEMV path's (same input, same arithmetic)
+            err16 = float(torch.linalg.vector_norm(ys[-1] - full["head"]) / torch.linalg.vector_norm(full["head"]))
+            del gs
+        finally:
+            L.nexus_gpu_stack_destroy(hs)
+        gbss = gbs16 * ms16 / mss
+        out["m16_stack"] = {"ms": round(mss, 4), "tok_s": round(M * 1e3 / mss, 1), "agg_weight_GBs": round(gbss, 1),
+                            "path": "tcgen05 GEMV stack, one launch per step",
+                            "head_vs_per_gemv_l2_rel": float(f"{err16:.3e}")}
+        del ys
     del layers, head, ws, full, part, gath
     torch.cuda.empty_cache()
     return out

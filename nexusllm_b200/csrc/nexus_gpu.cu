@@ -940,21 +940,25 @@ int32_t stack_kernel_attrs(const Device& d, size_t smem) {
     return NEXUS_GPU_SUCCESS;
 }
 
-template <class F, int MT>
+template <class F, int MT, int G>
 int32_t stack_mt_kernel_attrs(const Device& d, size_t smem) {
-    CUDA_TRY(cudaFuncSetAttribute(gemv_stack_mt_kernel<F, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    CUDA_TRY(cudaFuncSetAttribute(gemv_stack_mt_kernel<F, MT, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   d.smem_optin));
     int per_sm = 0;
-    CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_stack_mt_kernel<F, MT>, kGemvThreads, smem));
+    CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_stack_mt_kernel<F, MT, G>, kGemvThreads, smem));
     if (per_sm < 1) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "stack kernel cannot be resident (smem %zu)", smem);
     return NEXUS_GPU_SUCCESS;
 }
 
 template <class F>
 int32_t stack_attrs_for(int group, bool fused, int tokens, const Device& d, size_t smem) {
-    if (tokens == 2) return stack_mt_kernel_attrs<F, 2>(d, smem);
-    if (tokens == 3) return stack_mt_kernel_attrs<F, 3>(d, smem);
-    if (tokens == 4) return stack_mt_kernel_attrs<F, 4>(d, smem);
+    if (tokens == 2) {
+        if constexpr (F::kGroup == 2)
+            if (group == 2) return stack_mt_kernel_attrs<F, 2, 2>(d, smem);
+        return stack_mt_kernel_attrs<F, 2, 1>(d, smem);
+    }
+    if (tokens == 3) return stack_mt_kernel_attrs<F, 3, 1>(d, smem);
+    if (tokens == 4) return stack_mt_kernel_attrs<F, 4, 1>(d, smem);
     const bool grouped = F::kGroup > 1 && group == F::kGroup;
     if (fused) return grouped ? stack_kernel_attrs<F, F::kGroup, true>(d, smem) : stack_kernel_attrs<F, 1, true>(d, smem);
     return grouped ? stack_kernel_attrs<F, F::kGroup, false>(d, smem) : stack_kernel_attrs<F, 1, false>(d, smem);
@@ -973,9 +977,17 @@ int32_t stack_launch_for(const StackHandle& h, cudaStream_t st) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     if (h.tokens > 1) {
-        if (h.tokens == 2) CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stack_mt_kernel<F, 2>, h.params));
-        else if (h.tokens == 3) CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stack_mt_kernel<F, 3>, h.params));
-        else CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stack_mt_kernel<F, 4>, h.params));
+        bool paired = false;
+        if constexpr (F::kGroup == 2) paired = h.group == 2;
+        if (h.tokens == 2 && paired) {
+            if constexpr (F::kGroup == 2) CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stack_mt_kernel<F, 2, F::kGroup>, h.params));
+        } else if (h.tokens == 2) {
+            CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stack_mt_kernel<F, 2, 1>, h.params));
+        } else if (h.tokens == 3) {
+            CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stack_mt_kernel<F, 3, 1>, h.params));
+        } else {
+            CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stack_mt_kernel<F, 4, 1>, h.params));
+        }
         return NEXUS_GPU_SUCCESS;
     }
     const bool grouped = F::kGroup > 1 && h.group == F::kGroup;
@@ -1122,7 +1134,8 @@ int32_t stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t 
         // multi-token stacks: one (two for 2 tokens) single-block work items per lane, smaller stages
         const bool ok_plan = tokens > 1
                                  ? plan_for(dtype, *d, (int)local_rows[i], (int)u.cols, rb, gp, sm, kStageTargetBytes,
-                                            kMaxJ / (tokens == 2 ? 2 : 4), false)
+                                            kMaxJ / (tokens == 2 ? 2 : 4),
+                                            tokens == 2 && (dtype == NEXUS_GPU_GGUF_Q4_0 || dtype == NEXUS_GPU_GGUF_Q8_0))
                                  : plan_for(dtype, *d, (int)local_rows[i], (int)u.cols, u.W_up ? 2 * rb : rb, gp, sm,
                                             kStackStageTargetBytes);
         if (!ok_plan)

@@ -14,7 +14,8 @@
 //    the library's 16-bit fixed point (quantize_x_pair, the same rule as
 //    every other path), token t in its own plane set.
 //  * A lane holds, for its work items (one 32-weight item per lane when MT >
-//    2, two when MT == 2), the x slices of every token in registers.  It
+//    2, two when MT == 2 -- a block pair for Q4_0 and Q8_0), the x slices of
+//    every token in registers.  It
 //    decodes a weight item once and takes its exact int32 dp2a dot product
 //    with each token's slice (Q4_0, Q8_0; the K-quant formats re-read the
 //    item per token), scaled once per item and token as the reference scales
@@ -62,6 +63,43 @@ __device__ __forceinline__ void dot_item_mt(uint32_t b, int wi, const XInt (&X)[
     }
 }
 
+// Two consecutive Q4_0 / Q8_0 blocks (a lane's pair of items when MT == 2) at
+// a 4-byte-aligned shared address against MT tokens' slices of each: one
+// realignment for both blocks, and lanes 9 (Q4_0) or 17 (Q8_0) words apart,
+// so their shared loads do not conflict.
+template <class F, int MT>
+__device__ __forceinline__ void dot_pair_mt(uint32_t p, const XInt (&X0)[MT], const XInt (&X1)[MT],
+                                            float (&acc)[MT]) {
+    if constexpr (F::kBlockBytes == 18) {
+        uint32_t w[9];
+#pragma unroll
+        for (int k = 0; k < 9; ++k) w[k] = lds32(p + 4 * k);
+        uint32_t q0[4], q1[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            q0[k] = __byte_perm(w[k], w[k + 1], 0x5432);  // bytes 2..17
+            q1[k] = w[5 + k];                             // bytes 20..35
+        }
+        const float d0 = nexus_fp16(w[0] & 0xffffu), d1 = nexus_fp16_hi(w[4]);
+#pragma unroll
+        for (int t = 0; t < MT; ++t) acc[t] += q4_0_block(d0, q0, X0[t]) + q4_0_block(d1, q1, X1[t]);
+    } else {
+        static_assert(F::kBlockBytes == 34, "block pairs serve Q4_0 and Q8_0");
+        uint32_t w[17];
+#pragma unroll
+        for (int k = 0; k < 17; ++k) w[k] = lds32(p + 4 * k);
+        uint32_t q0[8], q1[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            q0[k] = __byte_perm(w[k], w[k + 1], 0x5432);  // bytes 2..33
+            q1[k] = w[9 + k];                             // bytes 36..67
+        }
+        const float d0 = nexus_fp16(w[0] & 0xffffu), d1 = nexus_fp16_hi(w[8]);
+#pragma unroll
+        for (int t = 0; t < MT; ++t) acc[t] += q8_0_block(d0, q0, X0[t]) + q8_0_block(d1, q1, X1[t]);
+    }
+}
+
 // The token whose full sum lane `lane` holds after reduce_tokens, and whether
 // the lane is the one that stores it.
 template <int MT>
@@ -104,10 +142,12 @@ __device__ __forceinline__ void put_row_mt(float* y, uint32_t* tg, int N, uint32
     if (tg) st_tagged(tg + (size_t)t * N + r, v, par, false);
 }
 
-template <class F, int MT>
+// G = 2: a lane's two items are a block pair (MT == 2, Q4_0 / Q8_0).
+template <class F, int MT, int G>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_mt_kernel(const StackParams P) {
     static_assert(F::kIntX, "the stack kernel serves the integer formats");
     constexpr int JM = MtPlan<MT>::kJ;
+    static_assert(G == 1 || (G == 2 && JM == 2 && F::kGroup == 2), "block pairs: two tokens, Q4_0 or Q8_0");
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t sbase = smem_u32(smem);
     const uint32_t full_bar = sbase;
@@ -182,7 +222,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_mt_kernel(const St
         const int sg = warp % S, grp = warp / S, n_grp = kConsumerWarps / S;
         int wi4[kMaxJ];
         bool has4[kMaxJ];
-        lane_items<1>(lane, sg, SW, J, NW, wi4, has4);
+        lane_items<G>(lane, sg, SW, J, NW, wi4, has4);
         int wi[JM];
         bool has[JM];
         XInt X[JM][MT];
@@ -221,9 +261,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_mt_kernel(const St
                         float acc[MT];
 #pragma unroll
                         for (int k = 0; k < MT; ++k) acc[k] = 0.0f;
+                        if constexpr (G == 2) {
+                            if (has[0]) dot_pair_mt<F, MT>(row + wi_offset<F>(wi[0]), X[0], X[1], acc);
+                        } else {
 #pragma unroll
-                        for (int j = 0; j < JM; ++j)
-                            if (has[j]) dot_item_mt<F, MT>(row + wi_offset<F>(wi[j]), wi[j], X[j], acc);
+                            for (int j = 0; j < JM; ++j)
+                                if (has[j]) dot_item_mt<F, MT>(row + wi_offset<F>(wi[j]), wi[j], X[j], acc);
+                        }
                         const float v = reduce_tokens<MT>(acc, lane);
                         if (token_lead<MT>(lane)) {
                             const int tk = token_of<MT>(lane);
