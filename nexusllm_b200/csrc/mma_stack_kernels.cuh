@@ -280,30 +280,33 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         uint32_t r_issued = 0, x_issued = 0;
         int waited = -1;  // the last hop whose x this warp saw published
         bool ok = *abort == 0;
-        while (ok && xk.t < P.n_tasks) {
-            // raw chunks up to kRawStages ahead of the x tiles: weights depend on nothing, so
-            // they stream across a hop's barriers.  Raw chunk j reuses the slot of chunk
-            // j - kRawStages, whose x tile is already issued, so its MMA can free it.
-            while (rk.t < P.n_tasks && r_issued < x_issued + kRawStages) {
-                if (r_issued >= kRawStages && !warp_wait(raw_empty + 8 * rp.stage, rp.phase ^ 1u, abort)) {
-                    ok = false;
-                    break;
-                }
-                if (leader) {
-                    const int tile = (int)(rk.L / rk.nc), c = (int)(rk.L - (long long)tile * rk.nc);
-                    mbar_arrive_expect_tx(raw_full + 8 * rp.stage, kRawChunkBytes);
-                    tma_load_2d(sbase + kMmaSmemRaw + rp.stage * kRawChunkBytes, &P.tasks[rk.t].tmW, c * kRawRowBytes,
-                                tile * kMmaRows, raw_full + 8 * rp.stage);
-                }
-                __syncwarp();
-                ++r_issued;
-                rp.next(kRawStages);
-                mma_cursor_next(rk, P, b);
+        // issue raw chunk rk (waiting for its ring slot: the MMA of the chunk kRawStages
+        // earlier, whose x tile is already issued)
+        auto issue_raw = [&]() -> bool {
+            if (r_issued >= kRawStages && !warp_wait(raw_empty + 8 * rp.stage, rp.phase ^ 1u, abort)) return false;
+            if (leader) {
+                const int tile = (int)(rk.L / rk.nc), c = (int)(rk.L - (long long)tile * rk.nc);
+                mbar_arrive_expect_tx(raw_full + 8 * rp.stage, kRawChunkBytes);
+                tma_load_2d(sbase + kMmaSmemRaw + rp.stage * kRawChunkBytes, &P.tasks[rk.t].tmW, c * kRawRowBytes,
+                            tile * kMmaRows, raw_full + 8 * rp.stage);
             }
+            __syncwarp();
+            ++r_issued;
+            rp.next(kRawStages);
+            mma_cursor_next(rk, P, b);
+            return true;
+        };
+        while (ok && xk.t < P.n_tasks) {
+            // chunk j: its raw chunk, then its x tile, as the single GEMM issues them (both
+            // rings several chunks ahead of the MMAs)
+            while (ok && r_issued <= x_issued) ok = issue_raw();
             if (!ok) break;
-            // the next x tile: its hop's conversion published (bar_pub), then made
-            // visible to the tensor-copy (async) proxy
             if (xk.hidx > waited) {
+                // a hop's input: first the raw chunks up to kRawStages ahead (weights depend on
+                // nothing, so they stream across the barriers), then wait until the input is
+                // converted and published (bar_pub), made visible to the tensor-copy proxy
+                while (ok && rk.t < P.n_tasks && r_issued < x_issued + kRawStages) ok = issue_raw();
+                if (!ok) break;
                 bool go = true;
                 if (leader) {
                     go = grid_wait(P.bar_pub, pub_target(run, P.n_hops, xk.hidx, gridDim.x), P.abort_flag);
