@@ -514,7 +514,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
                     const int tok = tok_lo + j;
                     if (tok < tok_hi) mine[(size_t)tok * kMmaRows + r] = v[j];
                 }
-                __threadfence();
+                // the warps' partial stores reach the leader through part_done (CTA scope);
+                // its one GPU-scope fence then orders all of them before its arrival
                 __syncwarp();
                 if (lane == 0) mbar_arrive(part_done);
                 const int bf = sk_owner(total, G, (long long)tile * nc);
@@ -524,8 +525,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
                     if (mma_wait(part_done, n_part & 1, abort)) {
                         // the counter only grows: each run adds one arrival per sharing CTA
                         const unsigned n = (unsigned)(bl - bf + 1);
+                        __threadfence();  // release this CTA's partial sums ...
                         last = atomicAdd(arrivals + tile, 1u) % n == n - 1;
-                        __threadfence();
+                        __threadfence();  // ... and, for the last CTA, acquire the others'
                     }
                     *last_flag = last ? 1 : 0;
                     mbar_arrive(decided);
@@ -536,10 +538,10 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
                 }
                 ++n_part;
                 if (*last_flag && !*abort) {
-                    // the last CTA to finish the tile adds every partial in CTA order
-                    __threadfence();
+                    // the last CTA to finish the tile adds every partial in CTA order (the
+                    // leader's fence after its arrival acquired them; decided passes it on)
                     const int n4 = NB * (kMmaRows / 4);
-                    constexpr int kFixBatch = 4;
+                    constexpr int kFixBatch = 6;
                     for (int f = tid; f < n4; f += kDequantThreads) {
                         const int tok = f / (kMmaRows / 4);
                         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
