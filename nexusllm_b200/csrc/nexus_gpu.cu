@@ -104,14 +104,28 @@ struct TcPlan {
     int tiles, n_chunks, G;
     long long total;
 };
-// One persistent CTA per SM over the tiles x chunks sequence (stream-K), at
-// least two chunks a CTA.
+// CTAs of a tensor-core GEMM.  A tile-aligned split -- s CTAs a tile, s
+// dividing the tile's chunks, at least 2 chunks each -- when it keeps at least
+// 85 % of the SMs busy: every CTA then works on one tile, and a shared tile
+// has one fix-up.  Otherwise stream-K over every SM (at least 2 chunks a CTA),
+// where the CTAs whose range crosses a tile boundary carry two epilogues and
+// often a fix-up.
+int tc_ctas(int sms, int tiles, int n_chunks) {
+    const long long total = (long long)tiles * n_chunks;
+    for (int s = n_chunks / 2; s >= 1; --s)
+        if (n_chunks % s == 0 && (long long)tiles * s <= sms) {
+            if ((long long)tiles * s * 100 >= 85LL * sms) return tiles * s;
+            break;
+        }
+    return (int)std::max<long long>(1, std::min<long long>(sms, total / 2));
+}
+// At most one persistent CTA per SM over the tiles x chunks sequence.
 TcPlan tc_plan(int sms, size_t rows, size_t cols) {
     TcPlan p;
     p.n_chunks = (int)(cols / kRawK);
     p.tiles = (int)((rows + kMmaRows - 1) / kMmaRows);
     p.total = (long long)p.tiles * p.n_chunks;
-    p.G = (int)std::max<long long>(1, std::min<long long>(sms, p.total / 2));
+    p.G = tc_ctas(sms, p.tiles, p.n_chunks);
     return p;
 }
 // Workspace of one token group (<= kMaxTokens): the B operand (fp16 rows),
@@ -1384,7 +1398,7 @@ int32_t mma_stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint3
         T.tiles = (int)((u.rows + kMmaRows - 1) / kMmaRows);
         T.n_chunks = (int)(u.cols / kRawK);
         T.total = (long long)T.tiles * T.n_chunks;
-        T.G = (int)std::max<long long>(1, std::min<long long>(G, T.total / 2));
+        T.G = tc_ctas(G, T.tiles, T.n_chunks);
         T.hop = hop ? 1 : 0;
         T.hidx = hops - 1;
         T.gpos = gpos++;

@@ -175,11 +175,23 @@ def sk_owner(total, G, L):
     return b
 
 
+def tc_ctas(sms, tiles, n_chunks):
+    """Mirror of tc_ctas: a tile-aligned split (s CTAs a tile, s dividing the
+    chunks, >= 2 chunks each) when it keeps >= 85 % of the SMs busy, else
+    stream-K over every SM with >= 2 chunks a CTA."""
+    for s in range(n_chunks // 2, 0, -1):
+        if n_chunks % s == 0 and tiles * s <= sms:
+            if tiles * s * 100 >= 85 * sms:
+                return tiles * s
+            break
+    return max(1, min(sms, tiles * n_chunks // 2))
+
+
 def plan(sms, rows, cols):
     n_chunks = cols // RAW_K
     tiles = (rows + ROWS - 1) // ROWS
     total = tiles * n_chunks
-    G = max(1, min(sms, total // 2))
+    G = tc_ctas(sms, tiles, n_chunks)
     return tiles, n_chunks, total, G
 
 

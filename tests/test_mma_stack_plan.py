@@ -18,7 +18,7 @@ import random
 
 import pytest
 
-from tests.test_mma_plan import SMEM_BYTES, sk_lo, sk_owner
+from tests.test_mma_plan import SMEM_BYTES, sk_lo, sk_owner, tc_ctas
 
 ROWS, RAW_K = 128, 256
 SMS = 148
@@ -40,7 +40,7 @@ def stack_plan(tasks, input_cols, sms=SMS):
         nc = cols // RAW_K
         total = tiles * nc
         plan.append(dict(rows=rows, cols=cols, tiles=tiles, nc=nc, total=total,
-                         G=max(1, min(sms, total // 2)), hop=hop, hidx=hops - 1, gpos=gpos))
+                         G=tc_ctas(sms, tiles, nc), hop=hop, hidx=hops - 1, gpos=gpos))
         gpos += 1
     return plan, hops
 
