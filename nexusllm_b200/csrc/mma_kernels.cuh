@@ -247,6 +247,40 @@ __device__ __forceinline__ void q4_unit_tmem(uint32_t raw_row, uint32_t ta) {
     tmem_st16(ta + 32 * U, wa);
     tmem_st16(ta + 32 * U + 16, wb);
 }
+// The same, one block at a time: block 2U's 16 columns are stored before block
+// 2U+1 is decoded (fewer live registers, for kernels with more warps).
+template <int U>
+__device__ __forceinline__ void q4_unit_tmem_lean(uint32_t raw_row, uint32_t ta) {
+    uint32_t g[12];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const uint4 v = lds128(raw_row + 32 * U + 16 * k);
+        g[4 * k] = v.x;
+        g[4 * k + 1] = v.y;
+        g[4 * k + 2] = v.z;
+        g[4 * k + 3] = v.w;
+    }
+    uint32_t w[16];
+    const uint32_t dA = q4_scale_h2(g[U]), dB = q4_scale_h2(g[U + 4] >> 16);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 o = q4_word_f16(i == 0 ? __byte_perm(g[U], g[U + 4], 0x5432) : g[U + i], dA);
+        w[4 * i] = o.x;
+        w[4 * i + 1] = o.y;
+        w[4 * i + 2] = o.z;
+        w[4 * i + 3] = o.w;
+    }
+    tmem_st16(ta + 32 * U, w);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 e = q4_word_f16(g[U + 5 + i], dB);
+        w[4 * i] = e.x;
+        w[4 * i + 1] = e.y;
+        w[4 * i + 2] = e.z;
+        w[4 * i + 3] = e.w;
+    }
+    tmem_st16(ta + 32 * U + 16, w);
+}
 
 // Element of a 32-weight block stored at K position p (0..31) of the block by
 // q4_unit_decode: word i = p / 8 covers code bytes beta_i (block parity `odd`),

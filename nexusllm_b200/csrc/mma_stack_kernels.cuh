@@ -209,9 +209,49 @@ __device__ __forceinline__ void mma_convert_token(const MmaStackParams& P, const
     if (tid == 0) P.xscale[b] = real ? ldexpf(1.0f, ex) : 0.0f;
 }
 
-constexpr int kMmaStackSmemBytes = kMmaSmemBytes + 96;  // + the hop decision and 16 warp maxima
+// Warps of the stack kernel: the single GEMM's eighteen (copies, MMA, sixteen
+// dequantizing warps) and eight epilogue warps (warps 18..25, tensor-memory
+// lane quarters 2, 3, 0, 1 twice; the two halves take alternate groups of 16
+// tokens).  The epilogue warps read a finished accumulator, store y or the
+// partial sums and run the fix-up, while the other warps go on with the next
+// tile segment in the second accumulator.
+constexpr int kEpiWarps = 8;
+constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kEpiWarp0 = kMmaThreads / 32;
+constexpr int kMmaStackThreads = kMmaThreads + kEpiThreads;
+// Tensor memory: accumulator 0 in columns [0, 64), the A stages, accumulator
+// 1 in the last 64 columns.
+constexpr int kAcc1Col = kAccCols + kAStageCols * kAStages;
+static_assert(kAcc1Col + kAccCols <= kTmemCols, "two accumulators and the A stages exceed tensor memory");
+// + the hop decision, 16 warp maxima and the second accumulator's two barriers
+constexpr int kMmaStackSmemBytes = kMmaSmemBytes + 128;
 
-__global__ void __launch_bounds__(kMmaThreads, 1)
+// The hop barrier of the dequantizing and the epilogue warps (named barrier 2).
+__device__ __forceinline__ void hop_bar() {
+    asm volatile("bar.sync 2, %0;" ::"n"(kDequantThreads + kEpiThreads) : "memory");
+}
+
+// 16 consecutive accumulator columns of this warp's 32 lanes.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Every task segment (one tile's chunks of a task, for this CTA) takes the
+// accumulator k % 2, k the CTA's segment count so far: the MMA warp waits for
+// the epilogue's release of its use k - 2, the epilogue warps for its commit.
+// Neither the dequantizing nor the epilogue warps ever leave the task walk
+// early: both meet at the hop barrier of every hop, also after a failed wait
+// (they then skip all work), so the named barrier always completes.
+__global__ void __launch_bounds__(kMmaStackThreads, 1)
     gemm_q4_0_mma_stack_kernel(const __grid_constant__ CUtensorMap tmX, const MmaStackParams P) {
     extern __shared__ uint8_t mma_smem_raw[];
     const uint32_t sraw = smem_u32(mma_smem_raw);
@@ -221,13 +261,14 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     const uint32_t raw_full = bar0, raw_empty = raw_full + 8 * kRawStages;
     const uint32_t a_full = raw_empty + 8 * kRawStages, a_empty = a_full + 8 * kAStages;
     const uint32_t b_full = a_empty + 8 * kAStages, b_empty = b_full + 8 * kMaxBStages;
-    const uint32_t acc_full = b_empty + 8 * kMaxBStages, acc_empty = acc_full + 8, drain = acc_empty + 8;
+    const uint32_t acc_full0 = b_empty + 8 * kMaxBStages, acc_empty0 = acc_full0 + 8, drain = acc_empty0 + 8;
     const uint32_t part_done = drain + 8, decided = part_done + 8;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kMmaSmemBar + 8 * kMmaBarCount);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
     volatile int* s_go = reinterpret_cast<volatile int*>(tmem_slot + 3);
     volatile uint32_t* s_red = tmem_slot + 4;  // [16]
+    const uint32_t acc_full1 = smem_u32(tmem_slot + 20), acc_empty1 = acc_full1 + 8;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int b = blockIdx.x, NB = P.NB;
@@ -248,10 +289,12 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
             mbar_init(b_full + 8 * s, 1);
             mbar_init(b_empty + 8 * s, 1);
         }
-        mbar_init(acc_full, 1);
-        mbar_init(acc_empty, kDequantWarps);
+        mbar_init(acc_full0, 1);
+        mbar_init(acc_full1, 1);
+        mbar_init(acc_empty0, kEpiWarps);
+        mbar_init(acc_empty1, kEpiWarps);
         mbar_init(drain, 1);
-        mbar_init(part_done, kDequantWarps);
+        mbar_init(part_done, kEpiWarps);
         mbar_init(decided, 1);
         *abort = *reinterpret_cast<volatile unsigned*>(P.abort_flag) ? 1 : 0;  // a poisoned stack does nothing
         *last_flag = 0;
@@ -364,11 +407,13 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
             R.t1 = tr.t1;
             for (int tile = R.t0; tile <= R.t1 && ok; ++tile, ++k) {
                 const MmaSeg S = R.seg(tile, tr.nc);
-                if (k > 0 && !warp_wait(acc_empty, (k - 1) & 1, abort)) {
+                // accumulator k % 2: its use k - 2 read out by the epilogue warps
+                if (k >= 2 && !warp_wait((k & 1) ? acc_empty1 : acc_empty0, ((k >> 1) - 1) & 1, abort)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+                const uint32_t d = tmem_d + ((k & 1) ? (uint32_t)kAcc1Col : 0u);
                 for (int c = S.c0; c < S.c1; ++c, ap.next(kAStages), bp.next(nbs), rp.next(kRawStages)) {
                     if (!warp_wait(a_full + 8 * ap.stage, ap.phase, abort) ||
                         !warp_wait(b_full + 8 * bp.stage, bp.phase, abort)) {
@@ -382,10 +427,10 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
 #pragma unroll
                         for (int u = 0; u < kUnitsPerChunk; ++u) {
                             const uint64_t bu = b0 + (uint64_t)(u * b_unit16);
-                            umma_f16_tmem_a(tmem_d, a0 + 32 * u, bu, idesc, (c > S.c0 || u > 0) ? 1u : 0u);
-                            umma_f16_tmem_a(tmem_d, a0 + 32 * u + 8, bu + 2, idesc, 1u);
-                            umma_f16_tmem_a(tmem_d, a0 + 32 * u + 16, bu + 4, idesc, 1u);
-                            umma_f16_tmem_a(tmem_d, a0 + 32 * u + 24, bu + 6, idesc, 1u);
+                            umma_f16_tmem_a(d, a0 + 32 * u, bu, idesc, (c > S.c0 || u > 0) ? 1u : 0u);
+                            umma_f16_tmem_a(d, a0 + 32 * u + 8, bu + 2, idesc, 1u);
+                            umma_f16_tmem_a(d, a0 + 32 * u + 16, bu + 4, idesc, 1u);
+                            umma_f16_tmem_a(d, a0 + 32 * u + 24, bu + 6, idesc, 1u);
                         }
                         umma_commit(a_empty + 8 * ap.stage);
                         umma_commit(b_empty + 8 * bp.stage);
@@ -393,7 +438,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
                     }
                     __syncwarp();
                 }
-                if (ok && leader) umma_commit(acc_full);
+                if (ok && leader) umma_commit((k & 1) ? acc_full1 : acc_full0);
                 __syncwarp();
             }
         }
@@ -402,28 +447,25 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
             mbar_wait_bounded(drain, 0);
         }
         __syncwarp();
-    } else {
-        // ----------------------- hops (barriers, x conversion), dequantize, epilogue, fix-up
+    } else if (warp < kEpiWarp0) {
+        // ------------------------------- hops (barriers, x conversion) and the dequantization
         const int dw = warp - 2, grp = dw >> 2, quarter = warp & 3;
-        const int r = quarter * 32 + lane;  // accumulator lane = weight row of the tile
+        const int r = quarter * 32 + lane;  // tensor-memory lane = weight row of the tile
         const uint32_t lane_base = tmem_d + ((uint32_t)(quarter * 32) << 16);
         const bool leader = dw == 0 && lane == 0;
-        const int tid = (int)threadIdx.x - (kMmaThreads - kDequantThreads);
-        constexpr int kTokSlice = kMaxTokens / 4;
-        const int tok_lo = grp * (NB / 4), tok_hi = tok_lo + NB / 4;
+        const int tid = (int)threadIdx.x - 64;
         RingPos rp, ap;
-        uint32_t chunks = 0, n_part = 0;
-        int k = 0;  // segments so far: the accumulator's parity
+        uint32_t chunks = 0;
         bool ok = *abort == 0;
         for (int t = 0; t < P.n_tasks; ++t) {
             const MmaTask& T = P.tasks[t];
             if (__ldg(&T.hop)) {
                 // a new input: every CTA finished the tasks before it (which also ends every
-                // read of the x buffer), CTA b < NB converts token b, and the result is
-                // published at GPU scope for the other CTAs' tensor copies
+                // read of the x buffer and its scales), CTA b < NB converts token b, and the
+                // result is published at GPU scope for the other CTAs' tensor copies
                 const int hh = __ldg(&T.hidx);
                 if (!ok) *abort = 1;
-                dequant_bar();
+                hop_bar();  // with the epilogue warps, through every output before the hop
                 if (leader) {
                     bool go = *abort == 0;
                     if (go && hh > 0) {
@@ -433,87 +475,110 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
                     *s_go = (go && *abort == 0) ? 1 : 0;
                 }
                 dequant_bar();
-                if (!*s_go) {  // every dequantizing warp leaves together
+                if (!*s_go) {  // one verdict for every dequantizing warp: no more work
                     *abort = 1;
                     ok = false;
-                    break;
                 }
-                if (b < NB) {
-                    const float* x = reinterpret_cast<const float*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.x)));
-                    mma_convert_token(P, x != nullptr ? x : P.x_in, __ldg(&T.K), b, tid, s_red);
+                if (ok) {
+                    if (b < NB) {
+                        const float* x =
+                            reinterpret_cast<const float*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.x)));
+                        mma_convert_token(P, x != nullptr ? x : P.x_in, __ldg(&T.K), b, tid, s_red);
+                    }
+                    fence_proxy_async_global();
+                    dequant_bar();
+                    if (leader) grid_arrive(P.bar_pub);
                 }
-                fence_proxy_async_global();
-                dequant_bar();
-                if (leader) grid_arrive(P.bar_pub);
             }
             const MmaTaskRange tr = mma_task_range(T, b);
             if (!tr.any || !ok) continue;  // after a failed wait: no work, but the hops' structure
+            // this CTA's chunks of the task, in order (tile boundaries matter only to the MMA
+            // and epilogue warps)
+            for (long long L = tr.lo; L < tr.hi; ++L, ++chunks, rp.next(kRawStages), ap.next(kAStages)) {
+                if (!warp_wait(raw_full + 8 * rp.stage, rp.phase, abort) ||
+                    (chunks >= kAStages && !warp_wait(a_empty + 8 * ap.stage, ap.phase ^ 1u, abort))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t raw_row = sbase + kMmaSmemRaw + rp.stage * kRawChunkBytes + (uint32_t)r * kRawRowBytes;
+                const uint32_t ta = lane_base + kAccCols + kAStageCols * ap.stage;
+                switch (grp) {
+                    case 0: q4_unit_tmem_lean<0>(raw_row, ta); break;
+                    case 1: q4_unit_tmem_lean<1>(raw_row, ta); break;
+                    case 2: q4_unit_tmem_lean<2>(raw_row, ta); break;
+                    default: q4_unit_tmem_lean<3>(raw_row, ta); break;
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(a_full + 8 * ap.stage);
+            }
+        }
+        if (!ok) *abort = 1;
+    } else {
+        // ----------------------------- epilogue: accumulator read-out, y, partial sums, fix-up
+        const int quarter = warp & 3, half = (warp - kEpiWarp0) >> 2;
+        const int r = quarter * 32 + lane;  // tensor-memory lane = weight row of the tile
+        const uint32_t lane_base = tmem_d + ((uint32_t)(quarter * 32) << 16);
+        const bool leader = warp == kEpiWarp0 && lane == 0;
+        const int etid = (int)threadIdx.x - kMmaThreads;
+        uint32_t n_part = 0;
+        int k = 0;  // segments so far, as the MMA warp counts them
+        bool ok = *abort == 0;
+        for (int t = 0; t < P.n_tasks; ++t) {
+            const MmaTask& T = P.tasks[t];
+            if (__ldg(&T.hop)) {
+                if (!ok) *abort = 1;
+                hop_bar();  // every output before the hop is stored (and every xscale read done)
+            }
+            const MmaTaskRange tr = mma_task_range(T, b);
+            if (!tr.any) continue;
             MmaRange R;
             R.lo = tr.lo;
             R.hi = tr.hi;
             R.t0 = tr.t0;
             R.t1 = tr.t1;
-            const int nc = tr.nc, N = __ldg(&T.N), G = __ldg(&T.G);
+            const int nc = tr.nc, N = __ldg(&T.N), G = __ldg(&T.G), gp = __ldg(&T.gpos);
             const long long total = __ldg(&T.total);
             float* const y = reinterpret_cast<float*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.y)));
             unsigned* const arrivals =
                 reinterpret_cast<unsigned*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.arrivals)));
-            for (int tile = R.t0; tile <= R.t1 && ok; ++tile, ++k) {
+            for (int tile = R.t0; tile <= R.t1; ++tile, ++k) {
+                if (!ok) continue;  // no work after a failed wait, but the walk goes on to every hop
                 const MmaSeg S = R.seg(tile, nc);
-                for (int c = S.c0; c < S.c1; ++c, ++chunks, rp.next(kRawStages), ap.next(kAStages)) {
-                    if (!warp_wait(raw_full + 8 * rp.stage, rp.phase, abort) ||
-                        (chunks >= kAStages && !warp_wait(a_empty + 8 * ap.stage, ap.phase ^ 1u, abort))) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t raw_row =
-                        sbase + kMmaSmemRaw + rp.stage * kRawChunkBytes + (uint32_t)r * kRawRowBytes;
-                    const uint32_t ta = lane_base + kAccCols + kAStageCols * ap.stage;
-                    switch (grp) {
-                        case 0: q4_unit_tmem<0>(raw_row, ta); break;
-                        case 1: q4_unit_tmem<1>(raw_row, ta); break;
-                        case 2: q4_unit_tmem<2>(raw_row, ta); break;
-                        default: q4_unit_tmem<3>(raw_row, ta); break;
-                    }
-                    tmem_wait_st();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(a_full + 8 * ap.stage);
-                }
-                if (!ok || !warp_wait(acc_full, k & 1, abort)) {
+                if (!warp_wait((k & 1) ? acc_full1 : acc_full0, (k >> 1) & 1, abort)) {
                     ok = false;
-                    break;
-                }
-                tc_fence_after();
-                float v[kTokSlice];
-#pragma unroll
-                for (int j = 0; j < kTokSlice; j += 4)
-                    if (j < NB / 4) tmem_ld4(lane_base + (uint32_t)(tok_lo + j), v + j);
-                tmem_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(acc_empty);
-                const int row = tile * kMmaRows + r;
-                if (S.c0 == 0 && S.c1 == nc) {
-#pragma unroll
-                    for (int j = 0; j < kTokSlice; ++j) {
-                        const int tok = tok_lo + j;
-                        if (tok < tok_hi && tok < P.M && row < N) y[(size_t)tok * N + row] = v[j] * __ldcg(P.xscale + tok);
-                    }
                     continue;
                 }
-                // a tile shared with other CTAs: store this CTA's partial sums, in the two slots
-                // of this task in its hop group -- tasks of a group run without a barrier, so
-                // another CTA may still be adding up an earlier task's tile of this CTA
-                const int gp = __ldg(&T.gpos);
+                tc_fence_after();
+                const uint32_t acc = lane_base + ((k & 1) ? (uint32_t)kAcc1Col : 0u);
+                const int row = tile * kMmaRows + r;
+                const bool whole = S.c0 == 0 && S.c1 == nc;
+                // a tile shared with other CTAs: this CTA's partial sums go to the two slots of
+                // this task in its hop group -- tasks of a group run without a barrier, so another
+                // CTA may still be adding up an earlier task's tile of this CTA
                 const int slot = b * P.slots + 2 * gp + (tile == R.t0 ? 0 : 1);
-                float* mine = P.partial + (size_t)slot * NB * kMmaRows;
+                float* const mine = P.partial + (size_t)slot * NB * kMmaRows;
+                for (int j0 = 16 * half; j0 < NB; j0 += 32) {
+                    float v[16];
+                    tmem_ld16(acc + (uint32_t)j0, v);
+                    tmem_wait_ld();
+                    if (whole) {
 #pragma unroll
-                for (int j = 0; j < kTokSlice; ++j) {
-                    const int tok = tok_lo + j;
-                    if (tok < tok_hi) mine[(size_t)tok * kMmaRows + r] = v[j];
+                        for (int j = 0; j < 16; ++j) {
+                            const int tok = j0 + j;
+                            if (tok < P.M && row < N) y[(size_t)tok * N + row] = v[j] * __ldcg(P.xscale + tok);
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) mine[(size_t)(j0 + j) * kMmaRows + r] = v[j];
+                    }
                 }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive((k & 1) ? acc_empty1 : acc_empty0);
+                if (whole) continue;
                 // the warps' partial stores reach the leader through part_done (CTA scope);
                 // its one GPU-scope fence then orders all of them before its arrival
                 __syncwarp();
@@ -534,42 +599,55 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
                 }
                 if (!warp_wait(decided, n_part & 1, abort)) {
                     ok = false;
-                    break;
+                    continue;
                 }
                 ++n_part;
                 if (*last_flag && !*abort) {
                     // the last CTA to finish the tile adds every partial in CTA order (the
                     // leader's fence after its arrival acquired them; decided passes it on)
+                    // two float4s a thread per pass (n4 is a multiple of 2 * 256), partials
+                    // loaded three CTAs at a time: six loads in flight; sums in CTA order
                     const int n4 = NB * (kMmaRows / 4);
-                    constexpr int kFixBatch = 6;
-                    for (int f = tid; f < n4; f += kDequantThreads) {
-                        const int tok = f / (kMmaRows / 4);
-                        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                    constexpr int kFixBatch = 3;
+                    for (int f0 = etid; f0 < n4; f0 += 2 * kEpiThreads) {
+                        const int f1 = f0 + kEpiThreads;
+                        float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
                         for (int b0 = bf; b0 <= bl; b0 += kFixBatch) {
-                            float4 p[kFixBatch];
+                            float4 p0[kFixBatch], p1[kFixBatch];
 #pragma unroll
                             for (int i = 0; i < kFixBatch; ++i) {
                                 const int bb = b0 + i;
                                 if (bb <= bl) {
                                     const int sl = bb * P.slots + 2 * gp + (tile == (int)(sk_lo(total, G, bb) / nc) ? 0 : 1);
-                                    p[i] = __ldcg(reinterpret_cast<const float4*>(P.partial + (size_t)sl * NB * kMmaRows) + f);
+                                    const float4* src = reinterpret_cast<const float4*>(P.partial + (size_t)sl * NB * kMmaRows);
+                                    p0[i] = __ldcg(src + f0);
+                                    p1[i] = __ldcg(src + f1);
                                 }
                             }
 #pragma unroll
                             for (int i = 0; i < kFixBatch; ++i)
                                 if (b0 + i <= bl) {
-                                    acc.x += p[i].x;
-                                    acc.y += p[i].y;
-                                    acc.z += p[i].z;
-                                    acc.w += p[i].w;
+                                    s0.x += p0[i].x;
+                                    s0.y += p0[i].y;
+                                    s0.z += p0[i].z;
+                                    s0.w += p0[i].w;
+                                    s1.x += p1[i].x;
+                                    s1.y += p1[i].y;
+                                    s1.z += p1[i].z;
+                                    s1.w += p1[i].w;
                                 }
                         }
-                        if (tok >= P.M) continue;
-                        const float sc = __ldcg(P.xscale + tok), a4[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int rr = tile * kMmaRows + 4 * (f % (kMmaRows / 4)) + e;
-                            if (rr < N) y[(size_t)tok * N + rr] = a4[e] * sc;
+                        for (int q = 0; q < 2; ++q) {
+                            const int f = q ? f1 : f0, tok = f / (kMmaRows / 4);
+                            if (tok >= P.M) continue;
+                            const float4 a = q ? s1 : s0;
+                            const float sc = __ldcg(P.xscale + tok), a4[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const int rr = tile * kMmaRows + 4 * (f % (kMmaRows / 4)) + e;
+                                if (rr < N) y[(size_t)tok * N + rr] = a4[e] * sc;
+                            }
                         }
                     }
                 }

@@ -1480,9 +1480,16 @@ int32_t mma_stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint3
         CUDA_TRY(cudaFuncSetAttribute(gemm_q4_0_mma_stack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       kMmaStackSmemBytes));
         int per_sm = 0;
-        CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemm_q4_0_mma_stack_kernel, kMmaThreads,
+        CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemm_q4_0_mma_stack_kernel, kMmaStackThreads,
                                                                kMmaStackSmemBytes));
-        if (per_sm < 1) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "tensor-core stack kernel cannot be resident");
+        if (per_sm < 1) {
+            cudaFuncAttributes fa = {};
+            cudaFuncGetAttributes(&fa, gemm_q4_0_mma_stack_kernel);
+            return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT,
+                        "tensor-core stack kernel cannot be resident (%d registers a thread, at most %d threads, "
+                        "%d threads and %d bytes of shared memory asked)",
+                        fa.numRegs, fa.maxThreadsPerBlock, kMmaStackThreads, kMmaStackSmemBytes);
+        }
         return NEXUS_GPU_SUCCESS;
     };
     if ((rc = attrs())) {
@@ -1497,7 +1504,7 @@ int32_t mma_stack_launch(StackHandle& h, const float* x_in, cudaStream_t st) {
     h.mparams.x_in = x_in;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(h.grid);
-    cfg.blockDim = dim3(kMmaThreads);
+    cfg.blockDim = dim3(kMmaStackThreads);
     cfg.dynamicSmemBytes = kMmaStackSmemBytes;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];

@@ -199,7 +199,45 @@ def test_grid_barriers_order_conversion_and_copies(seed, tasks):
 
 
 def test_shared_memory_budget():
-    stack_smem = SMEM_BYTES + 96
+    stack_smem = SMEM_BYTES + 128
     assert stack_smem <= SMEM_OPTIN
-    # the hop decision and 16 warp maxima follow the TMEM address, abort and last flags
-    assert 4 * (3 + 1 + 16) <= 16 + 96
+    # the hop decision and 16 warp maxima follow the TMEM address, abort and last flags;
+    # then the second accumulator's full and empty barriers (8-byte aligned)
+    assert 4 * (3 + 1 + 16) == 80 and 80 + 2 * 8 <= 16 + 128
+
+
+def test_two_accumulators_parities():
+    """Segment k uses accumulator k % 2.  The MMA warp waits on its empty
+    barrier with parity ((k >> 1) - 1) & 1 (k >= 2), the epilogue warps on its
+    full barrier with parity (k >> 1) & 1; an mbarrier wait on parity p passes
+    once the barrier's completion with that parity is the latest one.  Random
+    interleavings: every wait passes only for the completion it means, and no
+    barrier ever runs two completions ahead of a waiter (no parity aliasing)."""
+    for seed in range(50):
+        rng = random.Random(seed)
+        n_seg = rng.randint(1, 40)
+        full, empty = [0, 0], [0, 0]  # completions so far
+        mma_k = epi_k = 0
+        steps = 0
+        while epi_k < n_seg:
+            steps += 1
+            assert steps < 100_000
+            who = rng.choice(["mma", "epi"])
+            if who == "mma" and mma_k < n_seg:
+                k, a = mma_k, mma_k & 1
+                if k >= 2:
+                    want = (k >> 1) - 1
+                    # parity wait: passes when the latest completion has parity want & 1
+                    if empty[a] == 0 or (empty[a] - 1) & 1 != want & 1:
+                        continue
+                    assert empty[a] - 1 == want  # the completion meant, never a later one
+                full[a] += 1  # MMAs of segment k, then the commit
+                mma_k += 1
+            elif who == "epi" and epi_k < mma_k:
+                k, a = epi_k, epi_k & 1
+                want = k >> 1
+                if full[a] == 0 or (full[a] - 1) & 1 != want & 1:
+                    continue
+                assert full[a] - 1 == want
+                empty[a] += 1  # read out, release
+                epi_k += 1
