@@ -20,9 +20,12 @@
 //    into the fp16 B operand (x * 2^-e per token, K permuted to the decode's
 //    order, as mma_xprep_kernel does), and a second grid barrier publishes
 //    it.  Tasks that share an input run back to back with no barrier.
-//  * The producer streams the next task's raw weight chunks across the
-//    barriers (weights depend on nothing); only its x-tile copies wait for
-//    the second barrier.
+//  * Two copy warps: one streams the raw weight chunks through the barriers
+//    (weights depend on nothing; a ring slot frees as soon as its chunk is
+//    decoded), the other the x tiles, which wait for the second barrier and
+//    then run as far ahead as their ring allows.  Each walks its tasks with
+//    incremental tile and chunk counters, so a copy costs a few instructions
+//    on a scheduler it shares with the decoding warps.
 //  * The per-tile arrival counters of the fix-up only grow: a tile shared by
 //    n CTAs is complete at the arrival whose previous count is n - 1 modulo n,
 //    so no run resets them.  The grid barrier counter and the run counter
@@ -209,16 +212,17 @@ __device__ __forceinline__ void mma_convert_token(const MmaStackParams& P, const
     if (tid == 0) P.xscale[b] = real ? ldexpf(1.0f, ex) : 0.0f;
 }
 
-// Warps of the stack kernel: the single GEMM's eighteen (copies, MMA, sixteen
-// dequantizing warps) and eight epilogue warps (warps 18..25, tensor-memory
-// lane quarters 2, 3, 0, 1 twice; the two halves take alternate groups of 16
-// tokens).  The epilogue warps read a finished accumulator, store y or the
+// Warps of the stack kernel: the single GEMM's eighteen (raw-chunk copies,
+// MMA, sixteen dequantizing warps), eight epilogue warps (warps 18..25,
+// tensor-memory lane quarters 2, 3, 0, 1 twice; the two halves take alternate
+// groups of 16 tokens) and the x-tile copy warp (26).  The epilogue warps read a finished accumulator, store y or the
 // partial sums and run the fix-up, while the other warps go on with the next
 // tile segment in the second accumulator.
 constexpr int kEpiWarps = 8;
 constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kEpiWarp0 = kMmaThreads / 32;
-constexpr int kMmaStackThreads = kMmaThreads + kEpiThreads;
+constexpr int kXWarp = kEpiWarp0 + kEpiWarps;  // the x-tile copies
+constexpr int kMmaStackThreads = kMmaThreads + kEpiThreads + 32;
 // Tensor memory: accumulator 0 in columns [0, 64), the A stages, accumulator
 // 1 in the last 64 columns.
 constexpr int kAcc1Col = kAccCols + kAStageCols * kAStages;
@@ -279,7 +283,7 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < kRawStages; ++s) {
             mbar_init(raw_full + 8 * s, 1);
-            mbar_init(raw_empty + 8 * s, 1);
+            mbar_init(raw_empty + 8 * s, kDequantWarps);
         }
         for (int s = 0; s < kAStages; ++s) {
             mbar_init(a_full + 8 * s, kDequantWarps);
@@ -314,45 +318,58 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
     const uint32_t tmem_d = __shfl_sync(0xffffffffu, *reinterpret_cast<volatile uint32_t*>(tmem_slot), 0);
 
     if (warp == 0) {
-        // ------------------- raw weight chunks (run ahead) and x tiles (after each hop's publication)
+        // ---------------- raw weight chunks: weights depend on nothing, so they stream through
+        // the hops; a ring slot is free once the dequantizing warps have decoded its chunk
         const bool leader = elect_one();
-        MmaChunkCursor rk, xk;
-        mma_cursor_seek(rk, P, 0, b);
-        mma_cursor_seek(xk, P, 0, b);
-        RingPos rp, bp;
-        uint32_t r_issued = 0, x_issued = 0;
+        RingPos rp;
+        uint32_t issued = 0;
+        bool ok = *abort == 0;
+        for (int t = 0; t < P.n_tasks && ok; ++t) {
+            const MmaTaskRange tr = mma_task_range(P.tasks[t], b);
+            if (!tr.any) continue;
+            const CUtensorMap* map = &P.tasks[t].tmW;
+            int tile = tr.t0, c = (int)(tr.lo - (long long)tr.t0 * tr.nc);
+            for (long long L = tr.lo; L < tr.hi; ++L) {
+                if (issued >= kRawStages && !warp_wait(raw_empty + 8 * rp.stage, rp.phase ^ 1u, abort)) {
+                    ok = false;
+                    break;
+                }
+                if (leader) {
+                    mbar_arrive_expect_tx(raw_full + 8 * rp.stage, kRawChunkBytes);
+                    tma_load_2d(sbase + kMmaSmemRaw + rp.stage * kRawChunkBytes, map, c * kRawRowBytes, tile * kMmaRows,
+                                raw_full + 8 * rp.stage);
+                }
+                __syncwarp();
+                ++issued;
+                rp.next(kRawStages);
+                if (++c == tr.nc) {
+                    c = 0;
+                    ++tile;
+                }
+            }
+        }
+        if (leader && *abort)  // leave no copy in flight
+            for (uint32_t k = 0; k < issued && k < (uint32_t)kRawStages; ++k) {
+                const uint32_t j = issued - 1 - k;
+                mbar_wait_bounded(raw_full + 8 * (j % kRawStages), (j / kRawStages) & 1);
+            }
+        __syncwarp();
+    } else if (warp == kXWarp) {
+        // ---------------- x tiles: a hop's after its input is converted and published (bar_pub),
+        // made visible to the tensor-copy proxy; then as far ahead as the x ring allows
+        const bool leader = elect_one();
+        RingPos bp;
+        uint32_t issued = 0;
         int waited = -1;  // the last hop whose x this warp saw published
         bool ok = *abort == 0;
-        // issue raw chunk rk (waiting for its ring slot: the MMA of the chunk kRawStages
-        // earlier, whose x tile is already issued)
-        auto issue_raw = [&]() -> bool {
-            if (r_issued >= kRawStages && !warp_wait(raw_empty + 8 * rp.stage, rp.phase ^ 1u, abort)) return false;
-            if (leader) {
-                const int tile = (int)(rk.L / rk.nc), c = (int)(rk.L - (long long)tile * rk.nc);
-                mbar_arrive_expect_tx(raw_full + 8 * rp.stage, kRawChunkBytes);
-                tma_load_2d(sbase + kMmaSmemRaw + rp.stage * kRawChunkBytes, &P.tasks[rk.t].tmW, c * kRawRowBytes,
-                            tile * kMmaRows, raw_full + 8 * rp.stage);
-            }
-            __syncwarp();
-            ++r_issued;
-            rp.next(kRawStages);
-            mma_cursor_next(rk, P, b);
-            return true;
-        };
-        while (ok && xk.t < P.n_tasks) {
-            // chunk j: its raw chunk, then its x tile, as the single GEMM issues them (both
-            // rings several chunks ahead of the MMAs)
-            while (ok && r_issued <= x_issued) ok = issue_raw();
-            if (!ok) break;
-            if (xk.hidx > waited) {
-                // a hop's input: first the raw chunks up to kRawStages ahead (weights depend on
-                // nothing, so they stream across the barriers), then wait until the input is
-                // converted and published (bar_pub), made visible to the tensor-copy proxy
-                while (ok && rk.t < P.n_tasks && r_issued < x_issued + kRawStages) ok = issue_raw();
-                if (!ok) break;
+        for (int t = 0; t < P.n_tasks && ok; ++t) {
+            const MmaTaskRange tr = mma_task_range(P.tasks[t], b);
+            if (!tr.any) continue;
+            const int hidx = __ldg(&P.tasks[t].hidx);
+            if (hidx > waited) {
                 bool go = true;
                 if (leader) {
-                    go = grid_wait(P.bar_pub, pub_target(run, P.n_hops, xk.hidx, gridDim.x), P.abort_flag);
+                    go = grid_wait(P.bar_pub, pub_target(run, P.n_hops, hidx, gridDim.x), P.abort_flag);
                     if (go) fence_proxy_async_global();
                     else *abort = 1;
                 }
@@ -360,41 +377,39 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
                     ok = false;
                     break;
                 }
-                waited = xk.hidx;
+                waited = hidx;
             }
-            if (x_issued >= nbs && !warp_wait(b_empty + 8 * bp.stage, bp.phase ^ 1u, abort)) {
-                ok = false;
-                break;
-            }
-            if (leader) {
-                const int c = (int)(xk.L % xk.nc);
-                const uint32_t dst = sbase + kMmaSmemB + bp.stage * b_stage, bar = b_full + 8 * bp.stage;
-                mbar_arrive_expect_tx(bar, b_stage);
+            int c = (int)(tr.lo - (long long)tr.t0 * tr.nc);
+            for (long long L = tr.lo; L < tr.hi; ++L) {
+                if (issued >= nbs && !warp_wait(b_empty + 8 * bp.stage, bp.phase ^ 1u, abort)) {
+                    ok = false;
+                    break;
+                }
+                if (leader) {
+                    const uint32_t dst = sbase + kMmaSmemB + bp.stage * b_stage, bar = b_full + 8 * bp.stage;
+                    mbar_arrive_expect_tx(bar, b_stage);
 #pragma unroll
-                for (int u = 0; u < kUnitsPerChunk; ++u) tma_load_2d(dst + u * b_unit, &tmX, c * kRawK + u * kUnitK, 0, bar);
+                    for (int u = 0; u < kUnitsPerChunk; ++u)
+                        tma_load_2d(dst + u * b_unit, &tmX, c * kRawK + u * kUnitK, 0, bar);
+                }
+                __syncwarp();
+                ++issued;
+                bp.next(nbs);
+                if (++c == tr.nc) c = 0;
             }
-            __syncwarp();
-            ++x_issued;
-            bp.next(nbs);
-            mma_cursor_next(xk, P, b);
         }
-        if (leader && *abort) {  // leave no copy in flight
-            for (uint32_t k = 0; k < r_issued && k < (uint32_t)kRawStages; ++k) {
-                const uint32_t j = r_issued - 1 - k;
-                mbar_wait_bounded(raw_full + 8 * (j % kRawStages), (j / kRawStages) & 1);
-            }
-            for (uint32_t k = 0; k < x_issued && k < nbs; ++k) {
-                const uint32_t j = x_issued - 1 - k;
+        if (leader && *abort)
+            for (uint32_t k = 0; k < issued && k < nbs; ++k) {
+                const uint32_t j = issued - 1 - k;
                 mbar_wait_bounded(b_full + 8 * (j % nbs), (j / nbs) & 1);
             }
-        }
         __syncwarp();
     } else if (warp == 1) {
         // --------------------------------------------------------------- MMA
         const uint32_t idesc = (1u << 4) | ((uint32_t)(NB >> 3) << 17) | ((uint32_t)(kMmaRows >> 4) << 24);
         const uint32_t b_unit16 = b_unit >> 4;
         const bool leader = elect_one();
-        RingPos ap, bp, rp;
+        RingPos ap, bp;
         bool ok = *abort == 0;
         int k = 0;  // segments (accumulator uses) so far
         for (int t = 0; t < P.n_tasks && ok; ++t) {
@@ -414,7 +429,7 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t d = tmem_d + ((k & 1) ? (uint32_t)kAcc1Col : 0u);
-                for (int c = S.c0; c < S.c1; ++c, ap.next(kAStages), bp.next(nbs), rp.next(kRawStages)) {
+                for (int c = S.c0; c < S.c1; ++c, ap.next(kAStages), bp.next(nbs)) {
                     if (!warp_wait(a_full + 8 * ap.stage, ap.phase, abort) ||
                         !warp_wait(b_full + 8 * bp.stage, bp.phase, abort)) {
                         ok = false;
@@ -434,7 +449,6 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
                         }
                         umma_commit(a_empty + 8 * ap.stage);
                         umma_commit(b_empty + 8 * bp.stage);
-                        umma_commit(raw_empty + 8 * rp.stage);
                     }
                     __syncwarp();
                 }
@@ -509,6 +523,8 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
                     case 2: q4_unit_tmem_lean<2>(raw_row, ta); break;
                     default: q4_unit_tmem_lean<3>(raw_row, ta); break;
                 }
+                __syncwarp();  // the warp's shared loads of the raw chunk are consumed
+                if (lane == 0) mbar_arrive(raw_empty + 8 * rp.stage);
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
