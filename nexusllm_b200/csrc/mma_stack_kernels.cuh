@@ -51,24 +51,27 @@ struct __align__(64) MmaTask {
     int N, K, tiles, n_chunks;
     long long total;        // tiles * n_chunks
     int G;                  // CTAs that share the task's chunks (stream-K), <= gridDim.x
-    int hop;                // 1: a new input -- barriers and x conversion before the task
+    int hop;                // 1: a hop -- the "done" grid barrier (hop index > 0) before the task
     int hidx;               // index of the last hop at or before this task
     int gpos;               // position of the task in its hop group (tasks from one hop to the next)
+    int conv;               // 1 (hops only): convert the input into its x slot, then the "published" barrier
+    int pidx;               // index of the "published" barrier that covers this task's x
+    int xslot;              // x slot: 0 the stack input (converted once a run), 1 an earlier task's y
 };
 static_assert(sizeof(MmaTask) % 64 == 0, "tensor maps in an MmaTask array must stay 64-byte aligned");
 
 struct MmaStackParams {
     const MmaTask* tasks;
-    int n_tasks, n_hops;
+    int n_tasks, n_hops, n_pubs;  // tasks; hops ("done" barriers + 1); "published" barriers a run
     int M, NB;               // tokens; tokens rounded up to 16 (the UMMA N)
-    int kmax;                // row stride of the fp16 x buffer
+    int kmax;                // row stride of the fp16 x slots
     int b_stages;            // x-tile ring depth in chunks
-    __half* xbuf;            // [NB][kmax] the current input in fp16 (B operand)
-    float* xscale;           // [NB] 2^e per token of the current input
+    __half* xbuf;            // [2][NB][kmax] x slots in fp16 (B operand): the stack input, the current y input
+    float* xscale;           // [2][kMaxTokens] 2^e per token of each slot
     float* partial;          // [gridDim.x][slots][NB][128] partial sums of shared tiles
     int slots;               // partial-sum slots per CTA: 2 per task of the largest hop group
     unsigned long long* bar_done;  // arrivals "done with the tasks before hop h" (hops 1..), all runs
-    unsigned long long* bar_pub;   // arrivals "hop h's input converted and published", all runs
+    unsigned long long* bar_pub;   // arrivals "conversion p published", all runs
     unsigned long long* epoch;     // runs completed
     unsigned long long* fin;       // CTAs that left, all runs
     unsigned* abort_flag;          // sticky: an expired wait poisons the stack
@@ -102,24 +105,31 @@ __device__ __forceinline__ bool grid_wait(const unsigned long long* ctr, unsigne
         }
     }
 }
+// Fetch-and-add with release and acquire semantics at GPU scope.
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
 __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 // The 16 dequantizing warps' barrier (named barrier 1, 512 threads).
 __device__ __forceinline__ void dequant_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kDequantThreads) : "memory"); }
 
-// Two grid barriers per hop, each kind on its own counter: hop h >= 1 has a
-// "done" barrier before its conversion (bar_done reaches (run*(H-1) + h) * G),
-// every hop a "published" barrier after it (bar_pub reaches (run*H + h + 1) *
-// G), H hops a run.  With one counter per kind a CTA's next arrival on a
-// counter always follows its own wait for that counter's current target, so
-// early arrivals of a CTA that has no work between two hops cannot complete a
+// Two kinds of grid barrier, each on its own counter: hop h >= 1 has a "done"
+// barrier (bar_done reaches (run*(H-1) + h) * G, H hops a run), and every
+// conversion p a "published" barrier after it (bar_pub reaches (run*C + p + 1)
+// * G, C conversions a run; a hop whose input is the stack input converts only
+// the first time).  With one counter per kind a CTA's next arrival on a counter
+// always follows its own wait for that counter's current target, so early
+// arrivals of a CTA that has no work between two hops cannot complete a
 // barrier for a CTA that has not arrived.
 __device__ __forceinline__ unsigned long long done_target(unsigned long long run, int n_hops, int h, int G) {
     return (run * (unsigned long long)(n_hops - 1) + (unsigned long long)h) * (unsigned long long)G;
 }
-__device__ __forceinline__ unsigned long long pub_target(unsigned long long run, int n_hops, int h, int G) {
-    return (run * (unsigned long long)n_hops + (unsigned long long)h + 1ull) * (unsigned long long)G;
+__device__ __forceinline__ unsigned long long pub_target(unsigned long long run, int n_pubs, int p, int G) {
+    return (run * (unsigned long long)n_pubs + (unsigned long long)p + 1ull) * (unsigned long long)G;
 }
 
 // This CTA's chunks of a task: the linear range [lo, hi) of tiles x chunks
@@ -145,36 +155,13 @@ __device__ __forceinline__ MmaTaskRange mma_task_range(const MmaTask& T, int b) 
     return r;
 }
 
-// The producer's walk over this CTA's chunks of every task, in order.
-struct MmaChunkCursor {
-    int t = 0, nc = 1, hidx = 0;
-    long long L = 0, hi = 0;
-};
-__device__ __forceinline__ void mma_cursor_seek(MmaChunkCursor& k, const MmaStackParams& P, int t, int b) {
-    for (; t < P.n_tasks; ++t) {
-        const MmaTaskRange r = mma_task_range(P.tasks[t], b);
-        if (r.any) {
-            k.t = t;
-            k.L = r.lo;
-            k.hi = r.hi;
-            k.nc = r.nc;
-            k.hidx = __ldg(&P.tasks[t].hidx);
-            return;
-        }
-    }
-    k.t = P.n_tasks;
-}
-__device__ __forceinline__ void mma_cursor_next(MmaChunkCursor& k, const MmaStackParams& P, int b) {
-    if (++k.L == k.hi) mma_cursor_seek(k, P, k.t + 1, b);
-}
-
 // Token b of a hop's input (fp32 [M][K]; rows b >= M are zero) -> row b of
-// the fp16 B operand: x * 2^-e with amax * 2^-e in [2^13, 2^14), K permuted
-// inside every 32-weight block as q4_unit_decode orders the weights, and
-// xscale[b] = 2^e (mma_xprep_kernel's rule).  Run by the 512 dequantizing
+// x slot `slot` (the fp16 B operand): x * 2^-e with amax * 2^-e in [2^13,
+// 2^14), K permuted inside every 32-weight block as q4_unit_decode orders the
+// weights, and the slot's xscale[b] = 2^e (mma_xprep_kernel's rule).  Run by the 512 dequantizing
 // threads of CTA b; s_red holds their 16 warps' maxima.
-__device__ __forceinline__ void mma_convert_token(const MmaStackParams& P, const float* x, int K, int b, int tid,
-                                                  volatile uint32_t* s_red) {
+__device__ __forceinline__ void mma_convert_token(const MmaStackParams& P, const float* x, int K, int b, int slot,
+                                                  int tid, volatile uint32_t* s_red) {
     const bool real = b < P.M;
     const float* row = x + (size_t)b * K;
     uint32_t m = 0;
@@ -193,7 +180,7 @@ __device__ __forceinline__ void mma_convert_token(const MmaStackParams& P, const
     int ex = 0;
     if (amax != 0 && amax < 0x7f800000u) ex = max((int)((amax >> 23) & 0xff) - 127 - 13, -110);
     const float down = ldexpf(1.0f, -ex);
-    __half* out = P.xbuf + (size_t)b * P.kmax;
+    __half* out = P.xbuf + ((size_t)slot * P.NB + b) * P.kmax;
     for (int e = 4 * tid; e < K; e += 4 * kDequantThreads) {
         float v4[4] = {0.f, 0.f, 0.f, 0.f};
         if (real) {
@@ -209,7 +196,7 @@ __device__ __forceinline__ void mma_convert_token(const MmaStackParams& P, const
             out[32 * blk + q4_perm_dst(s & 31, blk & 1)] = __float2half_rn(v4[k] * down);
         }
     }
-    if (tid == 0) P.xscale[b] = real ? ldexpf(1.0f, ex) : 0.0f;
+    if (tid == 0) P.xscale[slot * kMaxTokens + b] = real ? ldexpf(1.0f, ex) : 0.0f;
 }
 
 // Warps of the stack kernel: the single GEMM's eighteen (raw-chunk copies,
@@ -256,7 +243,8 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 // early: both meet at the hop barrier of every hop, also after a failed wait
 // (they then skip all work), so the named barrier always completes.
 __global__ void __launch_bounds__(kMmaStackThreads, 1)
-    gemm_q4_0_mma_stack_kernel(const __grid_constant__ CUtensorMap tmX, const MmaStackParams P) {
+    gemm_q4_0_mma_stack_kernel(const __grid_constant__ CUtensorMap tmXin, const __grid_constant__ CUtensorMap tmX,
+                               const MmaStackParams P) {
     extern __shared__ uint8_t mma_smem_raw[];
     const uint32_t sraw = smem_u32(mma_smem_raw);
     const uint32_t sbase = (sraw + 1023u) & ~1023u;  // 1024-byte aligned: swizzle atoms
@@ -360,16 +348,17 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
         const bool leader = elect_one();
         RingPos bp;
         uint32_t issued = 0;
-        int waited = -1;  // the last hop whose x this warp saw published
+        int waited = -1;  // the last conversion this warp saw published
         bool ok = *abort == 0;
         for (int t = 0; t < P.n_tasks && ok; ++t) {
             const MmaTaskRange tr = mma_task_range(P.tasks[t], b);
             if (!tr.any) continue;
-            const int hidx = __ldg(&P.tasks[t].hidx);
-            if (hidx > waited) {
+            const int pidx = __ldg(&P.tasks[t].pidx);
+            const CUtensorMap* map = __ldg(&P.tasks[t].xslot) ? &tmX : &tmXin;
+            if (pidx > waited) {
                 bool go = true;
                 if (leader) {
-                    go = grid_wait(P.bar_pub, pub_target(run, P.n_hops, hidx, gridDim.x), P.abort_flag);
+                    go = grid_wait(P.bar_pub, pub_target(run, P.n_pubs, pidx, gridDim.x), P.abort_flag);
                     if (go) fence_proxy_async_global();
                     else *abort = 1;
                 }
@@ -377,7 +366,7 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
                     ok = false;
                     break;
                 }
-                waited = hidx;
+                waited = pidx;
             }
             int c = (int)(tr.lo - (long long)tr.t0 * tr.nc);
             for (long long L = tr.lo; L < tr.hi; ++L) {
@@ -390,7 +379,7 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
                     mbar_arrive_expect_tx(bar, b_stage);
 #pragma unroll
                     for (int u = 0; u < kUnitsPerChunk; ++u)
-                        tma_load_2d(dst + u * b_unit, &tmX, c * kRawK + u * kUnitK, 0, bar);
+                        tma_load_2d(dst + u * b_unit, map, c * kRawK + u * kUnitK, 0, bar);
                 }
                 __syncwarp();
                 ++issued;
@@ -474,9 +463,9 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
         for (int t = 0; t < P.n_tasks; ++t) {
             const MmaTask& T = P.tasks[t];
             if (__ldg(&T.hop)) {
-                // a new input: every CTA finished the tasks before it (which also ends every
-                // read of the x buffer and its scales), CTA b < NB converts token b, and the
-                // result is published at GPU scope for the other CTAs' tensor copies
+                // every CTA finished the tasks before it (which also ends every read of the
+                // y-input x slot and its scales); for a new input CTA b < NB converts token b,
+                // and the result is published at GPU scope for the other CTAs' tensor copies
                 const int hh = __ldg(&T.hidx);
                 if (!ok) *abort = 1;
                 hop_bar();  // with the epilogue warps, through every output before the hop
@@ -493,11 +482,11 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
                     *abort = 1;
                     ok = false;
                 }
-                if (ok) {
+                if (ok && __ldg(&T.conv)) {
                     if (b < NB) {
                         const float* x =
                             reinterpret_cast<const float*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.x)));
-                        mma_convert_token(P, x != nullptr ? x : P.x_in, __ldg(&T.K), b, tid, s_red);
+                        mma_convert_token(P, x != nullptr ? x : P.x_in, __ldg(&T.K), b, __ldg(&T.xslot), tid, s_red);
                     }
                     fence_proxy_async_global();
                     dequant_bar();
@@ -556,6 +545,7 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
             R.t0 = tr.t0;
             R.t1 = tr.t1;
             const int nc = tr.nc, N = __ldg(&T.N), G = __ldg(&T.G), gp = __ldg(&T.gpos);
+            const float* const xscale = P.xscale + __ldg(&T.xslot) * kMaxTokens;
             const long long total = __ldg(&T.total);
             float* const y = reinterpret_cast<float*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.y)));
             unsigned* const arrivals =
@@ -584,7 +574,7 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
                             const int tok = j0 + j;
-                            if (tok < P.M && row < N) y[(size_t)tok * N + row] = v[j] * __ldcg(P.xscale + tok);
+                            if (tok < P.M && row < N) y[(size_t)tok * N + row] = v[j] * __ldcg(xscale + tok);
                         }
                     } else {
 #pragma unroll
@@ -596,7 +586,7 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
                 if (lane == 0) mbar_arrive((k & 1) ? acc_empty1 : acc_empty0);
                 if (whole) continue;
                 // the warps' partial stores reach the leader through part_done (CTA scope);
-                // its one GPU-scope fence then orders all of them before its arrival
+                // its GPU-scope release then orders all of them before its arrival
                 __syncwarp();
                 if (lane == 0) mbar_arrive(part_done);
                 const int bf = sk_owner(total, G, (long long)tile * nc);
@@ -606,9 +596,8 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
                     if (mma_wait(part_done, n_part & 1, abort)) {
                         // the counter only grows: each run adds one arrival per sharing CTA
                         const unsigned n = (unsigned)(bl - bf + 1);
-                        __threadfence();  // release this CTA's partial sums ...
-                        last = atomicAdd(arrivals + tile, 1u) % n == n - 1;
-                        __threadfence();  // ... and, for the last CTA, acquire the others'
+                        // release this CTA's partial sums and, for the last CTA, acquire the others'
+                        last = atom_add_acq_rel_gpu(arrivals + tile, 1u) % n == n - 1;
                     }
                     *last_flag = last ? 1 : 0;
                     mbar_arrive(decided);
@@ -658,7 +647,7 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
                             const int f = q ? f1 : f0, tok = f / (kMmaRows / 4);
                             if (tok >= P.M) continue;
                             const float4 a = q ? s1 : s0;
-                            const float sc = __ldcg(P.xscale + tok), a4[4] = {a.x, a.y, a.z, a.w};
+                            const float sc = __ldcg(xscale + tok), a4[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
                             for (int e = 0; e < 4; ++e) {
                                 const int rr = tile * kMmaRows + 4 * (f % (kMmaRows / 4)) + e;

@@ -926,7 +926,7 @@ struct StackHandle {
     int tokens = 1;         // activation vectors per run (2..4: the multi-token kernel; 16..64: tensor cores)
     bool mma = false;       // the tcgen05 stack (tokens >= 16): mparams, tmX, d_block
     MmaStackParams mparams{};
-    CUtensorMap tmX{};
+    CUtensorMap tmXin{}, tmX{};  // tensor-core stack: x slots 0 (stack input) and 1
     uint64_t fingerprint = 0;
     StackParams params{};
     StackTask* d_tasks = nullptr;
@@ -1353,7 +1353,7 @@ int32_t mma_stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint3
     std::vector<MmaTask> ht(n);
     std::vector<size_t> arr_off(n);
     size_t arr_words = 0;
-    int kmax = 0, hops = 0, last_hop = 0, gpos = 0, max_group = 1;
+    int kmax = 0, hops = 0, last_hop = 0, gpos = 0, max_group = 1, pubs = 0, in_pub = -1, cur_pub = -1;
     for (uint32_t i = 0; i < n; ++i) {
         const NexusGpuStackTaskEx& u = tasks[i];
         if (!u.W || !u.y || u.rows == 0 || u.rows > (uint64_t)INT32_MAX)
@@ -1402,6 +1402,15 @@ int32_t mma_stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint3
         T.hop = hop ? 1 : 0;
         T.hidx = hops - 1;
         T.gpos = gpos++;
+        // x slot 0 holds the stack input, converted at its first hop of a run; slot 1 the
+        // latest earlier task's y, converted at every hop that reads one
+        T.xslot = u.x_source < 0 ? 0 : 1;
+        if (hop && (u.x_source >= 0 || in_pub < 0)) {
+            T.conv = 1;
+            cur_pub = pubs++;
+            if (u.x_source < 0) in_pub = cur_pub;
+        }
+        T.pidx = u.x_source < 0 ? in_pub : cur_pub;
         arr_off[i] = arr_words;
         arr_words += (size_t)T.tiles;
         kmax = std::max(kmax, T.K);
@@ -1412,9 +1421,9 @@ int32_t mma_stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint3
     const size_t o_tasks = off;
     off = align256(off + n * sizeof(MmaTask));
     const size_t o_x = off;
-    off = align256(off + (size_t)NB * kmax * sizeof(__half));
+    off = align256(off + 2 * (size_t)NB * kmax * sizeof(__half));
     const size_t o_scale = off;
-    off = align256(off + kMaxTokens * sizeof(float));
+    off = align256(off + 2 * kMaxTokens * sizeof(float));
     const size_t o_part = off;
     off = align256(off + (size_t)G * 2 * max_group * NB * kMmaRows * sizeof(float));
     const size_t o_arr = off;
@@ -1443,12 +1452,13 @@ int32_t mma_stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint3
         stack_free(h);
         return fail(NEXUS_GPU_ERROR_CUDA, "stack upload failed: %s", cudaGetErrorString(e));
     }
-    {
+    for (int slot = 0; slot < 2; ++slot) {
         const cuuint64_t dims[2] = {(cuuint64_t)kmax, (cuuint64_t)NB};
         const cuuint64_t strides[1] = {(cuuint64_t)kmax * sizeof(__half)};
         const cuuint32_t box[2] = {(cuuint32_t)kUnitK, (cuuint32_t)NB};
         const cuuint32_t estr[2] = {1, 1};
-        if (encode(&h->tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, blk + o_x, dims, strides, box, estr,
+        if (encode(slot ? &h->tmX : &h->tmXin, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                   blk + o_x + (size_t)slot * NB * kmax * sizeof(__half), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
             stack_free(h);
@@ -1459,6 +1469,7 @@ int32_t mma_stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint3
     P.tasks = reinterpret_cast<const MmaTask*>(blk + o_tasks);
     P.n_tasks = (int)n;
     P.n_hops = hops;
+    P.n_pubs = pubs;
     P.M = tokens;
     P.NB = NB;
     P.kmax = kmax;
@@ -1512,7 +1523,7 @@ int32_t mma_stack_launch(StackHandle& h, const float* x_in, cudaStream_t st) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_q4_0_mma_stack_kernel, h.tmX, h.mparams));
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_q4_0_mma_stack_kernel, h.tmXin, h.tmX, h.mparams));
     return NEXUS_GPU_SUCCESS;
 }
 

@@ -26,8 +26,12 @@ SMEM_OPTIN = 232448
 
 
 def stack_plan(tasks, input_cols, sms=SMS):
-    """tasks: (rows, cols, x_source, after).  Mirror of mma_stack_create."""
+    """tasks: (rows, cols, x_source, after).  Mirror of mma_stack_create:
+    hops, hop index, stream-K CTAs, group position, and the x slot (0: the
+    stack input, converted at its first hop of a run; 1: an earlier task's y,
+    converted at every hop) with the "published" barrier that covers it."""
     plan, hops, last_hop, gpos = [], 0, 0, 0
+    pubs, in_pub, cur_pub = 0, -1, -1
     for i, (rows, cols, src, after) in enumerate(tasks):
         assert cols % RAW_K == 0
         assert (input_cols if src < 0 else tasks[src][0]) == cols
@@ -39,9 +43,17 @@ def stack_plan(tasks, input_cols, sms=SMS):
         tiles = -(-rows // ROWS)
         nc = cols // RAW_K
         total = tiles * nc
+        conv = hop and (src >= 0 or in_pub < 0)
+        if conv:
+            cur_pub = pubs
+            pubs += 1
+            if src < 0:
+                in_pub = cur_pub
         plan.append(dict(rows=rows, cols=cols, tiles=tiles, nc=nc, total=total,
-                         G=tc_ctas(sms, tiles, nc), hop=hop, hidx=hops - 1, gpos=gpos))
+                         G=tc_ctas(sms, tiles, nc), hop=hop, hidx=hops - 1, gpos=gpos,
+                         conv=conv, pidx=in_pub if src < 0 else cur_pub, xslot=0 if src < 0 else 1))
         gpos += 1
+    stack_plan.pubs = pubs
     return plan, hops
 
 
@@ -63,6 +75,15 @@ def test_hops_of_a_decode_step():
     assert hops == 4 * 3 + 1  # q, o, gate, down per layer; the head reads the stack input again
     for i, p in enumerate(plan):
         assert p["hidx"] == sum(q["hop"] for q in plan[:i + 1]) - 1
+    # the stack input is converted once (q of layer 0); o, gate and down convert every layer
+    assert [p["conv"] for p in plan[:14]] == [True, False, False, True, True, False, True,
+                                             False, False, False, True, True, False, True]
+    assert stack_plan.pubs == 1 + 3 * 3 and not plan[-1]["conv"]
+    assert all(plan[i]["pidx"] == 0 and plan[i]["xslot"] == 0 for i in (0, 7, len(plan) - 1))
+    # a task's "published" barrier is its own group's conversion, or the stack input's
+    for i, p in enumerate(plan):
+        last_conv = max(j for j in range(i + 1) if plan[j]["conv"] and plan[j]["xslot"] == p["xslot"])
+        assert p["pidx"] == plan[last_conv]["pidx"]
     # an `after` on the previous task with the same input forces a hop
     plan, hops = stack_plan([(256, 256, -1, -1), (256, 256, -1, 0)], 256)
     assert plan[1]["hop"] and hops == 2
@@ -133,12 +154,15 @@ def test_partial_slots_are_never_shared_within_a_hop_group():
 
 def _simulate(plan, hops, runs, seed, sms=12, tokens=16):
     """Random interleavings of every CTA's roles over `runs` runs.  Per hop h:
-    the dequantizing warps wait for "done" (h >= 1), convert (CTAs < NB), and
-    publish; the producer waits for "published" before the x tiles of a task
-    in hop h when the CTA has chunks there; the dequantizing warps then finish
-    the CTA's tasks of hop h.  Returns the number of scheduling steps."""
+    the dequantizing warps wait for "done" (h >= 1) and, when the hop converts,
+    convert (CTAs < NB) and publish; the x-tile warp waits for the hop's
+    "published" barrier before the x tiles of a task in hop h when the CTA has
+    chunks there; the dequantizing warps then finish the CTA's tasks of hop h.
+    Returns the number of scheduling steps."""
     rng = random.Random(seed)
     NB = tokens
+    n_pubs = stack_plan.pubs
+    hop_task = [next(p for p in plan if p["hidx"] == h) for h in range(hops)]
     done = pub = 0
     # per CTA, the hops in which it has chunks
     work = []
@@ -162,15 +186,17 @@ def _simulate(plan, hops, runs, seed, sms=12, tokens=16):
                         yield
                     # every CTA is done with the tasks before hop h
                     assert len(finished.get((run, h - 1), ())) == sms
-                if b < NB:
-                    yield
-                    converted.setdefault((run, h), set()).add(b)
-                pub += 1
-                if h in work[b]:
-                    while pub < (run * hops + h + 1) * sms:
+                head = hop_task[h]
+                if head["conv"]:
+                    if b < NB:
                         yield
-                    # the producer copies hop h's x tiles: every conversion is published
-                    assert len(converted.get((run, h), ())) == min(NB, sms)
+                        converted.setdefault((run, head["pidx"]), set()).add(b)
+                    pub += 1
+                if h in work[b]:
+                    while pub < (run * n_pubs + head["pidx"] + 1) * sms:
+                        yield
+                    # the x-tile warp copies hop h's x tiles: every conversion is published
+                    assert len(converted.get((run, head["pidx"]), ())) == min(NB, sms)
                     yield
                 finished.setdefault((run, h), set()).add(b)
         gens = {b: cta(b) for b in range(sms)}
