@@ -45,31 +45,38 @@ constexpr int kMmaMinTokens = 16;  // below this the CUDA-core stacks serve (nor
 // tasks keeps every map 64-byte aligned (sizeof is a multiple of 64).
 struct __align__(64) MmaTask {
     CUtensorMap tmW;        // raw Q4_0 rows: {row bytes, N}, box {144, 128}
-    const float* x;         // input [M][K] fp32: an earlier task's y, or null: the stack input
     float* y;               // output [M][N] fp32
     unsigned* arrivals;     // [tiles] fix-up arrival counters (only grow)
-    int N, K, tiles, n_chunks;
-    long long total;        // tiles * n_chunks
-    int G;                  // CTAs that share the task's chunks (stream-K), <= gridDim.x
-    int hop;                // 1: a hop -- the "done" grid barrier (hop index > 0) before the task
-    int hidx;               // index of the last hop at or before this task
-    int gpos;               // position of the task in its hop group (tasks from one hop to the next)
-    int conv;               // 1 (hops only): convert the input into its x slot, then the "published" barrier
-    int pidx;               // index of the "published" barrier that covers this task's x
-    int xslot;              // x slot: 0 the stack input (converted once a run), 1 an earlier task's y
+    int N, tiles;           // rows; 128-row tiles
+    int tile0;              // the task's first tile in its group's tile sequence
 };
 static_assert(sizeof(MmaTask) % 64 == 0, "tensor maps in an MmaTask array must stay 64-byte aligned");
 
+// A hop group: the tasks from one hop to the next, which share one input and
+// run as ONE GEMM over their concatenated tiles (q, k and v; gate and up), so
+// the stream-K split balances the whole group over the CTAs.
+struct MmaGroup {
+    const float* x;         // input [M][K] fp32: an earlier task's y, or null: the stack input
+    long long total;        // tiles * n_chunks
+    int first, count;       // member tasks [first, first + count), their tiles in this order
+    int tiles, n_chunks, K;
+    int G;                  // CTAs that share the group's chunks (stream-K), <= gridDim.x
+    int hidx;               // hop index: the "done" grid barrier before the group when > 0
+    int conv;               // 1: convert the input into its x slot, then the "published" barrier
+    int pidx;               // index of the "published" barrier that covers the group's x
+    int xslot;              // x slot: 0 the stack input (converted once a run), 1 an earlier task's y
+};
+
 struct MmaStackParams {
     const MmaTask* tasks;
-    int n_tasks, n_hops, n_pubs;  // tasks; hops ("done" barriers + 1); "published" barriers a run
+    const MmaGroup* groups;
+    int n_groups, n_pubs;    // groups (= hops: "done" barriers + 1); "published" barriers a run
     int M, NB;               // tokens; tokens rounded up to 16 (the UMMA N)
     int kmax;                // row stride of the fp16 x slots
     int b_stages;            // x-tile ring depth in chunks
     __half* xbuf;            // [2][NB][kmax] x slots in fp16 (B operand): the stack input, the current y input
     float* xscale;           // [2][kMaxTokens] 2^e per token of each slot
-    float* partial;          // [gridDim.x][slots][NB][128] partial sums of shared tiles
-    int slots;               // partial-sum slots per CTA: 2 per task of the largest hop group
+    float* partial;          // [gridDim.x][2][NB][128] partial sums of a CTA's first and last shared tile
     unsigned long long* bar_done;  // arrivals "done with the tasks before hop h" (hops 1..), all runs
     unsigned long long* bar_pub;   // arrivals "conversion p published", all runs
     unsigned long long* epoch;     // runs completed
@@ -132,19 +139,19 @@ __device__ __forceinline__ unsigned long long pub_target(unsigned long long run,
     return (run * (unsigned long long)n_pubs + (unsigned long long)p + 1ull) * (unsigned long long)G;
 }
 
-// This CTA's chunks of a task: the linear range [lo, hi) of tiles x chunks
-// (none when b is past the task's G CTAs).
+// This CTA's chunks of a group: the linear range [lo, hi) of tiles x chunks
+// (none when b is past the group's G CTAs).
 struct MmaTaskRange {
     long long lo = 0, hi = 0;
     int nc = 1, t0 = 0, t1 = -1;
     bool any = false;
 };
-__device__ __forceinline__ MmaTaskRange mma_task_range(const MmaTask& T, int b) {
+__device__ __forceinline__ MmaTaskRange mma_group_range(const MmaGroup& g, int b) {
     MmaTaskRange r;
-    const int G = __ldg(&T.G);
-    r.nc = __ldg(&T.n_chunks);
+    const int G = __ldg(&g.G);
+    r.nc = __ldg(&g.n_chunks);
     if (b >= G) return r;
-    const long long total = __ldg(&T.total);
+    const long long total = __ldg(&g.total);
     r.lo = sk_lo(total, G, b);
     r.hi = sk_lo(total, G, b + 1);
     r.any = r.hi > r.lo;
@@ -153,6 +160,14 @@ __device__ __forceinline__ MmaTaskRange mma_task_range(const MmaTask& T, int b) 
         r.t1 = (int)((r.hi - 1) / r.nc);
     }
     return r;
+}
+
+// The member task of a group tile (members' tiles are consecutive).
+__device__ __forceinline__ int mma_member(const MmaStackParams& P, const MmaGroup& g, int tile) {
+    int m = __ldg(&g.first);
+    const int end = m + __ldg(&g.count);
+    while (m + 1 < end && __ldg(&P.tasks[m + 1].tile0) <= tile) ++m;
+    return m;
 }
 
 // Token b of a hop's input (fp32 [M][K]; rows b >= M are zero) -> row b of
@@ -312,11 +327,13 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
         RingPos rp;
         uint32_t issued = 0;
         bool ok = *abort == 0;
-        for (int t = 0; t < P.n_tasks && ok; ++t) {
-            const MmaTaskRange tr = mma_task_range(P.tasks[t], b);
+        for (int g = 0; g < P.n_groups && ok; ++g) {
+            const MmaGroup& Gr = P.groups[g];
+            const MmaTaskRange tr = mma_group_range(Gr, b);
             if (!tr.any) continue;
-            const CUtensorMap* map = &P.tasks[t].tmW;
-            int tile = tr.t0, c = (int)(tr.lo - (long long)tr.t0 * tr.nc);
+            int m = mma_member(P, Gr, tr.t0);
+            int local = tr.t0 - __ldg(&P.tasks[m].tile0), mt = __ldg(&P.tasks[m].tiles);
+            int c = (int)(tr.lo - (long long)tr.t0 * tr.nc);
             for (long long L = tr.lo; L < tr.hi; ++L) {
                 if (issued >= kRawStages && !warp_wait(raw_empty + 8 * rp.stage, rp.phase ^ 1u, abort)) {
                     ok = false;
@@ -324,15 +341,19 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
                 }
                 if (leader) {
                     mbar_arrive_expect_tx(raw_full + 8 * rp.stage, kRawChunkBytes);
-                    tma_load_2d(sbase + kMmaSmemRaw + rp.stage * kRawChunkBytes, map, c * kRawRowBytes, tile * kMmaRows,
-                                raw_full + 8 * rp.stage);
+                    tma_load_2d(sbase + kMmaSmemRaw + rp.stage * kRawChunkBytes, &P.tasks[m].tmW, c * kRawRowBytes,
+                                local * kMmaRows, raw_full + 8 * rp.stage);
                 }
                 __syncwarp();
                 ++issued;
                 rp.next(kRawStages);
-                if (++c == tr.nc) {
+                if (++c == tr.nc) {  // next tile, of the next member at the end of this one's
                     c = 0;
-                    ++tile;
+                    if (++local == mt && L + 1 < tr.hi) {
+                        ++m;
+                        local = 0;
+                        mt = __ldg(&P.tasks[m].tiles);
+                    }
                 }
             }
         }
@@ -350,11 +371,12 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
         uint32_t issued = 0;
         int waited = -1;  // the last conversion this warp saw published
         bool ok = *abort == 0;
-        for (int t = 0; t < P.n_tasks && ok; ++t) {
-            const MmaTaskRange tr = mma_task_range(P.tasks[t], b);
+        for (int g = 0; g < P.n_groups && ok; ++g) {
+            const MmaGroup& Gr = P.groups[g];
+            const MmaTaskRange tr = mma_group_range(Gr, b);
             if (!tr.any) continue;
-            const int pidx = __ldg(&P.tasks[t].pidx);
-            const CUtensorMap* map = __ldg(&P.tasks[t].xslot) ? &tmX : &tmXin;
+            const int pidx = __ldg(&Gr.pidx);
+            const CUtensorMap* map = __ldg(&Gr.xslot) ? &tmX : &tmXin;
             if (pidx > waited) {
                 bool go = true;
                 if (leader) {
@@ -401,8 +423,8 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
         RingPos ap, bp;
         bool ok = *abort == 0;
         int k = 0;  // segments (accumulator uses) so far
-        for (int t = 0; t < P.n_tasks && ok; ++t) {
-            const MmaTaskRange tr = mma_task_range(P.tasks[t], b);
+        for (int g = 0; g < P.n_groups && ok; ++g) {
+            const MmaTaskRange tr = mma_group_range(P.groups[g], b);
             if (!tr.any) continue;
             MmaRange R;
             R.lo = tr.lo;
@@ -460,20 +482,21 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
         RingPos rp, ap;
         uint32_t chunks = 0;
         bool ok = *abort == 0;
-        for (int t = 0; t < P.n_tasks; ++t) {
-            const MmaTask& T = P.tasks[t];
-            if (__ldg(&T.hop)) {
-                // every CTA finished the tasks before it (which also ends every read of the
-                // y-input x slot and its scales); for a new input CTA b < NB converts token b,
-                // and the result is published at GPU scope for the other CTAs' tensor copies
-                const int hh = __ldg(&T.hidx);
+        for (int g = 0; g < P.n_groups; ++g) {
+            const MmaGroup& Gr = P.groups[g];
+            {
+                // the group's hop: every CTA finished the groups before it (which also ends
+                // every read of the y-input x slot and its scales); for a new input CTA b < NB
+                // converts token b, and the result is published at GPU scope for the other
+                // CTAs' tensor copies
+                const int hh = __ldg(&Gr.hidx);
                 if (!ok) *abort = 1;
                 hop_bar();  // with the epilogue warps, through every output before the hop
                 if (leader) {
                     bool go = *abort == 0;
                     if (go && hh > 0) {
                         grid_arrive(P.bar_done);
-                        go = grid_wait(P.bar_done, done_target(run, P.n_hops, hh, gridDim.x), P.abort_flag);
+                        go = grid_wait(P.bar_done, done_target(run, P.n_groups, hh, gridDim.x), P.abort_flag);
                     }
                     *s_go = (go && *abort == 0) ? 1 : 0;
                 }
@@ -482,18 +505,18 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
                     *abort = 1;
                     ok = false;
                 }
-                if (ok && __ldg(&T.conv)) {
+                if (ok && __ldg(&Gr.conv)) {
                     if (b < NB) {
                         const float* x =
-                            reinterpret_cast<const float*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.x)));
-                        mma_convert_token(P, x != nullptr ? x : P.x_in, __ldg(&T.K), b, __ldg(&T.xslot), tid, s_red);
+                            reinterpret_cast<const float*>(__ldg(reinterpret_cast<const unsigned long long*>(&Gr.x)));
+                        mma_convert_token(P, x != nullptr ? x : P.x_in, __ldg(&Gr.K), b, __ldg(&Gr.xslot), tid, s_red);
                     }
                     fence_proxy_async_global();
                     dequant_bar();
                     if (leader) grid_arrive(P.bar_pub);
                 }
             }
-            const MmaTaskRange tr = mma_task_range(T, b);
+            const MmaTaskRange tr = mma_group_range(Gr, b);
             if (!tr.any || !ok) continue;  // after a failed wait: no work, but the hops' structure
             // this CTA's chunks of the task, in order (tile boundaries matter only to the MMA
             // and epilogue warps)
@@ -531,40 +554,39 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
         uint32_t n_part = 0;
         int k = 0;  // segments so far, as the MMA warp counts them
         bool ok = *abort == 0;
-        for (int t = 0; t < P.n_tasks; ++t) {
-            const MmaTask& T = P.tasks[t];
-            if (__ldg(&T.hop)) {
-                if (!ok) *abort = 1;
-                hop_bar();  // every output before the hop is stored (and every xscale read done)
-            }
-            const MmaTaskRange tr = mma_task_range(T, b);
+        for (int g = 0; g < P.n_groups; ++g) {
+            const MmaGroup& Gr = P.groups[g];
+            if (!ok) *abort = 1;
+            hop_bar();  // every output before the hop is stored (and every xscale read done)
+            const MmaTaskRange tr = mma_group_range(Gr, b);
             if (!tr.any) continue;
             MmaRange R;
             R.lo = tr.lo;
             R.hi = tr.hi;
             R.t0 = tr.t0;
             R.t1 = tr.t1;
-            const int nc = tr.nc, N = __ldg(&T.N), G = __ldg(&T.G), gp = __ldg(&T.gpos);
-            const float* const xscale = P.xscale + __ldg(&T.xslot) * kMaxTokens;
-            const long long total = __ldg(&T.total);
-            float* const y = reinterpret_cast<float*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.y)));
-            unsigned* const arrivals =
-                reinterpret_cast<unsigned*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.arrivals)));
+            const int nc = tr.nc, G = __ldg(&Gr.G);
+            const float* const xscale = P.xscale + __ldg(&Gr.xslot) * kMaxTokens;
+            const long long total = __ldg(&Gr.total);
             for (int tile = R.t0; tile <= R.t1; ++tile, ++k) {
                 if (!ok) continue;  // no work after a failed wait, but the walk goes on to every hop
                 const MmaSeg S = R.seg(tile, nc);
+                const MmaTask& T = P.tasks[mma_member(P, Gr, tile)];
+                const int N = __ldg(&T.N), lt = tile - __ldg(&T.tile0);  // the member's rows, its tile
+                float* const y = reinterpret_cast<float*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.y)));
+                unsigned* const arrivals =
+                    reinterpret_cast<unsigned*>(__ldg(reinterpret_cast<const unsigned long long*>(&T.arrivals)));
                 if (!warp_wait((k & 1) ? acc_full1 : acc_full0, (k >> 1) & 1, abort)) {
                     ok = false;
                     continue;
                 }
                 tc_fence_after();
                 const uint32_t acc = lane_base + ((k & 1) ? (uint32_t)kAcc1Col : 0u);
-                const int row = tile * kMmaRows + r;
+                const int row = lt * kMmaRows + r;
                 const bool whole = S.c0 == 0 && S.c1 == nc;
-                // a tile shared with other CTAs: this CTA's partial sums go to the two slots of
-                // this task in its hop group -- tasks of a group run without a barrier, so another
-                // CTA may still be adding up an earlier task's tile of this CTA
-                const int slot = b * P.slots + 2 * gp + (tile == R.t0 ? 0 : 1);
+                // a tile shared with other CTAs: this CTA's partial sums go to its slot for its
+                // first or its last tile of the group (groups are apart by a grid barrier)
+                const int slot = 2 * b + (tile == R.t0 ? 0 : 1);
                 float* const mine = P.partial + (size_t)slot * NB * kMmaRows;
                 for (int j0 = 16 * half; j0 < NB; j0 += 32) {
                     float v[16];
@@ -597,7 +619,7 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
                         // the counter only grows: each run adds one arrival per sharing CTA
                         const unsigned n = (unsigned)(bl - bf + 1);
                         // release this CTA's partial sums and, for the last CTA, acquire the others'
-                        last = atom_add_acq_rel_gpu(arrivals + tile, 1u) % n == n - 1;
+                        last = atom_add_acq_rel_gpu(arrivals + lt, 1u) % n == n - 1;
                     }
                     *last_flag = last ? 1 : 0;
                     mbar_arrive(decided);
@@ -611,9 +633,12 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
                     // the last CTA to finish the tile adds every partial in CTA order (the
                     // leader's fence after its arrival acquired them; decided passes it on)
                     // two float4s a thread per pass (n4 is a multiple of 2 * 256), partials
-                    // loaded three CTAs at a time: six loads in flight; sums in CTA order
+                    // loaded two CTAs at a time: four loads in flight; sums in CTA order
                     const int n4 = NB * (kMmaRows / 4);
-                    constexpr int kFixBatch = 3;
+                    constexpr int kFixBatch = 2;
+                    // CTA bb's slot: every CTA after the first one starts inside this tile (slot
+                    // 0); the first one's slot is 1 when it started in an earlier tile
+                    const int slot_f = 2 * bf + (sk_lo(total, G, bf) < (long long)tile * nc ? 1 : 0);
                     for (int f0 = etid; f0 < n4; f0 += 2 * kEpiThreads) {
                         const int f1 = f0 + kEpiThreads;
                         float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
@@ -623,7 +648,7 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
                             for (int i = 0; i < kFixBatch; ++i) {
                                 const int bb = b0 + i;
                                 if (bb <= bl) {
-                                    const int sl = bb * P.slots + 2 * gp + (tile == (int)(sk_lo(total, G, bb) / nc) ? 0 : 1);
+                                    const int sl = bb == bf ? slot_f : 2 * bb;
                                     const float4* src = reinterpret_cast<const float4*>(P.partial + (size_t)sl * NB * kMmaRows);
                                     p0[i] = __ldcg(src + f0);
                                     p1[i] = __ldcg(src + f1);
@@ -650,7 +675,7 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
                             const float sc = __ldcg(xscale + tok), a4[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
                             for (int e = 0; e < 4; ++e) {
-                                const int rr = tile * kMmaRows + 4 * (f % (kMmaRows / 4)) + e;
+                                const int rr = lt * kMmaRows + 4 * (f % (kMmaRows / 4)) + e;
                                 if (rr < N) y[(size_t)tok * N + rr] = a4[e] * sc;
                             }
                         }

@@ -1351,9 +1351,10 @@ int32_t mma_stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint3
     if (!encode) return fail(NEXUS_GPU_ERROR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
     const int NB = (tokens + 15) / 16 * 16, G = d->sms;
     std::vector<MmaTask> ht(n);
+    std::vector<MmaGroup> hg;
     std::vector<size_t> arr_off(n);
     size_t arr_words = 0;
-    int kmax = 0, hops = 0, last_hop = 0, gpos = 0, max_group = 1, pubs = 0, in_pub = -1, cur_pub = -1;
+    int kmax = 0, last_hop = 0, pubs = 0, in_pub = -1, cur_pub = -1;
     for (uint32_t i = 0; i < n; ++i) {
         const NexusGpuStackTaskEx& u = tasks[i];
         if (!u.W || !u.y || u.rows == 0 || u.rows > (uint64_t)INT32_MAX)
@@ -1372,14 +1373,29 @@ int32_t mma_stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint3
         if (u.after >= (int32_t)i || u.after < -1)
             return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "task %u: after=%d is not an earlier task", i, u.after);
         // a hop (grid barriers, x conversion) where the input changes, or where an `after`
-        // task has not been behind a barrier yet
+        // task has not been behind a barrier yet: it starts a new group
         const bool hop = i == 0 || u.x_source != tasks[i - 1].x_source || (u.after >= 0 && u.after >= last_hop);
         if (hop) {
-            ++hops;
             last_hop = (int)i;
-            gpos = 0;
+            MmaGroup g;
+            memset(&g, 0, sizeof(g));
+            g.x = u.x_source < 0 ? nullptr : tasks[u.x_source].y;
+            g.first = (int)i;
+            g.n_chunks = (int)(u.cols / kRawK);
+            g.K = (int)u.cols;
+            g.hidx = (int)hg.size();
+            // x slot 0 holds the stack input, converted at its first hop of a run; slot 1 the
+            // latest earlier task's y, converted at every hop that reads one
+            g.xslot = u.x_source < 0 ? 0 : 1;
+            if (u.x_source >= 0 || in_pub < 0) {
+                g.conv = 1;
+                cur_pub = pubs++;
+                if (u.x_source < 0) in_pub = cur_pub;
+            }
+            g.pidx = u.x_source < 0 ? in_pub : cur_pub;
+            hg.push_back(g);
         }
-        max_group = std::max(max_group, gpos + 1);
+        MmaGroup& grp = hg.back();
         MmaTask& T = ht[i];
         memset(&T, 0, sizeof(T));
         const uint64_t rb = u.cols / 32 * 18;
@@ -1391,41 +1407,34 @@ int32_t mma_stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint3
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return fail(NEXUS_GPU_ERROR_CUDA, "task %u: weight tensor map rejected", i);
-        T.x = u.x_source < 0 ? nullptr : tasks[u.x_source].y;
         T.y = u.y;
         T.N = (int)u.rows;
-        T.K = (int)u.cols;
         T.tiles = (int)((u.rows + kMmaRows - 1) / kMmaRows);
-        T.n_chunks = (int)(u.cols / kRawK);
-        T.total = (long long)T.tiles * T.n_chunks;
-        T.G = tc_ctas(G, T.tiles, T.n_chunks);
-        T.hop = hop ? 1 : 0;
-        T.hidx = hops - 1;
-        T.gpos = gpos++;
-        // x slot 0 holds the stack input, converted at its first hop of a run; slot 1 the
-        // latest earlier task's y, converted at every hop that reads one
-        T.xslot = u.x_source < 0 ? 0 : 1;
-        if (hop && (u.x_source >= 0 || in_pub < 0)) {
-            T.conv = 1;
-            cur_pub = pubs++;
-            if (u.x_source < 0) in_pub = cur_pub;
-        }
-        T.pidx = u.x_source < 0 ? in_pub : cur_pub;
+        T.tile0 = grp.tiles;
+        grp.tiles += T.tiles;
+        grp.count += 1;
         arr_off[i] = arr_words;
         arr_words += (size_t)T.tiles;
-        kmax = std::max(kmax, T.K);
+        kmax = std::max(kmax, (int)u.cols);
     }
+    for (MmaGroup& g : hg) {  // each group one stream-K GEMM over its members' tiles
+        g.total = (long long)g.tiles * g.n_chunks;
+        g.G = tc_ctas(G, g.tiles, g.n_chunks);
+    }
+    const int n_groups = (int)hg.size();
     // device block: tasks (64-byte aligned maps), fp16 x, scales, partial sums, arrival
     // counters, grid barrier / run / exit counters and the abort flag
     size_t off = 0;
     const size_t o_tasks = off;
     off = align256(off + n * sizeof(MmaTask));
+    const size_t o_groups = off;
+    off = align256(off + n_groups * sizeof(MmaGroup));
     const size_t o_x = off;
     off = align256(off + 2 * (size_t)NB * kmax * sizeof(__half));
     const size_t o_scale = off;
     off = align256(off + 2 * kMaxTokens * sizeof(float));
     const size_t o_part = off;
-    off = align256(off + (size_t)G * 2 * max_group * NB * kMmaRows * sizeof(float));
+    off = align256(off + (size_t)G * 2 * NB * kMmaRows * sizeof(float));
     const size_t o_arr = off;
     off = align256(off + arr_words * sizeof(unsigned));
     const size_t o_ctrl = off;
@@ -1447,6 +1456,8 @@ int32_t mma_stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint3
     uint8_t* blk = h->d_block;
     for (uint32_t i = 0; i < n; ++i) ht[i].arrivals = reinterpret_cast<unsigned*>(blk + o_arr) + arr_off[i];
     e = cudaMemcpy(blk + o_tasks, ht.data(), n * sizeof(MmaTask), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(blk + o_groups, hg.data(), n_groups * sizeof(MmaGroup), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         stack_free(h);
@@ -1467,8 +1478,8 @@ int32_t mma_stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint3
     }
     MmaStackParams& P = h->mparams;
     P.tasks = reinterpret_cast<const MmaTask*>(blk + o_tasks);
-    P.n_tasks = (int)n;
-    P.n_hops = hops;
+    P.groups = reinterpret_cast<const MmaGroup*>(blk + o_groups);
+    P.n_groups = n_groups;
     P.n_pubs = pubs;
     P.M = tokens;
     P.NB = NB;
@@ -1477,7 +1488,6 @@ int32_t mma_stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint3
     P.xbuf = reinterpret_cast<__half*>(blk + o_x);
     P.xscale = reinterpret_cast<float*>(blk + o_scale);
     P.partial = reinterpret_cast<float*>(blk + o_part);
-    P.slots = 2 * max_group;
     unsigned long long* ctrl = reinterpret_cast<unsigned long long*>(blk + o_ctrl);
     P.bar_done = ctrl;
     P.bar_pub = ctrl + 1;

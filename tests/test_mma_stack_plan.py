@@ -2,12 +2,15 @@
 nexusllm_b200/csrc/mma_stack_kernels.cuh; mma_stack_create in nexus_gpu.cu),
 restated in Python before any GPU run:
 
-* the host plan: which tasks are hops (a new input, or an `after` task not yet
-  behind a barrier), each task's hop index and stream-K CTA count;
-* every task's chunks are covered once by its CTAs' ranges, and the CTAs the
-  fix-up counts for a shared tile (sk_owner of its first and last chunk) are
-  exactly the CTAs that work on it, so a grow-only arrival counter marks
-  exactly one last arrival per tile in every run;
+* the host plan: the hop groups (tasks from one hop -- a new input, or an
+  `after` task not yet behind a barrier -- to the next), their members' tile
+  offsets, x slots, conversions and stream-K CTA counts;
+* every group's chunks are covered once by its CTAs' ranges, the raw-copy
+  warp's incremental walk names the right member, tile and chunk, the CTAs
+  the fix-up counts for a shared tile (sk_owner of its first and last chunk)
+  are exactly the CTAs that work on it, so a grow-only arrival counter marks
+  exactly one last arrival per tile in every run, and the partial-sum slots
+  the fix-up reads are the ones its CTAs wrote;
 * the two grid barrier counters, simulated with many random interleavings of
   the CTAs' roles over several runs: no conversion starts before every CTA is
   done with the tasks before its hop, no x tile is copied before every CTA
@@ -26,35 +29,38 @@ SMEM_OPTIN = 232448
 
 
 def stack_plan(tasks, input_cols, sms=SMS):
-    """tasks: (rows, cols, x_source, after).  Mirror of mma_stack_create:
-    hops, hop index, stream-K CTAs, group position, and the x slot (0: the
-    stack input, converted at its first hop of a run; 1: an earlier task's y,
-    converted at every hop) with the "published" barrier that covers it."""
-    plan, hops, last_hop, gpos = [], 0, 0, 0
+    """tasks: (rows, cols, x_source, after).  Mirror of mma_stack_create: the
+    hop groups (tasks from one hop to the next, one input) with their members'
+    tile offsets, stream-K CTAs, the x slot (0: the stack input, converted at
+    its first hop of a run; 1: an earlier task's y, converted at every hop) and
+    the "published" barrier that covers it.  Returns (groups, tile0 per task)."""
+    groups, tile0, last_hop = [], [], 0
     pubs, in_pub, cur_pub = 0, -1, -1
     for i, (rows, cols, src, after) in enumerate(tasks):
         assert cols % RAW_K == 0
         assert (input_cols if src < 0 else tasks[src][0]) == cols
         hop = i == 0 or src != tasks[i - 1][2] or (after >= 0 and after >= last_hop)
         if hop:
-            hops += 1
             last_hop = i
-            gpos = 0
-        tiles = -(-rows // ROWS)
-        nc = cols // RAW_K
-        total = tiles * nc
-        conv = hop and (src >= 0 or in_pub < 0)
-        if conv:
-            cur_pub = pubs
-            pubs += 1
-            if src < 0:
-                in_pub = cur_pub
-        plan.append(dict(rows=rows, cols=cols, tiles=tiles, nc=nc, total=total,
-                         G=tc_ctas(sms, tiles, nc), hop=hop, hidx=hops - 1, gpos=gpos,
-                         conv=conv, pidx=in_pub if src < 0 else cur_pub, xslot=0 if src < 0 else 1))
-        gpos += 1
+            conv = src >= 0 or in_pub < 0
+            if conv:
+                cur_pub = pubs
+                pubs += 1
+                if src < 0:
+                    in_pub = cur_pub
+            groups.append(dict(first=i, count=0, tiles=0, nc=cols // RAW_K, hidx=len(groups), conv=conv,
+                               pidx=in_pub if src < 0 else cur_pub, xslot=0 if src < 0 else 1, member_tiles=[]))
+        g = groups[-1]
+        t = -(-rows // ROWS)
+        tile0.append(g["tiles"])
+        g["member_tiles"].append(t)
+        g["tiles"] += t
+        g["count"] += 1
+    for g in groups:
+        g["total"] = g["tiles"] * g["nc"]
+        g["G"] = tc_ctas(sms, g["tiles"], g["nc"])
     stack_plan.pubs = pubs
-    return plan, hops
+    return groups, tile0
 
 
 def decode_tasks(layers, h=4096, kv=1024, f=14336, vocab=128256):
@@ -70,30 +76,70 @@ def decode_tasks(layers, h=4096, kv=1024, f=14336, vocab=128256):
 
 
 def test_hops_of_a_decode_step():
-    plan, hops = stack_plan(decode_tasks(3), 4096)
-    assert [p["hop"] for p in plan[:7]] == [True, False, False, True, True, False, True]
-    assert hops == 4 * 3 + 1  # q, o, gate, down per layer; the head reads the stack input again
-    for i, p in enumerate(plan):
-        assert p["hidx"] == sum(q["hop"] for q in plan[:i + 1]) - 1
+    groups, tile0 = stack_plan(decode_tasks(3), 4096)
+    # q+k+v, o, gate+up, down per layer; the head reads the stack input again
+    assert [g["count"] for g in groups] == [3, 1, 2, 1] * 3 + [1]
+    assert [g["first"] for g in groups[:5]] == [0, 3, 4, 6, 7]
+    assert groups[0]["tiles"] == 32 + 8 + 8 and tile0[:3] == [0, 32, 40] and tile0[4:6] == [0, 112]
     # the stack input is converted once (q of layer 0); o, gate and down convert every layer
-    assert [p["conv"] for p in plan[:14]] == [True, False, False, True, True, False, True,
-                                             False, False, False, True, True, False, True]
-    assert stack_plan.pubs == 1 + 3 * 3 and not plan[-1]["conv"]
-    assert all(plan[i]["pidx"] == 0 and plan[i]["xslot"] == 0 for i in (0, 7, len(plan) - 1))
-    # a task's "published" barrier is its own group's conversion, or the stack input's
-    for i, p in enumerate(plan):
-        last_conv = max(j for j in range(i + 1) if plan[j]["conv"] and plan[j]["xslot"] == p["xslot"])
-        assert p["pidx"] == plan[last_conv]["pidx"]
+    assert [g["conv"] for g in groups[:8]] == [True, True, True, True, False, True, True, True]
+    assert stack_plan.pubs == 1 + 3 * 3 and not groups[-1]["conv"]
+    assert all(groups[i]["pidx"] == 0 and groups[i]["xslot"] == 0 for i in (0, 4, len(groups) - 1))
+    for i, g in enumerate(groups):  # a y-input group's barrier is its own conversion
+        if g["xslot"]:
+            assert g["conv"] and g["pidx"] == sum(h["conv"] for h in groups[:i + 1]) - 1
     # an `after` on the previous task with the same input forces a hop
-    plan, hops = stack_plan([(256, 256, -1, -1), (256, 256, -1, 0)], 256)
-    assert plan[1]["hop"] and hops == 2
+    groups, _ = stack_plan([(256, 256, -1, -1), (256, 256, -1, 0)], 256)
+    assert len(groups) == 2 and not groups[1]["conv"]
+
+
+def member_walk(g, lo, hi):
+    """The raw-copy warp's incremental walk over a CTA's chunks [lo, hi) of a
+    group: (member, member tile, chunk) per chunk."""
+    nc, mtiles = g["nc"], g["member_tiles"]
+    t0 = lo // nc
+    m, acc = 0, 0
+    while m + 1 < len(mtiles) and acc + mtiles[m] <= t0:  # mma_member
+        acc += mtiles[m]
+        m += 1
+    local, mt, c = t0 - acc, mtiles[m], lo - t0 * nc
+    out = []
+    for L in range(lo, hi):
+        out.append((m, local, c))
+        c += 1
+        if c == nc:
+            c = 0
+            local += 1
+            if local == mt and L + 1 < hi:
+                m, local, mt = m + 1, 0, mtiles[m + 1]
+    return out
+
+
+@pytest.mark.parametrize("layers", [1, 2])
+def test_member_walk_and_stream_k_cover(layers):
+    groups, tile0 = stack_plan(decode_tasks(layers), 4096)
+    for g in groups:
+        total, G, nc = g["total"], g["G"], g["nc"]
+        assert 1 <= G <= SMS
+        seen = {}
+        starts = [sum(g["member_tiles"][:m]) for m in range(g["count"])]
+        for b in range(G):
+            lo, hi = sk_lo(total, G, b), sk_lo(total, G, b + 1)
+            assert hi > lo
+            for L, (m, local, c) in zip(range(lo, hi), member_walk(g, lo, hi)):
+                tile = L // nc
+                assert (m, local, c) == (max(k for k in range(g["count"]) if starts[k] <= tile),
+                                         tile - starts[m], L % nc)
+                assert 0 <= local < g["member_tiles"][m]
+                seen[L] = seen.get(L, 0) + 1
+        assert sorted(seen) == list(range(total)) and set(seen.values()) == {1}
 
 
 @pytest.mark.parametrize("rows,cols", [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336), (128256, 4096),
                                        (300, 256), (128, 256), (1, 512), (8192, 28672)])
 def test_stream_k_cover_and_fixup_arrivals(rows, cols):
-    plan, _ = stack_plan([(rows, cols, -1, -1)], cols)
-    p = plan[0]
+    groups, _ = stack_plan([(rows, cols, -1, -1)], cols)
+    p = groups[0]
     total, G, nc = p["total"], p["G"], p["nc"]
     seen = [0] * total
     workers = {}
@@ -122,55 +168,57 @@ def test_stream_k_cover_and_fixup_arrivals(rows, cols):
             assert lasts == 1
 
 
-def test_partial_slots_are_never_shared_within_a_hop_group():
-    """Tasks of one hop group run with no barrier between them: a CTA's
-    partial-sum slots for its shared tiles (2 per task: its range's first and
-    last tile) must differ across the group's tasks, and the slots the fix-up
-    reads for a tile are the ones its CTAs wrote."""
-    plan, _ = stack_plan(decode_tasks(2), 4096)
-    n_slots = 2 * (max(p["gpos"] for p in plan) + 1)
-    assert n_slots == 6  # q, k, v
-    for b in range(SMS):
-        used = {}
-        for t, p in enumerate(plan):
-            G, nc, total = p["G"], p["nc"], p["total"]
-            if b >= G:
-                continue
+@pytest.mark.parametrize("layers", [1, 2])
+def test_partial_slots_of_a_group(layers):
+    """A CTA's partial sums for a group's shared tiles go to slot 2b (its first
+    tile) or 2b + 1 (its last); groups are apart by a grid barrier, so two
+    slots a CTA suffice.  The fix-up reads slot 2 bb for every sharing CTA
+    after the first, and for the first CTA slot 2 bf + 1 exactly when its
+    range started in an earlier tile."""
+    groups, _ = stack_plan(decode_tasks(layers), 4096)
+    for g in groups:
+        total, G, nc = g["total"], g["G"], g["nc"]
+        written = {}  # tile -> {cta: slot}
+        for b in range(G):
             lo, hi = sk_lo(total, G, b), sk_lo(total, G, b + 1)
             t0, t1 = lo // nc, (hi - 1) // nc
+            used = set()
             for tile in range(t0, t1 + 1):
                 c0 = lo - tile * nc if tile == t0 else 0
                 c1 = hi - tile * nc if tile == t1 else nc
                 if c0 == 0 and c1 == nc:
                     continue
-                slot = 2 * p["gpos"] + (0 if tile == t0 else 1)
-                assert slot < n_slots
-                key = (p["hidx"], slot)
-                assert key not in used, (b, t, tile, used.get(key))
-                used[key] = (t, tile)
-                # the fix-up's slot for CTA b of this tile
-                assert 2 * p["gpos"] + (0 if tile == sk_lo(total, G, b) // nc else 1) == slot
+                slot = 2 * b + (0 if tile == t0 else 1)
+                assert slot not in used
+                used.add(slot)
+                written.setdefault(tile, {})[b] = slot
+        for tile, w in written.items():
+            bf, bl = sk_owner(total, G, tile * nc), sk_owner(total, G, (tile + 1) * nc - 1)
+            assert sorted(w) == list(range(bf, bl + 1))
+            slot_f = 2 * bf + (1 if sk_lo(total, G, bf) < tile * nc else 0)
+            for bb, slot in w.items():
+                assert slot == (slot_f if bb == bf else 2 * bb)
 
 
-def _simulate(plan, hops, runs, seed, sms=12, tokens=16):
-    """Random interleavings of every CTA's roles over `runs` runs.  Per hop h:
-    the dequantizing warps wait for "done" (h >= 1) and, when the hop converts,
-    convert (CTAs < NB) and publish; the x-tile warp waits for the hop's
-    "published" barrier before the x tiles of a task in hop h when the CTA has
-    chunks there; the dequantizing warps then finish the CTA's tasks of hop h.
+def _simulate(groups, runs, seed, sms=12, tokens=16):
+    """Random interleavings of every CTA's roles over `runs` runs.  Per group
+    (hop) h: the dequantizing warps wait for "done" (h >= 1) and, when the hop
+    converts, convert (CTAs < NB) and publish; the x-tile warp waits for the
+    group's "published" barrier before its x tiles when the CTA has chunks
+    there; the dequantizing warps then finish the CTA's chunks of the group.
     Returns the number of scheduling steps."""
     rng = random.Random(seed)
     NB = tokens
     n_pubs = stack_plan.pubs
-    hop_task = [next(p for p in plan if p["hidx"] == h) for h in range(hops)]
+    hops = len(groups)
     done = pub = 0
-    # per CTA, the hops in which it has chunks
+    # per CTA, the groups in which it has chunks
     work = []
     for b in range(sms):
         w = set()
-        for p in plan:
-            if b < min(p["G"], sms) and sk_lo(p["total"], min(p["G"], sms), b + 1) > sk_lo(p["total"], min(p["G"], sms), b):
-                w.add(p["hidx"])
+        for g in groups:
+            if b < g["G"] and sk_lo(g["total"], g["G"], b + 1) > sk_lo(g["total"], g["G"], b):
+                w.add(g["hidx"])
         work.append(w)
     converted = {}  # (run, hop) -> CTAs whose conversion finished
     finished = {}   # (run, hop) -> CTAs done with the hop's tasks
@@ -186,7 +234,7 @@ def _simulate(plan, hops, runs, seed, sms=12, tokens=16):
                         yield
                     # every CTA is done with the tasks before hop h
                     assert len(finished.get((run, h - 1), ())) == sms
-                head = hop_task[h]
+                head = groups[h]
                 if head["conv"]:
                     if b < NB:
                         yield
@@ -220,8 +268,8 @@ SMALL = [(2048, 1024, -1, -1), (256, 2048, 0, -1), (1024, 256, 1, -1), (2048, 10
 @pytest.mark.parametrize("seed", range(20))
 @pytest.mark.parametrize("tasks", [decode_tasks(2, h=1024, kv=256, f=2048, vocab=3072), SMALL], ids=["decode", "small"])
 def test_grid_barriers_order_conversion_and_copies(seed, tasks):
-    plan, hops = stack_plan(tasks, 1024, sms=12)
-    _simulate(plan, hops, runs=3, seed=seed, sms=12, tokens=8)
+    groups, _ = stack_plan(tasks, 1024, sms=12)
+    _simulate(groups, runs=3, seed=seed, sms=12, tokens=8)
 
 
 def test_shared_memory_budget():

@@ -4,8 +4,11 @@ persistent tcgen05 launch.
 
 Every task of every token must stay within the 1e-3 L2-relative GEMV
 tolerance of the C oracle, fed the input the stack gave that task, and match
-the single tcgen05 GEMM (nexus_gpu_gemv with M rows) on that input: same x
-conversion rule, same stream-K split and fix-up order.  Runs repeat bit for
+the single tcgen05 GEMM (nexus_gpu_gemv with M rows) on that input within
+SAME_TOL: the same x conversion rule and products, but the stack splits a
+hop group's concatenated tiles (q, k and v together), so its stream-K
+boundaries -- the grouping of the fp32 chunk sums -- differ from the single
+GEMM's.  Runs repeat bit for
 bit, also as CUDA-graph replays, with no stale rows after a run with other
 inputs.  Shapes outside the path are refused with an error.
 """
@@ -22,6 +25,7 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 TOL = 1e-3
+SAME_TOL = 1e-5  # fp32 reassociation of the chunk sums only
 
 
 @pytest.fixture(scope="module")
@@ -82,7 +86,7 @@ def test_mma_stack_matches_oracle_and_single_gemm(L, port, tokens, hidden, kv, f
             ref = single_gemm(L, Ws[i], xin.contiguous(), rows, cols)
             torch.cuda.synchronize()
             err = oracle.l2_rel(ys[i].cpu().numpy().reshape(-1), ref.cpu().numpy().reshape(-1))
-            assert err <= 1e-6, (i, name, err)
+            assert err <= SAME_TOL, (i, name, err)
         Wh = {i: Ws[i].cpu().numpy() for i in (0, 3, 6, len(spec) - 1)}
         for t in (0, tokens // 2, tokens - 1):
             for i in Wh:
