@@ -516,6 +516,9 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
                     if (leader) grid_arrive(P.bar_pub);
                 }
             }
+            // a group's chunks are decoded only after its hop, so none of its MMAs -- and none of
+            // its partial sums, which reuse the previous group's slots -- comes before every
+            // CTA is through the "done" barrier, even where the x tiles need no publication
             const MmaTaskRange tr = mma_group_range(Gr, b);
             if (!tr.any || !ok) continue;  // after a failed wait: no work, but the hops' structure
             // this CTA's chunks of the task, in order (tile boundaries matter only to the MMA
