@@ -74,6 +74,8 @@ struct MmaStackParams {
     int M, NB;               // tokens; tokens rounded up to 16 (the UMMA N)
     int kmax;                // row stride of the fp16 x slots
     int b_stages;            // x-tile ring depth in chunks
+    int raw_stages;          // raw-chunk ring depth (the rest of the ring budget after the x tiles)
+    int raw_base;            // byte offset of the raw-chunk ring (after the x tiles, 1024-aligned)
     __half* xbuf;            // [2][NB][kmax] x slots in fp16 (B operand): the stack input, the current y input
     float* xscale;           // [2][kMaxTokens] 2^e per token of each slot
     float* partial;          // [gridDim.x][2][NB][128] partial sums of a CTA's first and last shared tile
@@ -229,8 +231,17 @@ constexpr int kMmaStackThreads = kMmaThreads + kEpiThreads + 32;
 // 1 in the last 64 columns.
 constexpr int kAcc1Col = kAccCols + kAStageCols * kAStages;
 static_assert(kAcc1Col + kAccCols <= kTmemCols, "two accumulators and the A stages exceed tensor memory");
-// + the hop decision, 16 warp maxima and the second accumulator's two barriers
-constexpr int kMmaStackSmemBytes = kMmaSmemBytes + 128;
+// Shared memory: one ring budget, split by the host between the x tiles (a
+// few chunks: they come from L2) and the raw weight chunks (as many as fit:
+// they come from HBM, about 3 us after their copies are issued under load,
+// so the raw ring's depth sets the streaming rate); then the barriers, the
+// TMEM address and flags, the hop decision, 16 warp maxima and the second
+// accumulator's two barriers, and the 1024-byte alignment slack.
+constexpr int kStackRingBytes = 224 * 1024;
+constexpr int kStackRawMax = 12;
+constexpr int kStackBarCount = 2 * kStackRawMax + 2 * kAStages + 2 * kMaxBStages + 5;
+constexpr int kStackSmemBar = kStackRingBytes;
+constexpr int kMmaStackSmemBytes = kStackSmemBar + 8 * kStackBarCount + 16 + 128 + 1024;
 
 // The hop barrier of the dequantizing and the epilogue warps (named barrier 2).
 __device__ __forceinline__ void hop_bar() {
@@ -264,13 +275,13 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
     const uint32_t sraw = smem_u32(mma_smem_raw);
     const uint32_t sbase = (sraw + 1023u) & ~1023u;  // 1024-byte aligned: swizzle atoms
     uint8_t* smem = mma_smem_raw + (sbase - sraw);
-    const uint32_t bar0 = sbase + kMmaSmemBar;
-    const uint32_t raw_full = bar0, raw_empty = raw_full + 8 * kRawStages;
-    const uint32_t a_full = raw_empty + 8 * kRawStages, a_empty = a_full + 8 * kAStages;
+    const uint32_t bar0 = sbase + kStackSmemBar;
+    const uint32_t raw_full = bar0, raw_empty = raw_full + 8 * kStackRawMax;
+    const uint32_t a_full = raw_empty + 8 * kStackRawMax, a_empty = a_full + 8 * kAStages;
     const uint32_t b_full = a_empty + 8 * kAStages, b_empty = b_full + 8 * kMaxBStages;
     const uint32_t acc_full0 = b_empty + 8 * kMaxBStages, acc_empty0 = acc_full0 + 8, drain = acc_empty0 + 8;
     const uint32_t part_done = drain + 8, decided = part_done + 8;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kMmaSmemBar + 8 * kMmaBarCount);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kStackSmemBar + 8 * kStackBarCount);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
     volatile int* s_go = reinterpret_cast<volatile int*>(tmem_slot + 3);
@@ -280,11 +291,12 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int b = blockIdx.x, NB = P.NB;
     const uint32_t nbs = (uint32_t)P.b_stages, b_unit = (uint32_t)NB * 128u, b_stage = 4u * b_unit;
+    const uint32_t nrs = (uint32_t)P.raw_stages, raw_ring = sbase + (uint32_t)P.raw_base;
     // this run's number (runs are stream-ordered; the epoch advances after every CTA left)
     const unsigned long long run = *reinterpret_cast<volatile unsigned long long*>(P.epoch);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kRawStages; ++s) {
+        for (int s = 0; s < kStackRawMax; ++s) {
             mbar_init(raw_full + 8 * s, 1);
             mbar_init(raw_empty + 8 * s, kDequantWarps);
         }
@@ -335,18 +347,18 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
             int local = tr.t0 - __ldg(&P.tasks[m].tile0), mt = __ldg(&P.tasks[m].tiles);
             int c = (int)(tr.lo - (long long)tr.t0 * tr.nc);
             for (long long L = tr.lo; L < tr.hi; ++L) {
-                if (issued >= kRawStages && !warp_wait(raw_empty + 8 * rp.stage, rp.phase ^ 1u, abort)) {
+                if (issued >= nrs && !warp_wait(raw_empty + 8 * rp.stage, rp.phase ^ 1u, abort)) {
                     ok = false;
                     break;
                 }
                 if (leader) {
                     mbar_arrive_expect_tx(raw_full + 8 * rp.stage, kRawChunkBytes);
-                    tma_load_2d(sbase + kMmaSmemRaw + rp.stage * kRawChunkBytes, &P.tasks[m].tmW, c * kRawRowBytes,
+                    tma_load_2d(raw_ring + rp.stage * kRawChunkBytes, &P.tasks[m].tmW, c * kRawRowBytes,
                                 local * kMmaRows, raw_full + 8 * rp.stage);
                 }
                 __syncwarp();
                 ++issued;
-                rp.next(kRawStages);
+                rp.next(nrs);
                 if (++c == tr.nc) {  // next tile, of the next member at the end of this one's
                     c = 0;
                     if (++local == mt && L + 1 < tr.hi) {
@@ -358,9 +370,9 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
             }
         }
         if (leader && *abort)  // leave no copy in flight
-            for (uint32_t k = 0; k < issued && k < (uint32_t)kRawStages; ++k) {
+            for (uint32_t k = 0; k < issued && k < nrs; ++k) {
                 const uint32_t j = issued - 1 - k;
-                mbar_wait_bounded(raw_full + 8 * (j % kRawStages), (j / kRawStages) & 1);
+                mbar_wait_bounded(raw_full + 8 * (j % nrs), (j / nrs) & 1);
             }
         __syncwarp();
     } else if (warp == kXWarp) {
@@ -397,7 +409,7 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
                     break;
                 }
                 if (leader) {
-                    const uint32_t dst = sbase + kMmaSmemB + bp.stage * b_stage, bar = b_full + 8 * bp.stage;
+                    const uint32_t dst = sbase + bp.stage * b_stage, bar = b_full + 8 * bp.stage;
                     mbar_arrive_expect_tx(bar, b_stage);
 #pragma unroll
                     for (int u = 0; u < kUnitsPerChunk; ++u)
@@ -448,7 +460,7 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
                     }
                     tc_fence_after();
                     const uint32_t a0 = tmem_d + kAccCols + kAStageCols * ap.stage;
-                    const uint64_t b0 = umma_desc_sw128(sbase + kMmaSmemB + bp.stage * b_stage);
+                    const uint64_t b0 = umma_desc_sw128(sbase + bp.stage * b_stage);
                     if (leader) {
 #pragma unroll
                         for (int u = 0; u < kUnitsPerChunk; ++u) {
@@ -523,14 +535,14 @@ __global__ void __launch_bounds__(kMmaStackThreads, 1)
             if (!tr.any || !ok) continue;  // after a failed wait: no work, but the hops' structure
             // this CTA's chunks of the task, in order (tile boundaries matter only to the MMA
             // and epilogue warps)
-            for (long long L = tr.lo; L < tr.hi; ++L, ++chunks, rp.next(kRawStages), ap.next(kAStages)) {
+            for (long long L = tr.lo; L < tr.hi; ++L, ++chunks, rp.next(nrs), ap.next(kAStages)) {
                 if (!warp_wait(raw_full + 8 * rp.stage, rp.phase, abort) ||
                     (chunks >= kAStages && !warp_wait(a_empty + 8 * ap.stage, ap.phase ^ 1u, abort))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t raw_row = sbase + kMmaSmemRaw + rp.stage * kRawChunkBytes + (uint32_t)r * kRawRowBytes;
+                const uint32_t raw_row = raw_ring + rp.stage * kRawChunkBytes + (uint32_t)r * kRawRowBytes;
                 const uint32_t ta = lane_base + kAccCols + kAStageCols * ap.stage;
                 switch (grp) {
                     case 0: q4_unit_tmem_lean<0>(raw_row, ta); break;

@@ -1484,7 +1484,10 @@ int32_t mma_stack_create(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint3
     P.M = tokens;
     P.NB = NB;
     P.kmax = kmax;
-    P.b_stages = std::min(kMaxBStages, kBRingBytes / (NB * 512));
+    // the ring budget: x tiles for about 6 chunks' MMAs (at least 3), raw chunks in the rest
+    P.b_stages = std::max(3, std::min(6, 48 * 1024 / (NB * 512)));
+    P.raw_base = (P.b_stages * NB * 512 + 1023) / 1024 * 1024;
+    P.raw_stages = std::min(kStackRawMax, (kStackRingBytes - P.raw_base) / kRawChunkBytes);
     P.xbuf = reinterpret_cast<__half*>(blk + o_x);
     P.xscale = reinterpret_cast<float*>(blk + o_scale);
     P.partial = reinterpret_cast<float*>(blk + o_part);

@@ -21,7 +21,7 @@ import random
 
 import pytest
 
-from tests.test_mma_plan import SMEM_BYTES, sk_lo, sk_owner, tc_ctas
+from tests.test_mma_plan import sk_lo, sk_owner, tc_ctas
 
 ROWS, RAW_K = 128, 256
 SMS = 148
@@ -272,8 +272,29 @@ def test_grid_barriers_order_conversion_and_copies(seed, tasks):
     _simulate(groups, runs=3, seed=seed, sms=12, tokens=8)
 
 
+RING, RAW_MAX, RAW_CHUNK, A_STAGES, B_MAX = 224 * 1024, 12, 128 * 144, 3, 12
+
+
+def ring_split(NB):
+    """Mirror of mma_stack_create's split of the ring budget: x-tile stages
+    for about 6 chunks (at least 3), the raw-chunk ring 1024-aligned after
+    them with as many stages as fit."""
+    b_stages = max(3, min(6, 48 * 1024 // (NB * 512)))
+    raw_base = -(-b_stages * NB * 512 // 1024) * 1024
+    return b_stages, raw_base, min(RAW_MAX, (RING - raw_base) // RAW_CHUNK)
+
+
+@pytest.mark.parametrize("NB", [16, 32, 48, 64])
+def test_ring_split(NB):
+    b_stages, raw_base, raw_stages = ring_split(NB)
+    assert 3 <= b_stages <= B_MAX and raw_base % 1024 == 0 and raw_base >= b_stages * NB * 512
+    assert 5 <= raw_stages <= RAW_MAX and raw_base + raw_stages * RAW_CHUNK <= RING
+    assert (NB * 512) % 1024 == 0  # every x stage starts on a 128-byte-swizzle atom
+
+
 def test_shared_memory_budget():
-    stack_smem = SMEM_BYTES + 128
+    bars = 2 * RAW_MAX + 2 * A_STAGES + 2 * B_MAX + 5
+    stack_smem = RING + 8 * bars + 16 + 128 + 1024
     assert stack_smem <= SMEM_OPTIN
     # the hop decision and 16 warp maxima follow the TMEM address, abort and last flags;
     # then the second accumulator's full and empty barriers (8-byte aligned)
