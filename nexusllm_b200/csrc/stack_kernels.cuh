@@ -811,13 +811,20 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                         float rv = 0.0f;
                         if (FX && lane == 0) rv = residual_of(s_ep + warp, r0 + rl, sys, par, P, s_res, rr.x);
                         float acc = row_partial<F, G>(row, wi, has, X);
-#pragma unroll
-                        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
                         float up = 0.0f;  // a pair's up row: the same row of W2, half a slot on
                         if (FX && half) {
-                            up = row_partial<F, G>(row + half, wi, has, X);
+                            // both dot products, then one reduction for both as the two-row path
+                            // does (lanes 0-15 the gate row's sum, 16-31 the up row's: the same
+                            // trees as two one-row reductions)
+                            const float u = row_partial<F, G>(row + half, wi, has, X);
+                            float v = (lane < 16 ? acc : u) + __shfl_xor_sync(0xffffffffu, lane < 16 ? u : acc, 16);
 #pragma unroll
-                            for (int o = 16; o > 0; o >>= 1) up += __shfl_xor_sync(0xffffffffu, up, o);
+                            for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                            acc = v;
+                            up = __shfl_sync(0xffffffffu, v, 16);
+                        } else {
+#pragma unroll
+                            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
                         }
                         if (S == 1) {
                             if (lane == 0) put_row<FX>(P, yl, yo, to, par, r0 + rl, acc, s_ep + warp, rv, up);
