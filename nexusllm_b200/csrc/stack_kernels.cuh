@@ -673,14 +673,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
         const int t_head = t;
         const int K = __ldg(&H.K), S = __ldg(&H.segments);
         const int NW = __ldg(&H.nwi), SW = __ldg(&H.seg_wi), J = __ldg(&H.wi_per_lane);
-        // ordering dependency: every row of `after` stored in this run; each
-        // thread checks its share of the rows (a residual's rows are checked as
-        // they are read, residual_of)
         bool ok = *reinterpret_cast<volatile unsigned*>(P.abort_flag) == 0;  // poisoned by an earlier run
         const int src = __ldg(&H.src), after = __ldg(&H.after);
-        if (ok && after >= 0)
-            ok = wait_rows_tagged(ld_task_ptr(&P.tasks[after].tg), __ldg(&H.after_rows), par, sys, tid, P.abort_flag,
-                                  P.wait_polls);
         consumer_bar();  // every warp is done with the previous group's x staging
         const float4* nw =
             FX ? reinterpret_cast<const float4*>(__ldg(reinterpret_cast<const unsigned long long*>(&H.norm_w))) : nullptr;
@@ -699,6 +693,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                 if (lane == 0) s_norm[warp] = ss;
             }
         }
+        // ordering dependency: every row of `after` stored in this run, checked after the
+        // staging (which never depends on it: the stack input is fixed for the run and a
+        // task's output carries its own tags), so the staging's L2 reads overlap the wait
+        // for the other CTAs' last rows; each thread checks its share of the rows (a
+        // residual's rows are checked as they are read, residual_of)
+        if (ok && after >= 0)
+            ok = wait_rows_tagged(ld_task_ptr(&P.tasks[after].tg), __ldg(&H.after_rows), par, sys, tid, P.abort_flag,
+                                  P.wait_polls);
         // fused variant: the head task's residual rows of this CTA into shared memory, read
         // once here with the staging (the residual's task finished before this group's input
         // in a decode layer), so the row stores read no global memory
