@@ -186,9 +186,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_mt_kernel(const St
         const int NW = __ldg(&H.nwi), SW = __ldg(&H.seg_wi), J = __ldg(&H.wi_per_lane);
         bool ok = *reinterpret_cast<volatile unsigned*>(P.abort_flag) == 0;
         const int src = __ldg(&H.src), after = __ldg(&H.after);
-        if (ok && after >= 0)
-            ok = wait_rows_tagged(ld_task_ptr(&P.tasks[after].tg), MT * __ldg(&H.after_rows), par, false, tid,
-                                  P.abort_flag, P.wait_polls);
         consumer_bar();  // every warp is done with the previous group's x staging
         const int nxb = K / 32, nxbp = x_stage_planes_len(K), hf = lane & 1;
         const uint32_t tok_bytes = 80u * (uint32_t)nxbp;  // one token's plane set
@@ -218,6 +215,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_mt_kernel(const St
                 quantize_x_pair(e, hf, idx < MT * nxb, xs + (uint32_t)min(tk, MT - 1) * tok_bytes, nxbp, b);
             }
         }
+        // the `after` rows after the staging, which never depends on them (as the
+        // single-token kernel does): the staging's L2 reads overlap the wait
+        if (ok && after >= 0)
+            ok = wait_rows_tagged(ld_task_ptr(&P.tasks[after].tg), MT * __ldg(&H.after_rows), par, false, tid,
+                                  P.abort_flag, P.wait_polls);
         if (consumer_bar_any(!ok)) break;  // every consumer leaves together after a failed wait
         const int sg = warp % S, grp = warp / S, n_grp = kConsumerWarps / S;
         int wi4[kMaxJ];
