@@ -249,6 +249,7 @@ __device__ __forceinline__ bool wait_rows_tagged(const uint32_t* tg, int n, uint
 // sums, the per-warp epilogue descriptors, the per-warp output offsets and the
 // group head task's residual rows of this CTA (fused variant)
 constexpr int kResStageMax = 128;
+static_assert(kResStageMax <= kConsumers, "a group head stages at most one residual row a thread");
 constexpr int kStackBarBytes = 16 * kMaxStages + 32 + 4 * 16 + 16 * 16 + 16 * 16 + 4 * kResStageMax;
 constexpr int kStackSmemHeader = ((kStackBarBytes + 127) / 128) * 128 + kSmemHeader - kBarBytes;
 
@@ -415,12 +416,14 @@ __device__ __forceinline__ uint32_t residual_wait(const uint32_t* p, uint32_t pa
     }
     return w;
 }
-constexpr uint64_t kResInSmem = 2;
-__device__ __forceinline__ float residual_of(const volatile float4* ep, int r, bool sys, uint32_t par,
-                                             const StackParams& P, const volatile float* s_res, int row0) {
-    const uint64_t a = ep_residual(ld_ep(ep));
-    if (!a) return 0.0f;
-    if (a == kResInSmem) return s_res[r - row0];
+constexpr uint32_t kResInSmem = 2;
+// The residual of row r under the descriptor e: the CTA's rows staged in shared
+// memory (e.x = kResInSmem, e.y = the first staged row), a task's tagged copy
+// (bit 0 set) or the stack input's floats.
+__device__ __forceinline__ float residual_of(const float4 e, int r, bool sys, uint32_t par, const StackParams& P,
+                                             const volatile float* s_res) {
+    if (__float_as_uint(e.x) == kResInSmem) return s_res[r - __float_as_int(e.y)];
+    const uint64_t a = ep_residual(e);
     if (a & 1u) {
         const uint32_t* p = reinterpret_cast<const uint32_t*>(a - 1) + r;
         uint32_t w = ld_tagged1(p, sys);
@@ -433,17 +436,17 @@ __device__ __forceinline__ float residual_of(const volatile float4* ep, int r, b
 // Write row r (of this rank's slice) of task T: this rank's output and --
 // sharded -- every peer's copy (plain stores over NVLink).  v is the row's
 // dot product; in the fused variant (FX) the epilogue of the descriptor ep
-// is applied: y = v * scale + rv, or silu(v * scale) * (u * scale) + rv for
-// a gate+up pair (u: the up row's dot product, rv: residual_of).
-// yl: this rank's output at its first row.  The warp's output descriptor od
-// (shared, written once per task) holds yo, the float offset of that row in
-// every rank's stack block (sharded stacks), and to, the word offset of that
+// is applied: y = v * scale + res, or silu(v * scale) * (u * scale) + res for
+// a gate+up pair (u: the up row's dot product, res: residual_of, read here
+// after the dot product so that nothing of it is live during the row).
+// yl: this rank's output at its first row; yo: the float offset of that row
+// in every rank's stack block (sharded stacks); to: the word offset of that
 // row of the task's tagged copy in every rank's block (0 when no task depends
-// on this one); reading it at the store keeps both out of the row loop's
-// registers.
+// on this one).
 template <bool FX>
 __device__ __forceinline__ void put_row(const StackParams& P, float* yl, uint64_t yo, uint64_t to, uint32_t par,
-                                        int r, float v, const volatile float4* ep, float rv, float u) {
+                                        int r, float v, const volatile float4* ep, const volatile float* s_res,
+                                        float u) {
     if constexpr (FX) {
         const float4 e = ld_ep(ep);
         if (e.z != 1.0f) v = __fmul_rn(v, e.z);
@@ -451,7 +454,7 @@ __device__ __forceinline__ void put_row(const StackParams& P, float* yl, uint64_
             if (e.z != 1.0f) u = __fmul_rn(u, e.z);
             v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u);
         }
-        if (ep_residual(e)) v = __fadd_rn(v, rv);
+        if (ep_residual(e)) v = __fadd_rn(v, residual_of(e, r, P.world > 1, par, P, s_res));
     }
     yl[r] = v;
     const bool sys = P.world > 1;
@@ -482,9 +485,28 @@ __device__ __forceinline__ float stage_x(const float4* xv, const uint32_t* xt,
     for (int base = 0; base < nxb; base += kConsumers / 2) {
         const int b = base + (tid >> 1);
         float e[16];
+        // fused variant: the RMSNorm weights are loaded before the wait for x, so that
+        // their L2 latency overlaps it instead of following it
+        float4 wv[4];
+        if (FX && nw != nullptr && b < nxb) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) wv[q] = __ldg(nw + 8 * b + 4 * hf + q);
+        }
         if (b >= nxb) {
 #pragma unroll
             for (int k = 0; k < 16; ++k) e[k] = 0.0f;
+        } else if (FX && xt2 != nullptr && xt != nullptr) {
+            // SwiGLU input: both tagged vectors read at once, then waited for if either is stale
+            float u[16];
+            const bool fresh = ld_tagged16(xt + 32 * b + 16 * hf, par, sys, e);
+            const bool fresh2 = ld_tagged16(xt2 + 32 * b + 16 * hf, par, sys, u);
+            if (!fresh) ok = wait_tagged16(xt + 32 * b + 16 * hf, par, sys, e, P.abort_flag, P.wait_polls) && ok;
+            if (!fresh2) ok = wait_tagged16(xt2 + 32 * b + 16 * hf, par, sys, u, P.abort_flag, P.wait_polls) && ok;
+            // silu(gate) * up (transformer_ops.hpp:86-95).  Every CTA computes the whole
+            // vector, so with the __expf / __fdividef intrinsics (relative error ~1e-6, far
+            // below the 16-bit fixed-point quantization that follows)
+#pragma unroll
+            for (int k = 0; k < 16; ++k) e[k] = __fmul_rn(__fdividef(e[k], __fadd_rn(1.0f, __expf(-e[k]))), u[k]);
         } else if (xt != nullptr) {
             ok = wait_tagged16(xt + 32 * b + 16 * hf, par, sys, e, P.abort_flag, P.wait_polls) && ok;
         } else {
@@ -498,19 +520,10 @@ __device__ __forceinline__ float stage_x(const float4* xv, const uint32_t* xt,
             }
         }
         if constexpr (FX) {
-            // SwiGLU (transformer_ops.hpp:86-95): silu(gate) * up.  Every CTA computes the
-            // whole vector, so with the __expf / __fdividef intrinsics (relative error ~1e-6,
-            // far below the 16-bit fixed-point quantization that follows)
-            if (xt2 != nullptr && b < nxb) {
-                float u[16];
-                ok = wait_tagged16(xt2 + 32 * b + 16 * hf, par, sys, u, P.abort_flag, P.wait_polls) && ok;
-#pragma unroll
-                for (int k = 0; k < 16; ++k) e[k] = __fmul_rn(__fdividef(e[k], __fadd_rn(1.0f, __expf(-e[k]))), u[k]);
-            }
             if (nw != nullptr && b < nxb) {  // RMSNorm: sum x^2 here, quantize x * w; 1/rms scales the rows
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    const float4 w = __ldg(nw + 8 * b + 4 * hf + q);
+                    const float4 w = wv[q];
                     const float ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
@@ -670,7 +683,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
     for (int t = 0; t < P.n_tasks && !stop;) {
         // ---- group head: wait for the input, stage it, load the x slices
         const StackTask& H = P.tasks[t];
-        const int t_head = t;
         const int K = __ldg(&H.K), S = __ldg(&H.segments);
         const int NW = __ldg(&H.nwi), SW = __ldg(&H.seg_wi), J = __ldg(&H.wi_per_lane);
         bool ok = *reinterpret_cast<volatile unsigned*>(P.abort_flag) == 0;  // poisoned by an earlier run
@@ -678,6 +690,24 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
         consumer_bar();  // every warp is done with the previous group's x staging
         const float4* nw =
             FX ? reinterpret_cast<const float4*>(__ldg(reinterpret_cast<const unsigned long long*>(&H.norm_w))) : nullptr;
+        // fused variant: the head task's residual rows of this CTA (at most one a thread),
+        // loaded before the staging so that their L2 latency overlaps it; checked and
+        // written to shared memory after it
+        int res_rows = 0;  // > 0: the head task's residual rows of this CTA are staged
+        bool res_in = false;
+        uint32_t res_w = 0;
+        if constexpr (FX) {
+            const int rs = __ldg(&H.res_src);
+            res_in = __ldg(&H.res_input) != 0;
+            const int2 hr = __ldg(P.cta_rows + (size_t)t * n_cta + c);
+            if ((res_in || rs >= 0) && hr.y - hr.x <= kResStageMax) {
+                res_rows = hr.y - hr.x;
+                const int first = __ldg(&H.row_off) + hr.x;
+                if (tid < res_rows)
+                    res_w = res_in ? __float_as_uint(__ldcg(P.x_in + first + tid))
+                                   : ld_tagged1(ld_task_ptr(&P.tasks[rs].tg) + first + tid, sys);
+            }
+        }
         {   // read x (L2; a task's output waits for this run's tags), apply the fusions,
             // quantize, two lanes per 32-element block
             const float4* xv = reinterpret_cast<const float4*>(P.x_in);
@@ -701,25 +731,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
         if (ok && after >= 0)
             ok = wait_rows_tagged(ld_task_ptr(&P.tasks[after].tg), __ldg(&H.after_rows), par, sys, tid, P.abort_flag,
                                   P.wait_polls);
-        // fused variant: the head task's residual rows of this CTA into shared memory, read
-        // once here with the staging (the residual's task finished before this group's input
-        // in a decode layer), so the row stores read no global memory
-        int res_rows = 0;
+        // fused variant: the head task's residual rows of this CTA into shared memory (the
+        // residual's task finished before this group's input in a decode layer, so its word
+        // loaded above almost always carries this run's parity), so the row stores read no
+        // global memory
         if constexpr (FX) {
-            const int rs = __ldg(&H.res_src), rin = __ldg(&H.res_input);
-            const int2 hr = __ldg(P.cta_rows + (size_t)t * n_cta + c);
-            if ((rin || rs >= 0) && hr.y - hr.x <= kResStageMax) {
-                res_rows = hr.y - hr.x;
-                const int first = __ldg(&H.row_off) + hr.x;
-                const uint32_t* rt = rs >= 0 ? ld_task_ptr(&P.tasks[rs].tg) + first : nullptr;
-                for (int i = tid; i < res_rows; i += kConsumers) {
-                    if (rin) {
-                        s_res[i] = __ldcg(P.x_in + first + i);
-                    } else {
-                        uint32_t w = ld_tagged1(rt + i, sys);
-                        if (((w ^ par) & 1u) != 0) w = residual_wait(rt + i, par, sys, P.abort_flag, P.wait_polls);
-                        s_res[i] = untag(w);
+            if (tid < res_rows) {
+                if (res_in) {
+                    s_res[tid] = __uint_as_float(res_w);
+                } else {
+                    if (((res_w ^ par) & 1u) != 0) {  // not yet stored: wait for it (rare)
+                        const int2 hr = __ldg(P.cta_rows + (size_t)t * n_cta + c);
+                        res_w = residual_wait(ld_task_ptr(&P.tasks[__ldg(&H.res_src)].tg) + __ldg(&H.row_off) + hr.x + tid,
+                                              par, sys, P.abort_flag, P.wait_polls);
                     }
+                    s_res[tid] = untag(res_w);
                 }
             }
         }
@@ -751,6 +777,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
         }
 
         // ---- the group's tasks
+        bool res_head = res_rows > 0;  // the next task is the head: its residual rows are staged
         for (;;) {
             const StackTask& T = P.tasks[t];
             // task constants, held in registers for the task's rows
@@ -768,11 +795,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                 uint64_t rp = 0;
                 if (ld_task_i32(&T.res_input)) rp = (uint64_t)(P.x_in + ld_task_i32(&T.row_off));
                 else if (rs >= 0) rp = (uint64_t)(ld_task_ptr(&P.tasks[rs].tg) + ld_task_i32(&T.row_off)) | 1u;
-                if (rp && t == t_head && res_rows > 0) rp = kResInSmem;
-                s_ep[warp].x = __uint_as_float((uint32_t)rp);
-                s_ep[warp].y = __uint_as_float((uint32_t)(rp >> 32));
+                if (rp && res_head) {  // staged at the group head: e.y = the CTA's first row
+                    s_ep[warp].x = __uint_as_float(kResInSmem);
+                    s_ep[warp].y = __int_as_float(rr.x);
+                } else {
+                    s_ep[warp].x = __uint_as_float((uint32_t)rp);
+                    s_ep[warp].y = __uint_as_float((uint32_t)(rp >> 32));
+                }
                 s_ep[warp].w = __int_as_float(half != 0u);
             }
+            res_head = false;
             int rot = 0;  // (stage index * R) % n_grp: the group that takes a stage's first row
             for (int r0 = rr.x; r0 < rr.y; r0 += R) {
                 const int nr = min(R, rr.y - r0);
@@ -801,17 +833,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                             const int rme = rl + (lane < 16 ? 0 : n_grp);
                             if ((lane & 15) == 0) {
                                 if (S == 1)
-                                    put_row<FX>(P, yl, yo, to, par, r0 + rme, v, s_ep + warp,
-                                                FX ? residual_of(s_ep + warp, r0 + rme, sys, par, P, s_res, rr.x) : 0.0f,
-                                                0.0f);
+                                    put_row<FX>(P, yl, yo, to, par, r0 + rme, v, s_ep + warp, s_res, 0.0f);
                                 else slots[s * P.slot_stride + rme * S + sg] = v;
                             }
                         }
                     }
                     for (; rl < nr; rl += n_grp) {
                         const uint32_t row = base + (uint32_t)(rl * rbytes);
-                        float rv = 0.0f;
-                        if (FX && lane == 0) rv = residual_of(s_ep + warp, r0 + rl, sys, par, P, s_res, rr.x);
                         float acc = row_partial<F, G>(row, wi, has, X);
                         float up = 0.0f;  // a pair's up row: the same row of W2, half a slot on
                         if (FX && half) {
@@ -829,7 +857,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                             for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
                         }
                         if (S == 1) {
-                            if (lane == 0) put_row<FX>(P, yl, yo, to, par, r0 + rl, acc, s_ep + warp, rv, up);
+                            if (lane == 0) put_row<FX>(P, yl, yo, to, par, r0 + rl, acc, s_ep + warp, s_res, up);
                         } else if (lane == 0) {  // this segment's partial (summed below)
                             float* sl = slots + s * P.slot_stride + rl * S * (half ? 2 : 1);
                             sl[sg] = acc;
@@ -854,8 +882,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
                             for (int k = 0; k < S; ++k) v += sl[k];
                             if (FX && half)
                                 for (int k = 0; k < S; ++k) u += sl[S + k];
-                            const float rv = FX ? residual_of(s_ep + warp, r0 + rl, sys, par, P, s_res, rr.x) : 0.0f;
-                            put_row<FX>(P, yl, yo, to, par, r0 + rl, v, s_ep + warp, rv, u);
+                            put_row<FX>(P, yl, yo, to, par, r0 + rl, v, s_ep + warp, s_res, u);
                         }
                     }
                 }
