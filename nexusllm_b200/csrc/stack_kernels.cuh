@@ -542,11 +542,20 @@ __device__ __forceinline__ float stage_x(const float4* xv, const uint32_t* xt,
 // after task through the ring of NS stage slots, never waiting for
 // activations; a gate+up pair (FX) copies the same rows of both matrices into
 // one slot.  It leaves only after its last copies landed, on every path.
+// staged: null, or a shared counter of the x groups the consumers have
+// staged.  With it, the producer issues at most kAheadOfStaging stages of an
+// x group before the consumers staged that group's x: the stages it would
+// otherwise issue as the previous group's last slots free would cross the
+// memory system together with the staging's reads of the group's input and
+// delay them.
+constexpr int kAheadOfStaging = 1;
 template <bool FX>
 __device__ __forceinline__ void stack_producer(const StackParams& P, uint32_t full_bar, uint32_t empty_bar,
-                                               uint32_t stage0, int c, int n_cta) {
+                                               uint32_t stage0, int c, int n_cta,
+                                               const volatile int* staged = nullptr) {
     const int NS = P.n_stages;
     int it = 0, s = 0;
+    int grp = -1, in_grp = 0;  // the x group of task t, and its stages issued so far
     uint32_t phase = 0;
     bool ok = true;
     auto give_up = [&]() {
@@ -565,7 +574,29 @@ __device__ __forceinline__ void stack_producer(const StackParams& P, uint32_t fu
         const int row_begin = rr.x, row_end = rr.y;
         const uint64_t floor16 = total & ~(uint64_t)15;
         const uint64_t span = (uint64_t)R * rb, cta_end = (uint64_t)row_end * rb;
-        for (uint64_t start = (uint64_t)row_begin * rb; start < cta_end; ++it) {
+        if (!__ldg(&T.reuse_x)) {
+            ++grp;
+            in_grp = 0;
+        }
+        for (uint64_t start = (uint64_t)row_begin * rb; start < cta_end; ++it, ++in_grp) {
+            if (staged != nullptr && in_grp >= kAheadOfStaging && *staged <= grp) {
+                // wait (bounded) until the consumers staged this group's x
+                const uint64_t t0 = globaltimer_ns();
+                for (uint32_t k = 1; *staged <= grp; ++k) {
+                    __nanosleep(64);
+                    if ((k & 15u) == 0) {
+                        if (*reinterpret_cast<volatile unsigned*>(P.abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                            give_up();
+                            break;
+                        }
+                    }
+                }
+                if (!ok) break;
+            }
             if (it >= NS && !mbar_try_wait(empty_bar + 8 * s, phase)) {
                 // ring full: wait (sleeping in try_wait) for the slot to drain
                 const uint64_t t0 = globaltimer_ns();
@@ -655,6 +686,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
             mbar_init(empty_bar + 8 * s, kConsumerWarps);
         }
         s_flag[0] = 1;
+        s_flag[1] = 0;  // x groups staged by the consumers (read by the producer)
         for (int k = 0; k < 4; ++k) reinterpret_cast<volatile uint32_t*>(smem + 16 * kMaxStages + 16)[k] = 0;
         fence_mbar_init();
     }
@@ -662,7 +694,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
 
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------- producer
-        if (lane == 0) stack_producer<FX>(P, full_bar, empty_bar, stage0, c, n_cta);
+        // (the fused variant's producer runs ahead freely: its group heads wait on their
+        // norms and residuals too, and the gate measured slower there)
+        if (lane == 0) stack_producer<FX>(P, full_bar, empty_bar, stage0, c, n_cta, FX ? nullptr : s_flag + 1);
         return;
     }
 
@@ -753,6 +787,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_kernel(const Stack
             stop = true;
             break;
         }
+        if (tid == 0) s_flag[1] = s_flag[1] + 1;  // this group's x is staged: the producer may run ahead
         // RMSNorm scale of this group's input: 1 / sqrt(sum x^2 / K + eps)
         // (transformer_ops.hpp:23-30), the warps' sums added in warp order
         float gscale = 1.0f;

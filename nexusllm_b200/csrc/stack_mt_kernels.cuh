@@ -156,6 +156,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_mt_kernel(const St
     float* slots = reinterpret_cast<float*>(smem + kHdr);
     const uint32_t stage0 = sbase + kStackSmemHeader + (uint32_t)P.x_smem;  // after the x staging buffer
 
+    // x groups staged by the consumers (read by the producer, stack_producer)
+    volatile int* s_staged = reinterpret_cast<volatile int*>(smem + 16 * kMaxStages + 4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_cta = gridDim.x, c = blockIdx.x;
     if (threadIdx.x == 0) {
@@ -163,12 +165,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_mt_kernel(const St
             mbar_init(full_bar + 8 * s, 1);
             mbar_init(empty_bar + 8 * s, kConsumerWarps);
         }
+        s_staged[0] = 0;
         fence_mbar_init();
     }
     __syncthreads();
 
     if (warp == kConsumerWarps) {
-        if (lane == 0) stack_producer<false>(P, full_bar, empty_bar, stage0, c, n_cta);
+        if (lane == 0) stack_producer<false>(P, full_bar, empty_bar, stage0, c, n_cta, s_staged);
         return;
     }
 
@@ -221,6 +224,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stack_mt_kernel(const St
             ok = wait_rows_tagged(ld_task_ptr(&P.tasks[after].tg), MT * __ldg(&H.after_rows), par, false, tid,
                                   P.abort_flag, P.wait_polls);
         if (consumer_bar_any(!ok)) break;  // every consumer leaves together after a failed wait
+        if (tid == 0) s_staged[0] = s_staged[0] + 1;  // this group's x is staged: the producer may run ahead
         const int sg = warp % S, grp = warp / S, n_grp = kConsumerWarps / S;
         int wi4[kMaxJ];
         bool has4[kMaxJ];
