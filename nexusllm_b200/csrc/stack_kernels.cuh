@@ -200,15 +200,20 @@ __device__ __forceinline__ void tag_wait_expired(unsigned* abort_flag) {
     atomicExch(abort_flag, 1u);
 }
 // Read 16 words until every one carries this run's parity.  Bounded by an
-// iteration count (P.wait_polls: the stack's wait limit over the ~kTagPollNs
-// a poll takes, so the loop holds one counter, not a clock): false when
-// another CTA raised the abort flag or the polls ran out (raising it and the
-// status bit).
-constexpr uint32_t kTagPollNs = 200;
+// iteration count (P.wait_polls: the stack's wait limit over kTagPollNs, less
+// than any poll takes -- an L2 round trip plus the short sleep -- so the loop
+// holds one counter, not a clock, and gives up no earlier than the limit):
+// false when another CTA raised the abort flag or the polls ran out (raising
+// it and the status bit).  The sleep between polls is short: a poll is
+// already an L2 round trip, and a longer sleep only delays seeing the rows
+// (16 ns in place of 100 ns: 1.322 -> 1.280 ms on the 8B step whose layers
+// depend on each other through their data).
+constexpr uint32_t kTagPollNs = 100;
+constexpr uint32_t kTagPollSleepNs = 16;
 __device__ __forceinline__ bool wait_tagged16(const uint32_t* p, uint32_t par, bool sys, float (&e)[16],
                                               unsigned* abort_flag, uint32_t polls) {
     for (uint32_t k = 0; !ld_tagged16(p, par, sys, e); ++k) {
-        __nanosleep(kTagPollNs / 2);
+        __nanosleep(kTagPollSleepNs);
         if ((k & 7u) == 7u && *reinterpret_cast<volatile unsigned*>(abort_flag)) return false;
         if (k >= polls) {
             tag_wait_expired(abort_flag);
@@ -234,7 +239,7 @@ __device__ __forceinline__ bool wait_rows_tagged(const uint32_t* tg, int n, uint
     for (int i = 4 * tid; i < n; i += 4 * kConsumers) {
         const int m = min(4, n - i);
         for (uint32_t k = 0; !tagged_group_current(tg + i, m, par, sys); ++k) {
-            __nanosleep(kTagPollNs / 2);
+            __nanosleep(kTagPollSleepNs);
             if ((k & 7u) == 7u && *reinterpret_cast<volatile unsigned*>(abort_flag)) return false;
             if (k >= polls) {
                 tag_wait_expired(abort_flag);
@@ -406,7 +411,7 @@ __device__ __forceinline__ uint32_t residual_wait(const uint32_t* p, uint32_t pa
                                                   uint32_t polls) {
     uint32_t w = ld_tagged1(p, sys);
     for (uint32_t k = 0; ((w ^ par) & 1u) != 0; ++k) {
-        __nanosleep(kTagPollNs / 2);
+        __nanosleep(kTagPollSleepNs);
         w = ld_tagged1(p, sys);
         if ((k & 7u) == 7u && *reinterpret_cast<volatile unsigned*>(abort_flag)) break;
         if (k >= polls) {
