@@ -739,16 +739,17 @@ def batched_decode(torch, L, layers, head, stream, dev, timed, args, peak, stack
         out["M4_stack"] = {"ms": round(ms, 3), "tok_s": round(M * 1e3 / ms, 1),
                            "path": "GEMV stack once per token"}
         del g
-    for M in (2, 3, 4, 16, 64):
+    for M in (2, 3, 4, 8, 16, 64):
         out[f"M{M}_tokens_stack"] = tokens_stack(torch, L, layers, head, M, stream, dev, timed, args, peak)
     return out
 
 
 def tokens_stack(torch, L, layers, head, M, stream, dev, timed, args, peak):
-    """configs[3] at M = 2..4 and 16..64 tokens: the headline's task list (same
-    weights, same dependencies) as ONE stack launch per step
+    """configs[3] at M = 2..4, 8 and 16..64 tokens: the headline's task list
+    (same weights, same dependencies) as ONE stack per step
     (nexus_gpu_stack_create_tokens: CUDA cores below 16 tokens, tcgen05 tensor
-    cores from 16): every weight read once for all M tokens.
+    cores from 16): every weight read once for all M tokens (M = 8: two
+    4-token stacks, each weight read twice).
     Parity: 16 sampled rows of the first q, the first o, the last down and the
     LM head of the first and the last token against the C oracle, each fed the
     input the stack gave it."""
@@ -803,7 +804,8 @@ def tokens_stack(torch, L, layers, head, M, stream, dev, timed, args, peak):
     gbs = sb / (ms * 1e-3) / 1e9
     e = max(errs)
     path = ("tcgen05 GEMV stack (persistent, grid barriers at hops), one launch per step" if M >= 16
-            else "multi-token CUDA-core GEMV stack, one launch per step")
+            else "multi-token CUDA-core GEMV stack, one launch per step" if M <= 4
+            else f"{-(-M // 4)} multi-token CUDA-core GEMV stacks of 2-4 tokens per step (weights read {-(-M // 4)}x)")
     return {"ms": round(ms, 3), "tok_s": round(M * 1e3 / ms, 1), "GBs_weights_once": round(gbs, 1),
             "frac": round(gbs / peak, 4), "path": path,
             "parity_max_l2_rel": float(f"{e:.3e}"), "parity_pass": e <= 1e-3}

@@ -240,6 +240,9 @@ NEXUS_GPU_API int32_t nexus_gpu_stack_destroy(void* stack);
  *    multiple of 256; one persistent launch whose CTAs meet at grid barriers
  *    where a task's input changes.  Each task's outputs are within 1e-6 of
  *    nexus_gpu_gemv with `tokens` rows on the same input.
+ *  - tokens 5..15: ceil(tokens / 4) multi-token stacks of 2..4 tokens over
+ *    the same tasks, launched one after another by each run (so every weight
+ *    is read ceil(tokens / 4) times a run); each token's outputs as above.
  *  - tokens = 1 is nexus_gpu_stack_create; other counts are refused.
  * No counterpart in the reference. */
 NEXUS_GPU_API int32_t nexus_gpu_stack_create_tokens(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n_tasks,

@@ -934,6 +934,11 @@ struct StackHandle {
     StackLayout lay;
     std::vector<float*> outputs;        // this rank's output of each task
     std::vector<void*> peer_mappings;   // IPC mappings opened by connect
+    // 5..15 tokens: multi-token stacks of 2..4 tokens each, run one after another
+    // (part k serves tokens [part_tok0[k], part_tok0[k + 1])); no kernel of its own
+    std::vector<StackHandle*> parts;
+    std::vector<int> part_tok0;
+    uint64_t input_cols = 0;
 };
 
 // What a rank publishes to its peers (nexus_gpu_stack_export).
@@ -1017,6 +1022,7 @@ int32_t stack_launch_for(const StackHandle& h, cudaStream_t st) {
 
 void stack_free(StackHandle* h) {
     if (!h) return;
+    for (StackHandle* p : h->parts) stack_free(p);
     int cur = -1;
     cudaGetDevice(&cur);
     if (h->dev >= 0 && cur != h->dev) cudaSetDevice(h->dev);
@@ -1678,6 +1684,9 @@ int32_t stack_wait(void* handle, cudaStream_t st) {
     if (!h) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null handle");
     int32_t rc = stack_current_device(h);
     if (rc) return rc;
+    for (StackHandle* p : h->parts)
+        if ((rc = stack_wait(p, st))) return rc;
+    if (!h->parts.empty()) return NEXUS_GPU_SUCCESS;
     CUDA_TRY(cudaStreamSynchronize(st));
     unsigned aborted = 0;
     CUDA_TRY(cudaMemcpy(&aborted, h->params.abort_flag, sizeof(aborted), cudaMemcpyDeviceToHost));
@@ -1700,6 +1709,9 @@ int32_t stack_run(void* handle, const float* x_in, cudaStream_t st) {
     if (!h->connected) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "sharded stack not connected to its peers");
     int32_t rc = stack_current_device(h);
     if (rc) return rc;
+    for (size_t k = 0; k < h->parts.size(); ++k)  // a split stack: its parts in token order
+        if ((rc = stack_run(h->parts[k], x_in + (size_t)h->part_tok0[k] * h->input_cols, st))) return rc;
+    if (!h->parts.empty()) return NEXUS_GPU_SUCCESS;
     if (h->mma) return mma_stack_launch(*h, x_in, st);
     h->params.x_in = x_in;
     switch (h->dtype) {
@@ -1972,10 +1984,48 @@ NEXUS_GPU_API int32_t nexus_gpu_stack_create(uint32_t dtype, const NexusGpuStack
     return stack_create(dtype, tasks ? ex.data() : nullptr, n_tasks, input_cols, 1, 0, out_stack);
 }
 
+// 5..15 tokens (between the CUDA-core and the tensor-core stacks): ceil(tokens / 4)
+// multi-token stacks of 2..4 tokens each over the same tasks, part k writing its
+// tokens' rows of every y and reading its tokens' rows of the input; a run launches
+// them one after another, so every weight is read ceil(tokens / 4) times a run.
+int32_t stack_create_split(uint32_t dtype, const NexusGpuStackTaskEx* tasks, uint32_t n, uint64_t input_cols,
+                           int tokens, void** out) {
+    if (!out || !tasks || n == 0) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null argument or no tasks");
+    *out = nullptr;
+    const int k = (tokens + kMaxStackTokens - 1) / kMaxStackTokens;
+    auto h = new StackHandle();
+    h->dtype = dtype;
+    h->n_tasks = (int)n;
+    h->tokens = tokens;
+    h->input_cols = input_cols;
+    for (uint32_t i = 0; i < n; ++i) h->outputs.push_back(static_cast<float*>(tasks[i].y));
+    std::vector<NexusGpuStackTaskEx> part(tasks, tasks + n);
+    int tok0 = 0;
+    for (int j = 0; j < k; ++j) {
+        const int m = tokens / k + (j < tokens % k ? 1 : 0);  // 2..4: tokens >= 5 and k = ceil(tokens / 4)
+        for (uint32_t i = 0; i < n; ++i)
+            part[i].y = tasks[i].y ? static_cast<float*>(tasks[i].y) + (size_t)tok0 * tasks[i].rows : nullptr;
+        void* p = nullptr;
+        const int32_t rc = stack_create(dtype, part.data(), n, input_cols, 1, 0, &p, m);
+        if (rc) {
+            stack_free(h);
+            return rc;
+        }
+        h->parts.push_back(static_cast<StackHandle*>(p));
+        h->part_tok0.push_back(tok0);
+        tok0 += m;
+    }
+    h->dev = h->parts[0]->dev;
+    *out = h;
+    return NEXUS_GPU_SUCCESS;
+}
+
 NEXUS_GPU_API int32_t nexus_gpu_stack_create_tokens(uint32_t dtype, const NexusGpuStackTask* tasks, uint32_t n_tasks,
                                                     uint64_t input_cols, uint32_t tokens, void** out_stack) {
     t_last_error.clear();
     const auto ex = plain_tasks(tasks, n_tasks);
+    if (tokens > (uint32_t)kMaxStackTokens && tokens < (uint32_t)kMmaMinTokens)
+        return stack_create_split(dtype, tasks ? ex.data() : nullptr, n_tasks, input_cols, (int)tokens, out_stack);
     return stack_create(dtype, tasks ? ex.data() : nullptr, n_tasks, input_cols, 1, 0, out_stack,
                         tokens > (uint32_t)kMaxTokens ? kMaxTokens + 1 : (int)tokens);
 }
@@ -2028,6 +2078,7 @@ NEXUS_GPU_API int32_t nexus_gpu_stack_set_wait_limit(void* stack, uint64_t limit
     t_last_error.clear();
     StackHandle* h = static_cast<StackHandle*>(stack);
     if (!h) return fail(NEXUS_GPU_ERROR_INVALID_ARGUMENT, "null stack");
+    for (StackHandle* p : h->parts) nexus_gpu_stack_set_wait_limit(p, limit_ns);
     h->params.wait_ns = limit_ns ? limit_ns : kWaitLimitNs;
     h->params.wait_polls = (uint32_t)std::min<uint64_t>(h->params.wait_ns / kTagPollNs + 1, UINT32_MAX);
     return NEXUS_GPU_SUCCESS;

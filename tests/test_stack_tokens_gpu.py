@@ -1,5 +1,6 @@
 """GPU tests of multi-token GEMV stacks (nexus_gpu_stack_create_tokens): a
-decode step's GEMVs for 2-4 requests in one launch, every weight read once.
+decode step's GEMVs for 2-4 requests in one launch, every weight read once
+(5-15 requests: several such stacks, one after another, in one run).
 
 Per token, every task's output must stay within the 1e-3 L2-relative GEMV
 tolerance of the C oracle (fed the input the stack gave that task) and agree
@@ -64,7 +65,8 @@ def status_clean(L):
 @pytest.mark.parametrize("dt,tokens,hidden,kv,ffn", [(7, 4, 4096, 1024, 14336), (7, 2, 2048, 512, 5632),
                                                      (7, 3, 2048, 512, 5632), (9, 4, 2048, 512, 5632),
                                                      (9, 2, 4096, 1024, 14336), (12, 4, 2048, 512, 5632),
-                                                     (11, 2, 2048, 512, 5632)])
+                                                     (11, 2, 2048, 512, 5632), (7, 6, 2048, 512, 5632),
+                                                     (7, 11, 2048, 512, 5632), (9, 15, 2048, 512, 5632)])
 def test_tokens_stack_matches_oracle_and_single_token_stack(L, port, dt, tokens, hidden, kv, ffn):
     spec = layer_tasks(hidden, kv, ffn, layers=2, head_rows=3000)
     h, h1, Ws, ys, ys1 = build(L, dt, spec, 900 + dt, tokens)
@@ -133,7 +135,7 @@ def test_tokens_stack_refuses_bad_arguments(L):
     y = torch.empty(8 * 64, device="cuda")
     arr = (_native.StackTask * 1)(_native.StackTask(W.data_ptr(), 64, 1024, y.data_ptr(), -1, -1))
     h = ctypes.c_void_p()
-    for tokens in (0, 5, 1 << 31):
+    for tokens in (0, 65, 1 << 31):
         assert L.nexus_gpu_stack_create_tokens(7, arr, 1, 1024, tokens, ctypes.byref(h)) != 0
         assert b"tokens" in L.nexus_gpu_last_error()
     # tokens = 1 is the plain stack
