@@ -135,8 +135,11 @@ def test_mma_stack_refuses_shapes_outside_the_path(L):
     y = torch.empty(64 * 256, device="cuda")
     h = ctypes.c_void_p()
     arr = (_native.StackTask * 1)(_native.StackTask(W.data_ptr(), 256, 1024, y.data_ptr(), -1, -1))
-    for tokens in (5, 15, 65):
+    for tokens in (0, 65):
         assert L.nexus_gpu_stack_create_tokens(7, arr, 1, 1024, tokens, ctypes.byref(h)) != 0
+    for tokens in (5, 15):  # below the tensor-core range: several CUDA-core stacks, not this path
+        assert L.nexus_gpu_stack_create_tokens(7, arr, 1, 1024, tokens, ctypes.byref(h)) == 0, L.nexus_gpu_last_error()
+        L.nexus_gpu_stack_destroy(h)
     W8 = synth.blocks_torch(9, 256, 1024, 6)
     arr8 = (_native.StackTask * 1)(_native.StackTask(W8.data_ptr(), 256, 1024, y.data_ptr(), -1, -1))
     assert L.nexus_gpu_stack_create_tokens(9, arr8, 1, 1024, 16, ctypes.byref(h)) != 0  # Q4_0 only
