@@ -67,5 +67,26 @@ def test_device_api_rejects_null_or_reports_no_device(L):
     assert rc in (-9, -101), rc
 
 
+def test_stack_token_counts_checked_before_the_device(L):
+    # 0 and > 64 tokens are refused as arguments on any machine; 5..15 tokens
+    # (split into multi-token stacks of 2..4) get as far as the device: NO_DEVICE
+    # without a GPU, never an argument error
+    T = _native.StackTask
+    arr = (T * 1)(T(16, 64, 64, None, -1, -1))
+    h = ctypes.c_void_p()
+    for tokens in (0, 65):
+        assert L.nexus_gpu_stack_create_tokens(7, arr, 1, 64, tokens, ctypes.byref(h)) == -9
+        assert b"tokens" in L.nexus_gpu_last_error()
+    try:
+        import torch
+        has_gpu = torch.cuda.is_available()
+    except ImportError:
+        has_gpu = False
+    if not has_gpu:
+        for tokens in (5, 8, 15):
+            assert L.nexus_gpu_stack_create_tokens(7, arr, 1, 64, tokens, ctypes.byref(h)) == -101
+            assert h.value is None
+
+
 def test_version(L):
     assert L.nexus_gpu_version().startswith(b"nexus_gpu")
